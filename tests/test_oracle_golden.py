@@ -1,0 +1,103 @@
+"""Pin the CPU oracle to the reference's own outputs (fixtures from tests/golden/make_golden.py).
+
+Bit-exact for codes, E4M3 scale bytes, global scales, packing and the SF swizzle;
+fp32 tolerance for the GEMM and the emulated attention (matmul order differs).
+Mirrors the reference's known-answer tests: tests/test_format.py:5-17, test_pack.py:5-22,
+test_quant.py:5-26, test_four_over_six.py:16-77 of Dev-Jahn/vit-nvfp4.
+"""
+import numpy as np
+import pytest
+
+from conftest import oracle, golden
+
+
+def test_e2m1_rounding_points():
+    g = golden()
+    assert np.array_equal(oracle.round_to_e2m1_code(g["e2m1_in"]), g["e2m1_codes"])
+
+
+def test_e2m1_known_answers():
+    # reference tests/test_format.py:13-17
+    x = np.array([0.6, 0.8, 1.2, 5.5, 7.0, -0.6], np.float32)
+    val = oracle.code_to_value(oracle.round_to_e2m1_code(x))
+    assert np.allclose(val, [0.5, 1.0, 1.0, 6.0, 6.0, -0.5])
+    grid = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -.5, -1, -1.5, -2, -3, -4, -6], np.float32)
+    assert np.array_equal(oracle.code_to_value(oracle.round_to_e2m1_code(grid)), grid)
+
+
+def test_e4m3_rne_matches_torch():
+    g = golden()
+    assert np.array_equal(oracle.e4m3_encode(g["e4m3_in"]), g["e4m3_bits"])
+    # decode round trip over every finite byte
+    finite = np.array([b for b in range(256) if (b & 0x7F) != 0x7F], np.uint8)
+    assert np.array_equal(oracle.e4m3_encode(oracle.e4m3_decode(finite)), finite)
+
+
+def test_mean16_order_matches_aten():
+    g = golden()
+    assert np.array_equal(oracle.mean16_aten(g["mean_in"]), g["mean_out"])
+
+
+@pytest.mark.parametrize("name", list(golden()["q_cases"]))
+def test_quantize_bit_exact(name):
+    g = golden()
+    x = g[f"q_{name}_x"]
+    mse, static, bf16 = g[f"q_{name}_meta"]
+    if int(bf16):
+        x = oracle.from_bf16_bits(x)
+    c, b, gs = oracle.quantize_to_nvfp4(x, 16, global_scale=None if static < 0 else np.float32(static),
+                                       block_select="mse" if mse else "six")
+    assert np.float32(gs).tobytes() == np.float32(g[f"q_{name}_gs"]).tobytes()
+    assert np.array_equal(b, g[f"q_{name}_bs"]), (b != g[f"q_{name}_bs"]).sum()
+    assert np.array_equal(c, g[f"q_{name}_codes"]), (c != g[f"q_{name}_codes"]).sum()
+
+
+def test_pack_and_swizzle_bit_exact():
+    g = golden()
+    assert np.array_equal(oracle.pack_e2m1(g["pack_codes"]), g["pack_packed"])
+    assert np.array_equal(oracle.unpack_e2m1(g["pack_packed"]), g["pack_codes"])
+    # reference tests/test_pack.py:12-15 nibble order
+    assert oracle.pack_e2m1(np.array([[1, 2, 3, 4]], np.uint8)).tolist() == [[0x21, 0x43]]
+    for R, C in [(1, 1), (17, 3), (128, 4), (130, 5), (300, 48)]:
+        blk = oracle.to_blocked(g[f"blk_{R}x{C}_in"])
+        assert np.array_equal(blk, g[f"blk_{R}x{C}_out"])
+        assert np.array_equal(oracle.from_blocked(blk, R, C), g[f"blk_{R}x{C}_in"])
+
+
+def test_gemm_reference_matches():
+    g = golden()
+    aq = oracle.quantize_to_nvfp4(g["gemm_a"], 16)
+    bq = oracle.quantize_to_nvfp4(g["gemm_b"], 16, block_select="mse")
+    out = oracle.gemm_reference(*aq, *bq)
+    ref = g["gemm_out"]
+    assert np.abs(out - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("name", ["s20d64", "s33d80"])
+@pytest.mark.parametrize("mode", ["nvfp4", "fp8", "bf16"])
+def test_quant_sdpa_matches(name, mode):
+    g = golden()
+    out = oracle.quant_sdpa(g[f"att_{name}_q"], g[f"att_{name}_k"], g[f"att_{name}_v"], qk=mode, pv=mode)
+    ref = g[f"att_{name}_{mode}_{mode}"]
+    # the qdq codes are bit-exact; only fp32 matmul/softmax order differs
+    assert np.abs(out - ref).max() <= 2e-5 * max(1.0, np.abs(ref).max())
+
+
+def test_fp8_qdq_matches():
+    g = golden()
+    assert np.allclose(oracle.fp8_e4m3_quant_dequant(g["fp8_in"]), g["fp8_out"], rtol=0, atol=1e-6)
+
+
+def test_four_over_six_invariants():
+    # reference tests/test_four_over_six.py:16-61 restated on the oracle
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal((128, 768)) * 0.1).astype(np.float32)
+    x[0, :16] += (rng.standard_normal(16) * 2.0).astype(np.float32)
+    c6, b6, g6 = oracle.quantize_to_nvfp4(x, 16, block_select="six")
+    cm, bm, gm = oracle.quantize_to_nvfp4(x, 16, block_select="mse")
+    amax = np.abs(x).max()
+    assert np.isclose(g6, amax / 2688.0) and np.isclose(gm, amax / 1536.0)
+    xb = x.reshape(128, 48, 16)
+    mse6 = ((oracle.dequantize_nvfp4(c6, b6, g6).reshape(xb.shape) - xb) ** 2).mean()
+    msem = ((oracle.dequantize_nvfp4(cm, bm, gm).reshape(xb.shape) - xb) ** 2).mean()
+    assert msem < mse6
