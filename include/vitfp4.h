@@ -1,0 +1,121 @@
+/*
+ * vitfp4 — C ABI of the B200 (sm_100a) NVFP4 W4A4 ViT hot path (libvitfp4.so).
+ *
+ * Conventions (every entry point):
+ *   - plain pointers and sizes, no framework types; all data pointers are DEVICE pointers
+ *     owned by the caller (outputs pre-allocated by the caller);
+ *   - the CUDA stream is the last argument; every call is asynchronous on that stream;
+ *   - the return value is a vf4_status (0 = ok); vf4_last_error_string() describes the
+ *     last failure of the calling thread; nothing throws across the ABI;
+ *   - no entry point allocates device memory.
+ *
+ * Layouts:
+ *   packed codes : (rows, K/2) uint8, two E2M1 codes per byte, low nibble = even column
+ *   swizzled SF  : the 128x4-tiled E4M3 block-scale layout ("to_blocked"):
+ *                  padded to (ceil128(rows), ceil4(K/16)); tile (rb,cb) at (rb*nCB+cb)*512;
+ *                  element (r,c) of a tile at (r%32)*16 + (r/32)*4 + c
+ *   linear SF    : (rows, K/16) uint8 E4M3 bytes, row-major
+ *   global scale : one fp32 in device memory; decode x = e2m1 * e4m3 * gs
+ *
+ * The reference (Dev-Jahn/vit-nvfp4) is pure Python; each function below replaces the
+ * Python/Triton/cuBLASLt call named beside it (file:line in the reference project).
+ */
+#ifndef VITFP4_H_
+#define VITFP4_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VF4_API __attribute__((visibility("default")))
+#else
+#define VF4_API
+#endif
+
+typedef struct CUstream_st* vf4_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  VF4_OK = 0,
+  VF4_ERR_ARG = 1,         /* bad size / mode / null pointer */
+  VF4_ERR_ALIGN = 2,       /* pointer or leading dimension misaligned for the kernel */
+  VF4_ERR_ARCH = 3,        /* device is not sm_100 */
+  VF4_ERR_LAUNCH = 4,      /* kernel launch failed */
+  VF4_ERR_CUDA = 5,        /* other CUDA runtime/driver error */
+  VF4_ERR_UNSUPPORTED = 6, /* shape outside what the kernels implement */
+  VF4_ERR_DEVICE = 7       /* a kernel recorded a device-side timeout */
+} vf4_status;
+
+typedef enum { VF4_BF16 = 0, VF4_F32 = 1 } vf4_dtype;
+typedef enum { VF4_SIX = 0, VF4_MSE = 1 } vf4_block_select;
+typedef enum {
+  VF4_EPI_NONE = 0,      /* out = gs_a*gs_b*acc                                   */
+  VF4_EPI_BIAS = 1,      /* out = gs_a*gs_b*acc + bias                            */
+  VF4_EPI_GELU_NVFP4 = 2 /* h = GELU(bf16(gs_a*gs_b*acc + bias)); NVFP4-cast h    */
+} vf4_epilogue;
+
+/* Library version (major*10000 + minor*100 + patch). */
+VF4_API int vf4_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+VF4_API const char* vf4_last_error_string(void);
+
+/* Read (and optionally clear) the device-side error word of every kernel family
+ * (0 = none; otherwise a kernel gave up on a bounded wait). Synchronizes the device. */
+VF4_API int vf4_device_error(int clear);
+
+/* max|x| (or max|GELU(x)| when gelu != 0) over n elements, written to *amax_out.
+ * Replaces the amax pass inside quant.py:48-49 and fused_mlp.py:25-29. */
+VF4_API int vf4_amax(const void* x, int dtype, int64_t n, int gelu, float* amax_out, vf4_stream_t stream);
+
+/* *gs_out = max(*amax, 1e-12) / (6 * (block_select == VF4_MSE ? 256 : 448)).
+ * Replaces quant.py:48-53. amax and gs_out may alias. */
+VF4_API int vf4_global_scale(const float* amax, int block_select, float* gs_out, vf4_stream_t stream);
+
+/* NVFP4 activation / weight cast, bit-exact to quantize_to_nvfp4 + pack_e2m1 + to_blocked
+ * (quant.py:20-69, pack.py:4-9, pack.py:39-58) and the fused GELU cast of
+ * triton_cast.py:138 (cast_nvfp4) with the quant.py arithmetic.
+ *   x        : (M, K) rows of stride ld elements, dtype VF4_BF16 or VF4_F32, K % 16 == 0
+ *   gs       : device fp32 global scale to use (static), or NULL for dynamic: the amax of
+ *              the (GELU'd, biased) input is computed first and the scale written to gs_out
+ *   bias     : optional (K,) vector of the same dtype added before GELU / quantization
+ *   out_packed (M, K/2); out_sf_swizzled (ceil128(M)*ceil4(K/16) bytes, pads zeroed) and/or
+ *   out_sf_linear (M, K/16) — either may be NULL; gs_out (1 fp32) receives the scale used
+ *   (may be NULL when gs != NULL). */
+VF4_API int vf4_cast_nvfp4(const void* x, int dtype, int64_t M, int64_t K, int64_t ld, const float* gs,
+                   int block_select, int gelu, const void* bias, uint8_t* out_packed,
+                   uint8_t* out_sf_swizzled, uint8_t* out_sf_linear, float* gs_out,
+                   vf4_stream_t stream);
+
+/* pack_e2m1 (pack.py:4-9): codes (rows, K) -> (rows, K/2). K % 2 == 0. */
+VF4_API int vf4_pack_e2m1(const uint8_t* codes, int64_t rows, int64_t K, uint8_t* out, vf4_stream_t stream);
+
+/* unpack_e2m1 (pack.py:12-16): (rows, Kh) -> (rows, 2*Kh). */
+VF4_API int vf4_unpack_e2m1(const uint8_t* packed, int64_t rows, int64_t Kh, uint8_t* out,
+                    vf4_stream_t stream);
+
+/* to_blocked (pack.py:39-58): (R, C) E4M3 bytes -> ceil128(R)*ceil4(C) swizzled bytes. */
+VF4_API int vf4_to_blocked(const uint8_t* sf, int64_t R, int64_t C, uint8_t* out, vf4_stream_t stream);
+
+/* Block-scaled FP4 GEMM on tcgen05 tensor cores (replaces torch._scaled_mm_v2 in
+ * backends/torch_scaled_mm.py:14-46 and the emulation of backends/reference.py:6-10):
+ *   acc[m,n] = sum_k A[m,k]*B[n,k] (E2M1 x E4M3 block scales), fp32 accumulate;
+ *   A packed (M, K/2) + swizzled SF, B packed (N, K/2) + swizzled SF, a_gs/b_gs device fp32.
+ * epilogue VF4_EPI_NONE / VF4_EPI_BIAS write `out` (M, N) in out_dtype (bias: (N,) bf16);
+ * VF4_EPI_GELU_NVFP4 (the fused fc1 epilogue of fused_mlp.py:47-51) writes out_packed
+ * (M, N/2) and out_sf (swizzled, ceil128(M) x N/16) quantized with the static global
+ * scale epi_gs (six rule), and ignores `out`.
+ * Requirements: K % 32 == 0, N % 16 == 0 (N % 64 == 0 for VF4_EPI_GELU_NVFP4), 16-byte
+ * aligned pointers. */
+VF4_API int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                   const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs, int64_t M,
+                   int64_t N, int64_t K, const void* bias, int epilogue, void* out, int out_dtype,
+                   const float* epi_gs, uint8_t* out_packed, uint8_t* out_sf, vf4_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VITFP4_H_ */

@@ -1,0 +1,128 @@
+"""GPU parity of the tcgen05 block-scaled FP4 GEMM against the oracle (the reference's fp32
+emulated GEMM, backends/reference.py:6-10).
+
+Tolerances (fp32 accumulation order differs from the emulation, operands are identical):
+  fp32 out: max |out - ref| <= 1e-3 * max|ref| and cosine >= 0.9999
+  bf16 out: cosine >= 0.9999 and max error <= 1 bf16 ulp of max|ref| (2^-7 relative)
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import oracle
+from gpu_util import cos, oracle_operand, to_cuda_operand, vit_activation
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from vitfp4.nvfp4 import ops
+    return ops
+
+
+def _operands(M, N, K, seed=0, a_mode="six", b_mode="mse", dist="normal"):
+    rng = np.random.default_rng(seed)
+    a = vit_activation(M, K, seed=seed)
+    if dist == "heavy":
+        a = a * rng.exponential(0.5, size=a.shape).astype(np.float32)
+    elif dist == "outlier":
+        a[:2] *= 30.0
+    b = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    A = oracle_operand(a, a_mode)
+    B = oracle_operand(b, b_mode)
+    return A, B
+
+
+def _gemm_cuda(A, B, out_dtype=torch.float32, bias=None):
+    ops = _ops()
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    bt = None if bias is None else torch.from_numpy(bias).cuda().to(torch.bfloat16)
+    out = ops.gemm(ap, asf, ag, bp, bsf, bg, bias=bt, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+SHAPES = [  # (M, K, N)
+    (128, 64, 128), (256, 512, 768), (256, 1024, 1024), (1024, 1152, 4304), (512, 1408, 6144),
+    (17, 512, 768), (100, 1024, 4096), (197, 768, 2304), (333, 3072, 768), (64, 256, 64),
+    (130, 96, 144), (1, 32, 16), (257, 1024, 3072),
+]
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_gemm_fp32_matches_emulation(M, K, N):
+    A, B = _operands(M, N, K, seed=M + N + K)
+    out = _gemm_cuda(A, B)
+    ref = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    err = np.abs(out - ref).max() / max(np.abs(ref).max(), 1e-30)
+    assert not (out == 0).all()
+    assert err <= 1e-3 and cos(out, ref) >= 0.9999, (err, cos(out, ref))
+
+
+@pytest.mark.parametrize("dist", ["normal", "heavy", "outlier"])
+def test_gemm_distributions(dist):
+    A, B = _operands(256, 1024, 1024, seed=11, dist=dist)
+    out = _gemm_cuda(A, B)
+    ref = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    assert cos(out, ref) >= 0.9999
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 512, 768), (197, 1024, 3072), (100, 256, 128)])
+def test_gemm_bf16_bias(M, K, N):
+    A, B = _operands(M, N, K, seed=5)
+    bias = (np.random.default_rng(2).standard_normal(N) * 0.1).astype(np.float32)
+    out = _gemm_cuda(A, B, out_dtype=torch.bfloat16, bias=bias)
+    ref = oracle.to_bf16(oracle.to_bf16(oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2]))
+                         + oracle.to_bf16(bias))
+    assert cos(out, ref) >= 0.9999
+    assert np.abs(out - ref).max() <= 2.0 ** -7 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 4096), (197, 768, 3072), (130, 512, 128)])
+def test_gemm_gelu_nvfp4_epilogue(M, K, N):
+    """fc1 epilogue: NVFP4(GELU(bf16(bf16(gemm) + b1))) with a static global scale."""
+    ops = _ops()
+    A, B = _operands(M, N, K, seed=7)
+    bias = (np.random.default_rng(3).standard_normal(N) * 0.1).astype(np.float32)
+    ref_y = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    h = oracle.gelu(oracle.to_bf16(oracle.to_bf16(ref_y) + oracle.to_bf16(bias)))
+    gh = np.float32(np.abs(h).max() / 2688.0)
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, torch.from_numpy(bias).cuda().bfloat16(),
+                                  torch.tensor(gh, device="cuda"))
+    torch.cuda.synchronize()
+    c, b, _ = oracle.quantize_to_nvfp4(h, 16, global_scale=gh)
+    codes = oracle.unpack_e2m1(hp.cpu().numpy())
+    sf = oracle.from_blocked(hsf.cpu().numpy(), M, N // 16)
+    # accumulation order can move a value across a rounding boundary: require near-identity
+    assert (codes != c).mean() < 2e-3, (codes != c).mean()
+    assert (sf != b).mean() < 2e-3, (sf != b).mean()
+    deq = oracle.dequantize_nvfp4(codes, sf, gh)
+    assert cos(deq, oracle.dequantize_nvfp4(c, b, gh)) >= 0.999
+    # padded scale rows of the last 128-row tile are zero
+    full = hsf.cpu().numpy()
+    pad = oracle.from_blocked(full, (M + 127) // 128 * 128, N // 16)[M:]
+    assert (pad == 0).all()
+
+
+def test_gemm_full_size_sampled_rows():
+    """BASELINE config-2 fc2 shape (M=50432, K=3072, N=768): parity on sampled output rows."""
+    ops = _ops()
+    M, K, N = 50432, 3072, 768
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02)
+    ap, asf, _, ag = ops.cast(x, None, "six")
+    wp, wsf, wl, wg = ops.cast(w, None, "mse", linear=True)
+    out = ops.gemm(ap, asf, ag, wp, wsf, wg, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    rows = torch.randint(0, M, (48,), generator=torch.Generator().manual_seed(2))
+    a_codes = oracle.unpack_e2m1(ap[rows.cuda()].cpu().numpy())
+    a_bs = oracle.from_blocked(asf.cpu().numpy(), M, K // 16)[rows.numpy()]
+    b_codes = oracle.unpack_e2m1(wp.cpu().numpy())
+    ref = oracle.gemm_reference(a_codes, a_bs, np.float32(ag.item()), b_codes, wl.cpu().numpy(),
+                                np.float32(wg.item()))
+    got = out[rows.cuda()].cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-3 * np.abs(ref).max()

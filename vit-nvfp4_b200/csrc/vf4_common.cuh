@@ -1,0 +1,305 @@
+// Shared device helpers for the sm_100a NVFP4 kernels: exact fp32 arithmetic for the
+// quantizer, E4M3/E2M1 encoders, mbarrier / TMA / tcgen05 inline PTX with bounded waits.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vitfp4.h"
+
+#define VF4_DEV __device__ __forceinline__
+
+// A wait that exceeds this many nanoseconds of %globaltimer sets the device error word
+// and returns false, so a kernel never spins forever on the shared GPU.
+#ifndef VF4_WAIT_TIMEOUT_NS
+#define VF4_WAIT_TIMEOUT_NS 4000000000ull
+#endif
+
+namespace vf4 {
+
+// ---------------------------------------------------------------------------------------
+// Device error word (one per translation unit; read through the TU's *_device_error()).
+// ---------------------------------------------------------------------------------------
+enum DevErr : int {
+  kDevErrNone = 0,
+  kDevErrTimeoutFull = 1,     // producer data never arrived
+  kDevErrTimeoutEmpty = 2,    // consumer never released a stage
+  kDevErrTimeoutTmem = 3,     // accumulator hand-off timed out
+  kDevErrTimeoutDrain = 4,    // final drain of async tensor-core work timed out
+  kDevErrTimeoutOther = 5,
+};
+
+VF4_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------
+// Numeric formats
+// ---------------------------------------------------------------------------------------
+// fp32 -> E4M3 (float8_e4m3fn) bits, round-to-nearest-even with saturation to +-448.
+VF4_DEV uint32_t f32_to_e4m3(float x) {
+  __nv_fp8_storage_t r = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  return (uint32_t)r;
+}
+
+VF4_DEV float e4m3_to_f32(uint32_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(*reinterpret_cast<__half*>(&h));
+}
+
+// E2M1 code of q with the reference's rounding: ties go to the smaller magnitude,
+// NaN/+-inf saturate to index 7 (fminf(NaN, 6) == 6).
+VF4_DEV uint32_t e2m1_code(float q) {
+  uint32_t s = q < 0.f ? 8u : 0u;
+  float m = fminf(fabsf(q), 6.f);
+  uint32_t i = (uint32_t)(m > 0.25f) + (uint32_t)(m > 0.75f) + (uint32_t)(m > 1.25f) +
+               (uint32_t)(m > 1.75f) + (uint32_t)(m > 2.5f) + (uint32_t)(m > 3.5f) +
+               (uint32_t)(m > 5.0f);
+  return s | i;
+}
+
+VF4_DEV float e2m1_value(uint32_t c) {
+  // magnitudes {0,.5,1,1.5,2,3,4,6}
+  uint32_t i = c & 7u;
+  float m = i < 4 ? 0.5f * (float)i : (i == 7 ? 6.f : (float)(i - 2));
+  return (c & 8u) ? -m : m;
+}
+
+// Exact erf-GELU (0.5*x*(1+erf(x/sqrt2))) using CUDA's erff.
+VF4_DEV float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+}
+
+VF4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// ---------------------------------------------------------------------------------------
+// Quantize one 16-element block exactly as the reference quantizer (RTN "six" or
+// Four-Over-Six "mse").  v: fp32 values; gs: global scale; s_enc = 1/gs.
+// Returns the 8 packed bytes (low nibble = even element) and the E4M3 scale byte.
+// ---------------------------------------------------------------------------------------
+struct BlockQ {
+  uint64_t packed;
+  uint32_t sf;
+};
+
+VF4_DEV void encode_candidate(const float* v, float amax, float divisor, float s_enc, float gs,
+                              uint32_t* codes, uint32_t* sf, float* dec_out) {
+  float bs_f = fminf(__fmul_rn(__fdiv_rn(amax, divisor), s_enc), 448.f);
+  uint32_t b = f32_to_e4m3(bs_f);
+  float dec = __fmul_rn(e4m3_to_f32(b), gs);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) codes[i] = e2m1_code(__fdiv_rn(v[i], dec));
+  *sf = b;
+  *dec_out = dec;
+}
+
+VF4_DEV float block_mse_aten(const float* v, const uint32_t* codes, float dec) {
+  float e[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float d = __fsub_rn(__fmul_rn(e2m1_value(codes[i]), dec), v[i]);
+    e[i] = __fmul_rn(d, d);
+  }
+  float s = __fadd_rn(e[0], e[8]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) s = __fadd_rn(s, __fadd_rn(e[i], e[i + 8]));
+  return __fdiv_rn(s, 16.f);
+}
+
+template <bool kMse>
+VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, 1e-12f);
+  uint32_t c6[16], sf6;
+  float dec6;
+  encode_candidate(v, amax, 6.f, s_enc, gs, c6, &sf6, &dec6);
+  BlockQ r;
+  if constexpr (kMse) {
+    uint32_t c4[16], sf4;
+    float dec4;
+    encode_candidate(v, amax, 4.f, s_enc, gs, c4, &sf4, &dec4);
+    bool pick4 = block_mse_aten(v, c4, dec4) < block_mse_aten(v, c6, dec6);
+    uint64_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p |= (uint64_t)(pick4 ? c4[i] : c6[i]) << (4 * i);
+    r.packed = p;
+    r.sf = pick4 ? sf4 : sf6;
+  } else {
+    uint64_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p |= (uint64_t)c6[i] << (4 * i);
+    r.packed = p;
+    r.sf = sf6;
+  }
+  return r;
+}
+
+// Offset of scale factor (row r, column c) inside the 128x4-tiled ("to_blocked") layout.
+VF4_DEV int64_t sf_swizzle_offset(int64_t r, int64_t c, int64_t n_col_blocks) {
+  return ((r >> 7) * n_col_blocks + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
+}
+
+// ---------------------------------------------------------------------------------------
+// Shared memory, mbarrier and TMA helpers
+// ---------------------------------------------------------------------------------------
+VF4_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+VF4_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+VF4_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+VF4_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+VF4_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+VF4_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+VF4_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (after recording `code` in *err) if the phase never completes.
+VF4_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*(volatile int*)err != 0) return false;  // another role already gave up
+      if (globaltimer() - t0 > VF4_WAIT_TIMEOUT_NS) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+VF4_DEV void tma_prefetch(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+VF4_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* m, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Plain (non-tensor) bulk copy global -> shared; dst/src 16B aligned, bytes % 16 == 0.
+VF4_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor core) helpers
+// ---------------------------------------------------------------------------------------
+VF4_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+VF4_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+VF4_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+VF4_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+VF4_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Arrive on an mbarrier once all previously issued tcgen05 async ops of this thread finish.
+VF4_DEV void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// Block-scaled FP4 MMA: D[tmem] (+)= A[smem] * B[smem]^T with UE4M3 scales (16-element
+// vectors) read from tensor memory.  M=128, N from the instruction descriptor, K=64.
+VF4_DEV void mma_mxf4nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], "
+      "[%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Copy a 32-row x 16-byte matrix from shared memory into tensor memory, replicated into
+// all four 32-lane sub-partitions (the scale-factor staging the MMA expects).
+VF4_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+VF4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+VF4_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format).
+//   layout 2 = 128-byte swizzle (K-major operand tiles written by TMA SWIZZLE_128B),
+//   layout 0 = no swizzle (scale-factor staging for tcgen05.cp).
+VF4_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::mxf4nvf4: A/B E2M1, UE4M3 scales, K-major A and B,
+// M=128, N=n (multiple of 16, <= 256), dense, K=64.
+__host__ __device__ constexpr uint32_t idesc_mxf4nvf4(uint32_t n) {
+  return (1u << 7)             // A format: E2M1
+         | (1u << 10)          // B format: E2M1
+         | ((n >> 3) << 17)    // N >> 3
+         | (0u << 23)          // scale type UE4M3
+         | ((128u >> 4) << 24);  // M >> 4
+}
+
+}  // namespace vf4

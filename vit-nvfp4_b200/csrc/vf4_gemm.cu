@@ -1,0 +1,442 @@
+// Block-scaled NVFP4 GEMM on sm_100a tensor cores (tcgen05.mma kind::mxf4nvf4).
+//
+//   D[m, n] = gs_a * gs_b * sum_k A[m, k] * B[n, k]      (E2M1 operands, UE4M3 scales / 16)
+//
+// Replaces torch._scaled_mm_v2 (BlockWise1x16 + TensorWise) used by the reference in
+// src/vit_nvfp4/nvfp4/backends/torch_scaled_mm.py:14-46, and fuses the bias add
+// (gemm.py:36-37) and the fc1 "+b1 -> GELU -> NVFP4 cast" step (fused_mlp.py:47-51).
+//
+// Structure (persistent, one CTA per SM, 320 threads):
+//   warp 0      TMA producer: A/B tiles (128-byte swizzle) + the tile's 512-byte scale atoms
+//               (plain bulk copies: the operand scale layout is already the MMA's layout)
+//   warp 1      TMEM allocator and MMA issuer: tcgen05.cp scale atoms -> TMEM, one
+//               tcgen05.mma per K=64 block, tcgen05.commit releases smem stages / hands
+//               the accumulator to the epilogue
+//   warps 2..9  epilogue: tcgen05.ld the 128 x BN fp32 accumulator (two warps per TMEM lane
+//               quadrant, each half of the columns), release TMEM, then scale / bias /
+//               GELU / NVFP4-quantize from registers and store
+// Every wait is bounded (mbar_wait); a timeout records a device error and unwinds.
+#include "vf4_common.cuh"
+#include "vf4_host.h"
+
+namespace vf4 {
+
+static __device__ int g_gemm_err;
+
+int gemm_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int KB_PER_STAGE = 4;                   // 4 x K64 MMAs = 256 elements = 128 B
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int SFA_BYTES = KB_PER_STAGE * 512;
+  static constexpr int SFB_BYTES = (BN / 128) * KB_PER_STAGE * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int ACC_STAGES = BN == 256 ? 1 : 2;
+  static constexpr int SFA_TCOL = 256;                      // TMEM columns of the scale slots
+  static constexpr int SFA_SLOT = KB_PER_STAGE * 4;         // 4 columns per K64 block (M=128)
+  static constexpr int SFB_TCOL = SFA_TCOL + 2 * SFA_SLOT;
+  static constexpr int SFB_PER_KB = BN / 32;                // 4 (N=128) or 8 (N=256) columns
+  static constexpr int SFB_SLOT = KB_PER_STAGE * SFB_PER_KB;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 320;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 16;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(ACC_STAGES * BN <= SFA_TCOL, "accumulators overlap the scale slots");
+  static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment");
+};
+
+struct GemmParams {
+  const uint8_t* a_sf;
+  const uint8_t* b_sf;
+  const float* a_gs;
+  const float* b_gs;
+  int M, N, K;
+  int n_kb;     // ceil(K / 64): K64 blocks == scale column-blocks of A and B
+  int n_rb_b;   // ceil(N / 128): scale row-blocks of B
+  int tiles_m, tiles_n;
+  const __nv_bfloat16* bias;
+  void* out;
+  const float* epi_gs;
+  uint8_t* out_packed;
+  uint8_t* out_sf;
+  int out_ncb;  // scale column-blocks of the NVFP4 output (N / 64)
+};
+
+template <int BN, int EPI, bool kF32>
+__global__ void __launch_bounds__(320, 1)
+    gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmParams p) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + C::ACC_STAGES + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 2 * C::ACC_STAGES);
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 2 * C::ACC_STAGES + 1));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = &g_gemm_err;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < C::ACC_STAGES; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int n_st = (p.n_kb + C::KB_PER_STAGE - 1) / C::KB_PER_STAGE;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int mb = tile / p.tiles_n, nb = tile - mb * p.tiles_n;
+        for (int st = 0; st < n_st; ++st, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int kb0 = st * C::KB_PER_STAGE;
+          const int nkb = min(C::KB_PER_STAGE, p.n_kb - kb0);
+          const uint32_t sf_bytes = (uint32_t)nkb * 512u;
+          mbar_arrive_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES + sf_bytes * (1 + BN / 128));
+          const uint32_t sa = base + s * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t ssfa = sb + C::B_BYTES;
+          const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          tma_load_2d(sa, &tmA, st * 128, mb * 128, full_bar(s));
+          tma_load_2d(sb, &tmB, st * 128, nb * BN, full_bar(s));
+          bulk_load(ssfa, p.a_sf + ((int64_t)mb * p.n_kb + kb0) * 512, sf_bytes, full_bar(s));
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j) {
+            int rb = nb * (BN / 128) + j;
+            if (rb >= p.n_rb_b) rb = nb * (BN / 128);  // N tail: finite stand-in, columns discarded
+            bulk_load(ssfb + j * C::KB_PER_STAGE * 512, p.b_sf + ((int64_t)rb * p.n_kb + kb0) * 512,
+                      sf_bytes, full_bar(s));
+          }
+        }
+      }
+      // wait (bounded) for our own copies still in flight before the CTA can retire
+      for (int k = it - C::STAGES < 0 ? 0 : it - C::STAGES; k < it; ++k)
+        mbar_wait(full_bar(k % C::STAGES), (uint32_t)(k / C::STAGES) & 1u, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_mxf4nvf4(BN);
+    int it = 0, lt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
+      const int acc = lt % C::ACC_STAGES;
+      const uint32_t aph = (uint32_t)(lt / C::ACC_STAGES) & 1u;
+      if (!mbar_wait(tempty_bar(acc), aph ^ 1u, err, kDevErrTimeoutTmem)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+      for (int st = 0; st < n_st; ++st, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+        if (!mbar_wait(full_bar(s), ph, err, kDevErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const int nkb = min(C::KB_PER_STAGE, p.n_kb - st * C::KB_PER_STAGE);
+          const uint32_t slot = (uint32_t)(it & 1);
+          const uint32_t sfa_t = tmem + C::SFA_TCOL + slot * C::SFA_SLOT;
+          const uint32_t sfb_t = tmem + C::SFB_TCOL + slot * C::SFB_SLOT;
+          const uint32_t sa = base + s * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t ssfa = sb + C::B_BYTES;
+          const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          for (int kb = 0; kb < nkb; ++kb) {
+            tmem_cp_32x128b_x4(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tmem_cp_32x128b_x4(sfb_t + kb * C::SFB_PER_KB + j * 4,
+                                 smem_desc(ssfb + j * C::KB_PER_STAGE * 512 + kb * 512, 0, 128, 0));
+          }
+          for (int kb = 0; kb < nkb; ++kb) {
+            const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
+            mma_mxf4nvf4(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::SFB_PER_KB,
+                         (st > 0 || kb > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(s));
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(tfull_bar(acc));
+      __syncwarp();
+    }
+    // every tcgen05 op issued above completes before TMEM is released
+    if (lane == 0) {
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    constexpr int NC = BN / 2;  // accumulator columns per thread
+    const int q = warp & 3;     // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;
+    const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
+    float egs = 1.f, esenc = 1.f;
+    if constexpr (EPI == VF4_EPI_GELU_NVFP4) {
+      egs = __ldg(p.epi_gs);
+      esenc = __fdiv_rn(1.0f, egs);
+    }
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+      const int mb = tile / p.tiles_n, nb = tile - mb * p.tiles_n;
+      const int acc = lt % C::ACC_STAGES;
+      const uint32_t aph = (uint32_t)(lt / C::ACC_STAGES) & 1u;
+      if (!mbar_wait(tfull_bar(acc), aph, err, kDevErrTimeoutTmem)) break;
+      tc_fence_after();
+      uint32_t v[NC];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * NC);
+#pragma unroll
+      for (int c = 0; c < NC / 32; ++c) tmem_ld_32x32b_x32(taddr + c * 32, v + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+
+      const int64_t row = (int64_t)mb * 128 + q * 32 + lane;
+      const int col0 = nb * BN + half * NC;
+      if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
+        if (row < p.M) {
+#pragma unroll
+          for (int g = 0; g < NC / 8; ++g) {
+            const int col = col0 + g * 8;
+            if (col < p.N) {
+              float y[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[g * 8 + i]) * alpha;
+              if constexpr (kF32) {
+                if (EPI == VF4_EPI_BIAS && p.bias) {
+                  uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+                  const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    y[2 * i] += __uint_as_float(b4[i] << 16);
+                    y[2 * i + 1] += __uint_as_float(b4[i] & 0xFFFF0000u);
+                  }
+                }
+                float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
+                o[0] = make_float4(y[0], y[1], y[2], y[3]);
+                o[1] = make_float4(y[4], y[5], y[6], y[7]);
+              } else {
+                if (EPI == VF4_EPI_BIAS && p.bias) {
+                  // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
+                  uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+                  const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
+                    y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
+                  }
+                }
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+                  w[i] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+        }
+      } else {
+        // +b1 (bf16, after rounding the GEMM to bf16) -> exact GELU -> NVFP4 "six" cast
+#pragma unroll
+        for (int g4 = 0; g4 < NC / 64; ++g4) {
+          uint32_t sfw = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int blk = g4 * 4 + b;
+            const int col = col0 + blk * 16;
+            float h[16];
+            if (col < p.N) {
+              float bb[16];
+              if (p.bias) {
+                const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
+                uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+                const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  bb[2 * i] = __uint_as_float(bw[i] << 16);
+                  bb[2 * i + 1] = __uint_as_float(bw[i] & 0xFFFF0000u);
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) bb[i] = 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float t = bf16_round(bf16_round(__uint_as_float(v[blk * 16 + i]) * alpha) + bb[i]);
+                h[i] = gelu_erf(t);
+              }
+              BlockQ qz = quantize_block<false>(h, egs, esenc);
+              if (row < p.M) {
+                *reinterpret_cast<uint64_t*>(p.out_packed + row * (int64_t)(p.N / 2) + col / 2) = qz.packed;
+                sfw |= qz.sf << (8 * b);
+              }
+            }
+          }
+          const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
+          if (col0 + g4 * 64 < p.N) {
+            int64_t off = ((row >> 7) * p.out_ncb + (c0 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+            *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t kbytes, int box_rows) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kbytes};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VF4_OK;
+}
+
+template <int BN, int EPI, bool kF32>
+static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
+  using C = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
+  if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, BN)) return st;
+  auto kern = gemm_nvfp4_kernel<BN, EPI, kF32>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  p.tiles_m = (p.M + 127) / 128;
+  p.tiles_n = (p.N + BN - 1) / BN;
+  int tiles = p.tiles_m * p.tiles_n;
+  int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, p);
+  return launch_status("vf4_gemm_nvfp4");
+}
+
+template <int BN>
+static int dispatch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32,
+                         cudaStream_t s) {
+  if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm<BN, VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS) {
+    return f32 ? launch_gemm<BN, VF4_EPI_BIAS, true>(a, b, p, s)
+               : launch_gemm<BN, VF4_EPI_BIAS, false>(a, b, p, s);
+  }
+  return f32 ? launch_gemm<BN, VF4_EPI_NONE, true>(a, b, p, s)
+             : launch_gemm<BN, VF4_EPI_NONE, false>(a, b, p, s);
+}
+
+}  // namespace vf4
+
+using namespace vf4;
+
+extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                              const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs,
+                              int64_t M, int64_t N, int64_t K, const void* bias, int epilogue,
+                              void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed,
+                              uint8_t* out_sf, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (M < 0 || N <= 0 || K <= 0) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad sizes M=%lld N=%lld K=%lld",
+                                             (long long)M, (long long)N, (long long)K);
+  if (M > (int64_t)INT32_MAX / 2 || N > 65535 * 128 || K > (1 << 20))
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: sizes too large");
+  if (K % 32 != 0 || N % 16 != 0)
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: need K %% 32 == 0 and N %% 16 == 0 (K=%lld N=%lld)",
+                (long long)K, (long long)N);
+  if (epilogue < VF4_EPI_NONE || epilogue > VF4_EPI_GELU_NVFP4)
+    return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad epilogue %d", epilogue);
+  if (!a_packed || !a_sf || !a_gs || !b_packed || !b_sf || !b_gs)
+    return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: null operand");
+  if (!aligned16(a_packed) || !aligned16(b_packed) || !aligned16(a_sf) || !aligned16(b_sf) ||
+      (bias && !aligned16(bias)))
+    return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: operands, scales and bias must be 16-byte aligned");
+  if (epilogue == VF4_EPI_GELU_NVFP4) {
+    if (N % 64 != 0) return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: GELU-NVFP4 epilogue needs N %% 64 == 0");
+    if (!epi_gs || !out_packed || !out_sf) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: GELU-NVFP4 outputs missing");
+    if ((reinterpret_cast<uintptr_t>(out_packed) & 7u) || (reinterpret_cast<uintptr_t>(out_sf) & 3u))
+      return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: out_packed 8-byte / out_sf 4-byte alignment");
+  } else {
+    if (!out) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: out is NULL");
+    if (out_dtype != VF4_BF16 && out_dtype != VF4_F32) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad out_dtype");
+    if (!aligned16(out)) return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: out must be 16-byte aligned");
+  }
+  if (M == 0) return VF4_OK;
+  GemmParams p{};
+  p.a_sf = a_sf;
+  p.b_sf = b_sf;
+  p.a_gs = a_gs;
+  p.b_gs = b_gs;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.n_kb = (int)((K + 63) / 64);
+  p.n_rb_b = (int)((N + 127) / 128);
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.out = out;
+  p.epi_gs = epi_gs;
+  p.out_packed = out_packed;
+  p.out_sf = out_sf;
+  p.out_ncb = (int)((N / 16 + 3) / 4);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
+  return dispatch_gemm<128>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
+}

@@ -1,0 +1,188 @@
+"""Tensor-level wrappers over the C ABI (include/vitfp4.h).
+
+Every function here launches the sm_100a kernels of libvitfp4.so on torch's current CUDA
+stream and allocates its outputs with torch.  Inputs must be CUDA tensors; there is no
+CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+SF_TORCH_DTYPE = torch.uint8  # E4M3 bytes are carried as uint8 internally
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise _lib.VitFp4Error("vitfp4 kernels run on CUDA (sm_100a) tensors only; got a "
+                                   f"{t.device} tensor (no CPU fallback)")
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.VF4_BF16
+    if t.dtype == torch.float32:
+        return _lib.VF4_F32
+    raise _lib.VitFp4Error(f"unsupported dtype {t.dtype} (bf16 or fp32)")
+
+
+def sf_swizzled_numel(rows: int, k: int) -> int:
+    """Bytes of the 128x4-tiled scale layout for (rows, k/16) scales."""
+    nb = k // 16
+    return ((rows + 127) // 128 * 128) * ((nb + 3) // 4 * 4)
+
+
+def _as_2d_input(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
+    """(M, K) view with unit column stride and 16-byte-aligned rows (copies only if needed)."""
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.dtype not in (torch.bfloat16, torch.float32):
+        x2 = x2.float()
+    esz = x2.element_size()
+    if x2.stride(-1) != 1 or (x2.stride(0) * esz) % 16 or x2.data_ptr() % 16 or x2.stride(0) < K:
+        x2 = x2.contiguous()
+        if x2.data_ptr() % 16:
+            x2 = x2.clone()
+    return x2, x2.shape[0], K, x2.stride(0) if x2.shape[0] > 1 else K
+
+
+def amax(x: torch.Tensor, gelu: bool = False) -> torch.Tensor:
+    """max|x| (or max|GELU(x)|) as a 0-dim fp32 device tensor."""
+    _need_cuda(x)
+    xc = x.contiguous()
+    if xc.dtype not in (torch.bfloat16, torch.float32):
+        xc = xc.float()
+    out = torch.empty((), dtype=torch.float32, device=x.device)
+    _lib.call("vf4_amax", _ptr(xc), _dtype_code(xc), xc.numel(), int(gelu), _ptr(out), _stream())
+    return out
+
+
+def global_scale(amax_t: torch.Tensor, block_select: str = "six") -> torch.Tensor:
+    _need_cuda(amax_t)
+    out = torch.empty((), dtype=torch.float32, device=amax_t.device)
+    _lib.call("vf4_global_scale", _ptr(amax_t.float().contiguous()), 1 if block_select == "mse" else 0,
+              _ptr(out), _stream())
+    return out
+
+
+def cast(x: torch.Tensor, gs: torch.Tensor | None = None, block_select: str = "six", gelu: bool = False,
+         bias: torch.Tensor | None = None, swizzled: bool = True, linear: bool = False):
+    """NVFP4 cast of x (..., K) along K.
+
+    Returns (packed uint8 (M, K/2), sf_swizzled uint8 flat or None, sf_linear uint8 (M, K/16) or
+    None, gs 0-dim fp32).  ``gs`` None -> dynamic global scale from the tensor amax.
+    """
+    _need_cuda(x, gs, bias)
+    x2, M, K, ld = _as_2d_input(x)
+    if K % 16:
+        raise _lib.VitFp4Error(f"NVFP4 needs K % 16 == 0 (K={K})")
+    dev = x.device
+    packed = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+    sfs = torch.empty(sf_swizzled_numel(M, K), dtype=torch.uint8, device=dev) if swizzled else None
+    sfl = torch.empty((M, K // 16), dtype=torch.uint8, device=dev) if linear else None
+    gs_out = torch.empty((), dtype=torch.float32, device=dev)
+    gs_in = None if gs is None else gs.reshape(()).to(torch.float32).contiguous()
+    b = None
+    if bias is not None:
+        b = bias.to(x2.dtype).contiguous()
+    _lib.call("vf4_cast_nvfp4", _ptr(x2), _dtype_code(x2), M, K, ld, _ptr(gs_in),
+              1 if block_select == "mse" else 0, int(gelu), _ptr(b), _ptr(packed), _ptr(sfs), _ptr(sfl),
+              _ptr(gs_out), _stream())
+    return packed, sfs, sfl, gs_out
+
+
+def pack_e2m1(codes: torch.Tensor) -> torch.Tensor:
+    _need_cuda(codes)
+    c = codes.contiguous()
+    assert c.dtype == torch.uint8 and c.shape[-1] % 2 == 0
+    out = torch.empty((*c.shape[:-1], c.shape[-1] // 2), dtype=torch.uint8, device=c.device)
+    rows = c.numel() // max(c.shape[-1], 1) if c.numel() else 0
+    _lib.call("vf4_pack_e2m1", _ptr(c), rows, c.shape[-1], _ptr(out), _stream())
+    return out
+
+
+def unpack_e2m1(packed: torch.Tensor) -> torch.Tensor:
+    _need_cuda(packed)
+    p = packed.contiguous()
+    if p.dtype != torch.uint8:
+        p = p.view(torch.uint8)
+    out = torch.empty((*p.shape[:-1], p.shape[-1] * 2), dtype=torch.uint8, device=p.device)
+    rows = p.numel() // max(p.shape[-1], 1) if p.numel() else 0
+    _lib.call("vf4_unpack_e2m1", _ptr(p), rows, p.shape[-1], _ptr(out), _stream())
+    return out
+
+
+def to_blocked(sf: torch.Tensor) -> torch.Tensor:
+    """(R, C) E4M3 scales (uint8 or float8_e4m3fn) -> flat 128x4-tiled uint8."""
+    _need_cuda(sf)
+    s = sf.contiguous()
+    if s.dtype != torch.uint8:
+        s = s.view(torch.uint8)
+    R, C = s.shape
+    out = torch.empty(((R + 127) // 128 * 128) * ((C + 3) // 4 * 4), dtype=torch.uint8, device=s.device)
+    _lib.call("vf4_to_blocked", _ptr(s), R, C, _ptr(out), _stream())
+    return out
+
+
+def _u8(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.dtype == torch.uint8 else t.view(torch.uint8)
+
+
+def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packed: torch.Tensor,
+         b_sf: torch.Tensor, b_gs: torch.Tensor, bias: torch.Tensor | None = None,
+         out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """(M, K/2) x (N, K/2) packed NVFP4 with swizzled scales -> (M, N) out_dtype (+bias)."""
+    _need_cuda(a_packed, b_packed)
+    a, b = _u8(a_packed), _u8(b_packed)
+    M, Kh = a.shape
+    N = b.shape[0]
+    assert b.shape[1] == Kh, (a.shape, b.shape)
+    K = Kh * 2
+    od = torch.float32 if out_dtype == torch.float32 else torch.bfloat16
+    out = torch.empty((M, N), dtype=od, device=a.device)
+    bb = None
+    epi = _lib.VF4_EPI_NONE
+    post_bias = None
+    if bias is not None:
+        if od == torch.float32 and bias.dtype == torch.float32:
+            post_bias = bias
+        else:
+            bb = bias.to(torch.bfloat16).contiguous()
+            epi = _lib.VF4_EPI_BIAS
+    _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+              _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
+              _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
+    if post_bias is not None:
+        out += post_bias
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        out = out.to(out_dtype)
+    return out
+
+
+def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs):
+    """fc1 GEMM with the fused +bias -> GELU -> NVFP4 cast epilogue.
+
+    Returns (packed uint8 (M, N/2), sf_swizzled uint8 flat) quantized with the static epi_gs."""
+    _need_cuda(a_packed, b_packed, epi_gs)
+    a, b = _u8(a_packed), _u8(b_packed)
+    M, Kh = a.shape
+    N = b.shape[0]
+    packed = torch.empty((M, N // 2), dtype=torch.uint8, device=a.device)
+    sf = torch.empty(sf_swizzled_numel(M, N), dtype=torch.uint8, device=a.device)
+    bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
+    _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+              _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
+              _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16, _ptr(epi_gs.reshape(()).float().contiguous()),
+              _ptr(packed), _ptr(sf), _stream())
+    return packed, sf
