@@ -1,0 +1,316 @@
+"""Benchmark: ViT-L/14 NVFP4 W4A4 inference images/s on 1..8 B200 (one replica per GPU).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--attn bf16|nvfp4]
+    torchrun --nproc-per-node N ... bench.py --gpus N ...
+
+Workload: DINOv2-style ViT-L/14 at 224x224 (257 tokens), 24 blocks, dim 1024,
+16 heads, GELU MLP 4096, LayerScale 1e-5, random N(0, 0.02) weights, N(0,1) bf16 images, global
+batch 1024 sharded evenly over the ranks.  Every block's qkv/proj are QuantLinear (Four-Over-Six
+weights, dynamic NVFP4 activations) and every MLP is FusedNVFP4MLP (fused bias+GELU+NVFP4 fc1
+epilogue); attention runs bf16 SDPA (default, the reference's unflagged route) or the FP4
+attention kernels (--attn nvfp4).
+
+Printed JSON line (rank 0): ``value`` = images/s of the whole job with inputs resident in HBM,
+timed with CUDA events (max over ranks); ``e2e`` = the same through the public module call with
+the images copied from pinned host memory and the logits read back every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vit-nvfp4_b200"))
+
+GLOBAL_BATCH = 1024
+MODEL = "vit_l14_dinov2_style"
+METRIC = "ViT-L/14 W4A4 images/s"
+FP4_NOMINAL_TFLOPS = 9000.0
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="vitfp4", choices=["vitfp4", "reference"])
+    ap.add_argument("--attn", default="bf16", choices=["bf16", "nvfp4"])
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch (images)")
+    ap.add_argument("--depth", type=int, default=24)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------- reference arm
+def _oracle_modules():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import nvfp4_oracle  # noqa: F401
+    import vit_oracle
+    return vit_oracle
+
+
+def cpu_forward_rate(attn: str, sample_images: int, steps: int, warmup: int, depth: int):
+    """Time the CPU restatement of the reference's torch-backend ViT-L/14 W4A4 forward."""
+    import numpy as np
+    vo = _oracle_modules()
+    W = vo.make_weights(depth=depth)
+    rng = np.random.default_rng(0)
+    imgs = rng.standard_normal((sample_images, 3, 224, 224)).astype(np.float32)
+    for _ in range(warmup):
+        vo.forward(W, imgs, attn=attn)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        vo.forward(W, imgs, attn=attn)
+        times.append(time.perf_counter() - t0)
+    return sample_images / statistics.median(times), times
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    cores = os.cpu_count() or 1
+    try:
+        import torch
+        torch.set_num_threads(cores)
+    except Exception:
+        pass
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    sample = 2
+    steps = max(1, min(args.steps, 3))
+    rate, times = cpu_forward_rate(args.attn, sample, steps, min(args.warmup, 1), args.depth)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "images/s", "n_gpus": world,
+        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": round(1000 * statistics.median(times), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": f"{MODEL} W4A4 forward (attention {args.attn})",
+                                        "global_batch": args.batch, "seq_len": 257, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(rate, 4), "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} images per step (of the {args.batch}-image batch), "
+                                   f"numpy restatement of the reference torch backend"},
+        "e2e": {"value": round(rate, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------- vitfp4 arm
+def build_model(depth: int, attn: str, device):
+    import torch
+    from vitfp4 import vit
+    from vitfp4.ptq import enable_quant_attention, fuse_mlps, quantize_vit, vit_attn_policy
+    cfg = dict(vit.VIT_L14)
+    cfg["depth"] = depth
+    model = vit.build_vit(seed=0, **cfg).to(device=device, dtype=torch.bfloat16).eval()
+    n_mlp = fuse_mlps(model, skip_ends=0)
+    n_lin, spec = quantize_vit(model, skip_first=0, skip_last=0, w_block_select="mse")
+    n_att = 0
+    if attn == "nvfp4":
+        n_att = enable_quant_attention(model, vit_attn_policy(depth, 0, 0, "blocks"), qk="nvfp4", pv="nvfp4")
+    return model, {"fused_mlps": n_mlp, "quant_linears": n_lin, "fp4_attention": n_att}
+
+
+def run_vitfp4(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    from vitfp4.nvfp4 import ops
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    per_rank = args.batch // world
+    torch.manual_seed(1234 + rank)
+    model, counts = build_model(args.depth, args.attn, dev)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    images = torch.randn(per_rank, 3, 224, 224, device=dev, generator=gen).to(torch.bfloat16)
+    host_images = images.cpu().pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            logits = model(images)
+        torch.cuda.synchronize()
+
+        # ---- device-resident timing (the headline `value`)
+        sampler = ClockSampler(local_rank) if rank == 0 else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        ops.probe.reset()
+        ops.probe.timing = True
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            logits = model(images)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ops.probe.timing = False
+        launches = ops.probe.launches
+        records = list(ops.probe.records)
+        clocks = sampler.stop() if sampler else None
+        ms = t0.elapsed_time(t1)
+
+        # ---- end-to-end through the public call with host buffers
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x = host_images.to(dev, non_blocking=True)
+            out = model(x).float().cpu()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = e0.elapsed_time(e1)
+
+    # per-kernel GEMM timing from the live events of the timed region
+    by_kind: dict = {}
+    for kind, flops, s, e in records:
+        d = by_kind.setdefault(kind, [0, 0.0, 0.0])
+        d[0] += 1
+        d[1] += flops
+        d[2] += s.elapsed_time(e)
+    t = torch.tensor([ms, ms_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gathered = [torch.empty_like(logits) for _ in range(world)]
+        dist.all_gather(gathered, logits.contiguous())          # the single final gather of logits
+    ms, ms_e2e = float(t[0]), float(t[1])
+    if rank != 0:
+        return 0
+
+    peaks = _peaks()
+    bf16_tf = peaks.get("bf16_tflops")
+    fp4_peak = 4 * bf16_tf if bf16_tf else FP4_NOMINAL_TFLOPS
+    dom = max(by_kind.items(), key=lambda kv: kv[1][2]) if by_kind else None
+    kernels = {k: {"launches": v[0], "ms_total": round(v[2], 3),
+                   "tflops": round(v[1] / (v[2] * 1e-3) / 1e12, 1)} for k, v in sorted(by_kind.items())}
+    roofline = None
+    if dom:
+        achieved = dom[1][1] / (dom[1][2] * 1e-3) / 1e12
+        roofline = {"kernel": dom[0], "bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
+                    "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
+                    "peak_source": "4 x measured bf16 burst (MEASURED_PEAKS.json); FP4 itself not measured"
+                    if bf16_tf else "nominal dense FP4 (no measured peak)",
+                    "frac_of_nominal_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4), "traffic": None}
+    steps = args.steps
+    img_per_step = per_rank * world
+    line = {
+        "metric": METRIC, "value": round(img_per_step * steps / (ms * 1e-3), 2), "unit": "images/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms / steps, 3),
+        "higher_is_better": True, "scaling": "weak" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "nvfp4 W4A4 (fp32 accumulate, bf16 activations)", "data": "synthetic",
+        "config": {"workload": f"{MODEL} W4A4 forward, attention {args.attn}", "model": "ViT-L/14",
+                   "global_batch": img_per_step, "per_gpu_batch": per_rank, "seq_len": 257,
+                   "depth": args.depth, "parallelism": f"dp{world} (independent replicas)",
+                   "l2": "inputs larger than L2 (activations >= 0.5 GB per tensor)", **counts},
+        "e2e": {"value": round(img_per_step * steps / (ms_e2e * 1e-3), 2), "unit": "images/s",
+                "h2d_bytes_per_step": int(host_images.numel() * host_images.element_size() * world),
+                "d2h_bytes_per_step": int(out.numel() * 4 * world)},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "kernels": kernels,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            cores = os.cpu_count() or 1
+            torch.set_num_threads(cores)
+            rate, times = cpu_forward_rate(args.attn, 1, 1, 0, args.depth)
+            line["cpu_baseline"] = {"value": round(rate, 4), "unit": "images/s", "cores": cores, "kind": "port",
+                                    "sample": "1 image, 1 timed forward (numpy restatement of the "
+                                              "reference torch backend, same W4A4 ViT-L/14)"}
+        except Exception as ex:  # pragma: no cover
+            line["cpu_baseline"] = {"value": None, "error": repr(ex)[:200]}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = _args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if args.impl == "reference":
+            return run_reference(args, rank, world)
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+        try:
+            return run_vitfp4(args, rank, world, local_rank)
+        finally:
+            dist.destroy_process_group()
+    if args.impl == "reference":
+        return run_reference(args, 0, 1)
+    return run_vitfp4(args, 0, 1, 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -13,6 +13,44 @@ from .. import _lib
 SF_TORCH_DTYPE = torch.uint8  # E4M3 bytes are carried as uint8 internally
 
 
+class Probe:
+    """Launch accounting for the benchmark: counts libvitfp4 kernel launches and, when
+    ``timing`` is on, brackets every GEMM launch with CUDA events on the launching stream."""
+
+    def __init__(self):
+        self.launches = 0
+        self.timing = False
+        self.records: list = []   # (kind, flops, start_event, end_event)
+
+    def reset(self):
+        self.launches = 0
+        self.records = []
+
+
+probe = Probe()
+
+
+def _launched(n: int = 1) -> None:
+    probe.launches += n
+
+
+class _GemmTimer:
+    def __init__(self, kind: str, flops: float):
+        self.kind, self.flops = kind, flops
+
+    def __enter__(self):
+        if probe.timing:
+            self.s = torch.cuda.Event(enable_timing=True)
+            self.e = torch.cuda.Event(enable_timing=True)
+            self.s.record()
+        return self
+
+    def __exit__(self, *a):
+        if probe.timing:
+            self.e.record()
+            probe.records.append((self.kind, self.flops, self.s, self.e))
+
+
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
@@ -64,6 +102,7 @@ def amax(x: torch.Tensor, gelu: bool = False) -> torch.Tensor:
         xc = xc.float()
     out = torch.empty((), dtype=torch.float32, device=x.device)
     _lib.call("vf4_amax", _ptr(xc), _dtype_code(xc), xc.numel(), int(gelu), _ptr(out), _stream())
+    _launched()
     return out
 
 
@@ -72,6 +111,7 @@ def global_scale(amax_t: torch.Tensor, block_select: str = "six") -> torch.Tenso
     out = torch.empty((), dtype=torch.float32, device=amax_t.device)
     _lib.call("vf4_global_scale", _ptr(amax_t.float().contiguous()), 1 if block_select == "mse" else 0,
               _ptr(out), _stream())
+    _launched()
     return out
 
 
@@ -90,15 +130,16 @@ def cast(x: torch.Tensor, gs: torch.Tensor | None = None, block_select: str = "s
     packed = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
     sfs = torch.empty(sf_swizzled_numel(M, K), dtype=torch.uint8, device=dev) if swizzled else None
     sfl = torch.empty((M, K // 16), dtype=torch.uint8, device=dev) if linear else None
-    gs_out = torch.empty((), dtype=torch.float32, device=dev)
     gs_in = None if gs is None else gs.reshape(()).to(torch.float32).contiguous()
+    gs_out = torch.empty((), dtype=torch.float32, device=dev) if gs_in is None else None
     b = None
     if bias is not None:
         b = bias.to(x2.dtype).contiguous()
     _lib.call("vf4_cast_nvfp4", _ptr(x2), _dtype_code(x2), M, K, ld, _ptr(gs_in),
               1 if block_select == "mse" else 0, int(gelu), _ptr(b), _ptr(packed), _ptr(sfs), _ptr(sfl),
               _ptr(gs_out), _stream())
-    return packed, sfs, sfl, gs_out
+    _launched(1 if gs_in is not None else 3)
+    return packed, sfs, sfl, (gs_out if gs_in is None else gs_in)
 
 
 def pack_e2m1(codes: torch.Tensor) -> torch.Tensor:
@@ -108,6 +149,7 @@ def pack_e2m1(codes: torch.Tensor) -> torch.Tensor:
     out = torch.empty((*c.shape[:-1], c.shape[-1] // 2), dtype=torch.uint8, device=c.device)
     rows = c.numel() // max(c.shape[-1], 1) if c.numel() else 0
     _lib.call("vf4_pack_e2m1", _ptr(c), rows, c.shape[-1], _ptr(out), _stream())
+    _launched()
     return out
 
 
@@ -119,6 +161,7 @@ def unpack_e2m1(packed: torch.Tensor) -> torch.Tensor:
     out = torch.empty((*p.shape[:-1], p.shape[-1] * 2), dtype=torch.uint8, device=p.device)
     rows = p.numel() // max(p.shape[-1], 1) if p.numel() else 0
     _lib.call("vf4_unpack_e2m1", _ptr(p), rows, p.shape[-1], _ptr(out), _stream())
+    _launched()
     return out
 
 
@@ -131,6 +174,7 @@ def to_blocked(sf: torch.Tensor) -> torch.Tensor:
     R, C = s.shape
     out = torch.empty(((R + 127) // 128 * 128) * ((C + 3) // 4 * 4), dtype=torch.uint8, device=s.device)
     _lib.call("vf4_to_blocked", _ptr(s), R, C, _ptr(out), _stream())
+    _launched()
     return out
 
 
@@ -160,9 +204,11 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
         else:
             bb = bias.to(torch.bfloat16).contiguous()
             epi = _lib.VF4_EPI_BIAS
-    _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
-              _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
-              _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
+    with _GemmTimer(f"gemm_{'bias' if epi else 'none'}_{M}x{N}x{K}", 2.0 * M * N * K):
+        _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                  _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
+                  _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
+    _launched()
     if post_bias is not None:
         out += post_bias
     if out_dtype not in (torch.float32, torch.bfloat16):
@@ -181,8 +227,10 @@ def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs):
     packed = torch.empty((M, N // 2), dtype=torch.uint8, device=a.device)
     sf = torch.empty(sf_swizzled_numel(M, N), dtype=torch.uint8, device=a.device)
     bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
-    _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
-              _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
-              _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16, _ptr(epi_gs.reshape(()).float().contiguous()),
-              _ptr(packed), _ptr(sf), _stream())
+    with _GemmTimer(f"gemm_gelu_nvfp4_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
+        _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                  _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
+                  _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16, _ptr(epi_gs.reshape(()).float().contiguous()),
+                  _ptr(packed), _ptr(sf), _stream())
+    _launched()
     return packed, sf

@@ -1,0 +1,14 @@
+"""Post-training W4A4 conversion and the quantized modules (reference API: src/vit_nvfp4/ptq/__init__.py)."""
+from .qlinear import QuantLinear
+from .policy import vit_block_policy, block_index
+from .qattention import enable_quant_attention, vit_attn_policy
+from .fused_mlp import FusedNVFP4MLP, fuse_mlps
+from .convert import quantize_model
+from .models import ModelSpec, model_spec, find_block_container, quantize_vit
+from .diagnostics import tensor_cosine
+
+__all__ = [
+    "QuantLinear", "vit_block_policy", "block_index", "enable_quant_attention", "vit_attn_policy",
+    "FusedNVFP4MLP", "fuse_mlps", "quantize_model", "ModelSpec", "model_spec", "find_block_container",
+    "quantize_vit", "tensor_cosine",
+]
