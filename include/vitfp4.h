@@ -114,6 +114,22 @@ VF4_API int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const f
                    int64_t N, int64_t K, const void* bias, int epilogue, void* out, int out_dtype,
                    const float* epi_gs, uint8_t* out_packed, uint8_t* out_sf, vf4_stream_t stream);
 
+/* Bytes of workspace vf4_attn_nvfp4 needs for (B, H, S, D) (0 for invalid sizes). */
+VF4_API int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D);
+
+/* NVFP4 attention (replaces the emulated quant_sdpa(qk='nvfp4', pv='nvfp4'),
+ * nvfp4/attention.py:53-86, reached through ptq/qattention.py:20-30):
+ *   q, k, v : bf16, element (b, h, s, d) at ptr + b*stride_b + h*stride_h + s*stride_s + d
+ *             (the packed qkv projection output and (B, H, S, D) tensors both fit)
+ *   out     : bf16, element (b, h, s, d) at out + b*out_stride_b + h*out_stride_h + s*out_stride_s + d
+ *   smooth-K / smooth-V always on; per-(b,h) global scales for Q, K~, V~; fixed P global
+ *   1/(6*448); no mask, not causal.  D % 16 == 0, D <= 128; S <= 1152 for D > 64.
+ *   workspace: at least vf4_attn_workspace_size(B, H, S, D) bytes, 16-byte aligned. */
+VF4_API int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
+                           int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
+                           void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
+                           void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,43 @@ def test_cast_matches_oracle(M, K, mode, dtype):
     assert np.array_equal(sfs, oracle.to_blocked(b))
 
 
+def test_cast_exact_ties_and_boundaries():
+    """Blocks whose max is 6*2^k with members exactly on, and one ulp around, every E2M1
+    rounding boundary (global scale 1 -> block scale 2^k, decode exact): the reference rounds
+    ties DOWN, so this pins the tie handling of the fast encoder bit-for-bit."""
+    rng = np.random.default_rng(11)
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    cand = np.concatenate([mids, np.nextafter(mids, 0), np.nextafter(mids, 10), [0.0, -0.0, 6.0, 0.5, 3.0]])
+    rows, K = 512, 256
+    x = np.empty((rows, K), np.float32)
+    for r in range(rows):
+        for b in range(K // 16):
+            k = rng.integers(-8, 8)
+            blk = rng.choice(cand, 16).astype(np.float32) * rng.choice([-1, 1], 16)
+            blk[rng.integers(16)] = 6.0
+            x[r, 16 * b:16 * b + 16] = blk * np.float32(2.0 ** k)
+    xt = torch.from_numpy(x).cuda()
+    packed, sfs, sfl, _ = _run_cast(xt, "six", torch.tensor(1.0, device="cuda"))
+    c, b, _ = oracle.quantize_to_nvfp4(x, 16, global_scale=np.float32(1.0))
+    assert np.array_equal(sfl, b)
+    assert np.array_equal(packed, oracle.pack_e2m1(c)), int((packed != oracle.pack_e2m1(c)).sum())
+
+
+def test_cast_random_scales_bit_exact():
+    """2M elements with per-row magnitudes spanning 2^-30..2^30 (bf16 and fp32 inputs)."""
+    rng = np.random.default_rng(12)
+    x = (rng.standard_normal((4096, 512)) * np.exp2(rng.uniform(-30, 30, (4096, 1)))).astype(np.float32)
+    for mode in ("six",):
+        packed, _, sfl, gsv = _run_cast(torch.from_numpy(x).cuda(), mode)
+        c, b, g = oracle.quantize_to_nvfp4(x, 16, block_select=mode)
+        assert gsv == g and np.array_equal(sfl, b)
+        assert np.array_equal(packed, oracle.pack_e2m1(c))
+        xb = oracle.to_bf16(x)
+        packed, _, sfl, gsv = _run_cast(bf16_tensor(x), mode)
+        c, b, g = oracle.quantize_to_nvfp4(xb, 16, block_select=mode)
+        assert gsv == g and np.array_equal(sfl, b) and np.array_equal(packed, oracle.pack_e2m1(c))
+
+
 def test_cast_static_scale_and_strided_rows():
     x = vit_activation(64, 256, seed=3)
     big = np.zeros((64, 384), np.float32)

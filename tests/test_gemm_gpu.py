@@ -81,12 +81,13 @@ def test_gemm_bf16_bias(M, K, N):
 
 @pytest.mark.parametrize("M,K,N", [(256, 1024, 4096), (197, 768, 3072), (130, 512, 128)])
 def test_gemm_gelu_nvfp4_epilogue(M, K, N):
-    """fc1 epilogue: NVFP4(GELU(bf16(bf16(gemm) + b1))) with a static global scale."""
+    """fc1 epilogue: NVFP4(GELU(gemm + b1)) with a static global scale; the intermediate stays fp32
+    (the unfused reference rounds it to bf16), GELU uses the A&S 7.1.26 erf (|err| <= 1.5e-7)."""
     ops = _ops()
     A, B = _operands(M, N, K, seed=7)
     bias = (np.random.default_rng(3).standard_normal(N) * 0.1).astype(np.float32)
     ref_y = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
-    h = oracle.gelu(oracle.to_bf16(oracle.to_bf16(ref_y) + oracle.to_bf16(bias)))
+    h = oracle.gelu(ref_y + oracle.to_bf16(bias))
     gh = np.float32(np.abs(h).max() / 2688.0)
     ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
     bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])

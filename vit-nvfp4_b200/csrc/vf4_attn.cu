@@ -1,0 +1,610 @@
+// NVFP4 attention for ViT on sm_100a: QK^T and PV as block-scaled tcgen05 MMAs.
+//
+// Semantics follow the reference's emulated quant_sdpa(qk='nvfp4', pv='nvfp4', smooth_k,
+// smooth_v) (src/vit_nvfp4/nvfp4/attention.py:53-86):
+//   k~ = k - mean_S(k);  S = deq(Q) deq(K~)^T * scale;  P = softmax(S);
+//   v~ = v - mean_S(v);  out = deq(P) deq(V~) + mean_S(v)
+// with Q, K~ quantized along the head dim and V~ along tokens (16-element NVFP4 blocks, E4M3
+// block scales, "six" rule, ties-down codes).  Two deliberate differences, both forced by a
+// single-pass kernel: the fp32 global scale of Q, K~ and V~ is taken per (image, head) rather
+// than over the whole tensor, and P (exactly normalised, <= 1) uses the fixed global 1/(6*448)
+// instead of the amax of the whole P tensor.
+//
+// Kernel 1 (attn_prep, one CTA per (b, h)): means, per-head amax, and NVFP4 packing of Q, K~
+//   and V~^T into the MMA operand layouts (128x4-tiled scales) in a workspace.
+// Kernel 2 (attn_fwd, one CTA per (b, h, 128-query tile)): TMA loads Q tile, all K~ and V~^T
+//   of the head; warp 0 issues the MMAs, warps 2..5 (one query row per thread) run an exact
+//   two-pass softmax from TMEM (pass 1: row max / sum; pass 2: recompute S, P = exp(S-m)/l),
+//   re-quantize P to NVFP4 in shared memory (scales staged for tcgen05.cp), and the PV MMA
+//   accumulates O in TMEM; the epilogue adds mean(v) and writes bf16 (B, S, H, D).
+#include "vf4_common.cuh"
+#include "vf4_host.h"
+
+namespace vf4 {
+
+static __device__ int g_attn_err;
+
+int attn_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_attn_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+constexpr int kScalStride = 4 + 128;   // per head: gs_q, gs_k, gs_v, pad, mean_v[128]
+constexpr float kInv2688 = 1.0f / 2688.0f;
+
+struct AttnGeom {
+  int B, H, S, D;
+  int S_pad, Dp, Dv, nc;
+  int64_t BH;
+  int64_t q_head, vt_head, qsf_head, vsf_head;  // bytes per head
+  int64_t off_q, off_k, off_v, off_qsf, off_ksf, off_vsf, off_scal, total;
+};
+
+static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+static AttnGeom make_geom(int64_t B, int64_t H, int64_t S, int64_t D) {
+  AttnGeom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.S_pad = (int)align_up(S, 128);
+  g.Dp = D <= 64 ? 64 : 128;
+  g.Dv = g.Dp;
+  g.nc = g.S_pad / 128;
+  g.BH = B * H;
+  g.q_head = (int64_t)g.S_pad * g.Dp / 2;
+  g.vt_head = (int64_t)g.Dv * g.S_pad / 2;
+  g.qsf_head = (int64_t)(g.S_pad / 128) * (g.Dp / 64) * 512;
+  g.vsf_head = (int64_t)(g.S_pad / 64) * 512;
+  int64_t o = 0;
+  g.off_q = o;   o = align_up(o + g.BH * g.q_head, 1024);
+  g.off_k = o;   o = align_up(o + g.BH * g.q_head, 1024);
+  g.off_v = o;   o = align_up(o + g.BH * g.vt_head, 1024);
+  g.off_qsf = o; o = align_up(o + g.BH * g.qsf_head, 1024);
+  g.off_ksf = o; o = align_up(o + g.BH * g.qsf_head, 1024);
+  g.off_vsf = o; o = align_up(o + g.BH * g.vsf_head, 1024);
+  g.off_scal = o; o = align_up(o + g.BH * kScalStride * 4, 1024);
+  g.total = o;
+  return g;
+}
+
+// ---------------------------------------------------------------------------------------
+// Kernel 1: per-(b,h) smoothing, global scales and NVFP4 packing
+// ---------------------------------------------------------------------------------------
+VF4_DEV void load8(const __nv_bfloat16* p, float* v) {
+  uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+VF4_DEV float block_max(float m, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float r = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+__global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __restrict__ q,
+                                                        const __nv_bfloat16* __restrict__ k,
+                                                        const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                        int64_t sh, int64_t ss, AttnGeom g,
+                                                        uint8_t* __restrict__ ws) {
+  __shared__ float part[2][2048];
+  __shared__ float mu[2][128];
+  __shared__ float red[8];
+  const int bh = blockIdx.x;
+  const int b = bh / g.H, h = bh - b * g.H;
+  const __nv_bfloat16* qh = q + b * sb + h * sh;
+  const __nv_bfloat16* kh = k + b * sb + h * sh;
+  const __nv_bfloat16* vh = v + b * sb + h * sh;
+  const int S = g.S, D = g.D, D8 = D / 8;
+  const int rpi = 256 / D8, active = rpi * D8;
+  const int t = threadIdx.x, c8 = t % D8, r0 = t / D8;
+
+  // pass A: column sums of k and v, amax of q
+  float sk[8], sv[8], aq = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sk[i] = sv[i] = 0.f;
+  if (t < active) {
+    for (int r = r0; r < S; r += rpi) {
+      float a[8], bk[8], bv[8];
+      load8(qh + r * ss + c8 * 8, a);
+      load8(kh + r * ss + c8 * 8, bk);
+      load8(vh + r * ss + c8 * 8, bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        aq = fmaxf(aq, fabsf(a[i]));
+        sk[i] += bk[i];
+        sv[i] += bv[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      part[0][r0 * D + c8 * 8 + i] = sk[i];
+      part[1][r0 * D + c8 * 8 + i] = sv[i];
+    }
+  }
+  __syncthreads();
+  if (t < D) {
+    float a = 0.f, bb = 0.f;
+    for (int r = 0; r < rpi; ++r) {  // fixed order: deterministic means
+      a += part[0][r * D + t];
+      bb += part[1][r * D + t];
+    }
+    mu[0][t] = __fdiv_rn(a, (float)S);
+    mu[1][t] = __fdiv_rn(bb, (float)S);
+  }
+  aq = block_max(aq, red);  // contains __syncthreads: mu visible afterwards
+
+  // pass B: amax of the centred k and v
+  float ak = 0.f, av = 0.f;
+  if (t < active) {
+    for (int r = r0; r < S; r += rpi) {
+      float bk[8], bv[8];
+      load8(kh + r * ss + c8 * 8, bk);
+      load8(vh + r * ss + c8 * 8, bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ak = fmaxf(ak, fabsf(bk[i] - mu[0][c8 * 8 + i]));
+        av = fmaxf(av, fabsf(bv[i] - mu[1][c8 * 8 + i]));
+      }
+    }
+  }
+  ak = block_max(ak, red);
+  av = block_max(av, red);
+  const float gs_q = __fdiv_rn(fmaxf(aq, 1e-12f), 2688.f);
+  const float gs_k = __fdiv_rn(fmaxf(ak, 1e-12f), 2688.f);
+  const float gs_v = __fdiv_rn(fmaxf(av, 1e-12f), 2688.f);
+  float* scal = reinterpret_cast<float*>(ws + g.off_scal) + (int64_t)bh * kScalStride;
+  if (t == 0) {
+    scal[0] = gs_q;
+    scal[1] = gs_k;
+    scal[2] = gs_v;
+    scal[3] = 0.f;
+  }
+  if (t < 128) scal[4 + t] = t < D ? mu[1][t] : 0.f;
+  const float se_q = __fdiv_rn(1.f, gs_q), se_k = __fdiv_rn(1.f, gs_k), se_v = __fdiv_rn(1.f, gs_v);
+
+  const int lane = t & 31;
+  // pass C: Q and K~ along the head dim -> (S_pad, Dp/2) packed + (S_pad x Dp/16) tiled scales
+  {
+    const int nblk = g.Dp / 16, dblk = D / 16;
+    const int ncb = g.Dp / 64;
+    const int total = g.S_pad * nblk;
+    uint8_t* qp = ws + g.off_q + (int64_t)bh * g.q_head;
+    uint8_t* kp = ws + g.off_k + (int64_t)bh * g.q_head;
+    uint8_t* qsf = ws + g.off_qsf + (int64_t)bh * g.qsf_head;
+    uint8_t* ksf = ws + g.off_ksf + (int64_t)bh * g.qsf_head;
+    for (int i0 = t & ~31; i0 < total; i0 += 256) {
+      const int i = i0 + lane;
+      const int r = i / nblk, bb = i - r * nblk;
+      const bool in = i < total;
+      const bool valid = in && r < S && bb < dblk;
+      uint32_t sfq = 0, sfk = 0;
+      uint64_t pq = 0, pk = 0;
+      if (valid) {
+        float x[16];
+        load8(qh + r * ss + bb * 16, x);
+        load8(qh + r * ss + bb * 16 + 8, x + 8);
+        BlockQ z = quantize_block<false>(x, gs_q, se_q);
+        pq = z.packed;
+        sfq = z.sf;
+        load8(kh + r * ss + bb * 16, x);
+        load8(kh + r * ss + bb * 16 + 8, x + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = x[e] - mu[0][bb * 16 + e];
+        z = quantize_block<false>(x, gs_k, se_k);
+        pk = z.packed;
+        sfk = z.sf;
+      }
+      if (in) {
+        *reinterpret_cast<uint64_t*>(qp + (int64_t)r * (g.Dp / 2) + bb * 8) = pq;
+        *reinterpret_cast<uint64_t*>(kp + (int64_t)r * (g.Dp / 2) + bb * 8) = pk;
+      }
+      uint32_t wq = sfq << (8 * (bb & 3)), wk = sfk << (8 * (bb & 3));
+      wq |= __shfl_xor_sync(0xffffffffu, wq, 1);
+      wq |= __shfl_xor_sync(0xffffffffu, wq, 2);
+      wk |= __shfl_xor_sync(0xffffffffu, wk, 1);
+      wk |= __shfl_xor_sync(0xffffffffu, wk, 2);
+      if (in && (bb & 3) == 0) {
+        const int64_t off = sf_swizzle_offset(r, bb, ncb);
+        *reinterpret_cast<uint32_t*>(qsf + off) = wq;
+        *reinterpret_cast<uint32_t*>(ksf + off) = wk;
+      }
+    }
+  }
+  // pass D: V~^T along tokens -> (Dv, S_pad/2) packed + (128 x S_pad/16) tiled scales
+  {
+    const int nblk = g.S_pad / 16;
+    const int ncb = g.S_pad / 64;
+    const int total = 128 * nblk;  // scale rows are padded to 128
+    uint8_t* vp = ws + g.off_v + (int64_t)bh * g.vt_head;
+    uint8_t* vsf = ws + g.off_vsf + (int64_t)bh * g.vsf_head;
+    for (int i0 = t & ~31; i0 < total; i0 += 256) {
+      const int i = i0 + lane;
+      const int d = i / nblk, tb = i - d * nblk;
+      const bool in = i < total;
+      uint32_t sf = 0;
+      uint64_t pv = 0;
+      if (in && d < D) {
+        float x[16];
+        const float m = mu[1][d];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int tok = tb * 16 + e;
+          x[e] = tok < S ? __bfloat162float(vh[(int64_t)tok * ss + d]) - m : 0.f;
+        }
+        BlockQ z = quantize_block<false>(x, gs_v, se_v);
+        pv = z.packed;
+        sf = z.sf;
+      }
+      if (in && d < g.Dv) *reinterpret_cast<uint64_t*>(vp + (int64_t)d * (g.S_pad / 2) + tb * 8) = pv;
+      uint32_t w = sf << (8 * (tb & 3));
+      w |= __shfl_xor_sync(0xffffffffu, w, 1);
+      w |= __shfl_xor_sync(0xffffffffu, w, 2);
+      if (in && (tb & 3) == 0) *reinterpret_cast<uint32_t*>(vsf + sf_swizzle_offset(d, tb, ncb)) = w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Kernel 2: attention forward
+// ---------------------------------------------------------------------------------------
+template <int DP>
+struct AttnCfg {
+  static constexpr int DV = DP;
+  static constexpr int ROWB = DP / 2;                 // bytes per Q/K row
+  static constexpr int KB = DP / 64;                  // K64 blocks of QK^T
+  static constexpr int QBYTES = 128 * ROWB;
+  static constexpr int VBYTES = DV * 64;              // V~^T chunk: DV rows x 128 keys
+  static constexpr int PBYTES = 128 * 64;             // P chunk: 128 rows x 128 keys
+  static constexpr uint32_t QK_LAYOUT = DP == 64 ? 6u : 4u;   // SWIZZLE_32B / SWIZZLE_64B
+  static constexpr uint32_t QK_SBO = 8 * ROWB;
+  // TMEM columns
+  static constexpr int T_S = 0, T_O = 128, T_QSF = 128 + DV, T_KSF = T_QSF + 4 * KB;
+  static constexpr int T_PSF = T_KSF + 4 * KB, T_VSF = T_PSF + 8;
+  static constexpr int TMEM_COLS = (T_VSF + 8) <= 256 ? 256 : 512;
+  static constexpr int THREADS = 192;
+};
+
+struct AttnSmem {
+  uint32_t q, k, v, p, qsf, ksf, vsf, psf, bar, total;
+};
+
+template <int DP>
+static AttnSmem attn_smem_layout(int nc, int S_pad) {
+  using C = AttnCfg<DP>;
+  AttnSmem s{};
+  uint32_t o = 0;
+  s.q = o;   o += C::QBYTES;
+  s.k = o;   o += nc * C::QBYTES;
+  s.v = o;   o += nc * C::VBYTES;
+  s.p = o;   o += 2 * C::PBYTES;
+  s.qsf = o; o += C::KB * 512;
+  s.ksf = o; o += nc * C::KB * 512;
+  s.vsf = o; o += (S_pad / 64) * 512;
+  s.psf = o; o += 2 * 1024;
+  s.bar = o; o += 128;
+  s.total = o + 1024;  // slack for aligning the base to 1024
+  return s;
+}
+
+template <int DP>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnGeom g, const uint8_t* __restrict__ ws,
+                    const AttnSmem L, float scale, __nv_bfloat16* __restrict__ out, int64_t osb, int64_t osh,
+                    int64_t oss) {
+  using C = AttnCfg<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar = base + L.bar;
+  const uint32_t load_bar = bar, s_full = bar + 8, s_free = bar + 16, o_full = bar + 24, drain = bar + 32;
+  auto p_full = [&](int i) { return bar + 40 + 8u * i; };
+  auto p_free = [&](int i) { return bar + 56 + 8u * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L.bar + 72);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, bh = blockIdx.y;
+  const int nc = g.nc, S = g.S;
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(load_bar, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(p_full(i), 4);
+      mbar_init(p_free(i), 1);
+    }
+    fence_mbar_init();
+    tma_prefetch(&tmQ);
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const float* scal = reinterpret_cast<const float*>(ws + g.off_scal) + (int64_t)bh * kScalStride;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ loads
+      const uint32_t qsf_bytes = C::KB * 512, ksf_bytes = nc * C::KB * 512, vsf_bytes = (g.S_pad / 64) * 512;
+      const uint32_t tx = C::QBYTES + nc * (C::QBYTES + C::VBYTES) + qsf_bytes + ksf_bytes + vsf_bytes;
+      mbar_arrive_expect_tx(load_bar, tx);
+      tma_load_2d(base + L.q, &tmQ, 0, bh * g.S_pad + qt * 128, load_bar);
+      for (int j = 0; j < nc; ++j) {
+        tma_load_2d(base + L.k + j * C::QBYTES, &tmK, 0, bh * g.S_pad + j * 128, load_bar);
+        tma_load_2d(base + L.v + j * C::VBYTES, &tmV, j * 64, bh * C::DV, load_bar);
+      }
+      bulk_load(base + L.qsf, ws + g.off_qsf + (int64_t)bh * g.qsf_head + (int64_t)qt * C::KB * 512, qsf_bytes,
+                load_bar);
+      bulk_load(base + L.ksf, ws + g.off_ksf + (int64_t)bh * g.qsf_head, ksf_bytes, load_bar);
+      bulk_load(base + L.vsf, ws + g.off_vsf + (int64_t)bh * g.vsf_head, vsf_bytes, load_bar);
+
+      // ------------------------------------------------------------ MMA issue
+      bool ok = mbar_wait(load_bar, 0, err, kDevErrTimeoutFull);
+      tc_fence_after();
+      constexpr uint32_t id_s = idesc_mxf4nvf4(128);
+      constexpr uint32_t id_o = idesc_mxf4nvf4(C::DV);
+      const uint32_t t_s = tmem + C::T_S, t_o = tmem + C::T_O;
+      const uint32_t t_qsf = tmem + C::T_QSF, t_ksf = tmem + C::T_KSF;
+      const uint32_t t_psf = tmem + C::T_PSF, t_vsf = tmem + C::T_VSF;
+      uint32_t sfree_n = 0;
+      auto issue_s = [&](int j) {
+        for (int kb = 0; kb < C::KB; ++kb)
+          tmem_cp_32x128b_x4(t_ksf + kb * 4, smem_desc(base + L.ksf + (j * C::KB + kb) * 512, 0, 128, 0));
+        for (int kb = 0; kb < C::KB; ++kb) {
+          const uint64_t ad = smem_desc(base + L.q + kb * 32, 16, C::QK_SBO, C::QK_LAYOUT);
+          const uint64_t bd = smem_desc(base + L.k + j * C::QBYTES + kb * 32, 16, C::QK_SBO, C::QK_LAYOUT);
+          mma_mxf4nvf4(t_s, ad, bd, id_s, t_qsf + kb * 4, t_ksf + kb * 4, kb > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+      };
+      if (ok) {
+        for (int kb = 0; kb < C::KB; ++kb)
+          tmem_cp_32x128b_x4(t_qsf + kb * 4, smem_desc(base + L.qsf + kb * 512, 0, 128, 0));
+        // pass 1: scores for the row statistics
+        for (int j = 0; j < nc && ok; ++j) {
+          if (j > 0) ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
+          if (ok) issue_s(j);
+        }
+        // pass 2: recompute scores, PV
+        if (ok) ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
+        if (ok) issue_s(0);
+        for (int j = 0; j < nc && ok; ++j) {
+          if (j + 1 < nc) {
+            ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
+            if (!ok) break;
+            issue_s(j + 1);
+          }
+          ok = mbar_wait(p_full(j & 1), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t pb = base + L.p + (j & 1) * C::PBYTES;
+          for (int kb = 0; kb < 2; ++kb) {
+            tmem_cp_32x128b_x4(t_psf + kb * 4, smem_desc(base + L.psf + (j & 1) * 1024 + kb * 512, 0, 128, 0));
+            tmem_cp_32x128b_x4(t_vsf + kb * 4, smem_desc(base + L.vsf + (2 * j + kb) * 512, 0, 128, 0));
+          }
+          for (int kb = 0; kb < 2; ++kb) {
+            const uint64_t ad = smem_desc(pb + kb * 256, 128, 512, 0);           // interleaved, no swizzle
+            const uint64_t bd = smem_desc(base + L.v + j * C::VBYTES + kb * 32, 16, 512, 4);  // SWIZZLE_64B
+            mma_mxf4nvf4(t_o, ad, bd, id_o, t_psf + kb * 4, t_vsf + kb * 4, (j > 0 || kb > 0) ? 1u : 0u);
+          }
+          tc_commit(p_free(j & 1));
+        }
+        if (ok) tc_commit(o_full);
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;                 // row of the query tile == TMEM lane
+    const int tq = qt * 128 + r;                    // query token
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    const float cexp = scal[0] * scal[1] * scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    uint32_t sfull_n = 0;
+    bool ok = true;
+    uint32_t v[128];
+    auto load_s = [&](int j, int ncols) -> bool {
+      if (!mbar_wait(s_full, (sfull_n++) & 1u, err, kDevErrTimeoutFull)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c * 32 < ncols) tmem_ld_32x32b_x32(tmem + lane_addr + C::T_S + c * 32, v + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      return true;
+    };
+    // pass 1
+    for (int j = 0; j < nc && ok; ++j) {
+      const int nvalid = min(128, S - j * 128);
+      if (!(ok = load_s(j, nvalid))) break;
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i < nvalid) cm = fmaxf(cm, __uint_as_float(v[i]) * cexp);
+      const float mn = fmaxf(m, cm);
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i < nvalid) sum += exp2f(__uint_as_float(v[i]) * cexp - mn);
+      l = l * exp2f(m - mn) + sum;
+      m = mn;
+    }
+    const float inv_l = 1.0f / l;
+    // pass 2
+    for (int j = 0; j < nc && ok; ++j) {
+      const int nvalid = min(128, S - j * 128);
+      if (!(ok = load_s(j, nvalid))) break;
+      if (j >= 2 && !(ok = mbar_wait(p_free(j & 1), (uint32_t)((j >> 1) - 1) & 1u, err, kDevErrTimeoutEmpty)))
+        break;
+      uint8_t* pbuf = gbase + L.p + (j & 1) * C::PBYTES;
+      uint32_t sfw[2] = {0u, 0u};
+#pragma unroll
+      for (int blk = 0; blk < 8; ++blk) {
+        uint64_t codes = 0;
+        if (blk * 16 < nvalid) {
+          float pv[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int i = blk * 16 + e;
+            pv[e] = i < nvalid ? exp2f(__uint_as_float(v[i]) * cexp - m) * inv_l : 0.f;
+          }
+          float amax = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) amax = fmaxf(amax, pv[e]);
+          float dec;
+          const uint32_t sf = six_scale(amax, 2688.f, kInv2688, &dec);
+          codes = encode16_fast(pv, dec);
+          sfw[blk >> 2] |= sf << (8 * (blk & 3));
+        }
+        // interleaved K-major core matrices: (row group, 16-byte K chunk) at rg*512 + kc*128 + (r%8)*16
+        *reinterpret_cast<uint64_t*>(pbuf + (r >> 3) * 512 + (blk >> 1) * 128 + (r & 7) * 16 + (blk & 1) * 8) = codes;
+      }
+      uint8_t* psf = gbase + L.psf + (j & 1) * 1024;
+      const int so = (r & 31) * 16 + (r >> 5) * 4;
+      *reinterpret_cast<uint32_t*>(psf + so) = sfw[0];
+      *reinterpret_cast<uint32_t*>(psf + 512 + so) = sfw[1];
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(j & 1));
+    }
+    // epilogue
+    if (ok && mbar_wait(o_full, 0, err, kDevErrTimeoutTmem)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < C::DV / 32; ++c) tmem_ld_32x32b_x32(tmem + lane_addr + C::T_O + c * 32, v + c * 32);
+      tmem_wait_ld();
+      if (tq < S) {
+        const float ao = kInv2688 * scal[2];
+        const int b = bh / g.H, h = bh - b * g.H;
+        __nv_bfloat16* o = out + b * osb + (int64_t)tq * oss + h * osh;
+#pragma unroll
+        for (int d8 = 0; d8 < C::DV / 8; ++d8) {
+          if (d8 * 8 < g.D) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int d = d8 * 8 + 2 * e;
+              __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(v[d]) * ao + scal[4 + d],
+                                                        __uint_as_float(v[d + 1]) * ao + scal[4 + d + 1]);
+              w[e] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            *reinterpret_cast<uint4*>(o + d8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t rowbytes, int box_x, int box_y,
+                    CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)rowbytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VF4_OK;
+}
+
+template <int DP>
+static int launch_fwd(const AttnGeom& g, const uint8_t* ws, float scale, void* out, int64_t osb, int64_t osh,
+                      int64_t oss, cudaStream_t s) {
+  using C = AttnCfg<DP>;
+  AttnSmem L = attn_smem_layout<DP>(g.nc, g.S_pad);
+  if (L.total > 227 * 1024)
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: sequence %d too long for head dim %d", g.S, g.D);
+  CUtensorMap tq, tk, tv;
+  const CUtensorMapSwizzle qs = DP == 64 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (int st = make_map(&tq, ws + g.off_q, g.BH * g.S_pad, C::ROWB, C::ROWB, 128, qs)) return st;
+  if (int st = make_map(&tk, ws + g.off_k, g.BH * g.S_pad, C::ROWB, C::ROWB, 128, qs)) return st;
+  if (int st = make_map(&tv, ws + g.off_v, g.BH * C::DV, g.S_pad / 2, 64, C::DV, CU_TENSOR_MAP_SWIZZLE_64B))
+    return st;
+  auto kern = attn_fwd_kernel<DP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  dim3 grid(g.nc, (unsigned)g.BH);
+  kern<<<grid, C::THREADS, L.total, s>>>(tq, tk, tv, g, ws, L, scale, static_cast<__nv_bfloat16*>(out), osb, osh,
+                                         oss);
+  return launch_status("vf4_attn_nvfp4 (forward)");
+}
+
+}  // namespace vf4
+
+using namespace vf4;
+
+extern "C" {
+
+int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D) {
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
+  return make_geom(B, H, S, D).total;
+}
+
+int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                   int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
+                   int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, void* workspace,
+                   int64_t workspace_bytes, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: bad sizes");
+  if (D % 16 != 0 || D > 128) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim must be a multiple of 16, <= 128");
+  if (!q || !k || !v || !out || !workspace) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(workspace) ||
+      stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
+    return fail(VF4_ERR_ALIGN, "vf4_attn_nvfp4: 16-byte aligned pointers and strides (multiples of 8) needed");
+  if (B * H > 65535) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H must be <= 65535");
+  AttnGeom g = make_geom(B, H, S, D);
+  if (workspace_bytes < g.total)
+    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                (long long)g.total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  attn_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(q),
+                                                   static_cast<const __nv_bfloat16*>(k),
+                                                   static_cast<const __nv_bfloat16*>(v), stride_b, stride_h, stride_s,
+                                                   g, ws);
+  if (int st = launch_status("vf4_attn_nvfp4 (prep)")) return st;
+  if (g.Dp == 64) return launch_fwd<64>(g, ws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
+  return launch_fwd<128>(g, ws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
+}
+
+}  // extern "C"

@@ -111,19 +111,120 @@ VF4_DEV float block_mse_aten(const float* v, const uint32_t* codes, float dec) {
   return __fdiv_rn(s, 16.f);
 }
 
+// ---------------------------------------------------------------------------------------
+// Fast exact encoder.
+//
+// q = RN(x / dec) is obtained from inv = RN(1/dec) with one Markstein correction step
+// (P. Markstein, "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990): q0 = x*inv, r = x - q0*dec (exact with an FMA),
+// q = q0 + r*inv, which is the correctly rounded quotient for normal results.  The E2M1 code is
+// then produced by the hardware converter (cvt.rn.satfinite.e2m1x2.f32, nearest-even), and the
+// three ties where nearest-even rounds UP to an even code while the reference rounds DOWN
+// (|q| = 0.75, 1.75, 3.5) are moved one code down.  -0.0 is mapped to +0.0 first (the reference
+// sign is q < 0).  dec == 0 (scale underflow) gives q = +-inf or NaN in the reference: 7 / 15.
+// ---------------------------------------------------------------------------------------
+VF4_DEV float div_markstein(float x, float d, float inv) {
+  float q = __fmul_rn(x, inv);
+  float r = __fmaf_rn(-q, d, x);
+  return __fmaf_rn(r, inv, q);
+}
+
+// Four E2M1 bytes from eight values: byte i = (code(v[2i+1]) << 4) | code(v[2i]).
+VF4_DEV uint32_t cvt_e2m1x8(const float* v) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return out;
+}
+
+VF4_DEV uint32_t odd_tie(float q) {
+  float a = fabsf(q);
+  return (uint32_t)((a == 0.75f) | (a == 1.75f) | (a == 3.5f));
+}
+
+// Bit-exact reference encoding of 16 values with decode scale dec (>= 0).
+VF4_DEV uint64_t encode16_exact(const float* v, float dec) {
+  if (dec == 0.f) {
+    uint64_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p |= (uint64_t)(v[i] < 0.f ? 15u : 7u) << (4 * i);
+    return p;
+  }
+  const float inv = __frcp_rn(dec);
+  uint32_t w[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float q[8];
+    uint32_t fix = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      q[i] = __fadd_rn(div_markstein(v[8 * h + i], dec, inv), 0.0f);
+      fix |= odd_tie(q[i]) << (4 * i);
+    }
+    w[h] = cvt_e2m1x8(q) - fix;
+  }
+  return (uint64_t)w[0] | ((uint64_t)w[1] << 32);
+}
+
+// Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
+// (differs from the reference only within one ulp of a rounding boundary or on an exact tie).
+VF4_DEV uint64_t encode16_fast(const float* v, float dec) {
+  if (dec == 0.f) {
+    uint64_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p |= (uint64_t)(v[i] < 0.f ? 15u : 7u) << (4 * i);
+    return p;
+  }
+  const float inv = __frcp_rn(dec);
+  float q[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = v[i] * inv;
+  return (uint64_t)cvt_e2m1x8(q) | ((uint64_t)cvt_e2m1x8(q + 8) << 32);
+}
+
+// E4M3 block scale (six rule) and its decode value: bs = e4m3(min((amax/6)*s_enc, 448)).
+VF4_DEV uint32_t six_scale(float amax, float s_enc, float gs, float* dec) {
+  float bs_f = fminf(__fmul_rn(__fdiv_rn(fmaxf(amax, 1e-12f), 6.f), s_enc), 448.f);
+  uint32_t b = f32_to_e4m3(bs_f);
+  *dec = __fmul_rn(e4m3_to_f32(b), gs);
+  return b;
+}
+
+// GELU with erf from Abramowitz & Stegun 7.1.26 (|error of erf| <= 1.5e-7):
+//   erf(y) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-y^2),  t = 1/(1 + p y),  y >= 0.
+// gelu(x) = x * (1 - E) for x >= 0 and x * E for x < 0, with E = 0.5 (1 - erf(|x|/sqrt 2)).
+VF4_DEV float gelu_as(float x) {
+  const float y = fabsf(x) * 0.70710678118654752f;
+  float t, e;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(0.3275911f, y, 1.0f)));
+  float p = 0.5f * 1.061405429f;
+  p = __fmaf_rn(p, t, 0.5f * -1.453152027f);
+  p = __fmaf_rn(p, t, 0.5f * 1.421413741f);
+  p = __fmaf_rn(p, t, 0.5f * -0.284496736f);
+  p = __fmaf_rn(p, t, 0.5f * 0.254829592f);
+  p = p * t;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-y * y * 1.4426950408889634f));
+  const float E = p * e;
+  return x * (x >= 0.f ? 1.0f - E : E);
+}
+
 template <bool kMse>
 VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   amax = fmaxf(amax, 1e-12f);
-  uint32_t c6[16], sf6;
-  float dec6;
-  encode_candidate(v, amax, 6.f, s_enc, gs, c6, &sf6, &dec6);
   BlockQ r;
   if constexpr (kMse) {
-    uint32_t c4[16], sf4;
-    float dec4;
+    uint32_t c6[16], sf6, c4[16], sf4;
+    float dec6, dec4;
+    encode_candidate(v, amax, 6.f, s_enc, gs, c6, &sf6, &dec6);
     encode_candidate(v, amax, 4.f, s_enc, gs, c4, &sf4, &dec4);
     bool pick4 = block_mse_aten(v, c4, dec4) < block_mse_aten(v, c6, dec6);
     uint64_t p = 0;
@@ -132,11 +233,9 @@ VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
     r.packed = p;
     r.sf = pick4 ? sf4 : sf6;
   } else {
-    uint64_t p = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) p |= (uint64_t)c6[i] << (4 * i);
-    r.packed = p;
-    r.sf = sf6;
+    float dec;
+    r.sf = six_scale(amax, s_enc, gs, &dec);
+    r.packed = encode16_exact(v, dec);
   }
   return r;
 }

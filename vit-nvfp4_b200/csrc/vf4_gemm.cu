@@ -290,7 +290,8 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       } else {
-        // +b1 (bf16, after rounding the GEMM to bf16) -> exact GELU -> NVFP4 "six" cast
+        // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
+        // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32)
 #pragma unroll
         for (int g4 = 0; g4 < NC / 64; ++g4) {
           uint32_t sfw = 0;
@@ -315,11 +316,15 @@ __global__ void __launch_bounds__(320, 1)
                 for (int i = 0; i < 16; ++i) bb[i] = 0.f;
               }
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float t = bf16_round(bf16_round(__uint_as_float(v[blk * 16 + i]) * alpha) + bb[i]);
-                h[i] = gelu_erf(t);
-              }
-              BlockQ qz = quantize_block<false>(h, egs, esenc);
+              for (int i = 0; i < 16; ++i)
+                h[i] = gelu_as(__fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]));
+              float amax = 0.f;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+              float dec;
+              BlockQ qz;
+              qz.sf = six_scale(amax, esenc, egs, &dec);
+              qz.packed = encode16_fast(h, dec);
               if (row < p.M) {
                 *reinterpret_cast<uint64_t*>(p.out_packed + row * (int64_t)(p.N / 2) + col / 2) = qz.packed;
                 sfw |= qz.sf << (8 * b);

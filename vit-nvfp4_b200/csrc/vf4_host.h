@@ -32,6 +32,7 @@ EncodeTiledFn encode_tiled();
 // Per-family readers of the device error word (defined in each .cu).
 int cast_device_error(int clear);
 int gemm_device_error(int clear);
+int attn_device_error(int clear);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

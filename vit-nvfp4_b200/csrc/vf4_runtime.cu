@@ -92,7 +92,8 @@ int vf4_device_error(int clear) {
   if (e != cudaSuccess) return -1;
   int a = vf4::cast_device_error(clear);
   int b = vf4::gemm_device_error(clear);
-  return a ? a : b;
+  int c = vf4::attn_device_error(clear);
+  return a ? a : (b ? b : c);
 }
 
 }  // extern "C"

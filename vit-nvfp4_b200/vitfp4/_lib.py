@@ -34,8 +34,10 @@ SIGNATURES: dict[str, list] = {
     "vf4_unpack_e2m1": [_P, _L, _L, _P, _P],
     "vf4_to_blocked": [_P, _L, _L, _P, _P],
     "vf4_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _I, _P, _I, _P, _P, _P, _P],
+    "vf4_attn_workspace_size": [_L, _L, _L, _L],
+    "vf4_attn_nvfp4": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _L, _P],
 }
-_RESTYPE = {"vf4_last_error_string": ctypes.c_char_p}
+_RESTYPE = {"vf4_last_error_string": ctypes.c_char_p, "vf4_attn_workspace_size": ctypes.c_int64}
 
 
 class VitFp4Error(RuntimeError):

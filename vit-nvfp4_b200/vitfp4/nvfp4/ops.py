@@ -234,3 +234,61 @@ def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs):
                   _ptr(packed), _ptr(sf), _stream())
     _launched()
     return packed, sf
+
+
+_ws_cache: dict = {}
+
+
+def _attn_workspace(B: int, H: int, S: int, D: int, device) -> torch.Tensor:
+    n = int(_lib.lib().vf4_attn_workspace_size(B, H, S, D))
+    key = (device, torch.cuda.current_stream(device).cuda_stream)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < n:
+        ws = torch.empty(n, dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
+              strides: tuple[int, int, int], scale: float, out: torch.Tensor,
+              out_strides: tuple[int, int, int]) -> torch.Tensor:
+    """NVFP4 attention over bf16 q/k/v views sharing (stride_b, stride_h, stride_s) element strides."""
+    _need_cuda(q, k, v, out)
+    for t in (q, k, v, out):
+        if t.dtype != torch.bfloat16:
+            raise _lib.VitFp4Error("FP4 attention takes bf16 q/k/v/out")
+    ws = _attn_workspace(B, H, S, D, q.device)
+    _lib.call("vf4_attn_nvfp4", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _ptr(ws), ws.numel(),
+              _stream())
+    _launched(2)
+    return out
+
+
+def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """(B, H, S, D) q/k/v (any dtype; cast to bf16) -> (B, H, S, D) bf16."""
+    B, H, S, D = q.shape
+    qb, kb, vb = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
+    st = qb.stride()
+    shared = (kb.stride() == st and vb.stride() == st and st[3] == 1 and all(x % 8 == 0 for x in st[:3])
+              and all(t.data_ptr() % 16 == 0 for t in (qb, kb, vb)))
+    if shared:          # e.g. the (B,H,S,D) views of a packed qkv projection: read in place
+        strides = (st[0], st[1], st[2])
+    else:
+        qb, kb, vb = (t.contiguous() for t in (qb, kb, vb))
+        strides = (H * S * D, S * D, D)
+    out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
+    attention(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D))
+    return out.transpose(1, 2)
+
+
+def attention_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float) -> torch.Tensor:
+    """Packed (B, S, 3*H*D) projection output -> (B, S, H*D) bf16, read in place (no q/k/v copies)."""
+    B, S, C3 = qkv.shape
+    H = num_heads
+    D = C3 // (3 * H)
+    x = qkv if qkv.is_contiguous() else qkv.contiguous()
+    out = torch.empty((B, S, H * D), dtype=torch.bfloat16, device=qkv.device)
+    st = (S * C3, D, C3)
+    attention(x, x[..., H * D:], x[..., 2 * H * D:], B, H, S, D, st, scale, out, (S * H * D, D, H * D))
+    return out

@@ -130,12 +130,22 @@ class Block(nn.Module):
 
 
 class PatchEmbed(nn.Module):
+    """Non-overlapping patch projection.  Same parameters as timm's Conv2d(k=stride=patch),
+    evaluated as one (B*P, C*p*p) x (C*p*p, d) GEMM on the unfolded patches (the strided conv
+    is exactly this matmul, and cuDNN's conv path is several times slower on B200)."""
+
     def __init__(self, config: ViTConfig):
         super().__init__()
+        self.patch = config.patch_size
         self.proj = nn.Conv2d(config.in_chans, config.embed_dim, config.patch_size, config.patch_size)
 
     def forward(self, x):
-        return self.proj(x).flatten(2).transpose(1, 2)
+        B, C, Hh, Ww = x.shape
+        p = self.patch
+        g_h, g_w = Hh // p, Ww // p
+        patches = x.reshape(B, C, g_h, p, g_w, p).permute(0, 2, 4, 1, 3, 5).reshape(B, g_h * g_w, C * p * p)
+        w = self.proj.weight.reshape(self.proj.out_channels, -1)
+        return F.linear(patches, w, self.proj.bias)
 
 
 class VisionTransformer(nn.Module):
