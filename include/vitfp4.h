@@ -130,6 +130,19 @@ VF4_API int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t 
                            void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
                            void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
 
+/* vf4_attn_nvfp4 without a caller workspace, for callers that cannot allocate device memory
+ * (a runtime that owns all device memory through its own pool, or a plugin that may not
+ * allocate or synchronize the device while it serves requests).  No counterpart in the
+ * reference: the reference is Python and allocates freely.  The scratch is one fixed 16 MiB
+ * device array inside the library (held on every GPU that loads it until exit): calls needing
+ * more than vf4_attn_workspace_size(B,H,S,D) <= 16 MiB return VF4_ERR_UNSUPPORTED.  Its first
+ * call on a device resolves the array's device address, so make that call before any stream
+ * capture; all calls share the array, so calls that overlap on the GPU race.  Allocates nothing. */
+VF4_API int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* v, int64_t B, int64_t H,
+                                   int64_t S, int64_t D, int64_t stride_b, int64_t stride_h,
+                                   int64_t stride_s, float scale, void* out, int64_t out_stride_b,
+                                   int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

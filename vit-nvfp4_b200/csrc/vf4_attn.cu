@@ -17,6 +17,8 @@
 //   two-pass softmax from TMEM (pass 1: row max / sum; pass 2: recompute S, P = exp(S-m)/l),
 //   re-quantize P to NVFP4 in shared memory (scales staged for tcgen05.cp), and the PV MMA
 //   accumulates O in TMEM; the epilogue adds mean(v) and writes bf16 (B, S, H, D).
+#include <mutex>
+
 #include "vf4_common.cuh"
 #include "vf4_host.h"
 
@@ -608,3 +610,63 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc at all: a host runtime that has handed the whole device
+// to its own memory pool, or a plugin loaded into an inference server that forbids library
+// allocations (and the implicit device synchronisation cudaMalloc/cudaFree can cause) while
+// requests run.  vf4_attn_nvfp4_noalloc serves them: it runs the same two kernels as
+// vf4_attn_nvfp4, but its workspace is this file-scope device array instead of caller memory.
+//
+// Limits and contract:
+//   * at most kNoAllocScratchBytes (16 MiB) of workspace, i.e. vf4_attn_workspace_size(B,H,S,D)
+//     must not exceed it (about 25 ViT-L/14 images per call); larger calls return
+//     VF4_ERR_UNSUPPORTED and launch nothing;
+//   * the array lives on every GPU that loads the library until the process exits;
+//   * the host name g_attn_scratch is only a host-side stand-in for the symbol, never a device
+//     address: the first call on each device (with that device current) resolves the real
+//     address with cudaGetSymbolAddress and caches it, so make that first call before any
+//     stream capture;
+//   * every call shares the one array and it keeps the last call's contents; nothing in it
+//     has to start at zero (the prep kernel rewrites every byte the forward kernel reads);
+//   * calls whose kernels overlap on the GPU (different streams, no ordering) race on it.
+// ---------------------------------------------------------------------------------------
+namespace vf4 {
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;
+static __device__ __align__(256) uint8_t g_attn_scratch[kNoAllocScratchBytes];
+static uint8_t* g_scratch_ptr[64];
+static std::once_flag g_scratch_once[64];
+}  // namespace vf4
+
+extern "C" int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* v, int64_t B, int64_t H,
+                                      int64_t S, int64_t D, int64_t stride_b, int64_t stride_h,
+                                      int64_t stride_s, float scale, void* out, int64_t out_stride_b,
+                                      int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4_noalloc: bad sizes");
+  const int64_t need = (D % 16 == 0 && D <= 128) ? make_geom(B, H, S, D).total : 0;
+  if (need > kNoAllocScratchBytes)
+    return fail(VF4_ERR_UNSUPPORTED,
+                "vf4_attn_nvfp4_noalloc: needs %lld bytes of scratch, the fixed device array holds %lld; "
+                "split the batch or use vf4_attn_nvfp4 with a caller workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: no current device");
+  int setup = VF4_OK;
+  std::call_once(g_scratch_once[dev], [&] {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess) {
+      setup = fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return;
+    }
+    g_scratch_ptr[dev] = static_cast<uint8_t*>(p);
+  });
+  if (setup != VF4_OK) return setup;
+  if (!g_scratch_ptr[dev]) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: scratch address unavailable");
+  return vf4_attn_nvfp4(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b,
+                        out_stride_h, out_stride_s, g_scratch_ptr[dev], kNoAllocScratchBytes, stream);
+}
