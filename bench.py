@@ -167,11 +167,12 @@ def build_model(depth: int, attn: str, device):
 def run_vitfp4(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
+    from vitfp4 import replica
     from vitfp4.nvfp4 import ops
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    per_rank = args.batch // world
+    _, per_rank = replica.shard_range(args.batch, rank, world)
     torch.manual_seed(1234 + rank)
     model, counts = build_model(args.depth, args.attn, dev)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -232,12 +233,8 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
         d[0] += 1
         d[1] += flops
         d[2] += s.elapsed_time(e)
-    t = torch.tensor([ms, ms_e2e], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        gathered = [torch.empty_like(logits) for _ in range(world)]
-        dist.all_gather(gathered, logits.contiguous())          # the single final gather of logits
-    ms, ms_e2e = float(t[0]), float(t[1])
+    ms, ms_e2e = replica.max_over_ranks([ms, ms_e2e], device=dev)
+    replica.gather_logits(logits.float(), args.batch)        # the single final gather of logits
     if rank != 0:
         return 0
 
@@ -256,7 +253,7 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
                     if bf16_tf else "nominal dense FP4 (no measured peak)",
                     "frac_of_nominal_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4), "traffic": None}
     steps = args.steps
-    img_per_step = per_rank * world
+    img_per_step = args.batch
     line = {
         "metric": METRIC, "value": round(img_per_step * steps / (ms * 1e-3), 2), "unit": "images/s",
         "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms / steps, 3),
@@ -294,15 +291,14 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        import datetime
         import torch
         import torch.distributed as dist
+        from vitfp4 import replica
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         if args.impl == "reference":
             return run_reference(args, rank, world)
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+        replica.init_from_env("nccl", timeout_s=120.0, device=torch.device("cuda", local_rank))
         try:
             return run_vitfp4(args, rank, world, local_rank)
         finally:
