@@ -44,6 +44,7 @@ def _args():
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch (images)")
     ap.add_argument("--depth", type=int, default=24)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--unfused", action="store_true", help="keep the per-module path (no fused blocks)")
     return ap.parse_args()
 
 
@@ -149,10 +150,10 @@ def run_reference(args, rank: int, world: int):
 
 
 # ------------------------------------------------------------------------------- vitfp4 arm
-def build_model(depth: int, attn: str, device):
+def build_model(depth: int, attn: str, device, fused: bool = True):
     import torch
     from vitfp4 import vit
-    from vitfp4.ptq import enable_quant_attention, fuse_mlps, quantize_vit, vit_attn_policy
+    from vitfp4.ptq import enable_quant_attention, fuse_mlps, fuse_norms, quantize_vit, vit_attn_policy
     cfg = dict(vit.VIT_L14)
     cfg["depth"] = depth
     model = vit.build_vit(seed=0, **cfg).to(device=device, dtype=torch.bfloat16).eval()
@@ -161,7 +162,8 @@ def build_model(depth: int, attn: str, device):
     n_att = 0
     if attn == "nvfp4":
         n_att = enable_quant_attention(model, vit_attn_policy(depth, 0, 0, "blocks"), qk="nvfp4", pv="nvfp4")
-    return model, {"fused_mlps": n_mlp, "quant_linears": n_lin, "fp4_attention": n_att}
+    n_blk = fuse_norms(model) if fused else 0
+    return model, {"fused_mlps": n_mlp, "quant_linears": n_lin, "fp4_attention": n_att, "fused_blocks": n_blk}
 
 
 def run_vitfp4(args, rank: int, world: int, local_rank: int):
@@ -174,7 +176,7 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
     dev = torch.device("cuda", local_rank)
     _, per_rank = replica.shard_range(args.batch, rank, world)
     torch.manual_seed(1234 + rank)
-    model, counts = build_model(args.depth, args.attn, dev)
+    model, counts = build_model(args.depth, args.attn, dev, fused=not args.unfused)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     images = torch.randn(per_rank, 3, 224, 224, device=dev, generator=gen).to(torch.bfloat16)
     host_images = images.cpu().pin_memory()

@@ -89,6 +89,18 @@ VF4_API int vf4_cast_nvfp4(const void* x, int dtype, int64_t M, int64_t K, int64
                    uint8_t* out_sf_swizzled, uint8_t* out_sf_linear, float* gs_out,
                    vf4_stream_t stream);
 
+/* LayerNorm fused into the NVFP4 activation cast, optionally after a fused residual + LayerScale
+ * (replaces the bf16 chain  x = x + ls(y);  h = norm(x);  quantize_to_nvfp4(h)  that a timm-style
+ * block runs around qlinear.py:42-47 / fused_mlp.py:47; the reference leaves it to torch):
+ *   if y != NULL: x' = bf16(x + bf16(y * gamma)) (gamma NULL -> 1) is written to x_out (may be x)
+ *   h = bf16(LayerNorm(x'; ln_w, ln_b, eps)) is cast to NVFP4 (six rule) with the static global gs,
+ *   or, when gs == NULL, with the dynamic amax(|h|)/(6*448) written to gs_out (two passes).
+ * x, y, x_out: (M, K) bf16 contiguous; gamma, ln_w, ln_b: (K,) bf16; K % 64 == 0, K <= 1280.
+ * out_packed (M, K/2); out_sf swizzled (ceil128(M) x K/16, padding rows zeroed). */
+VF4_API int vf4_ln_cast_nvfp4(const void* x, const void* y, const void* gamma, void* x_out, const void* ln_w,
+                              const void* ln_b, float eps, int64_t M, int64_t K, const float* gs,
+                              uint8_t* out_packed, uint8_t* out_sf, float* gs_out, vf4_stream_t stream);
+
 /* pack_e2m1 (pack.py:4-9): codes (rows, K) -> (rows, K/2). K % 2 == 0. */
 VF4_API int vf4_pack_e2m1(const uint8_t* codes, int64_t rows, int64_t K, uint8_t* out, vf4_stream_t stream);
 

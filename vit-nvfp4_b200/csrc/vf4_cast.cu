@@ -265,6 +265,202 @@ static void dispatch_cast(const void* x, int64_t M, int64_t K, int64_t ld, const
 #undef VF4_CAST_CASE
 }
 
+// ---------------------------------------------------------------------------------------
+// LayerNorm fused into the NVFP4 cast (optionally with the residual + LayerScale before it).
+// One warp per row; lane l holds elements [256c + 8l, 256c + 8l + 8) of chunk c (16-byte
+// loads, coalesced), so an NVFP4 block of 16 is a lane pair.  Rounding points mirror the
+// unfused reference ops on bf16 tensors:  x' = bf16(x + bf16(y * gamma)),
+// h = bf16((x' - mean) * rstd * w + b), then the six-rule quantizer on h.
+//   kMode 0: write x' (if kRes) and atomically max |h| into amax_out (dynamic global scale)
+//   kMode 1: write x' (if kRes) and quantize h with the global scale *gs
+// ---------------------------------------------------------------------------------------
+VF4_DEV float bf16_bits_lo(uint32_t w) { return __uint_as_float(w << 16); }
+VF4_DEV float bf16_bits_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+template <int NC, bool kRes, int kMode>
+__global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      const __nv_bfloat16* __restrict__ y,
+                                                      const __nv_bfloat16* __restrict__ gamma,
+                                                      __nv_bfloat16* __restrict__ x_out,
+                                                      const __nv_bfloat16* __restrict__ ln_w,
+                                                      const __nv_bfloat16* __restrict__ ln_b, float eps,
+                                                      int64_t M, int K, const float* __restrict__ gs_ptr,
+                                                      float* __restrict__ amax_out,
+                                                      uint8_t* __restrict__ out_packed,
+                                                      uint8_t* __restrict__ out_sf) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_g = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t Mp = (M + 127) & ~int64_t(127);
+  const int ncb = K / 64;
+  float gs = 1.f, s_enc = 1.f;
+  if constexpr (kMode == 1) {
+    gs = *gs_ptr;
+    s_enc = __fdiv_rn(1.0f, gs);
+  }
+  // LayerNorm affine parameters of this lane's elements
+  float w[NC][8], bb[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int e0 = 256 * c + 8 * lane;
+    if (e0 < K) {
+      uint4 a = __ldg(reinterpret_cast<const uint4*>(ln_w + e0));
+      uint4 b = __ldg(reinterpret_cast<const uint4*>(ln_b + e0));
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w[c][2 * i] = bf16_bits_lo(aw[i]);
+        w[c][2 * i + 1] = bf16_bits_hi(aw[i]);
+        bb[c][2 * i] = bf16_bits_lo(bw[i]);
+        bb[c][2 * i + 1] = bf16_bits_hi(bw[i]);
+      }
+    }
+  }
+  float lane_amax = 0.f;
+  for (int64_t row = warp_g; row < Mp; row += nwarps) {
+    if (row >= M) {  // zero the scale padding rows of the last 128-row tile
+      if constexpr (kMode == 1) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const int e0 = 256 * c + 8 * lane;
+          if (e0 < K && (lane & 7) == 0) {
+            const int col = e0 / 16;
+            *reinterpret_cast<uint32_t*>(out_sf + ((row >> 7) * ncb + (col >> 2)) * 512 + (row & 31) * 16 +
+                                         ((row >> 5) & 3) * 4) = 0u;
+          }
+        }
+      }
+      continue;
+    }
+    float v[NC][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int e0 = 256 * c + 8 * lane;
+      if (e0 < K) {
+        uint4 a = __ldg(reinterpret_cast<const uint4*>(x + row * K + e0));
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[c][2 * i] = bf16_bits_lo(aw[i]);
+          v[c][2 * i + 1] = bf16_bits_hi(aw[i]);
+        }
+        if constexpr (kRes) {
+          uint4 yv = __ldg(reinterpret_cast<const uint4*>(y + row * K + e0));
+          const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+          float g[8];
+          if (gamma) {
+            uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + e0));
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              g[2 * i] = bf16_bits_lo(gw[i]);
+              g[2 * i + 1] = bf16_bits_hi(gw[i]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) g[i] = 1.f;
+          }
+          uint32_t ow[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float y0 = bf16_round(bf16_bits_lo(yw[i]) * g[2 * i]);
+            const float y1 = bf16_round(bf16_bits_hi(yw[i]) * g[2 * i + 1]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[c][2 * i] + y0, v[c][2 * i + 1] + y1);
+            ow[i] = *reinterpret_cast<uint32_t*>(&h2);
+            v[c][2 * i] = bf16_bits_lo(ow[i]);
+            v[c][2 * i + 1] = bf16_bits_hi(ow[i]);
+          }
+          *reinterpret_cast<uint4*>(x_out + row * K + e0) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum += v[c][i];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / (float)K;
+    float sq = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+      if (256 * c + 8 * lane < K) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d = v[c][i] - mean;
+          sq += d * d;
+        }
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = rsqrtf(sq / (float)K + eps);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int e0 = 256 * c + 8 * lane;
+      const bool in = e0 < K;   // warp-uniform per (c, lane group of 8) -> shuffles stay converged
+      float h[8];
+      float am = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        h[i] = in ? bf16_round((v[c][i] - mean) * rstd * w[c][i] + bb[c][i]) : 0.f;
+        am = fmaxf(am, fabsf(h[i]));
+      }
+      if constexpr (kMode == 0) {
+        lane_amax = fmaxf(lane_amax, am);
+      } else {
+        const float bam = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        float dec;
+        const uint32_t sf = six_scale(bam, s_enc, gs, &dec);
+        const uint32_t codes = encode8_exact(h, dec);
+        if (in) *reinterpret_cast<uint32_t*>(out_packed + row * (K / 2) + e0 / 2) = codes;
+        // scale bytes of SF columns 16c + 4g .. +3 live in lanes 8g, 8g+2, 8g+4, 8g+6
+        uint32_t b1 = __shfl_down_sync(0xffffffffu, sf, 2);
+        uint32_t b2 = __shfl_down_sync(0xffffffffu, sf, 4);
+        uint32_t b3 = __shfl_down_sync(0xffffffffu, sf, 6);
+        if (in && (lane & 7) == 0) {
+          const int col = e0 / 16;
+          *reinterpret_cast<uint32_t*>(out_sf + ((row >> 7) * ncb + (col >> 2)) * 512 + (row & 31) * 16 +
+                                       ((row >> 5) & 3) * 4) = sf | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+      }
+    }
+  }
+  if constexpr (kMode == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lane_amax = fmaxf(lane_amax, __shfl_xor_sync(0xffffffffu, lane_amax, o));
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), __float_as_uint(lane_amax));
+  }
+}
+
+template <int NC>
+static void launch_ln(bool res, int mode, const void* x, const void* y, const void* gamma, void* x_out,
+                      const void* w, const void* b, float eps, int64_t M, int K, const float* gs, float* amax,
+                      uint8_t* op, uint8_t* sf, cudaStream_t s) {
+  const int64_t Mp = (M + 127) & ~int64_t(127);
+  int grid = grid_for(Mp * 32);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto Y = static_cast<const __nv_bfloat16*>(y);
+  auto G = static_cast<const __nv_bfloat16*>(gamma);
+  auto XO = static_cast<__nv_bfloat16*>(x_out);
+  auto W = static_cast<const __nv_bfloat16*>(w);
+  auto B = static_cast<const __nv_bfloat16*>(b);
+  if (res && mode == 0) ln_cast_kernel<NC, true, 0><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
+  else if (res) ln_cast_kernel<NC, true, 1><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
+  else if (mode == 0) ln_cast_kernel<NC, false, 0><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
+  else ln_cast_kernel<NC, false, 1><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
+}
+
+static void dispatch_ln(int nc, bool res, int mode, const void* x, const void* y, const void* gamma, void* x_out,
+                        const void* w, const void* b, float eps, int64_t M, int K, const float* gs, float* amax,
+                        uint8_t* op, uint8_t* sf, cudaStream_t s) {
+  switch (nc) {
+    case 1: launch_ln<1>(res, mode, x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s); break;
+    case 2: launch_ln<2>(res, mode, x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s); break;
+    case 3: launch_ln<3>(res, mode, x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s); break;
+    case 4: launch_ln<4>(res, mode, x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s); break;
+    default: launch_ln<5>(res, mode, x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s); break;
+  }
+}
+
 }  // namespace vf4
 
 using namespace vf4;
@@ -347,6 +543,35 @@ int vf4_cast_nvfp4(const void* x, int dtype, int64_t M, int64_t K, int64_t ld, c
     dispatch_cast<float>(x, M, K, ld, use_gs, block_select == VF4_MSE, gelu, bias, out_packed,
                          out_sf_swizzled, out_sf_linear, s);
   return launch_status("vf4_cast_nvfp4");
+}
+
+int vf4_ln_cast_nvfp4(const void* x, const void* y, const void* gamma, void* x_out, const void* ln_w,
+                      const void* ln_b, float eps, int64_t M, int64_t K, const float* gs, uint8_t* out_packed,
+                      uint8_t* out_sf, float* gs_out, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (M < 0 || K <= 0 || K % 64 != 0 || K > 1280)
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_ln_cast_nvfp4: need K %% 64 == 0 and K <= 1280 (K=%lld)", (long long)K);
+  if (!ln_w || !ln_b || (M > 0 && (!x || !out_packed || !out_sf)) || (y && !x_out) || (!gs && !gs_out))
+    return fail(VF4_ERR_ARG, "vf4_ln_cast_nvfp4: missing pointer");
+  const void* ps[] = {x, y, gamma, x_out, ln_w, ln_b, out_packed, out_sf};
+  for (const void* p : ps)
+    if (p && !aligned16(p)) return fail(VF4_ERR_ALIGN, "vf4_ln_cast_nvfp4: pointers must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int nc = (int)((K + 255) / 256);
+  const bool res = y != nullptr;
+  if (gs) {
+    if (gs_out && gs_out != gs && cudaMemcpyAsync(gs_out, gs, 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return fail(VF4_ERR_CUDA, "vf4_ln_cast_nvfp4: gs copy failed");
+    dispatch_ln(nc, res, 1, x, y, gamma, x_out, ln_w, ln_b, eps, M, (int)K, gs, nullptr, out_packed, out_sf, s);
+    return launch_status("vf4_ln_cast_nvfp4");
+  }
+  // dynamic global scale: pass 1 (residual write + amax of the normalised rows), scale, pass 2
+  if (cudaMemsetAsync(gs_out, 0, 4, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_ln_cast_nvfp4: memset");
+  dispatch_ln(nc, res, 0, x, y, gamma, x_out, ln_w, ln_b, eps, M, (int)K, nullptr, gs_out, nullptr, nullptr, s);
+  global_scale_kernel<<<1, 32, 0, s>>>(gs_out, 6.f * 448.f, gs_out);
+  dispatch_ln(nc, false, 1, res ? x_out : x, nullptr, nullptr, nullptr, ln_w, ln_b, eps, M, (int)K, gs_out, nullptr,
+              out_packed, out_sf, s);
+  return launch_status("vf4_ln_cast_nvfp4");
 }
 
 int vf4_pack_e2m1(const uint8_t* codes, int64_t rows, int64_t K, uint8_t* out, vf4_stream_t stream) {

@@ -172,6 +172,25 @@ VF4_DEV uint64_t encode16_exact(const float* v, float dec) {
   return (uint64_t)w[0] | ((uint64_t)w[1] << 32);
 }
 
+// Bit-exact reference encoding of 8 values (half a block) with decode scale dec (>= 0).
+VF4_DEV uint32_t encode8_exact(const float* v, float dec) {
+  if (dec == 0.f) {
+    uint32_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p |= (v[i] < 0.f ? 15u : 7u) << (4 * i);
+    return p;
+  }
+  const float inv = __frcp_rn(dec);
+  float q[8];
+  uint32_t fix = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    q[i] = __fadd_rn(div_markstein(v[i], dec, inv), 0.0f);
+    fix |= odd_tie(q[i]) << (4 * i);
+  }
+  return cvt_e2m1x8(q) - fix;
+}
+
 // Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
 // (differs from the reference only within one ulp of a rounding boundary or on an exact tie).
 VF4_DEV uint64_t encode16_fast(const float* v, float dec) {

@@ -292,3 +292,27 @@ def attention_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float) -> tor
     st = (S * C3, D, C3)
     attention(x, x[..., H * D:], x[..., 2 * H * D:], B, H, S, D, st, scale, out, (S * H * D, D, H * D))
     return out
+
+
+def ln_cast(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float, gs: torch.Tensor | None = None,
+            y: torch.Tensor | None = None, gamma: torch.Tensor | None = None, x_out: torch.Tensor | None = None):
+    """LayerNorm fused into the NVFP4 cast, optionally after x' = x + y * gamma (written to x_out).
+
+    x, y: (M, K) bf16 contiguous.  Returns (packed (M, K/2), sf_swizzled, gs, x') where x' is x when
+    no residual is given.  ``gs`` None -> dynamic global scale of the normalised rows."""
+    _need_cuda(x, y, gamma, ln_w, ln_b)
+    M, K = x.shape
+    dev = x.device
+    if y is not None and x_out is None:
+        x_out = torch.empty_like(x)
+    packed = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+    sf = torch.empty(sf_swizzled_numel(M, K), dtype=torch.uint8, device=dev)
+    gs_in = None if gs is None else gs.reshape(()).to(torch.float32).contiguous()
+    gs_out = torch.empty((), dtype=torch.float32, device=dev) if gs_in is None else None
+    w = ln_w.to(torch.bfloat16).contiguous()
+    b = ln_b.to(torch.bfloat16).contiguous()
+    g = None if gamma is None else gamma.to(torch.bfloat16).contiguous()
+    _lib.call("vf4_ln_cast_nvfp4", _ptr(x), _ptr(y), _ptr(g), _ptr(x_out), _ptr(w), _ptr(b), float(eps), M, K,
+              _ptr(gs_in), _ptr(packed), _ptr(sf), _ptr(gs_out), _stream())
+    _launched(1 if gs_in is not None else 3)
+    return packed, sf, (gs_out if gs_in is None else gs_in), (x if y is None else x_out)

@@ -3,6 +3,7 @@ from .qlinear import QuantLinear
 from .policy import vit_block_policy, block_index
 from .qattention import enable_quant_attention, vit_attn_policy
 from .fused_mlp import FusedNVFP4MLP, fuse_mlps
+from .fused_block import FusedNVFP4Block, fuse_norms
 from .convert import quantize_model
 from .models import ModelSpec, model_spec, find_block_container, quantize_vit
 from .diagnostics import tensor_cosine
@@ -10,5 +11,5 @@ from .diagnostics import tensor_cosine
 __all__ = [
     "QuantLinear", "vit_block_policy", "block_index", "enable_quant_attention", "vit_attn_policy",
     "FusedNVFP4MLP", "fuse_mlps", "quantize_model", "ModelSpec", "model_spec", "find_block_container",
-    "quantize_vit", "tensor_cosine",
+    "quantize_vit", "tensor_cosine", "FusedNVFP4Block", "fuse_norms",
 ]

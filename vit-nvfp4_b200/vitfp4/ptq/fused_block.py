@@ -1,0 +1,94 @@
+"""Fused timm / DINOv2-style transformer block for the W4A4 path.
+
+A converted block (``norm1 -> attn{qkv: QuantLinear, proj: QuantLinear} -> ls1 -> +x -> norm2 ->
+mlp: FusedNVFP4MLP -> ls2 -> +x``) spends most of its non-GEMM time in bf16 LayerNorm,
+LayerScale, residual adds and the activation casts that follow them.  ``FusedNVFP4Block`` runs the
+same computation with those steps fused:
+
+  norm1 + dynamic NVFP4 cast ............ one kernel pair (amax pass, quantize pass)
+  qkv GEMM (+bias) -> attention -> proj QuantLinear (cast + GEMM + bias)
+  x + ls1(proj) + norm2 + static cast .... one kernel (residual written once, normalised rows
+                                           quantized with the MLP's calibrated gx)
+  fc1 GEMM (+b1 -> GELU -> NVFP4 epilogue) -> fc2 GEMM (+b2)
+  x + ls2(fc2) ........................... one fused multiply-add
+
+Numerics follow the unfused modules (bf16 rounding after LayerScale, after the residual add and
+after LayerNorm); only the kernels change.  ``fuse_norms`` converts every eligible block in place.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..nvfp4 import ops
+from .fused_mlp import FusedNVFP4MLP, _u8
+from .qlinear import QuantLinear
+
+
+def _gamma(ls: nn.Module):
+    return getattr(ls, "gamma", None) if not isinstance(ls, nn.Identity) else None
+
+
+class FusedNVFP4Block(nn.Module):
+    def __init__(self, block: nn.Module):
+        super().__init__()
+        self.norm1, self.attn, self.ls1 = block.norm1, block.attn, block.ls1
+        self.norm2, self.mlp, self.ls2 = block.norm2, block.mlp, block.ls2
+
+    @staticmethod
+    def eligible(block: nn.Module) -> bool:
+        attn = getattr(block, "attn", None)
+        return (not isinstance(block, FusedNVFP4Block) and isinstance(getattr(block, "norm1", None), nn.LayerNorm) and isinstance(getattr(block, "norm2", None), nn.LayerNorm)
+                and attn is not None and isinstance(getattr(attn, "qkv", None), QuantLinear)
+                and isinstance(getattr(attn, "proj", None), QuantLinear) and isinstance(getattr(block, "mlp", None), FusedNVFP4MLP)
+                and block.norm1.weight is not None and block.norm1.bias is not None
+                and block.norm1.normalized_shape[0] % 64 == 0 and block.norm1.normalized_shape[0] <= 1280)
+
+    def _attention(self, qkv: torch.Tensor) -> torch.Tensor:
+        a = self.attn
+        B, S, _ = qkv.shape
+        H, D = a.num_heads, a.head_dim
+        if getattr(a, "_nvfp4_attn", False) and a._nvfp4_qk == "nvfp4" and a._nvfp4_pv == "nvfp4":
+            return ops.attention_packed_qkv(qkv, H, a.scaling)
+        if getattr(a, "_nvfp4_attn", False):
+            raise NotImplementedError("fused block: only the nvfp4/nvfp4 and bf16 attention routes are built")
+        q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+        return F.scaled_dot_product_attention(q, k, v, scale=a.scaling).transpose(1, 2).reshape(B, S, H * D)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, S, C = x.shape
+        x2 = x.reshape(B * S, C)
+        if x2.dtype != torch.bfloat16 or not x2.is_contiguous():
+            x2 = x2.to(torch.bfloat16).contiguous()
+        qkv_l: QuantLinear = self.attn.qkv
+        proj_l: QuantLinear = self.attn.proj
+        # norm1 -> NVFP4 (QuantLinear's activation global: static if calibrated, else dynamic)
+        ap, asf, ag, _ = ops.ln_cast(x2, self.norm1.weight, self.norm1.bias, self.norm1.eps, gs=qkv_l.x_global_scale)
+        wp, wsf = qkv_l._packed_weight()
+        qkv = ops.gemm(ap, asf, ag, wp, wsf, qkv_l.w_global_scale, bias=qkv_l.bias).reshape(B, S, -1)
+        o = self._attention(qkv)
+        y = proj_l(o).reshape(B * S, C)
+        mlp: FusedNVFP4MLP = self.mlp
+        if mlp.gx is None:   # first call: calibrate the MLP's static globals exactly as the module does
+            x_mid = (x2 + self.ls1(y.reshape(B, S, C)).reshape(B * S, C))
+            mlp._calibrate(F.layer_norm(x_mid, (C,), self.norm2.weight, self.norm2.bias, self.norm2.eps))
+        # x + ls1(y) -> norm2 -> NVFP4 with the MLP's static gx; the new residual x_mid is written once
+        hp, hsf, gx, x_mid = ops.ln_cast(x2, self.norm2.weight, self.norm2.bias, self.norm2.eps, gs=mlp.gx, y=y,
+                                         gamma=_gamma(self.ls1))
+        gp, gsf = ops.gemm_gelu_nvfp4(hp, hsf, gx, _u8(mlp.w1q), _u8(mlp.w1sf), mlp.w1g, mlp.b1, mlp.gh)
+        y2 = ops.gemm(gp, gsf, mlp.gh, _u8(mlp.w2q), _u8(mlp.w2sf), mlp.w2g, bias=mlp.b2)
+        g2 = _gamma(self.ls2)
+        out = torch.addcmul(x_mid, y2, g2) if g2 is not None else x_mid + y2
+        return out.reshape(B, S, C)
+
+
+def fuse_norms(model: nn.Module) -> int:
+    """Replace every eligible converted block (see FusedNVFP4Block.eligible) in place; returns the count."""
+    n = 0
+    for name, mod in list(model.named_modules()):
+        for cname, child in list(mod.named_children()):
+            if FusedNVFP4Block.eligible(child):
+                setattr(mod, cname, FusedNVFP4Block(child))
+                n += 1
+    return n

@@ -59,9 +59,16 @@ class QuantLinear(nn.Module):
         codes, bscale, gscale = quantize_to_nvfp4(w.float(), 16, block_select=w_block_select)
         return cls(codes, bscale, gscale, linear.bias, linear.in_features, linear.out_features)
 
+    @staticmethod
+    def _version(t: torch.Tensor) -> int:
+        try:
+            return t._version
+        except RuntimeError:   # inference-mode tensors carry no version counter
+            return -1
+
     def _packed_weight(self):
-        key = (self.w_codes.data_ptr(), self.w_codes._version, self.w_block_scale.data_ptr(),
-               self.w_block_scale._version, self.w_codes.device)
+        key = (self.w_codes.data_ptr(), self._version(self.w_codes), self.w_block_scale.data_ptr(),
+               self._version(self.w_block_scale), self.w_codes.device)
         if self.w_packed is None or key != self._packed_key:
             self.w_packed = ops.pack_e2m1(self.w_codes.contiguous())
             self.w_sf = ops.to_blocked(self.w_block_scale.contiguous())
