@@ -326,6 +326,18 @@ VF4_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* m, int32_t x, int32_t 
       : "memory");
 }
 
+// 2-D tensor store shared -> global (bulk-group completion); coordinates in elements.
+VF4_DEV void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+VF4_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has finished READING shared memory.
+VF4_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+VF4_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Plain (non-tensor) bulk copy global -> shared; dst/src 16B aligned, bytes % 16 == 0.
 VF4_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(

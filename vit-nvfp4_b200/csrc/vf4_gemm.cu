@@ -16,6 +16,8 @@
 //               quadrant, each half of the columns), release TMEM, then scale / bias /
 //               GELU / NVFP4-quantize from registers and store
 // Every wait is bounded (mbar_wait); a timeout records a device error and unwinds.
+#include <string.h>
+
 #include "vf4_common.cuh"
 #include "vf4_host.h"
 
@@ -37,7 +39,7 @@ template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int KB_PER_STAGE = 4;                   // 4 x K64 MMAs = 256 elements = 128 B
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int SFA_BYTES = KB_PER_STAGE * 512;
@@ -51,8 +53,10 @@ struct GemmCfg {
   static constexpr int SFB_SLOT = KB_PER_STAGE * SFB_PER_KB;
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 320;
+  static constexpr int EPI_WARP_BYTES = 4096;               // per epilogue warp: 32 rows x 128 B
+  static constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 16;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(ACC_STAGES * BN <= SFA_TCOL, "accumulators overlap the scale slots");
   static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
   static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment");
@@ -78,20 +82,22 @@ struct GemmParams {
 template <int BN, int EPI, bool kF32>
 __global__ void __launch_bounds__(320, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;   // epilogue staging buffers
+  const uint32_t bar0 = epi0 + C::EPI_BYTES;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + C::ACC_STAGES + a); };
   const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 2 * C::ACC_STAGES);
   uint32_t* tmem_slot =
-      reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 2 * C::ACC_STAGES + 1));
+      reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES +
+                                  8 * (2 * C::STAGES + 2 * C::ACC_STAGES + 1));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = &g_gemm_err;
@@ -109,6 +115,7 @@ __global__ void __launch_bounds__(320, 1)
     fence_mbar_init();
     tma_prefetch(&tmA);
     tma_prefetch(&tmB);
+    if (!kF32) tma_prefetch(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -243,8 +250,11 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) mbar_arrive(tempty_bar(acc));
 
       const int64_t row = (int64_t)mb * 128 + q * 32 + lane;
+      const int row0 = mb * 128 + q * 32;        // first row of this warp's 32-row slab
       const int col0 = nb * BN + half * NC;
-      if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
+      const uint32_t ebuf = epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES;
+      uint8_t* ebuf_g = gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES;
+      if constexpr (EPI != VF4_EPI_GELU_NVFP4 && kF32) {
         if (row < p.M) {
 #pragma unroll
           for (int g = 0; g < NC / 8; ++g) {
@@ -253,45 +263,69 @@ __global__ void __launch_bounds__(320, 1)
               float y[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[g * 8 + i]) * alpha;
-              if constexpr (kF32) {
-                if (EPI == VF4_EPI_BIAS && p.bias) {
-                  uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-                  const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    y[2 * i] += __uint_as_float(b4[i] << 16);
-                    y[2 * i + 1] += __uint_as_float(b4[i] & 0xFFFF0000u);
-                  }
-                }
-                float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
-                o[0] = make_float4(y[0], y[1], y[2], y[3]);
-                o[1] = make_float4(y[4], y[5], y[6], y[7]);
-              } else {
-                if (EPI == VF4_EPI_BIAS && p.bias) {
-                  // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
-                  uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-                  const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
-                    y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
-                  }
-                }
-                uint32_t w[4];
+              if (EPI == VF4_EPI_BIAS && p.bias) {
+                uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+                const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                  __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
-                  w[i] = *reinterpret_cast<uint32_t*>(&h);
+                  y[2 * i] += __uint_as_float(b4[i] << 16);
+                  y[2 * i + 1] += __uint_as_float(b4[i] & 0xFFFF0000u);
                 }
-                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
               }
+              float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
+              o[0] = make_float4(y[0], y[1], y[2], y[3]);
+              o[1] = make_float4(y[4], y[5], y[6], y[7]);
+            }
+          }
+        }
+      } else if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
+        // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
+        // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
+#pragma unroll
+        for (int c = 0; c < NC / 64; ++c) {
+          const int colc = col0 + c * 64;
+          if (colc < p.N) {
+            if (lane == 0) bulk_wait_read();      // the previous store has left the buffer
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int col = colc + j * 8;
+              float y[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * 64 + j * 8 + i]) * alpha;
+              if (EPI == VF4_EPI_BIAS && p.bias && col < p.N) {
+                // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
+                uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+                const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
+                  y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
+                }
+              }
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              *reinterpret_cast<uint4*>(ebuf_g + lane * 128 + ((j ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmOut, ebuf, colc, row0);   // rows >= M and columns >= N are clipped
+              bulk_commit();
             }
           }
         }
       } else {
         // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
-        // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32)
+        // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).
+        // Packed codes (NC/2 bytes per row) are staged in shared memory and stored by TMA;
+        // the 4-byte scale words go straight to the 128x4-tiled layout.
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
 #pragma unroll
         for (int g4 = 0; g4 < NC / 64; ++g4) {
           uint32_t sfw = 0;
@@ -300,6 +334,7 @@ __global__ void __launch_bounds__(320, 1)
             const int blk = g4 * 4 + b;
             const int col = col0 + blk * 16;
             float h[16];
+            uint64_t packed = 0;
             if (col < p.N) {
               float bb[16];
               if (p.bias) {
@@ -322,14 +357,11 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
               float dec;
-              BlockQ qz;
-              qz.sf = six_scale(amax, esenc, egs, &dec);
-              qz.packed = encode16_fast(h, dec);
-              if (row < p.M) {
-                *reinterpret_cast<uint64_t*>(p.out_packed + row * (int64_t)(p.N / 2) + col / 2) = qz.packed;
-                sfw |= qz.sf << (8 * b);
-              }
+              const uint32_t sf = six_scale(amax, esenc, egs, &dec);
+              packed = encode16_fast(h, dec);
+              if (row < p.M) sfw |= sf << (8 * b);
             }
+            *reinterpret_cast<uint64_t*>(ebuf_g + lane * (NC / 2) + blk * 8) = packed;
           }
           const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
           if (col0 + g4 * 64 < p.N) {
@@ -337,8 +369,16 @@ __global__ void __launch_bounds__(320, 1)
             *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
           }
         }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0 && col0 < p.N) {
+          tma_store_2d(&tmOut, ebuf, col0 / 2, row0);
+          bulk_commit();
+        }
       }
     }
+    if (lane == 0) bulk_wait_all();   // stores issued by this warp complete before the CTA retires
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -361,12 +401,36 @@ static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_
   return VF4_OK;
 }
 
+// Output map for the TMA-store epilogue: bf16 (M, N) with 64x32 boxes and the 128-byte swizzle,
+// or packed FP4 codes (M, N/2) bytes with (BN/4)x32 boxes, no swizzle.
+static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, bool fp4, int bn) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int64_t rowbytes = fp4 ? cols / 2 : cols * 2;
+  cuuint64_t dims[2] = {(cuuint64_t)(fp4 ? cols / 2 : cols), (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+  cuuint32_t box[2] = {(cuuint32_t)(fp4 ? bn / 4 : 64), 32u};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   fp4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return VF4_OK;
+}
+
 template <int BN, int EPI, bool kF32>
 static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
   using C = GemmCfg<BN>;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
+  memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, BN)) return st;
+  if (EPI == VF4_EPI_GELU_NVFP4) {
+    if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, BN)) return st;
+  } else if (!kF32) {
+    if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN)) return st;
+  }
   auto kern = gemm_nvfp4_kernel<BN, EPI, kF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -374,7 +438,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   p.tiles_n = (p.N + BN - 1) / BN;
   int tiles = p.tiles_m * p.tiles_n;
   int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, p);
+  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, to, p);
   return launch_status("vf4_gemm_nvfp4");
 }
 
