@@ -127,3 +127,17 @@ def test_gemm_full_size_sampled_rows():
                                 np.float32(wg.item()))
     got = out[rows.cuda()].cpu().numpy()
     assert np.abs(got - ref).max() <= 1e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 1024), (333, 3072, 768), (1024, 1152, 4304), (300, 512, 512)])
+def test_gemm_cta_pair_kernel(M, K, N, monkeypatch):
+    """The CTA-pair (cta_group::2, 256x256 tile) kernel, selected with VF4_GEMM_TILE=pair."""
+    monkeypatch.setenv("VF4_GEMM_TILE", "pair")
+    A, B = _operands(M, N, K, seed=M + K)
+    out = _gemm_cuda(A, B)
+    ref = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    assert np.abs(out - ref).max() <= 1e-3 * np.abs(ref).max() and cos(out, ref) >= 0.9999
+    bias = (np.random.default_rng(4).standard_normal(N) * 0.1).astype(np.float32)
+    out = _gemm_cuda(A, B, out_dtype=torch.bfloat16, bias=bias)
+    refb = oracle.to_bf16(oracle.to_bf16(ref) + oracle.to_bf16(bias))
+    assert cos(out, refb) >= 0.9999

@@ -314,6 +314,34 @@ VF4_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
   }
 }
 
+VF4_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (for barriers that the peer CTA arrives on).
+VF4_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*(volatile int*)err != 0) return false;
+      if (globaltimer() - t0 > VF4_WAIT_TIMEOUT_NS) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 VF4_DEV void tma_prefetch(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
@@ -409,6 +437,60 @@ VF4_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 
+// ---- CTA-pair (cluster of 2) helpers for cta_group::2 MMAs
+VF4_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+VF4_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory variable in CTA `cta` of the cluster.
+VF4_DEV uint32_t mapa_shared(uint32_t addr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta));
+  return r;
+}
+VF4_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+VF4_DEV void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+VF4_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+VF4_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrive (once the issuing thread's tcgen05 ops complete) on the barrier at this shared offset in
+// every CTA of `mask` (bit i = cluster CTA i).
+VF4_DEV void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+// Pair MMA: M = 256 split over the two CTAs (128 rows each, A and D in each CTA's own smem / TMEM),
+// B's N rows split in halves across the two CTAs' shared memory at the same offsets.
+VF4_DEV void mma_mxf4nvf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa_tmem,
+                               uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], "
+      "[%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// Scale staging for the pair MMA: each CTA copies the 32x16-byte atom at this smem offset into
+// its own TMEM (replicated to the four lane sub-partitions).
+VF4_DEV void tmem_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // Shared-memory matrix descriptor (tcgen05 "version 1" format).
 //   layout 2 = 128-byte swizzle (K-major operand tiles written by TMA SWIZZLE_128B),
 //   layout 0 = no swizzle (scale-factor staging for tcgen05.cp).
@@ -424,12 +506,12 @@ VF4_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_byte
 
 // Instruction descriptor for kind::mxf4nvf4: A/B E2M1, UE4M3 scales, K-major A and B,
 // M=128, N=n (multiple of 16, <= 256), dense, K=64.
-__host__ __device__ constexpr uint32_t idesc_mxf4nvf4(uint32_t n) {
+__host__ __device__ constexpr uint32_t idesc_mxf4nvf4(uint32_t n, uint32_t m = 128) {
   return (1u << 7)             // A format: E2M1
          | (1u << 10)          // B format: E2M1
          | ((n >> 3) << 17)    // N >> 3
          | (0u << 23)          // scale type UE4M3
-         | ((128u >> 4) << 24);  // M >> 4
+         | ((m >> 4) << 24);   // M >> 4
 }
 
 }  // namespace vf4

@@ -16,6 +16,7 @@
 //               quadrant, each half of the columns), release TMEM, then scale / bias /
 //               GELU / NVFP4-quantize from registers and store
 // Every wait is bounded (mbar_wait); a timeout records a device error and unwinds.
+#include <stdlib.h>
 #include <string.h>
 
 #include "vf4_common.cuh"
@@ -70,6 +71,7 @@ struct GemmParams {
   int M, N, K;
   int n_kb;     // ceil(K / 64): K64 blocks == scale column-blocks of A and B
   int n_rb_b;   // ceil(N / 128): scale row-blocks of B
+  int n_rb_a;   // ceil(M / 128): scale row-blocks of A
   int tiles_m, tiles_n;
   const __nv_bfloat16* bias;
   void* out;
@@ -78,6 +80,137 @@ struct GemmParams {
   uint8_t* out_sf;
   int out_ncb;  // scale column-blocks of the NVFP4 output (N / 64)
 };
+
+// Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
+// [col0, col0 + NC) of row row0 + lane; ebuf is the warp's 4 KB staging buffer.
+template <int NC, int EPI, bool kF32>
+VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtensorMap* tmOut, int row0,
+                           int col0, int lane, float alpha, float egs, float esenc, uint32_t ebuf,
+                           uint8_t* ebuf_g) {
+  const int64_t row = (int64_t)row0 + lane;
+  if constexpr (EPI != VF4_EPI_GELU_NVFP4 && kF32) {
+    if (row < p.M) {
+#pragma unroll
+      for (int g = 0; g < NC / 8; ++g) {
+        const int col = col0 + g * 8;
+        if (col < p.N) {
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[g * 8 + i]) * alpha;
+          if (EPI == VF4_EPI_BIAS && p.bias) {
+            uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+            const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              y[2 * i] += __uint_as_float(b4[i] << 16);
+              y[2 * i + 1] += __uint_as_float(b4[i] & 0xFFFF0000u);
+            }
+          }
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
+          o[0] = make_float4(y[0], y[1], y[2], y[3]);
+          o[1] = make_float4(y[4], y[5], y[6], y[7]);
+        }
+      }
+    }
+  } else if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
+    // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
+    // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
+#pragma unroll
+    for (int c = 0; c < NC / 64; ++c) {
+      const int colc = col0 + c * 64;
+      if (colc < p.N) {
+        if (lane == 0) bulk_wait_read();      // the previous store has left the buffer
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = colc + j * 8;
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * 64 + j * 8 + i]) * alpha;
+          if (EPI == VF4_EPI_BIAS && p.bias && col < p.N) {
+            // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
+            uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+            const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
+              y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
+            }
+          }
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(ebuf_g + lane * 128 + ((j ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmOut, ebuf, colc, row0);   // rows >= M and columns >= N are clipped
+          bulk_commit();
+        }
+      }
+    }
+  } else {
+    // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
+    // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).
+    // Packed codes (NC/2 bytes per row) are staged in shared memory and stored by TMA;
+    // the 4-byte scale words go straight to the 128x4-tiled layout.
+    if (lane == 0) bulk_wait_read();
+    __syncwarp();
+#pragma unroll
+    for (int g4 = 0; g4 < NC / 64; ++g4) {
+      uint32_t sfw = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int blk = g4 * 4 + b;
+        const int col = col0 + blk * 16;
+        float h[16];
+        uint64_t packed = 0;
+        if (col < p.N) {
+          float bb[16];
+          if (p.bias) {
+            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
+            uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              bb[2 * i] = __uint_as_float(bw[i] << 16);
+              bb[2 * i + 1] = __uint_as_float(bw[i] & 0xFFFF0000u);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) bb[i] = 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            h[i] = gelu_as(__fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]));
+          float amax = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+          float dec;
+          const uint32_t sf = six_scale(amax, esenc, egs, &dec);
+          packed = encode16_fast(h, dec);
+          if (row < p.M) sfw |= sf << (8 * b);
+        }
+        *reinterpret_cast<uint64_t*>(ebuf_g + lane * (NC / 2) + blk * 8) = packed;
+      }
+      const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
+      if (col0 + g4 * 64 < p.N && row < (((int64_t)p.M + 127) & ~int64_t(127))) {
+        int64_t off = ((row >> 7) * p.out_ncb + (c0 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+        *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
+      }
+    }
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0 && col0 < p.N) {
+      tma_store_2d(tmOut, ebuf, col0 / 2, row0);
+      bulk_commit();
+    }
+  }
+}
 
 template <int BN, int EPI, bool kF32>
 __global__ void __launch_bounds__(320, 1)
@@ -195,14 +328,14 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t sb = sa + C::A_BYTES;
           const uint32_t ssfa = sb + C::B_BYTES;
           const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          // scale copies of K-block kb are issued right before its MMA (the tensor pipe runs
+          // copies and MMAs in issue order; interleaving lets the copies overlap earlier MMAs)
           for (int kb = 0; kb < nkb; ++kb) {
             tmem_cp_32x128b_x4(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
               tmem_cp_32x128b_x4(sfb_t + kb * C::SFB_PER_KB + j * 4,
                                  smem_desc(ssfb + j * C::KB_PER_STAGE * 512 + kb * 512, 0, 128, 0));
-          }
-          for (int kb = 0; kb < nkb; ++kb) {
             const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
             const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
             mma_mxf4nvf4(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::SFB_PER_KB,
@@ -249,133 +382,9 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
 
-      const int64_t row = (int64_t)mb * 128 + q * 32 + lane;
-      const int row0 = mb * 128 + q * 32;        // first row of this warp's 32-row slab
-      const int col0 = nb * BN + half * NC;
-      const uint32_t ebuf = epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES;
-      uint8_t* ebuf_g = gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES;
-      if constexpr (EPI != VF4_EPI_GELU_NVFP4 && kF32) {
-        if (row < p.M) {
-#pragma unroll
-          for (int g = 0; g < NC / 8; ++g) {
-            const int col = col0 + g * 8;
-            if (col < p.N) {
-              float y[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[g * 8 + i]) * alpha;
-              if (EPI == VF4_EPI_BIAS && p.bias) {
-                uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-                const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  y[2 * i] += __uint_as_float(b4[i] << 16);
-                  y[2 * i + 1] += __uint_as_float(b4[i] & 0xFFFF0000u);
-                }
-              }
-              float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
-              o[0] = make_float4(y[0], y[1], y[2], y[3]);
-              o[1] = make_float4(y[4], y[5], y[6], y[7]);
-            }
-          }
-        }
-      } else if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
-        // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
-        // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
-#pragma unroll
-        for (int c = 0; c < NC / 64; ++c) {
-          const int colc = col0 + c * 64;
-          if (colc < p.N) {
-            if (lane == 0) bulk_wait_read();      // the previous store has left the buffer
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int col = colc + j * 8;
-              float y[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * 64 + j * 8 + i]) * alpha;
-              if (EPI == VF4_EPI_BIAS && p.bias && col < p.N) {
-                // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
-                uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-                const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
-                  y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
-                }
-              }
-              uint32_t w[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
-                w[i] = *reinterpret_cast<uint32_t*>(&h);
-              }
-              *reinterpret_cast<uint4*>(ebuf_g + lane * 128 + ((j ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            fence_async_shared();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmOut, ebuf, colc, row0);   // rows >= M and columns >= N are clipped
-              bulk_commit();
-            }
-          }
-        }
-      } else {
-        // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
-        // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).
-        // Packed codes (NC/2 bytes per row) are staged in shared memory and stored by TMA;
-        // the 4-byte scale words go straight to the 128x4-tiled layout.
-        if (lane == 0) bulk_wait_read();
-        __syncwarp();
-#pragma unroll
-        for (int g4 = 0; g4 < NC / 64; ++g4) {
-          uint32_t sfw = 0;
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int blk = g4 * 4 + b;
-            const int col = col0 + blk * 16;
-            float h[16];
-            uint64_t packed = 0;
-            if (col < p.N) {
-              float bb[16];
-              if (p.bias) {
-                const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
-                uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-                const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  bb[2 * i] = __uint_as_float(bw[i] << 16);
-                  bb[2 * i + 1] = __uint_as_float(bw[i] & 0xFFFF0000u);
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) bb[i] = 0.f;
-              }
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                h[i] = gelu_as(__fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]));
-              float amax = 0.f;
-#pragma unroll
-              for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
-              float dec;
-              const uint32_t sf = six_scale(amax, esenc, egs, &dec);
-              packed = encode16_fast(h, dec);
-              if (row < p.M) sfw |= sf << (8 * b);
-            }
-            *reinterpret_cast<uint64_t*>(ebuf_g + lane * (NC / 2) + blk * 8) = packed;
-          }
-          const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
-          if (col0 + g4 * 64 < p.N) {
-            int64_t off = ((row >> 7) * p.out_ncb + (c0 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
-            *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
-          }
-        }
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0 && col0 < p.N) {
-          tma_store_2d(&tmOut, ebuf, col0 / 2, row0);
-          bulk_commit();
-        }
-      }
+      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha, egs, esenc,
+                                   epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
+                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES);
     }
     if (lane == 0) bulk_wait_all();   // stores issued by this warp complete before the CTA retires
     __syncwarp();
@@ -385,6 +394,227 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+
+// ---------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of 2 CTAs computes a 256 x 256 tile with cta_group::2 MMAs.
+// Each CTA TMA-loads its own 128 rows of A and its own 128-row half of B (no multicast), plus the
+// scale atoms (its SFA row-block and both SFB row-blocks).  A forwarder warp in each CTA waits on
+// its own "full" barrier and arrives on the leader's pair barrier; the leader (cluster rank 0)
+// issues the scale copies and MMAs for both CTAs and multicast-commits stage releases and the
+// accumulator hand-off to both CTAs' barriers; every epilogue warp of both CTAs releases TMEM by
+// arriving on the leader's barrier.  Per CTA and K64 step the shared-memory traffic is 8 KB of
+// TMA writes + 8 KB of MMA reads, within the SM's 128 B/clk (the 1-CTA 128x256 tile needs 24 KB).
+// Warps: 0 producer, 1 TMEM allocator + MMA issuer (leader), 2 forwarder, 3..10 epilogue.
+// ---------------------------------------------------------------------------------------
+struct Gemm2Cfg {
+  static constexpr int BN = 256;
+  static constexpr int KB_PER_STAGE = 4;
+  static constexpr int STAGES = 5;
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = 128 * 128;     // this CTA's half of the 256 B rows
+  static constexpr int SFA_BYTES = KB_PER_STAGE * 512;
+  static constexpr int SFB_BYTES = 2 * KB_PER_STAGE * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int SFA_TCOL = 256, SFA_SLOT = KB_PER_STAGE * 4;
+  static constexpr int SFB_TCOL = SFA_TCOL + 2 * SFA_SLOT, SFB_PER_KB = 8, SFB_SLOT = KB_PER_STAGE * SFB_PER_KB;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 352;
+  static constexpr int EPI_WARP_BYTES = 4096, EPI_BYTES = 8 * EPI_WARP_BYTES;
+  static constexpr int NBAR = 3 * STAGES + 3;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 8 * NBAR + 16;
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
+};
+
+template <int EPI, bool kF32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
+    gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
+  using C = Gemm2Cfg;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t bar0 = epi0 + C::EPI_BYTES;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };                 // own TMA completion
+  auto pair_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };   // leader: both CTAs' data ready
+  auto empty_bar = [&](int s) { return bar0 + 8u * (2 * C::STAGES + s); };
+  const uint32_t tfull_bar = bar0 + 8u * (3 * C::STAGES);
+  const uint32_t tempty_bar = tfull_bar + 8, drain_bar = tfull_bar + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES + 8 * C::NBAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  int* err = &g_gemm_err;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(pair_bar(s), 2);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, 16);
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+    if (!kF32) tma_prefetch(&tmOut);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles = p.tiles_m * p.tiles_n;   // tiles_m counts 256-row tiles here
+  const int n_st = (p.n_kb + C::KB_PER_STAGE - 1) / C::KB_PER_STAGE;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int pm = tile / p.tiles_n, nb = tile - pm * p.tiles_n;
+        int rba = pm * 2 + (int)rank;
+        if (rba >= p.n_rb_a) rba = p.n_rb_a - 1;   // M tail: A rows are zero-filled, scales unused
+        for (int st = 0; st < n_st; ++st, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int kb0 = st * C::KB_PER_STAGE;
+          const int nkb = min(C::KB_PER_STAGE, p.n_kb - kb0);
+          const uint32_t sf_bytes = (uint32_t)nkb * 512u;
+          mbar_arrive_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES + 3 * sf_bytes);
+          const uint32_t sa = base + s * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t ssfa = sb + C::B_BYTES;
+          const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          tma_load_2d(sa, &tmA, st * 128, pm * 256 + (int)rank * 128, full_bar(s));
+          tma_load_2d(sb, &tmB, st * 128, nb * BN + (int)rank * 128, full_bar(s));
+          bulk_load(ssfa, p.a_sf + ((int64_t)rba * p.n_kb + kb0) * 512, sf_bytes, full_bar(s));
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            int rb = nb * 2 + j;
+            if (rb >= p.n_rb_b) rb = nb * 2;   // N tail: finite stand-in, columns discarded
+            bulk_load(ssfb + j * C::KB_PER_STAGE * 512, p.b_sf + ((int64_t)rb * p.n_kb + kb0) * 512, sf_bytes,
+                      full_bar(s));
+          }
+        }
+      }
+      for (int k = it - C::STAGES < 0 ? 0 : it - C::STAGES; k < it; ++k)
+        mbar_wait(full_bar(k % C::STAGES), (uint32_t)(k / C::STAGES) & 1u, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ forwarder (both CTAs)
+    if (lane == 0) {
+      const uint32_t n_iter = (uint32_t)((tiles - pair + npairs - 1) / npairs) * (uint32_t)n_st;
+      for (uint32_t it = 0; it < (pair < tiles ? n_iter : 0u); ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(full_bar(s), (it / C::STAGES) & 1u, err, kDevErrTimeoutFull)) break;
+        mbar_arrive_remote(mapa_shared(pair_bar(s), 0));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (leader) {
+      constexpr uint32_t idesc = idesc_mxf4nvf4(BN, 256);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs, ++lt) {
+        if (!mbar_wait_cluster(tempty_bar, ((uint32_t)lt & 1u) ^ 1u, err, kDevErrTimeoutTmem)) break;
+        tc_fence_after();
+        for (int st = 0; st < n_st; ++st, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait_cluster(pair_bar(s), (uint32_t)(it / C::STAGES) & 1u, err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const int nkb = min(C::KB_PER_STAGE, p.n_kb - st * C::KB_PER_STAGE);
+            const uint32_t slot = (uint32_t)(it & 1);
+            const uint32_t sfa_t = tmem + C::SFA_TCOL + slot * C::SFA_SLOT;
+            const uint32_t sfb_t = tmem + C::SFB_TCOL + slot * C::SFB_SLOT;
+            const uint32_t sa = base + s * C::STAGE_BYTES;
+            const uint32_t sb = sa + C::A_BYTES;
+            const uint32_t ssfa = sb + C::B_BYTES;
+            const uint32_t ssfb = ssfa + C::SFA_BYTES;
+            for (int kb = 0; kb < nkb; ++kb) {
+              tmem_cp_32x128b_x4_pair(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                tmem_cp_32x128b_x4_pair(sfb_t + kb * C::SFB_PER_KB + j * 4,
+                                        smem_desc(ssfb + j * C::KB_PER_STAGE * 512 + kb * 512, 0, 128, 0));
+              const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
+              const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
+              mma_mxf4nvf4_pair(tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::SFB_PER_KB,
+                                (st > 0 || kb > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(empty_bar(s), 3);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) tc_commit_pair(tfull_bar, 3);
+        __syncwarp();
+      }
+      if (lane == 0) {
+        tc_commit_pair(drain_bar, 1);
+        mbar_wait(drain_bar, 0, err, kDevErrTimeoutDrain);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    constexpr int NC = BN / 2;
+    const int q = warp & 3;
+    const int half = (warp - 3) >> 2;
+    const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
+    float egs = 1.f, esenc = 1.f;
+    if constexpr (EPI == VF4_EPI_GELU_NVFP4) {
+      egs = __ldg(p.epi_gs);
+      esenc = __fdiv_rn(1.0f, egs);
+    }
+    const uint32_t tempty_leader = mapa_shared(tempty_bar, 0);
+    int lt = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++lt) {
+      const int pm = tile / p.tiles_n, nb = tile - pm * p.tiles_n;
+      if (!mbar_wait(tfull_bar, (uint32_t)lt & 1u, err, kDevErrTimeoutTmem)) break;
+      tc_fence_after();
+      uint32_t v[NC];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * NC);
+#pragma unroll
+      for (int c = 0; c < NC / 32; ++c) tmem_ld_32x32b_x32(taddr + c * 32, v + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_leader);
+      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, pm * 256 + (int)rank * 128 + q * 32, nb * BN + half * NC, lane,
+                                   alpha, egs, esenc, epi0 + (uint32_t)(warp - 3) * C::EPI_WARP_BYTES,
+                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 3) * C::EPI_WARP_BYTES);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, C::TMEM_COLS);
 }
 
 static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t kbytes, int box_rows) {
@@ -440,6 +670,37 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, to, p);
   return launch_status("vf4_gemm_nvfp4");
+}
+
+template <int EPI, bool kF32>
+static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
+  using C = Gemm2Cfg;
+  CUtensorMap ta, tb, to;
+  memset(&to, 0, sizeof(to));
+  if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
+  if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, 128)) return st;
+  if (EPI == VF4_EPI_GELU_NVFP4) {
+    if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, C::BN)) return st;
+  } else if (!kF32) {
+    if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
+  }
+  auto kern = gemm_nvfp4_pair_kernel<EPI, kF32>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  p.tiles_m = (p.M + 255) / 256;
+  p.tiles_n = (p.N + C::BN - 1) / C::BN;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int max_pairs = num_sms() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  kern<<<2 * pairs, C::THREADS, C::SMEM, s>>>(ta, tb, to, p);
+  return launch_status("vf4_gemm_nvfp4 (CTA pair)");
+}
+
+static int dispatch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32, cudaStream_t s) {
+  if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm_pair<VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS)
+    return f32 ? launch_gemm_pair<VF4_EPI_BIAS, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_BIAS, false>(a, b, p, s);
+  return f32 ? launch_gemm_pair<VF4_EPI_NONE, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_NONE, false>(a, b, p, s);
 }
 
 template <int BN>
@@ -499,6 +760,7 @@ extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, cons
   p.K = (int)K;
   p.n_kb = (int)((K + 63) / 64);
   p.n_rb_b = (int)((N + 127) / 128);
+  p.n_rb_a = (int)((M + 127) / 128);
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.out = out;
   p.epi_gs = epi_gs;
@@ -506,6 +768,9 @@ extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, cons
   p.out_sf = out_sf;
   p.out_ncb = (int)((N / 16 + 3) / 4);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const char* mode = getenv("VF4_GEMM_TILE");   // "pair" selects the CTA-pair 256x256 kernel
+  if (N >= 256 && M > 128 && mode && mode[0] == 'p')
+    return dispatch_gemm_pair(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   return dispatch_gemm<128>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
 }
