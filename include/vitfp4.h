@@ -53,7 +53,8 @@ typedef enum { VF4_SIX = 0, VF4_MSE = 1 } vf4_block_select;
 typedef enum {
   VF4_EPI_NONE = 0,      /* out = gs_a*gs_b*acc                                   */
   VF4_EPI_BIAS = 1,      /* out = gs_a*gs_b*acc + bias                            */
-  VF4_EPI_GELU_NVFP4 = 2 /* h = GELU(bf16(gs_a*gs_b*acc + bias)); NVFP4-cast h    */
+  VF4_EPI_GELU_NVFP4 = 2,    /* h = GELU(gs_a*gs_b*acc + bias) (tanh form), NVFP4-cast h */
+  VF4_EPI_GELU_ERF_NVFP4 = 3 /* same with erf-GELU (A&S 7.1.26, |erf error| <= 1.5e-7)     */
 } vf4_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -116,10 +117,14 @@ VF4_API int vf4_to_blocked(const uint8_t* sf, int64_t R, int64_t C, uint8_t* out
  *   acc[m,n] = sum_k A[m,k]*B[n,k] (E2M1 x E4M3 block scales), fp32 accumulate;
  *   A packed (M, K/2) + swizzled SF, B packed (N, K/2) + swizzled SF, a_gs/b_gs device fp32.
  * epilogue VF4_EPI_NONE / VF4_EPI_BIAS write `out` (M, N) in out_dtype (bias: (N,) bf16);
- * VF4_EPI_GELU_NVFP4 (the fused fc1 epilogue of fused_mlp.py:47-51) writes out_packed
- * (M, N/2) and out_sf (swizzled, ceil128(M) x N/16) quantized with the static global
- * scale epi_gs (six rule), and ignores `out`.
- * Requirements: K % 32 == 0, N % 16 == 0 (N % 64 == 0 for VF4_EPI_GELU_NVFP4), 16-byte
+ * VF4_EPI_GELU_NVFP4 / VF4_EPI_GELU_ERF_NVFP4 (the fused fc1 epilogue of fused_mlp.py:47-51)
+ * write out_packed (M, N/2) and out_sf (swizzled, ceil128(M) x N/16) quantized with the
+ * static global scale epi_gs (six rule), and ignore `out`.  The fc1 output stays fp32 (the
+ * unfused reference rounds it to bf16 first).  VF4_EPI_GELU_NVFP4 evaluates GELU as
+ * 0.5x(1 + tanh(0.79788456x + 0.03567741x^3)) with the hardware tanh (max |deviation from
+ * erf-GELU| ~1e-3, below the bf16 rounding the reference applies to this tensor);
+ * VF4_EPI_GELU_ERF_NVFP4 evaluates erf-GELU to 1.5e-7 at about 1.5x the epilogue cost.
+ * Requirements: K % 32 == 0, N % 16 == 0 (N % 64 == 0 for the GELU epilogues), 16-byte
  * aligned pointers. */
 VF4_API int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
                    const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs, int64_t M,

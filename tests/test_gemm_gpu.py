@@ -79,20 +79,27 @@ def test_gemm_bf16_bias(M, K, N):
     assert np.abs(out - ref).max() <= 2.0 ** -7 * np.abs(ref).max()
 
 
+def _gelu_tanh(x):
+    x = x.astype(np.float64)
+    return (0.5 * x * (1 + np.tanh(0.7978845608 * x + 0.0356774081 * x ** 3))).astype(np.float32)
+
+
+@pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("M,K,N", [(256, 1024, 4096), (197, 768, 3072), (130, 512, 128)])
-def test_gemm_gelu_nvfp4_epilogue(M, K, N):
+def test_gemm_gelu_nvfp4_epilogue(M, K, N, exact):
     """fc1 epilogue: NVFP4(GELU(gemm + b1)) with a static global scale; the intermediate stays fp32
-    (the unfused reference rounds it to bf16), GELU uses the A&S 7.1.26 erf (|err| <= 1.5e-7)."""
+    (the unfused reference rounds it to bf16).  exact: erf-GELU via A&S 7.1.26 (|err| <= 1.5e-7),
+    compared with erf; default: the tanh form with the hardware tanh, compared with the tanh form."""
     ops = _ops()
     A, B = _operands(M, N, K, seed=7)
     bias = (np.random.default_rng(3).standard_normal(N) * 0.1).astype(np.float32)
     ref_y = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
-    h = oracle.gelu(ref_y + oracle.to_bf16(bias))
+    h = (oracle.gelu if exact else _gelu_tanh)(ref_y + oracle.to_bf16(bias))
     gh = np.float32(np.abs(h).max() / 2688.0)
     ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
     bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
     hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, torch.from_numpy(bias).cuda().bfloat16(),
-                                  torch.tensor(gh, device="cuda"))
+                                  torch.tensor(gh, device="cuda"), exact=exact)
     torch.cuda.synchronize()
     c, b, _ = oracle.quantize_to_nvfp4(h, 16, global_scale=gh)
     codes = oracle.unpack_e2m1(hp.cpu().numpy())
@@ -102,6 +109,9 @@ def test_gemm_gelu_nvfp4_epilogue(M, K, N):
     assert (sf != b).mean() < 2e-3, (sf != b).mean()
     deq = oracle.dequantize_nvfp4(codes, sf, gh)
     assert cos(deq, oracle.dequantize_nvfp4(c, b, gh)) >= 0.999
+    # either flavour stays within FP4 resolution of the erf-GELU quantization
+    ce, be, _ = oracle.quantize_to_nvfp4(oracle.gelu(ref_y + oracle.to_bf16(bias)), 16, global_scale=gh)
+    assert cos(deq, oracle.dequantize_nvfp4(ce, be, gh)) >= 0.998
     # padded scale rows of the last 128-row tile are zero
     full = hsf.cpu().numpy()
     pad = oracle.from_blocked(full, (M + 127) // 128 * 128, N // 16)[M:]

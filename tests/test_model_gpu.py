@@ -99,14 +99,15 @@ def test_fused_mlp_matches_bf16(M, E):
         assert _cos(ref, torch.compile(mlp)(x)) >= 0.97                # custom op survives torch.compile
 
 
-def test_fused_mlp_matches_oracle_composition():
-    """FusedNVFP4MLP vs the reference's arithmetic composed on CPU: cos >= 0.999."""
+@pytest.mark.parametrize("exact", [False, True])
+def test_fused_mlp_matches_oracle_composition(exact):
+    """FusedNVFP4MLP vs the reference's arithmetic (erf-GELU) composed on CPU: cos >= 0.999."""
     from vitfp4.ptq import FusedNVFP4MLP
     torch.manual_seed(2)
     M, E = 512, 256
     x = torch.randn(M, E, device="cuda", dtype=torch.bfloat16)
     fc1, fc2 = nn.Linear(E, 4 * E).cuda().bfloat16(), nn.Linear(4 * E, E).cuda().bfloat16()
-    mlp = FusedNVFP4MLP(fc1, fc2)
+    mlp = FusedNVFP4MLP(fc1, fc2, exact_gelu=exact)
     out = mlp(x).detach().float().cpu().numpy()
     xn = x.detach().float().cpu().numpy()
     gx, gh = np.float32(mlp.gx.item()), np.float32(mlp.gh.item())

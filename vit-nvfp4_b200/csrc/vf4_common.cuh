@@ -259,6 +259,16 @@ VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
   return r;
 }
 
+// GELU in its tanh form, 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))), with the hardware
+// tanh.approx.f32: one special-function op per element (the A&S form above needs two).
+VF4_DEV float gelu_tanh(float x) {
+  const float v = x * __fmaf_rn(0.0356774081f, x * x, 0.7978845608f);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(v));
+  const float hx = 0.5f * x;
+  return __fmaf_rn(hx, t, hx);
+}
+
 // Offset of scale factor (row r, column c) inside the 128x4-tiled ("to_blocked") layout.
 VF4_DEV int64_t sf_swizzle_offset(int64_t r, int64_t c, int64_t n_col_blocks) {
   return ((r >> 7) * n_col_blocks + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);

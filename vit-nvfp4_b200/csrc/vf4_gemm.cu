@@ -88,7 +88,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
                            int col0, int lane, float alpha, float egs, float esenc, uint32_t ebuf,
                            uint8_t* ebuf_g) {
   const int64_t row = (int64_t)row0 + lane;
-  if constexpr (EPI != VF4_EPI_GELU_NVFP4 && kF32) {
+  if constexpr (EPI < VF4_EPI_GELU_NVFP4 && kF32) {
     if (row < p.M) {
 #pragma unroll
       for (int g = 0; g < NC / 8; ++g) {
@@ -112,7 +112,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
         }
       }
     }
-  } else if constexpr (EPI != VF4_EPI_GELU_NVFP4) {
+  } else if constexpr (EPI < VF4_EPI_GELU_NVFP4) {
     // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
     // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
 #pragma unroll
@@ -186,7 +186,10 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
           }
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            h[i] = gelu_as(__fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]));
+            {
+              const float t = __fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]);
+              h[i] = EPI == VF4_EPI_GELU_ERF_NVFP4 ? gelu_as(t) : gelu_tanh(t);
+            }
           float amax = 0.f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(320, 1)
     const int half = (warp - 2) >> 2;
     const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
     float egs = 1.f, esenc = 1.f;
-    if constexpr (EPI == VF4_EPI_GELU_NVFP4) {
+    if constexpr (EPI >= VF4_EPI_GELU_NVFP4) {
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
@@ -585,7 +588,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     const int half = (warp - 3) >> 2;
     const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
     float egs = 1.f, esenc = 1.f;
-    if constexpr (EPI == VF4_EPI_GELU_NVFP4) {
+    if constexpr (EPI >= VF4_EPI_GELU_NVFP4) {
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
@@ -656,7 +659,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, BN)) return st;
-  if (EPI == VF4_EPI_GELU_NVFP4) {
+  if (EPI >= VF4_EPI_GELU_NVFP4) {
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, BN)) return st;
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN)) return st;
@@ -679,7 +682,7 @@ static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, c
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, 128)) return st;
-  if (EPI == VF4_EPI_GELU_NVFP4) {
+  if (EPI >= VF4_EPI_GELU_NVFP4) {
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, C::BN)) return st;
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
@@ -698,6 +701,7 @@ static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, c
 
 static int dispatch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32, cudaStream_t s) {
   if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm_pair<VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_GELU_ERF_NVFP4) return launch_gemm_pair<VF4_EPI_GELU_ERF_NVFP4, false>(a, b, p, s);
   if (epi == VF4_EPI_BIAS)
     return f32 ? launch_gemm_pair<VF4_EPI_BIAS, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_BIAS, false>(a, b, p, s);
   return f32 ? launch_gemm_pair<VF4_EPI_NONE, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_NONE, false>(a, b, p, s);
@@ -707,6 +711,7 @@ template <int BN>
 static int dispatch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32,
                          cudaStream_t s) {
   if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm<BN, VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_GELU_ERF_NVFP4) return launch_gemm<BN, VF4_EPI_GELU_ERF_NVFP4, false>(a, b, p, s);
   if (epi == VF4_EPI_BIAS) {
     return f32 ? launch_gemm<BN, VF4_EPI_BIAS, true>(a, b, p, s)
                : launch_gemm<BN, VF4_EPI_BIAS, false>(a, b, p, s);
@@ -732,14 +737,14 @@ extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, cons
   if (K % 32 != 0 || N % 16 != 0)
     return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: need K %% 32 == 0 and N %% 16 == 0 (K=%lld N=%lld)",
                 (long long)K, (long long)N);
-  if (epilogue < VF4_EPI_NONE || epilogue > VF4_EPI_GELU_NVFP4)
+  if (epilogue < VF4_EPI_NONE || epilogue > VF4_EPI_GELU_ERF_NVFP4)
     return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad epilogue %d", epilogue);
   if (!a_packed || !a_sf || !a_gs || !b_packed || !b_sf || !b_gs)
     return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: null operand");
   if (!aligned16(a_packed) || !aligned16(b_packed) || !aligned16(a_sf) || !aligned16(b_sf) ||
       (bias && !aligned16(bias)))
     return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: operands, scales and bias must be 16-byte aligned");
-  if (epilogue == VF4_EPI_GELU_NVFP4) {
+  if (epilogue >= VF4_EPI_GELU_NVFP4) {
     if (N % 64 != 0) return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: GELU-NVFP4 epilogue needs N %% 64 == 0");
     if (!epi_gs || !out_packed || !out_sf) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: GELU-NVFP4 outputs missing");
     if ((reinterpret_cast<uintptr_t>(out_packed) & 7u) || (reinterpret_cast<uintptr_t>(out_sf) & 3u))

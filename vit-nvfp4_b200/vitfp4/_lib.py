@@ -16,7 +16,7 @@ _lib: ctypes.CDLL | None = None
 
 VF4_BF16, VF4_F32 = 0, 1
 VF4_SIX, VF4_MSE = 0, 1
-VF4_EPI_NONE, VF4_EPI_BIAS, VF4_EPI_GELU_NVFP4 = 0, 1, 2
+VF4_EPI_NONE, VF4_EPI_BIAS, VF4_EPI_GELU_NVFP4, VF4_EPI_GELU_ERF_NVFP4 = 0, 1, 2, 3
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int

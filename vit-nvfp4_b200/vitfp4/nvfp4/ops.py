@@ -216,9 +216,10 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
     return out
 
 
-def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs):
+def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs, exact: bool = False):
     """fc1 GEMM with the fused +bias -> GELU -> NVFP4 cast epilogue.
 
+    GELU is the tanh form (hardware tanh, ~1e-3 from erf-GELU) unless ``exact`` (erf to 1.5e-7).
     Returns (packed uint8 (M, N/2), sf_swizzled uint8 flat) quantized with the static epi_gs."""
     _need_cuda(a_packed, b_packed, epi_gs)
     a, b = _u8(a_packed), _u8(b_packed)
@@ -230,7 +231,8 @@ def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs):
     with _GemmTimer(f"gemm_gelu_nvfp4_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
         _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
                   _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
-                  _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16, _ptr(epi_gs.reshape(()).float().contiguous()),
+                  _lib.VF4_EPI_GELU_ERF_NVFP4 if exact else _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16,
+                  _ptr(epi_gs.reshape(()).float().contiguous()),
                   _ptr(packed), _ptr(sf), _stream())
     _launched()
     return packed, sf

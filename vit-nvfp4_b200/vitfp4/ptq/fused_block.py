@@ -76,7 +76,8 @@ class FusedNVFP4Block(nn.Module):
         # x + ls1(y) -> norm2 -> NVFP4 with the MLP's static gx; the new residual x_mid is written once
         hp, hsf, gx, x_mid = ops.ln_cast(x2, self.norm2.weight, self.norm2.bias, self.norm2.eps, gs=mlp.gx, y=y,
                                          gamma=_gamma(self.ls1))
-        gp, gsf = ops.gemm_gelu_nvfp4(hp, hsf, gx, _u8(mlp.w1q), _u8(mlp.w1sf), mlp.w1g, mlp.b1, mlp.gh)
+        gp, gsf = ops.gemm_gelu_nvfp4(hp, hsf, gx, _u8(mlp.w1q), _u8(mlp.w1sf), mlp.w1g, mlp.b1, mlp.gh,
+                                      exact=mlp.exact_gelu)
         y2 = ops.gemm(gp, gsf, mlp.gh, _u8(mlp.w2q), _u8(mlp.w2sf), mlp.w2g, bias=mlp.b2)
         g2 = _gamma(self.ls2)
         out = torch.addcmul(x_mid, y2, g2) if g2 is not None else x_mid + y2

@@ -1,10 +1,12 @@
 """Fused NVFP4 W4A4 transformer MLP ``fc1 -> GELU -> fc2`` (reference:
 src/vit_nvfp4/ptq/fused_mlp.py:25-167).
 
-The fc1 GEMM's epilogue applies ``+b1 -> exact GELU -> NVFP4 cast`` straight from the TMEM
+The fc1 GEMM's epilogue applies ``+b1 -> GELU -> NVFP4 cast`` straight from the TMEM
 accumulator, so the (M, 4d) intermediate never round-trips HBM in bf16; fc2 consumes the packed
 FP4 codes + swizzled scales directly and adds ``b2`` in its epilogue.  Three kernels per MLP:
-activation cast, fc1 GEMM (fused epilogue), fc2 GEMM (bias epilogue).
+activation cast, fc1 GEMM (fused epilogue), fc2 GEMM (bias epilogue).  The epilogue's GELU is the tanh form evaluated with the hardware tanh by default (its
+deviation from erf-GELU, ~1e-3 at most, is below the bf16 rounding the reference applies to the fc1
+output before its GELU); ``exact_gelu=True`` selects an erf-GELU epilogue accurate to 1.5e-7.
 
 Buffers and calibration follow the reference: weights are quantized once with the RTN "six"
 rule and stored packed (``float4_e2m1fn_x2``) with swizzled E4M3 scales; the activation globals
@@ -42,25 +44,27 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
 @torch.library.custom_op("vitfp4::fused_mlp", mutates_args=())
 def fused_mlp_op(x: torch.Tensor, w1q: torch.Tensor, w1sf: torch.Tensor, w1g: torch.Tensor,
                  b1: torch.Tensor | None, w2q: torch.Tensor, w2sf: torch.Tensor, w2g: torch.Tensor,
-                 b2: torch.Tensor | None, gx: torch.Tensor, gh: torch.Tensor, k1: int, n2: int) -> torch.Tensor:
+                 b2: torch.Tensor | None, gx: torch.Tensor, gh: torch.Tensor, k1: int, n2: int,
+                 exact_gelu: bool = False) -> torch.Tensor:
     M = x.numel() // k1
     x2 = x.reshape(M, k1)
     ap, asf, _, _ = ops.cast(x2, gx, "six")
-    hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, gx, _u8(w1q), _u8(w1sf), w1g, b1, gh)
+    hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, gx, _u8(w1q), _u8(w1sf), w1g, b1, gh, exact=exact_gelu)
     y = ops.gemm(hp, hsf, gh, _u8(w2q), _u8(w2sf), w2g, bias=b2, out_dtype=torch.bfloat16)
     return y.reshape(*x.shape[:-1], n2)
 
 
 @fused_mlp_op.register_fake
-def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2):
+def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2, exact_gelu=False):
     return x.new_empty(*x.shape[:-1], n2, dtype=torch.bfloat16)
 
 
 class FusedNVFP4MLP(nn.Module):
     """Drop-in replacement for a ``fc1 -> GELU -> fc2`` MLP with NVFP4 W4A4 and GELU fusion."""
 
-    def __init__(self, fc1: nn.Linear, fc2: nn.Linear):
+    def __init__(self, fc1: nn.Linear, fc2: nn.Linear, exact_gelu: bool = False):
         super().__init__()
+        self.exact_gelu = exact_gelu
         assert fc1.out_features == fc2.in_features, "not an fc1->fc2 MLP pair"
         assert fc1.in_features > 0 and fc1.in_features % 16 == 0 and fc2.in_features % 16 == 0, \
             "NVFP4 needs K > 0 and K % 16 == 0"
@@ -94,7 +98,7 @@ class FusedNVFP4MLP(nn.Module):
             self._calibrate(x)
         return fused_mlp_op(x.to(torch.bfloat16) if x.dtype != torch.bfloat16 else x,
                             self.w1q, self.w1sf, self.w1g, self.b1, self.w2q, self.w2sf, self.w2g,
-                            self.b2, self.gx, self.gh, self.k1, self.n2)
+                            self.b2, self.gx, self.gh, self.k1, self.n2, self.exact_gelu)
 
     def extra_repr(self) -> str:
         return f"in={self.k1}, hidden={self.w1q.shape[0]}, out={self.n2}, nvfp4=W4A4+gelu_fused"
