@@ -54,7 +54,9 @@ typedef enum {
   VF4_EPI_NONE = 0,      /* out = gs_a*gs_b*acc                                   */
   VF4_EPI_BIAS = 1,      /* out = gs_a*gs_b*acc + bias                            */
   VF4_EPI_GELU_NVFP4 = 2,    /* h = GELU(gs_a*gs_b*acc + bias) (tanh form), NVFP4-cast h */
-  VF4_EPI_GELU_ERF_NVFP4 = 3 /* same with erf-GELU (A&S 7.1.26, |erf error| <= 1.5e-7)     */
+  VF4_EPI_GELU_ERF_NVFP4 = 3, /* same with erf-GELU (A&S 7.1.26, |erf error| <= 1.5e-7)    */
+  VF4_EPI_BIAS_RESIDUAL = 4   /* out = residual + gamma * (gs_a*gs_b*acc + bias), bf16 only;
+                                 only through vf4_gemm_nvfp4_residual                       */
 } vf4_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -130,6 +132,18 @@ VF4_API int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const f
                    const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs, int64_t M,
                    int64_t N, int64_t K, const void* bias, int epilogue, void* out, int out_dtype,
                    const float* epi_gs, uint8_t* out_packed, uint8_t* out_sf, vf4_stream_t stream);
+
+/* GEMM with the transformer block's closing step fused into its epilogue:
+ *   out = residual + gamma * (bf16(bf16(gs_a*gs_b*acc) + bias))        (all bf16, (M, N))
+ * with the same rounding steps as the unfused block x + ls(fc2(h)) of a timm / DINOv2 block:
+ * the GEMM result rounds to bf16, the bias add rounds, the LayerScale product rounds, the
+ * residual add rounds (gamma NULL: no LayerScale; bias NULL: no bias).  The reference leaves this
+ * to eager torch / torch.compile after its fused MLP (ptq/fused_mlp.py:47-55).  residual, gamma
+ * and out are bf16, 16-byte aligned; out may be the residual buffer itself. */
+VF4_API int vf4_gemm_nvfp4_residual(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                                    const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs,
+                                    int64_t M, int64_t N, int64_t K, const void* bias, const void* residual,
+                                    const void* gamma, void* out, vf4_stream_t stream);
 
 /* Bytes of workspace vf4_attn_nvfp4 needs for (B, H, S, D) (0 for invalid sizes). */
 VF4_API int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D);

@@ -151,3 +151,28 @@ def test_gemm_cta_pair_kernel(M, K, N, monkeypatch):
     out = _gemm_cuda(A, B, out_dtype=torch.bfloat16, bias=bias)
     refb = oracle.to_bf16(oracle.to_bf16(ref) + oracle.to_bf16(bias))
     assert cos(out, refb) >= 0.9999
+
+
+@pytest.mark.parametrize("tile", ["", "pair"])
+@pytest.mark.parametrize("gamma", [True, False])
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 1024), (197, 3072, 768), (130, 512, 128)])
+def test_gemm_residual_epilogue(M, K, N, gamma, tile, monkeypatch):
+    """fc2 + LayerScale + residual epilogue equals the unfused bf16 steps bit for bit: the bias
+    GEMM rounded to bf16, then (y * gamma) and the residual add as bf16 torch ops."""
+    if tile:
+        monkeypatch.setenv("VF4_GEMM_TILE", tile)
+    ops = _ops()
+    A, B = _operands(M, N, K, seed=11)
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    g = torch.Generator(device="cpu").manual_seed(5)
+    bias = (torch.randn(N, generator=g) * 0.1).cuda().bfloat16()
+    res = torch.randn(M, N, generator=g).cuda().bfloat16()
+    gam = (torch.rand(N, generator=g) * 0.5 + 1e-5).cuda().bfloat16() if gamma else None
+    y = ops.gemm(ap, asf, ag, bp, bsf, bg, bias=bias, out_dtype=torch.bfloat16)
+    ref = res + (y * gam if gamma else y)
+    out = ops.gemm_residual(ap, asf, ag, bp, bsf, bg, bias, res, gamma=gam)
+    assert torch.equal(out, ref)
+    inplace = res.clone()
+    ops.gemm_residual(ap, asf, ag, bp, bsf, bg, bias, inplace, gamma=gam, out=inplace)
+    assert torch.equal(inplace, ref)

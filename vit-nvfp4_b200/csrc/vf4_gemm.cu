@@ -36,6 +36,8 @@ int gemm_device_error(int clear) {
   return v;
 }
 
+__host__ __device__ constexpr bool epi_gelu(int e) { return e == VF4_EPI_GELU_NVFP4 || e == VF4_EPI_GELU_ERF_NVFP4; }
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
@@ -79,7 +81,12 @@ struct GemmParams {
   uint8_t* out_packed;
   uint8_t* out_sf;
   int out_ncb;  // scale column-blocks of the NVFP4 output (N / 64)
+  const __nv_bfloat16* res;     // VF4_EPI_BIAS_RESIDUAL: residual (M, N) and LayerScale (N,) or NULL
+  const __nv_bfloat16* gamma;
 };
+
+VF4_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+VF4_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
 // [col0, col0 + NC) of row row0 + lane; ebuf is the warp's 4 KB staging buffer.
@@ -88,7 +95,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
                            int col0, int lane, float alpha, float egs, float esenc, uint32_t ebuf,
                            uint8_t* ebuf_g) {
   const int64_t row = (int64_t)row0 + lane;
-  if constexpr (EPI < VF4_EPI_GELU_NVFP4 && kF32) {
+  if constexpr (!epi_gelu(EPI) && kF32) {
     if (row < p.M) {
 #pragma unroll
       for (int g = 0; g < NC / 8; ++g) {
@@ -112,7 +119,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
         }
       }
     }
-  } else if constexpr (EPI < VF4_EPI_GELU_NVFP4) {
+  } else if constexpr (!epi_gelu(EPI)) {
     // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
     // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
 #pragma unroll
@@ -127,14 +134,31 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
           float y[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * 64 + j * 8 + i]) * alpha;
-          if (EPI == VF4_EPI_BIAS && p.bias && col < p.N) {
+          if (EPI != VF4_EPI_NONE && p.bias && col < p.N) {
             // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
             uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
             const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              y[2 * i] = bf16_round(y[2 * i]) + __uint_as_float(b4[i] << 16);
-              y[2 * i + 1] = bf16_round(y[2 * i + 1]) + __uint_as_float(b4[i] & 0xFFFF0000u);
+              y[2 * i] = bf16_round(y[2 * i]) + bf16_lo(b4[i]);
+              y[2 * i + 1] = bf16_round(y[2 * i + 1]) + bf16_hi(b4[i]);
+            }
+          }
+          if constexpr (EPI == VF4_EPI_BIAS_RESIDUAL) {
+            // x + ls(y): round y, round the LayerScale product, add the residual (rounded below);
+            // this lane's 8 residual values are 16 contiguous bytes of its row
+            uint4 rw = make_uint4(0, 0, 0, 0);
+            if (row < p.M && col < p.N) rw = *reinterpret_cast<const uint4*>(p.res + row * p.N + col);
+            const uint32_t r4[4] = {rw.x, rw.y, rw.z, rw.w};
+            uint32_t g4[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};   // 1.0 pairs
+            if (p.gamma && col < p.N) {
+              uint4 gw = __ldg(reinterpret_cast<const uint4*>(p.gamma + col));
+              g4[0] = gw.x; g4[1] = gw.y; g4[2] = gw.z; g4[3] = gw.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              y[2 * i] = bf16_lo(r4[i]) + bf16_round(bf16_round(y[2 * i]) * bf16_lo(g4[i]));
+              y[2 * i + 1] = bf16_hi(r4[i]) + bf16_round(bf16_round(y[2 * i + 1]) * bf16_hi(g4[i]));
             }
           }
           uint32_t w[4];
@@ -365,7 +389,7 @@ __global__ void __launch_bounds__(320, 1)
     const int half = (warp - 2) >> 2;
     const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
     float egs = 1.f, esenc = 1.f;
-    if constexpr (EPI >= VF4_EPI_GELU_NVFP4) {
+    if constexpr (epi_gelu(EPI)) {
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
@@ -588,7 +612,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     const int half = (warp - 3) >> 2;
     const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
     float egs = 1.f, esenc = 1.f;
-    if constexpr (EPI >= VF4_EPI_GELU_NVFP4) {
+    if constexpr (epi_gelu(EPI)) {
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
@@ -659,7 +683,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, BN)) return st;
-  if (EPI >= VF4_EPI_GELU_NVFP4) {
+  if (epi_gelu(EPI)) {
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, BN)) return st;
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN)) return st;
@@ -682,7 +706,7 @@ static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, c
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, 128)) return st;
-  if (EPI >= VF4_EPI_GELU_NVFP4) {
+  if (epi_gelu(EPI)) {
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, C::BN)) return st;
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
@@ -702,6 +726,7 @@ static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, c
 static int dispatch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32, cudaStream_t s) {
   if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm_pair<VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
   if (epi == VF4_EPI_GELU_ERF_NVFP4) return launch_gemm_pair<VF4_EPI_GELU_ERF_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS_RESIDUAL) return launch_gemm_pair<VF4_EPI_BIAS_RESIDUAL, false>(a, b, p, s);
   if (epi == VF4_EPI_BIAS)
     return f32 ? launch_gemm_pair<VF4_EPI_BIAS, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_BIAS, false>(a, b, p, s);
   return f32 ? launch_gemm_pair<VF4_EPI_NONE, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_NONE, false>(a, b, p, s);
@@ -712,6 +737,7 @@ static int dispatch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, int 
                          cudaStream_t s) {
   if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm<BN, VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
   if (epi == VF4_EPI_GELU_ERF_NVFP4) return launch_gemm<BN, VF4_EPI_GELU_ERF_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS_RESIDUAL) return launch_gemm<BN, VF4_EPI_BIAS_RESIDUAL, false>(a, b, p, s);
   if (epi == VF4_EPI_BIAS) {
     return f32 ? launch_gemm<BN, VF4_EPI_BIAS, true>(a, b, p, s)
                : launch_gemm<BN, VF4_EPI_BIAS, false>(a, b, p, s);
@@ -724,11 +750,10 @@ static int dispatch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, int 
 
 using namespace vf4;
 
-extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
-                              const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs,
-                              int64_t M, int64_t N, int64_t K, const void* bias, int epilogue,
-                              void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed,
-                              uint8_t* out_sf, vf4_stream_t stream) {
+static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs, const uint8_t* b_packed,
+                      const uint8_t* b_sf, const float* b_gs, int64_t M, int64_t N, int64_t K, const void* bias,
+                      int epilogue, void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed,
+                      uint8_t* out_sf, const void* residual, const void* gamma, vf4_stream_t stream) {
   if (int st = check_device()) return st;
   if (M < 0 || N <= 0 || K <= 0) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad sizes M=%lld N=%lld K=%lld",
                                              (long long)M, (long long)N, (long long)K);
@@ -737,14 +762,19 @@ extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, cons
   if (K % 32 != 0 || N % 16 != 0)
     return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: need K %% 32 == 0 and N %% 16 == 0 (K=%lld N=%lld)",
                 (long long)K, (long long)N);
-  if (epilogue < VF4_EPI_NONE || epilogue > VF4_EPI_GELU_ERF_NVFP4)
+  if (epilogue < VF4_EPI_NONE || epilogue > VF4_EPI_BIAS_RESIDUAL)
     return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad epilogue %d", epilogue);
   if (!a_packed || !a_sf || !a_gs || !b_packed || !b_sf || !b_gs)
     return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: null operand");
   if (!aligned16(a_packed) || !aligned16(b_packed) || !aligned16(a_sf) || !aligned16(b_sf) ||
       (bias && !aligned16(bias)))
     return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: operands, scales and bias must be 16-byte aligned");
-  if (epilogue >= VF4_EPI_GELU_NVFP4) {
+  if (epilogue == VF4_EPI_BIAS_RESIDUAL) {
+    if (!residual) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4_residual: residual is NULL");
+    if (!aligned16(residual) || (gamma && !aligned16(gamma)))
+      return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4_residual: residual and gamma must be 16-byte aligned");
+  }
+  if (epi_gelu(epilogue)) {
     if (N % 64 != 0) return fail(VF4_ERR_UNSUPPORTED, "vf4_gemm_nvfp4: GELU-NVFP4 epilogue needs N %% 64 == 0");
     if (!epi_gs || !out_packed || !out_sf) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: GELU-NVFP4 outputs missing");
     if ((reinterpret_cast<uintptr_t>(out_packed) & 7u) || (reinterpret_cast<uintptr_t>(out_sf) & 3u))
@@ -772,10 +802,31 @@ extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, cons
   p.out_packed = out_packed;
   p.out_sf = out_sf;
   p.out_ncb = (int)((N / 16 + 3) / 4);
+  p.res = static_cast<const __nv_bfloat16*>(residual);
+  p.gamma = static_cast<const __nv_bfloat16*>(gamma);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const char* mode = getenv("VF4_GEMM_TILE");   // "pair" selects the CTA-pair 256x256 kernel
   if (N >= 256 && M > 128 && mode && mode[0] == 'p')
     return dispatch_gemm_pair(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   return dispatch_gemm<128>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
+}
+
+extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                              const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs,
+                              int64_t M, int64_t N, int64_t K, const void* bias, int epilogue,
+                              void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed,
+                              uint8_t* out_sf, vf4_stream_t stream) {
+  if (epilogue == VF4_EPI_BIAS_RESIDUAL)
+    return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: the residual epilogue is vf4_gemm_nvfp4_residual");
+  return gemm_entry(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, M, N, K, bias, epilogue, out, out_dtype, epi_gs,
+                    out_packed, out_sf, nullptr, nullptr, stream);
+}
+
+extern "C" int vf4_gemm_nvfp4_residual(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                                       const uint8_t* b_packed, const uint8_t* b_sf, const float* b_gs,
+                                       int64_t M, int64_t N, int64_t K, const void* bias, const void* residual,
+                                       const void* gamma, void* out, vf4_stream_t stream) {
+  return gemm_entry(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, M, N, K, bias, VF4_EPI_BIAS_RESIDUAL, out, VF4_BF16,
+                    nullptr, nullptr, nullptr, residual, gamma, stream);
 }

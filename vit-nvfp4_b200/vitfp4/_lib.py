@@ -16,7 +16,7 @@ _lib: ctypes.CDLL | None = None
 
 VF4_BF16, VF4_F32 = 0, 1
 VF4_SIX, VF4_MSE = 0, 1
-VF4_EPI_NONE, VF4_EPI_BIAS, VF4_EPI_GELU_NVFP4, VF4_EPI_GELU_ERF_NVFP4 = 0, 1, 2, 3
+VF4_EPI_NONE, VF4_EPI_BIAS, VF4_EPI_GELU_NVFP4, VF4_EPI_GELU_ERF_NVFP4, VF4_EPI_BIAS_RESIDUAL = 0, 1, 2, 3, 4
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_unpack_e2m1": [_P, _L, _L, _P, _P],
     "vf4_to_blocked": [_P, _L, _L, _P, _P],
     "vf4_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _I, _P, _I, _P, _P, _P, _P],
+    "vf4_gemm_nvfp4_residual": [_P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _P, _P, _P, _P],
     "vf4_attn_workspace_size": [_L, _L, _L, _L],
     "vf4_attn_nvfp4": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _L, _P],
     "vf4_attn_nvfp4_noalloc": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],

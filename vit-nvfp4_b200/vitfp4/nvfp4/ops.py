@@ -216,6 +216,28 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
     return out
 
 
+def gemm_residual(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, residual: torch.Tensor,
+                  gamma: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + gamma * (A @ B^T + bias)`` in bf16 with the unfused block's roundings (GEMM
+    result, bias add, LayerScale product and residual add each round to bf16); ``out`` may be
+    ``residual`` itself."""
+    _need_cuda(a_packed, b_packed, residual)
+    a, b = _u8(a_packed), _u8(b_packed)
+    M, Kh = a.shape
+    N = b.shape[0]
+    assert residual.shape == (M, N) and residual.dtype == torch.bfloat16 and residual.is_contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
+    gg = None if gamma is None else gamma.to(torch.bfloat16).contiguous()
+    with _GemmTimer(f"gemm_residual_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
+        _lib.call("vf4_gemm_nvfp4_residual", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                  _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb), _ptr(residual),
+                  _ptr(gg), _ptr(out), _stream())
+    _launched()
+    return out
+
+
 def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs, exact: bool = False):
     """fc1 GEMM with the fused +bias -> GELU -> NVFP4 cast epilogue.
 

@@ -9,8 +9,7 @@ same computation with those steps fused:
   qkv GEMM (+bias) -> attention -> proj QuantLinear (cast + GEMM + bias)
   x + ls1(proj) + norm2 + static cast .... one kernel (residual written once, normalised rows
                                            quantized with the MLP's calibrated gx)
-  fc1 GEMM (+b1 -> GELU -> NVFP4 epilogue) -> fc2 GEMM (+b2)
-  x + ls2(fc2) ........................... one fused multiply-add
+  fc1 GEMM (+b1 -> GELU -> NVFP4 epilogue) -> fc2 GEMM (+b2 -> *ls2 -> +x epilogue)
 
 Numerics follow the unfused modules (bf16 rounding after LayerScale, after the residual add and
 after LayerNorm); only the kernels change.  ``fuse_norms`` converts every eligible block in place.
@@ -78,9 +77,8 @@ class FusedNVFP4Block(nn.Module):
                                          gamma=_gamma(self.ls1))
         gp, gsf = ops.gemm_gelu_nvfp4(hp, hsf, gx, _u8(mlp.w1q), _u8(mlp.w1sf), mlp.w1g, mlp.b1, mlp.gh,
                                       exact=mlp.exact_gelu)
-        y2 = ops.gemm(gp, gsf, mlp.gh, _u8(mlp.w2q), _u8(mlp.w2sf), mlp.w2g, bias=mlp.b2)
-        g2 = _gamma(self.ls2)
-        out = torch.addcmul(x_mid, y2, g2) if g2 is not None else x_mid + y2
+        out = ops.gemm_residual(gp, gsf, mlp.gh, _u8(mlp.w2q), _u8(mlp.w2sf), mlp.w2g, mlp.b2, x_mid,
+                                gamma=_gamma(self.ls2), out=x_mid)
         return out.reshape(B, S, C)
 
 
