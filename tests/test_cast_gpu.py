@@ -80,6 +80,55 @@ def test_cast_exact_ties_and_boundaries():
     assert np.array_equal(packed, oracle.pack_e2m1(c)), int((packed != oracle.pack_e2m1(c)).sum())
 
 
+def test_cast_near_boundary_and_underflow_bit_exact():
+    """Elements whose quotient x/dec lands on, or within a few ulp of, every E2M1 rounding
+    boundary for decode scales with full mantissas (the cast's bracketing fast path must hand
+    these blocks to the exact path), bf16 inputs one bf16 step around the boundaries, -0.0 in
+    every position, and fp32 blocks whose tiny negative members underflow x/dec to -0.0 (code 0
+    in the reference, code 8 for a tiny negative quotient that does not underflow)."""
+    rng = np.random.default_rng(21)
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    rows, K = 1024, 256
+    gs = np.float32(0.37)                                  # decode scales e4m3 * 0.37: full mantissas
+    x = np.empty((rows, K), np.float32)
+    for r in range(rows):
+        for b in range(K // 16):
+            amax = np.float32(np.exp2(rng.uniform(-4, 6)))
+            bs = oracle.e4m3_decode(oracle.e4m3_encode(np.minimum(amax / np.float32(6) * (np.float32(1) / gs),
+                                                                  np.float32(448))))
+            dec = np.float32(bs * gs)
+            m = rng.choice(mids, 16) * rng.choice([-1, 1], 16)
+            q = (m * dec).astype(np.float32)
+            steps = rng.integers(-3, 4, 16)
+            q = np.array([np.float32(v) if s == 0 else
+                          np.nextafter(v, np.float32(np.sign(s) * np.inf), dtype=np.float32) if abs(s) == 1 else
+                          np.float32(v) + np.float32(s) * np.spacing(np.float32(v)) for v, s in zip(q, steps)],
+                         np.float32)
+            q[rng.integers(16)] = amax
+            x[r, 16 * b:16 * b + 16] = q
+    # fp32 input: full-precision quotients around the boundaries
+    gt = torch.tensor(gs, device="cuda")
+    packed, _, sfl, _ = _run_cast(torch.from_numpy(x).cuda(), "six", gt)
+    c, b, _ = oracle.quantize_to_nvfp4(x, 16, global_scale=gs)
+    assert np.array_equal(sfl, b)
+    assert np.array_equal(packed, oracle.pack_e2m1(c)), int((packed != oracle.pack_e2m1(c)).sum())
+    # bf16 input of the same data, with -0.0 sprinkled in
+    xb = oracle.to_bf16(x)
+    xb[rng.random(xb.shape) < 0.02] = -0.0
+    packed, _, sfl, _ = _run_cast(bf16_tensor(xb), "six", gt)
+    c, b, _ = oracle.quantize_to_nvfp4(xb, 16, global_scale=gs)
+    assert np.array_equal(sfl, b) and np.array_equal(packed, oracle.pack_e2m1(c))
+    # fp32 underflow of the quotient: block max 1e4 (decode scale 448 with gs=1) and tiny negatives
+    xu = np.zeros((128, 64), np.float32)
+    xu[:, 0] = 1e4
+    xu[:, 1:] = -np.float32(1.4e-45) * rng.integers(1, 1000, (128, 63)).astype(np.float32)
+    xu[::2, 1:] *= np.float32(1e6)                     # these quotients stay tiny but non-zero
+    packed, _, sfl, _ = _run_cast(torch.from_numpy(xu).cuda(), "six", torch.tensor(1.0, device="cuda"))
+    c, b, _ = oracle.quantize_to_nvfp4(xu, 16, global_scale=np.float32(1.0))
+    assert (c == 0).any() and (c == 8).any()
+    assert np.array_equal(sfl, b) and np.array_equal(packed, oracle.pack_e2m1(c))
+
+
 def test_cast_random_scales_bit_exact():
     """2M elements with per-row magnitudes spanning 2^-30..2^30 (bf16 and fp32 inputs)."""
     rng = np.random.default_rng(12)

@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
         float x[16];
         load8(qh + r * ss + bb * 16, x);
         load8(qh + r * ss + bb * 16 + 8, x + 8);
-        BlockQ z = quantize_block<false>(x, gs_q, se_q);
+        BlockQ z = quantize_block<false>(x, gs_q, se_q, 0x1p17f);   // raw bf16 values
         pq = z.packed;
         sfq = z.sf;
         load8(kh + r * ss + bb * 16, x);

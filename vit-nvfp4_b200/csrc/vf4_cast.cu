@@ -7,6 +7,8 @@
 // The cast is HBM-bound: one thread quantizes one 16-element block (two 16-byte loads for
 // bf16), writes its 8 packed bytes, and each aligned group of four lanes merges its four
 // E4M3 scale bytes into one 32-bit store of the 128x4-tiled scale layout.
+#include <type_traits>
+
 #include "vf4_common.cuh"
 #include "vf4_host.h"
 
@@ -131,6 +133,9 @@ __global__ void global_scale_kernel(const float* amax, float denom, float* gs) {
 // The cast.  Thread t covers block (row, blk) of the padded (ceil128(M), ceil4(K/16)) grid;
 // threads outside (M, K/16) only contribute zero scale bytes to the padding.
 // ---------------------------------------------------------------------------------------
+template <typename T, bool kGelu, bool kBias>
+constexpr bool kBf16Exact = std::is_same<T, __nv_bfloat16>::value && !kGelu && !kBias;
+
 template <typename T, bool kMse, bool kGelu, bool kBias>
 __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int64_t M, int64_t K,
                                                    int64_t ld, const float* __restrict__ gs_ptr,
@@ -159,7 +164,8 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
       float v[16];
       load16<T>(x + row * ld + blk * 16, v);
       prologue16<T, kGelu, kBias>(v, bias, blk * 16);
-      BlockQ q = quantize_block<kMse>(v, gs, s_enc);
+      // bf16 inputs are >= 2^-133 in magnitude when non-zero (see encode16_bracket)
+      BlockQ q = quantize_block<kMse>(v, gs, s_enc, kBf16Exact<T, kGelu, kBias> ? 0x1p17f : 2.0f);
       *reinterpret_cast<uint64_t*>(out_packed + row * (K / 2) + blk * 8) = q.packed;
       sf = q.sf;
       if (sf_lin) sf_lin[row * nb + blk] = (uint8_t)sf;
@@ -410,7 +416,7 @@ __global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __res
         const float bam = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
         float dec;
         const uint32_t sf = six_scale(bam, s_enc, gs, &dec);
-        const uint32_t codes = encode8_exact(h, dec);
+        const uint32_t codes = encode8_bracket(h, dec, 0x1p17f);   // h is bf16-rounded
         if (in) *reinterpret_cast<uint32_t*>(out_packed + row * (K / 2) + e0 / 2) = codes;
         // scale bytes of SF columns 16c + 4g .. +3 live in lanes 8g, 8g+2, 8g+4, 8g+6
         uint32_t b1 = __shfl_down_sync(0xffffffffu, sf, 2);

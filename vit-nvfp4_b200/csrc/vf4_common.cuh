@@ -191,6 +191,80 @@ VF4_DEV uint32_t encode8_exact(const float* v, float dec) {
   return cvt_e2m1x8(q) - fix;
 }
 
+// Bracketing encoder, bit-exact with encode16_exact at a fraction of its cost.
+//
+// The reference code of x is round_half_down(q) with q = RN(x / dec).  Instead of q, two
+// brackets a = RN(x * lo) and b = RN(x * hi) are formed with lo, hi = (1 -+ 2^-20) / dec, so
+// a < q < b strictly (the approximate reciprocal and the three roundings move them by less
+// than 2^-21 relative), and both are converted with the hardware's nearest-even E2M1 rounding.
+// The conversion is monotone, so equal codes for a and b mean that no E2M1 rounding boundary
+// (midpoint) lies strictly between them; if a is itself an odd-type midpoint (0.75, 1.75, 3.5,
+// where nearest-even rounds up), q > a rounds up in the reference too, and if b is a midpoint
+// the codes differ unless nearest-even rounds b down, as the reference does for q < b.  So
+// equal codes are the reference codes, and unequal codes (an element within ~2^-20 of a
+// midpoint, rare for real data) send the block to encode16_exact.  The +0 in the FMA maps
+// x = -0 to code 0 (the reference's sign is q < 0).  The fast path needs 2^-120 <= dec <=
+// dec_max, where dec_max keeps every non-zero |x| / dec above 2^-150 so that q cannot round to
+// -0 (the one case where a negative x has reference code 0): 2^17 for bf16 inputs
+// (|x| >= 2^-133), 2 for fp32 inputs (|x| >= 2^-149).  Two packed FMAs per element pair
+// (fma.rn.f32x2) and two converts per pair replace the divide, correction and tie tests.
+VF4_DEV unsigned long long f32x2_pack(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+VF4_DEV void f32x2_unpack(unsigned long long r, float* a, float* b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(*a), "=f"(*b) : "l"(r));
+}
+
+VF4_DEV unsigned long long fma_f32x2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
+  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode16_exact(v, dec);
+  float inv;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
+  const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
+  const unsigned long long lo2 = f32x2_pack(lo, lo), hi2 = f32x2_pack(hi, hi), z2 = f32x2_pack(0.f, 0.f);
+  uint32_t wa[2], wb[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const unsigned long long x2 = f32x2_pack(v[8 * h + 2 * i], v[8 * h + 2 * i + 1]);
+      f32x2_unpack(fma_f32x2(x2, lo2, z2), &a[2 * i], &a[2 * i + 1]);
+      f32x2_unpack(fma_f32x2(x2, hi2, z2), &b[2 * i], &b[2 * i + 1]);
+    }
+    wa[h] = cvt_e2m1x8(a);
+    wb[h] = cvt_e2m1x8(b);
+  }
+  if ((wa[0] != wb[0]) | (wa[1] != wb[1])) return encode16_exact(v, dec);
+  return (uint64_t)wa[0] | ((uint64_t)wa[1] << 32);
+}
+
+// Half a block (8 values) with the bracketing scheme of encode16_bracket.
+VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
+  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode8_exact(v, dec);
+  float inv;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
+  const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
+  const unsigned long long lo2 = f32x2_pack(lo, lo), hi2 = f32x2_pack(hi, hi), z2 = f32x2_pack(0.f, 0.f);
+  float a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const unsigned long long x2 = f32x2_pack(v[2 * i], v[2 * i + 1]);
+    f32x2_unpack(fma_f32x2(x2, lo2, z2), &a[2 * i], &a[2 * i + 1]);
+    f32x2_unpack(fma_f32x2(x2, hi2, z2), &b[2 * i], &b[2 * i + 1]);
+  }
+  const uint32_t wa = cvt_e2m1x8(a), wb = cvt_e2m1x8(b);
+  return wa == wb ? wa : encode8_exact(v, dec);
+}
+
 // Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
 // (differs from the reference only within one ulp of a rounding boundary or on an exact tie).
 VF4_DEV uint64_t encode16_fast(const float* v, float dec) {
@@ -233,8 +307,10 @@ VF4_DEV float gelu_as(float x) {
   return x * (x >= 0.f ? 1.0f - E : E);
 }
 
+// dec_max: the largest decode scale for which encode16_bracket may take its fast path for the
+// inputs at hand (2^17 for bf16 values, 2 for arbitrary fp32 values).
 template <bool kMse>
-VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
+VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc, float dec_max = 2.0f) {
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -254,7 +330,7 @@ VF4_DEV BlockQ quantize_block(const float* v, float gs, float s_enc) {
   } else {
     float dec;
     r.sf = six_scale(amax, s_enc, gs, &dec);
-    r.packed = encode16_exact(v, dec);
+    r.packed = encode16_bracket(v, dec, dec_max);
   }
   return r;
 }
