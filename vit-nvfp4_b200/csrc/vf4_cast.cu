@@ -152,11 +152,12 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
   const float s_enc = __fdiv_rn(1.0f, gs);
   const int lane = threadIdx.x & 31;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); t0 < total;
-       t0 += stride) {
+  // (row, blk) of this thread's flat index, advanced by the grid stride without dividing
+  const int64_t t_first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t d_row = stride / nb4, d_blk = stride - d_row * nb4;
+  int64_t row = t_first / nb4, blk = t_first - row * nb4;
+  for (int64_t t0 = t_first - lane; t0 < total; t0 += stride) {
     const int64_t t = t0 + lane;
-    const int64_t row = t / nb4;
-    const int64_t blk = t - row * nb4;
     const bool in_grid = t < total;
     const bool valid = in_grid && row < M && blk < nb;
     uint32_t sf = 0;
@@ -177,6 +178,12 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
     if (sf_swz && in_grid && (blk & 3) == 0) {
       int64_t off = ((row >> 7) * ncb + (blk >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
       *reinterpret_cast<uint32_t*>(sf_swz + off) = w;
+    }
+    row += d_row;
+    blk += d_blk;
+    if (blk >= nb4) {
+      blk -= nb4;
+      ++row;
     }
   }
 }
@@ -284,7 +291,7 @@ VF4_DEV float bf16_bits_lo(uint32_t w) { return __uint_as_float(w << 16); }
 VF4_DEV float bf16_bits_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 template <int NC, bool kRes, int kMode>
-__global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_bfloat16* __restrict__ x,
                                                       const __nv_bfloat16* __restrict__ y,
                                                       const __nv_bfloat16* __restrict__ gamma,
                                                       __nv_bfloat16* __restrict__ x_out,
@@ -294,6 +301,16 @@ __global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __res
                                                       float* __restrict__ amax_out,
                                                       uint8_t* __restrict__ out_packed,
                                                       uint8_t* __restrict__ out_sf) {
+  // LayerNorm weight, bias and LayerScale as bf16 pairs in shared memory (16-byte chunks)
+  __shared__ uint4 s_par[3][NC * 32];
+  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
+    s_par[0][i] = __ldg(reinterpret_cast<const uint4*>(ln_w) + i);
+    s_par[1][i] = __ldg(reinterpret_cast<const uint4*>(ln_b) + i);
+    if constexpr (kRes)
+      s_par[2][i] = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma) + i)
+                          : make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warp_g = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -304,26 +321,32 @@ __global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __res
     gs = *gs_ptr;
     s_enc = __fdiv_rn(1.0f, gs);
   }
-  // LayerNorm affine parameters of this lane's elements
-  float w[NC][8], bb[NC][8];
+  // Raw bf16 words of the next row are loaded while the current row is processed.
+  constexpr int kAhead = 1;
+  uint4 nx[NC], ny[NC], nx2[NC];
+  auto fetch = [&](int64_t row, uint4* bx, uint4* by) {
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int e0 = 256 * c + 8 * lane;
-    if (e0 < K) {
-      uint4 a = __ldg(reinterpret_cast<const uint4*>(ln_w + e0));
-      uint4 b = __ldg(reinterpret_cast<const uint4*>(ln_b + e0));
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w[c][2 * i] = bf16_bits_lo(aw[i]);
-        w[c][2 * i + 1] = bf16_bits_hi(aw[i]);
-        bb[c][2 * i] = bf16_bits_lo(bw[i]);
-        bb[c][2 * i + 1] = bf16_bits_hi(bw[i]);
+    for (int c = 0; c < NC; ++c) {
+      const int e0 = 256 * c + 8 * lane;
+      if (row < M && e0 < K) {
+        bx[c] = __ldg(reinterpret_cast<const uint4*>(x + row * K + e0));
+        if constexpr (kRes) by[c] = __ldg(reinterpret_cast<const uint4*>(y + row * K + e0));
       }
     }
-  }
+  };
   float lane_amax = 0.f;
+  fetch(warp_g, nx, ny);
+  if constexpr (kAhead == 2) fetch(warp_g + nwarps, nx2, ny);
   for (int64_t row = warp_g; row < Mp; row += nwarps) {
+    uint4 cx[NC], cy[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      cx[c] = nx[c];
+      if constexpr (kRes) cy[c] = ny[c];
+      if constexpr (kAhead == 2) nx[c] = nx2[c];
+    }
+    if constexpr (kAhead == 2) fetch(row + 2 * nwarps, nx2, ny);
+    else fetch(row + nwarps, nx, ny);
     if (row >= M) {  // zero the scale padding rows of the last 128-row tile
       if constexpr (kMode == 1) {
 #pragma unroll
@@ -338,77 +361,81 @@ __global__ void __launch_bounds__(256) ln_cast_kernel(const __nv_bfloat16* __res
       }
       continue;
     }
-    float v[NC][8];
-    float sum = 0.f;
+    // r: this lane's 8*NC values as raw bf16 pairs (after the residual step when kRes); the
+    // fp32 pairs are re-derived from them in each pass, which keeps the register count low
+    // enough for 8 resident warps per scheduler
+    uint32_t r[NC][4];
+    unsigned long long sum2 = f32x2_pack(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int e0 = 256 * c + 8 * lane;
       if (e0 < K) {
-        uint4 a = __ldg(reinterpret_cast<const uint4*>(x + row * K + e0));
-        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[c][2 * i] = bf16_bits_lo(aw[i]);
-          v[c][2 * i + 1] = bf16_bits_hi(aw[i]);
-        }
+        const uint32_t xw[4] = {cx[c].x, cx[c].y, cx[c].z, cx[c].w};
         if constexpr (kRes) {
-          uint4 yv = __ldg(reinterpret_cast<const uint4*>(y + row * K + e0));
-          const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
-          float g[8];
-          if (gamma) {
-            uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + e0));
-            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              g[2 * i] = bf16_bits_lo(gw[i]);
-              g[2 * i + 1] = bf16_bits_hi(gw[i]);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) g[i] = 1.f;
-          }
-          uint32_t ow[4];
+          const uint32_t yw[4] = {cy[c].x, cy[c].y, cy[c].z, cy[c].w};
+          const uint4 gv = s_par[2][e0 / 8];
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float y0 = bf16_round(bf16_bits_lo(yw[i]) * g[2 * i]);
-            const float y1 = bf16_round(bf16_bits_hi(yw[i]) * g[2 * i + 1]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[c][2 * i] + y0, v[c][2 * i + 1] + y1);
-            ow[i] = *reinterpret_cast<uint32_t*>(&h2);
-            v[c][2 * i] = bf16_bits_lo(ow[i]);
-            v[c][2 * i + 1] = bf16_bits_hi(ow[i]);
+            // x' = bf16(x + bf16(y * gamma))
+            const uint32_t yg = bf16x2_round(mul_f32x2(bf16x2_to_f32x2(yw[i]), bf16x2_to_f32x2(gw[i])));
+            r[c][i] = bf16x2_round(add_f32x2(bf16x2_to_f32x2(xw[i]), bf16x2_to_f32x2(yg)));
           }
-          *reinterpret_cast<uint4*>(x_out + row * K + e0) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          *reinterpret_cast<uint4*>(x_out + row * K + e0) = make_uint4(r[c][0], r[c][1], r[c][2], r[c][3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) r[c][i] = xw[i];
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum += v[c][i];
+        for (int i = 0; i < 4; ++i) sum2 = add_f32x2(sum2, bf16x2_to_f32x2(r[c][i]));
       }
     }
+    float s0, s1;
+    f32x2_unpack(sum2, &s0, &s1);
+    float sum = s0 + s1;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float mean = sum / (float)K;
-    float sq = 0.f;
+    const unsigned long long nmean2 = f32x2_pack(-mean, -mean);
+    unsigned long long sq2 = f32x2_pack(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < NC; ++c)
       if (256 * c + 8 * lane < K) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float d = v[c][i] - mean;
-          sq += d * d;
+        for (int i = 0; i < 4; ++i) {
+          const unsigned long long d2 = add_f32x2(bf16x2_to_f32x2(r[c][i]), nmean2);
+          sq2 = fma_f32x2(d2, d2, sq2);
         }
       }
+    f32x2_unpack(sq2, &s0, &s1);
+    float sq = s0 + s1;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     const float rstd = rsqrtf(sq / (float)K + eps);
+    const unsigned long long rstd2 = f32x2_pack(rstd, rstd);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int e0 = 256 * c + 8 * lane;
       const bool in = e0 < K;   // warp-uniform per (c, lane group of 8) -> shuffles stay converged
       float h[8];
       float am = 0.f;
+      if (in) {
+        const uint4 wv = s_par[0][e0 / 8], bv = s_par[1][e0 / 8];
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        h[i] = in ? bf16_round((v[c][i] - mean) * rstd * w[c][i] + bb[c][i]) : 0.f;
-        am = fmaxf(am, fabsf(h[i]));
+        for (int i = 0; i < 4; ++i) {
+          // h = bf16((x - mean) * rstd * w + b)
+          const unsigned long long d2 = add_f32x2(bf16x2_to_f32x2(r[c][i]), nmean2);
+          const uint32_t hb = bf16x2_round(
+              fma_f32x2(mul_f32x2(d2, rstd2), bf16x2_to_f32x2(ww[i]), bf16x2_to_f32x2(bw[i])));
+          h[2 * i] = __uint_as_float(hb << 16);
+          h[2 * i + 1] = __uint_as_float(hb & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(h[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = 0.f;
       }
       if constexpr (kMode == 0) {
         lane_amax = fmaxf(lane_amax, am);

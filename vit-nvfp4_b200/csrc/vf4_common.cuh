@@ -224,6 +224,31 @@ VF4_DEV unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
   return d;
 }
 
+VF4_DEV unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+VF4_DEV unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// bf16 pair (low half = first element) <-> fp32 pair, and RN rounding of an fp32 pair to bf16
+VF4_DEV unsigned long long bf16x2_to_f32x2(uint32_t w) {
+  return f32x2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+VF4_DEV uint32_t bf16x2_round(unsigned long long p) {
+  float a, b;
+  f32x2_unpack(p, &a, &b);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));   // first operand -> upper half
+  return r;
+}
+
 VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
   if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode16_exact(v, dec);
   float inv;
@@ -282,8 +307,17 @@ VF4_DEV uint64_t encode16_fast(const float* v, float dec) {
 }
 
 // E4M3 block scale (six rule) and its decode value: bs = e4m3(min((amax/6)*s_enc, 448)).
+// RN(a / 6) for normal a by one Markstein correction step (q0 = a*y, r = a - 6*q0 exact by FMA,
+// q = q0 + r*y with y = RN(1/6)); checked against IEEE division for every significand in
+// [1, 2), which covers all a >= 1e-12 since both sides scale exactly by powers of two.
+VF4_DEV float div6_rn(float a) {
+  const float y = 0.16666667163372039795f;   // RN(1/6) = 0x3E2AAAAB
+  const float q = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(-q, 6.0f, a), y, q);
+}
+
 VF4_DEV uint32_t six_scale(float amax, float s_enc, float gs, float* dec) {
-  float bs_f = fminf(__fmul_rn(__fdiv_rn(fmaxf(amax, 1e-12f), 6.f), s_enc), 448.f);
+  float bs_f = fminf(__fmul_rn(div6_rn(fmaxf(amax, 1e-12f)), s_enc), 448.f);
   uint32_t b = f32_to_e4m3(bs_f);
   *dec = __fmul_rn(e4m3_to_f32(b), gs);
   return b;
