@@ -153,13 +153,28 @@ VF4_API int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t
  *   q, k, v : bf16, element (b, h, s, d) at ptr + b*stride_b + h*stride_h + s*stride_s + d
  *             (the packed qkv projection output and (B, H, S, D) tensors both fit)
  *   out     : bf16, element (b, h, s, d) at out + b*out_stride_b + h*out_stride_h + s*out_stride_s + d
- *   smooth-K / smooth-V always on; per-(b,h) global scales for Q, K~, V~; fixed P global
- *   1/(6*448); no mask, not causal.  D % 16 == 0, D <= 128; S <= 1152 for D > 64.
+ *   smooth-K / smooth-V always on; global scales of Q, K~, V~ over the whole tensors, as the
+ *   reference (a statistics kernel runs first); P quantized along keys with the fixed global
+ *   1/(6*448) instead of the amax of the whole P tensor; no mask, not causal.
+ *   D % 16 == 0, D <= 128; S <= 1152 for D > 64.  Head dim 64 with S <= 320 (ViT-S/B/L) runs
+ *   as one fused kernel that quantizes P = exp(S - rowmax) and divides the output by the row
+ *   sum; other shapes run prep + forward kernels with P normalised first.
  *   workspace: at least vf4_attn_workspace_size(B, H, S, D) bytes, 16-byte aligned. */
 VF4_API int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
                            int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
                            void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
                            void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
+
+/* vf4_attn_nvfp4 with options.  flags: VF4_ATTN_HEAD_GLOBALS takes the Q / K~ / V~ global scales per
+ * (image, head) instead of over the whole tensors as the reference does: no statistics pass and,
+ * for head dim 64 and S <= 320, no workspace at all (workspace may then be NULL), at the cost of
+ * differing from the reference's quantization by independent FP4 noise (cos ~0.98 instead of
+ * ~0.9999 against quant_sdpa).  0 = vf4_attn_nvfp4. */
+#define VF4_ATTN_HEAD_GLOBALS 1
+VF4_API int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
+                              int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
+                              void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
+                              int flags, void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
 
 /* vf4_attn_nvfp4 without a caller workspace, for callers that cannot allocate device memory
  * (a runtime that owns all device memory through its own pool, or a plugin that may not

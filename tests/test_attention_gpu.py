@@ -1,12 +1,13 @@
 """GPU parity of the NVFP4 attention kernels.
 
-The kernel's two deliberate differences from the reference's emulated quant_sdpa are per-(image,
-head) global scales for Q, K~, V~ and a fixed 1/(6*448) global for P.  Bars:
+The kernels' deliberate difference from the reference's emulated quant_sdpa is the fixed
+1/(6*448) global for P (and, on the fused route, P quantized before the 1/rowsum).  Bars:
   * vs a CPU restatement of exactly those semantics (``_oracle_kernel_semantics``): cos >= 0.999
-  * accuracy vs exact fp32 attention no worse than the reference's own (oracle.quant_sdpa with
-    qk = pv = 'nvfp4') minus 0.005, and > 0.95 (the reference's bar, tests/test_attention.py:60-64)
-  * vs the reference's quantized output: cos >= 0.97 (two independent FP4 noise draws of the same
-    attention agree to ~0.976-0.99 on these inputs; each is ~0.972-0.976 from exact)
+  * vs the reference's quantized output (oracle.quant_sdpa, qk = pv = 'nvfp4'): cos >= 0.995
+  * accuracy vs exact fp32 attention no worse than the reference's own minus 0.005, and > 0.95
+    (the reference's bar, tests/test_attention.py:60-64)
+The per-head-globals mode is a different FP4 noise draw (cos ~0.98 vs the reference), so it is
+held to its own oracle and to the reference's accuracy over many heads.
 """
 import math
 
@@ -34,21 +35,37 @@ def _qdq(x, gs, axis=-1):
     return np.moveaxis(d, -1, axis)
 
 
-def _oracle_kernel_semantics(q, k, v, scale):
+def _fused_path(S, D):
+    """The single-kernel route (head dim 64, S <= 320) quantizes P unnormalised."""
+    return D == 64 and S <= 320
+
+
+def _oracle_kernel_semantics(q, k, v, scale, head_globals=False):
+    """The kernels' arithmetic: smooth-K/V, NVFP4 Q, K~ (along d) and V~ (along tokens) with global
+    scales over the whole tensors (or per head), P with the fixed global 1/2688 (unnormalised on the
+    fused route)."""
     B, H, S, D = q.shape
+    unnormalised = _fused_path(S, D)
     out = np.empty((B, H, S, D), F32)
+    g = lambda t: F32(max(np.abs(t).max(), 1e-12) / 2688.0)
+    ktt = k - k.mean(2, keepdims=True)
+    vtt = v - v.mean(2, keepdims=True)
+    gq_all, gk_all, gv_all = g(q), g(ktt), g(vtt)
     for b in range(B):
         for h in range(H):
             qq, kk, vv = q[b, h], k[b, h], v[b, h]
             kt = kk - kk.mean(0, keepdims=True)
             mu = vv.mean(0, keepdims=True)
             vt = vv - mu
-            g = lambda t: F32(max(np.abs(t).max(), 1e-12) / 2688.0)
-            s = _qdq(qq, g(qq)) @ _qdq(kt, g(kt)).T * F32(scale)
-            p = oracle.softmax(s)
-            pd = _qdq(p, F32(1.0 / 2688.0))
-            vd = _qdq(vt, g(vt), axis=0)
-            out[b, h] = pd @ vd + mu
+            gq, gk, gv = (g(qq), g(kt), g(vt)) if head_globals else (gq_all, gk_all, gv_all)
+            s = _qdq(qq, gq) @ _qdq(kt, gk).T * F32(scale)
+            vd = _qdq(vt, gv, axis=0)
+            if unnormalised:   # P = exp(s - max) in [0, 1] quantized, 1/rowsum applied to the output
+                p = np.exp(s - s.max(-1, keepdims=True)).astype(F32)
+                out[b, h] = (_qdq(p, F32(1.0 / 2688.0)) @ vd) / p.sum(-1, keepdims=True) + mu
+            else:
+                p = oracle.softmax(s)
+                out[b, h] = _qdq(p, F32(1.0 / 2688.0)) @ vd + mu
     return out
 
 
@@ -65,7 +82,8 @@ def _qkv(B, H, S, D, seed=0, outlier=True):
 
 
 SHAPES = [(2, 4, 64, 64), (1, 2, 197, 64), (2, 3, 257, 64), (1, 2, 1025, 80), (1, 1, 20, 64),
-          (1, 2, 130, 128), (2, 2, 385, 64)]
+          (1, 2, 130, 128), (2, 2, 385, 64), (1, 1, 1, 64), (1, 2, 48, 64), (2, 3, 320, 64),
+          (8, 40, 197, 64)]   # the last one: more heads than SMs, several heads per persistent CTA
 
 
 @pytest.mark.parametrize("B,H,S,D", SHAPES)
@@ -80,7 +98,23 @@ def test_attention_matches_oracles(B, H, S, D):
     exact = oracle.quant_sdpa(qn, kn, vn, qk="bf16", pv="bf16", smooth_k=False, smooth_v=False)
     assert np.isfinite(out).all()
     c1, c2, c3, c_ref = cos(out, ref_kernel), cos(out, ref_sdpa), cos(out, exact), cos(ref_sdpa, exact)
-    assert c1 >= 0.999 and c2 >= 0.97 and c3 > 0.95 and c3 >= c_ref - 0.005, (c1, c2, c3, c_ref)
+    assert c1 >= 0.999 and c2 >= 0.995 and c3 > 0.95 and c3 >= c_ref - 0.005, (c1, c2, c3, c_ref)
+
+
+@pytest.mark.parametrize("B,H,S,D", [(2, 3, 257, 64), (16, 12, 197, 64), (1, 2, 1025, 80)])
+def test_attention_head_globals_mode(B, H, S, D):
+    """Per-head global scales (VF4_ATTN_HEAD_GLOBALS): exact to its own semantics, and as accurate
+    as the reference on average over many heads (each head is an independent FP4 noise draw)."""
+    from vitfp4.nvfp4 import ops
+    q, k, v = _qkv(B, H, S, D, seed=7 + S)
+    scale = 1.0 / math.sqrt(D)
+    out = ops.attention_bhsd(q.cuda(), k.cuda(), v.cuda(), scale, head_globals=True).float().cpu().numpy()
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref_kernel = _oracle_kernel_semantics(qn, kn, vn, scale, head_globals=True)
+    exact = oracle.quant_sdpa(qn, kn, vn, qk="bf16", pv="bf16", smooth_k=False, smooth_v=False)
+    ref_sdpa = oracle.quant_sdpa(qn, kn, vn, qk="nvfp4", pv="nvfp4")
+    assert cos(out, ref_kernel) >= 0.999
+    assert cos(out, exact) >= cos(ref_sdpa, exact) - 0.005 and cos(out, exact) > 0.95
 
 
 def test_attention_packed_qkv_path_equals_bhsd():

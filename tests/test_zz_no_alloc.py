@@ -48,7 +48,7 @@ def test_noalloc_matches_workspace_entry_point_twice(shapes):
 def test_noalloc_refuses_oversized_problem():
     from vitfp4 import _lib
     lib = _lib.lib()
-    B, H, S, D = 64, 16, 257, 64                      # ~41 MB of workspace > 16 MiB
+    B, H, S, D = 8, 16, 1025, 80                      # ViT-H/14 @448 heads: ~30 MB of workspace > 16 MiB
     assert lib.vf4_attn_workspace_size(B, H, S, D) > 16 << 20
     q = torch.zeros(B, H, S, D, dtype=torch.bfloat16, device="cuda")
     out = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device="cuda")

@@ -100,11 +100,126 @@ VF4_DEV float block_max(float m, float* red) {
   return r;
 }
 
+VF4_DEV float warp_max(float m) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
+// ---------------------------------------------------------------------------------------
+// Per-head statistics for the reference's tensor-wide global scales (attention.py:28-50 takes one
+// amax over the whole q, k~ and v~ tensors): column means of k and v per (b, h), written to
+// `stats` (mu_k[Dp], mu_v[Dp] per head), and atomic maxima over all heads of |q|, |k - mu_k|,
+// |v - mu_v| into amax3[0..2] (non-negative floats compare like their bit patterns).  The
+// centred maxima come from column max / min: rounding is monotone, so max_s |x_s - m| =
+// max(|max x - m|, |min x - m|) exactly.  One read of q, k and v; 256 threads per head.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __restrict__ q,
+                                                         const __nv_bfloat16* __restrict__ k,
+                                                         const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                         int64_t sh, int64_t ss, int H, int S, int D, int Dp,
+                                                         float* __restrict__ stats, float* __restrict__ amax3) {
+  extern __shared__ float part[];   // [6][rpi][D]: k sum/max/min, v sum/max/min per row group
+  __shared__ float red[3][8];
+  const int head = blockIdx.x;
+  const int b = head / H, h = head - b * H;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int D8 = D / 8, rpi = 256 / D8, active = rpi * D8;
+  const int j = t % D8, r0 = t / D8;
+  const int64_t off = (int64_t)b * sb + (int64_t)h * sh + 8 * j;
+  float ks[8], kx[8], kn[8], vs[8], vx[8], vn[8], qm = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    ks[e] = vs[e] = 0.f;
+    kx[e] = vx[e] = -INFINITY;
+    kn[e] = vn[e] = INFINITY;
+  }
+  if (t < active) {
+    // two rows per iteration: six 16-byte loads in flight per thread
+    for (int r = r0; r < S; r += 2 * rpi) {
+      const bool two = r + rpi < S;
+      float a[2][8], c[2][8], u[2][8];
+      load8(q + off + (int64_t)r * ss, a[0]);
+      load8(k + off + (int64_t)r * ss, c[0]);
+      load8(v + off + (int64_t)r * ss, u[0]);
+      if (two) {
+        load8(q + off + (int64_t)(r + rpi) * ss, a[1]);
+        load8(k + off + (int64_t)(r + rpi) * ss, c[1]);
+        load8(v + off + (int64_t)(r + rpi) * ss, u[1]);
+      }
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        if (m == 1 && !two) break;   // the means keep a fixed summation order: row r, then r + rpi
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          qm = fmaxf(qm, fabsf(a[m][e]));
+          ks[e] += c[m][e];
+          kx[e] = fmaxf(kx[e], c[m][e]);
+          kn[e] = fminf(kn[e], c[m][e]);
+          vs[e] += u[m][e];
+          vx[e] = fmaxf(vx[e], u[m][e]);
+          vn[e] = fminf(vn[e], u[m][e]);
+        }
+      }
+    }
+    const int RD = rpi * D;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = r0 * D + 8 * j + e;
+      part[i] = ks[e];
+      part[RD + i] = kx[e];
+      part[2 * RD + i] = kn[e];
+      part[3 * RD + i] = vs[e];
+      part[4 * RD + i] = vx[e];
+      part[5 * RD + i] = vn[e];
+    }
+  }
+  qm = warp_max(qm);
+  if (lane == 0) red[0][w] = qm;
+  __syncthreads();
+  float ak = 0.f, av = 0.f;
+  if (t < D) {
+    const int RD = rpi * D;
+    float sk = 0.f, xk = -INFINITY, nk = INFINITY, sv = 0.f, xv = -INFINITY, nv = INFINITY;
+    for (int r = 0; r < rpi; ++r) {   // fixed order: deterministic means
+      const int i = r * D + t;
+      sk += part[i];
+      xk = fmaxf(xk, part[RD + i]);
+      nk = fminf(nk, part[2 * RD + i]);
+      sv += part[3 * RD + i];
+      xv = fmaxf(xv, part[4 * RD + i]);
+      nv = fminf(nv, part[5 * RD + i]);
+    }
+    const float mk = __fdiv_rn(sk, (float)S), mv = __fdiv_rn(sv, (float)S);
+    stats[(int64_t)head * 2 * Dp + t] = mk;
+    stats[(int64_t)head * 2 * Dp + Dp + t] = mv;
+    ak = fmaxf(fabsf(xk - mk), fabsf(nk - mk));
+    av = fmaxf(fabsf(xv - mv), fabsf(nv - mv));
+  } else if (t < Dp) {
+    stats[(int64_t)head * 2 * Dp + t] = 0.f;
+    stats[(int64_t)head * 2 * Dp + Dp + t] = 0.f;
+  }
+  ak = warp_max(ak);
+  av = warp_max(av);
+  if (lane == 0) {
+    red[1][w] = ak;
+    red[2][w] = av;
+  }
+  __syncthreads();
+  if (t < 3) {
+    float m = 0.f;
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, red[t][i]);
+    atomicMax(reinterpret_cast<unsigned int*>(amax3) + t, __float_as_uint(m));
+  }
+}
+
 __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __restrict__ q,
                                                         const __nv_bfloat16* __restrict__ k,
                                                         const __nv_bfloat16* __restrict__ v, int64_t sb,
                                                         int64_t sh, int64_t ss, AttnGeom g,
-                                                        uint8_t* __restrict__ ws) {
+                                                        uint8_t* __restrict__ ws,
+                                                        const float* __restrict__ stats,
+                                                        const float* __restrict__ amax3) {
   __shared__ float part[2][2048];
   __shared__ float mu[2][128];
   __shared__ float red[8];
@@ -117,8 +232,19 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
   const int rpi = 256 / D8, active = rpi * D8;
   const int t = threadIdx.x, c8 = t % D8, r0 = t / D8;
 
+  float aq = 0.f, ak = 0.f, av = 0.f;
+  if (stats) {   // tensor-wide globals: means and amaxes from attn_stats_kernel
+    if (t < D) {
+      mu[0][t] = stats[(int64_t)bh * 2 * g.Dp + t];
+      mu[1][t] = stats[(int64_t)bh * 2 * g.Dp + g.Dp + t];
+    }
+    aq = amax3[0];
+    ak = amax3[1];
+    av = amax3[2];
+    __syncthreads();
+  } else {
   // pass A: column sums of k and v, amax of q
-  float sk[8], sv[8], aq = 0.f;
+  float sk[8], sv[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) sk[i] = sv[i] = 0.f;
   if (t < active) {
@@ -153,7 +279,6 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
   aq = block_max(aq, red);  // contains __syncthreads: mu visible afterwards
 
   // pass B: amax of the centred k and v
-  float ak = 0.f, av = 0.f;
   if (t < active) {
     for (int r = r0; r < S; r += rpi) {
       float bk[8], bv[8];
@@ -168,6 +293,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
   }
   ak = block_max(ak, red);
   av = block_max(av, red);
+  }
   const float gs_q = __fdiv_rn(fmaxf(aq, 1e-12f), 2688.f);
   const float gs_k = __fdiv_rn(fmaxf(ak, 1e-12f), 2688.f);
   const float gs_v = __fdiv_rn(fmaxf(av, 1e-12f), 2688.f);
@@ -534,6 +660,572 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---------------------------------------------------------------------------------------
+// Fused attention for head dim <= 64 and S <= 320 (ViT-S/16, ViT-B/16, ViT-L/14): one kernel,
+// no workspace.  Persistent CTAs (one per SM, 18 warps) walk over the B*H heads.  Per head:
+//   warp 0      TMA loads of the head's q, k, v rows (bf16, 128-byte swizzle) into "raw"
+//   warps 2-17  prep: column means of k and v, amax of q, k~ = k - mean, v~ = v - mean ->
+//               per-head globals; Q and K~ (blocks along d) and V~^T (blocks along tokens) to
+//               NVFP4 in shared memory, in the MMA's K-major core-matrix layout (8 rows x 16
+//               bytes, no swizzle), with their scales in tcgen05.cp atoms.  The raw buffer is
+//               released here, so the next head's loads overlap this head's tiles.
+//   per 128-query tile:
+//     warp 1      S = Q K~^T: mxf4nvf4 MMAs over key chunks of 256/128/64 into TMEM
+//     warps 2-17  (TMEM lane quadrant x key slice) pass 1: row max; pass 2: P = exp(S - max)
+//                 in [0, 1] (row max exactly 1), row sums, P -> NVFP4 (fixed global 1/2688)
+//     warp 1      O = P V~ (mxf4nvf4, K = keys) into TMEM
+//     warps 2-17  out = O * gs_v / (2688 * rowsum) + mean(v) -> bf16 -> TMA store
+// P is quantized unnormalised and the 1/rowsum applied to O (the reference normalises P first;
+// with the fixed P global both are quantizations of the same probabilities).
+// Named barriers: 1 = all 16 compute warps, 2 + q = the four warps of TMEM lane quadrant q.
+// ---------------------------------------------------------------------------------------
+constexpr int kFusedWarps = 18, kFusedCompute = 16;
+constexpr uint32_t kFusedTmemS = 0, kFusedTmemO = 384, kFusedTmemQsf = 448, kFusedTmemKsf = 452,
+                   kFusedTmemPsf = 464, kFusedTmemVsf = 488;
+
+struct FusedGeom {
+  int B, H, S, D;
+  int nq, skp;          // query tiles of 128; keys padded to a multiple of 64
+  int box_rows, nbox;   // raw TMA boxes per tensor
+  int heads;
+  int qkv_hs, out_hs;   // tensor-map dimension order (d, h, s, b) instead of (d, s, h, b)
+  float scale;
+  const float* stats;   // per-head means (tensor-wide globals) or NULL (per-head globals)
+  const float* amax3;
+  uint32_t raw_q, raw_k, raw_v, fq, fk, fv, sfq, sfk, sfv, fp, sfp, zero_end, stg, red, bar, total;
+};
+
+static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
+  FusedGeom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.nq = (int)((S + 127) / 128);
+  g.skp = (int)((S + 63) / 64 * 64);
+  g.nbox = S <= 256 ? 1 : 2;
+  g.box_rows = (int)align_up((S + g.nbox - 1) / g.nbox, 8);
+  g.heads = (int)(B * H);
+  g.scale = scale;
+  const uint32_t rawb = (uint32_t)(g.nbox * g.box_rows * 128);
+  uint32_t o = 0;
+  g.raw_q = o; o += rawb;
+  g.raw_k = o; o += rawb;
+  g.raw_v = o; o += rawb;
+  g.fq = o;  o += (uint32_t)g.nq * 4096u;
+  g.fk = o;  o += (uint32_t)g.skp * 32u;
+  g.fv = o;  o += (uint32_t)g.skp * 32u;
+  g.sfq = o; o += (uint32_t)g.nq * 512u;
+  g.sfk = o; o += (uint32_t)((g.skp + 127) / 128) * 512u;
+  g.sfv = o; o += (uint32_t)(g.skp / 64) * 512u;
+  g.fp = o;  o += (uint32_t)g.skp * 64u;
+  g.sfp = o; o += (uint32_t)(g.skp / 64) * 512u;
+  g.zero_end = o;
+  o = (uint32_t)align_up(o, 1024);
+  g.stg = o; o += 4 * 4096;
+  g.red = o; o += 13312;
+  g.bar = o; o += 128;
+  g.total = o + 1024;
+  return g;
+}
+
+static bool fused_ok(int64_t S, int64_t D) {
+  if (D != 64 || S > 320) return false;
+  return make_fused_geom(1, 1, S, D, 1.f).total <= 227u * 1024u;
+}
+
+// 8 bf16 of row s, 16-byte chunk j (elements 8j..8j+7) of a 128-byte-swizzled raw tile, as fp32.
+VF4_DEV void raw_load8(const uint8_t* raw, int s, int j, float* v) {
+  const uint4 a = *reinterpret_cast<const uint4*>(raw + s * 128 + ((j ^ (s & 7)) << 4));
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+VF4_DEV float raw_elem(const uint8_t* raw, int s, int d) {
+  const uint16_t b = *reinterpret_cast<const uint16_t*>(raw + s * 128 + (((d >> 3) ^ (s & 7)) << 4) + (d & 7) * 2);
+  return __uint_as_float((uint32_t)b << 16);
+}
+
+VF4_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// byte offset of (row, 8-byte half-chunk h) in a K-major core-matrix operand with sbo bytes per
+// 8-row group: 16-byte chunk h/2 of the row, half h%2
+VF4_DEV uint32_t cm_off(int row, int h, uint32_t sbo) {
+  return (uint32_t)(row >> 3) * sbo + (uint32_t)(h >> 1) * 128u + (uint32_t)(row & 7) * 16u + (uint32_t)(h & 1) * 8u;
+}
+
+// scale-factor atom offset of (row, scale column c) for 128-row atoms of 4 columns
+VF4_DEV uint32_t sf_atom_off(int row, int c) {
+  return (uint32_t)(row >> 7) * 512u + (uint32_t)(row & 31) * 16u + (uint32_t)((row >> 5) & 3) * 4u + (uint32_t)c;
+}
+
+__global__ void __launch_bounds__(kFusedWarps * 32, 1)
+    attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                      const FusedGeom g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (base - raw0);
+  const uint32_t bar = base + g.bar;
+  const uint32_t raw_full = bar, raw_free = bar + 8, ops_ready = bar + 16, s_full = bar + 24, s_free = bar + 32,
+                 p_full = bar + 40, o_full = bar + 48, o_free = bar + 56, drain = bar + 64;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 72);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbo_kv = (uint32_t)(g.skp / 32) * 128u;   // bytes per 8-row group of P and V~^T
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(raw_full, 1);
+    mbar_init(raw_free, kFusedCompute);
+    mbar_init(ops_ready, kFusedCompute);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, kFusedCompute);
+    mbar_init(p_full, kFusedCompute);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, kFusedCompute);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmQ);
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+    tma_prefetch(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp >= 2) {
+    // scale atoms and P codes start at zero: padding keys, rows and head-dim columns stay zero
+    for (uint32_t o = g.sfq + 16u * (threadIdx.x - 64); o < g.zero_end; o += 16u * 32u * kFusedCompute)
+      *reinterpret_cast<uint4*>(gb + o) = make_uint4(0, 0, 0, 0);
+  }
+  fence_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ raw loads
+    if (lane == 0) {
+      const uint32_t bytes = 3u * (uint32_t)(g.nbox * g.box_rows) * 128u;
+      int hi = 0;
+      for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+        if (hi > 0 && !mbar_wait(raw_free, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutEmpty)) break;
+        const int b = head / g.H, h = head - b * g.H;
+        mbar_arrive_expect_tx(raw_full, bytes);
+        for (int j = 0; j < g.nbox; ++j) {
+          const uint32_t off = (uint32_t)(j * g.box_rows) * 128u;
+          const int c1 = g.qkv_hs ? h : j * g.box_rows, c2 = g.qkv_hs ? j * g.box_rows : h;
+          tma_load_4d(base + g.raw_q + off, &tmQ, 0, c1, c2, b, raw_full);
+          tma_load_4d(base + g.raw_k + off, &tmK, 0, c1, c2, b, raw_full);
+          tma_load_4d(base + g.raw_v + off, &tmV, 0, c1, c2, b, raw_full);
+        }
+      }
+      if (hi > 0) mbar_wait(raw_full, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutFull);   // own copies landed
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    bool ok = true;
+    int hi = 0, it = 0;
+    const uint32_t t_o = tmem + kFusedTmemO, t_qsf = tmem + kFusedTmemQsf, t_ksf = tmem + kFusedTmemKsf;
+    const uint32_t t_psf = tmem + kFusedTmemPsf, t_vsf = tmem + kFusedTmemVsf;
+    const int nkb = g.skp / 64;
+    for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
+      if (!mbar_wait(ops_ready, (uint32_t)hi & 1u, err, kDevErrTimeoutFull)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        for (int a = 0; a < (g.skp + 127) / 128; ++a)
+          tmem_cp_32x128b_x4(t_ksf + 4 * a, smem_desc(base + g.sfk + 512 * a, 0, 128, 0));
+        for (int kb = 0; kb < nkb; ++kb)
+          tmem_cp_32x128b_x4(t_vsf + 4 * kb, smem_desc(base + g.sfv + 512 * kb, 0, 128, 0));
+      }
+      __syncwarp();
+      for (int t = 0; t < g.nq; ++t, ++it) {
+        if (it > 0 && !mbar_wait(s_free, (uint32_t)(it - 1) & 1u, err, kDevErrTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          tmem_cp_32x128b_x4(t_qsf, smem_desc(base + g.sfq + 512 * t, 0, 128, 0));
+          const uint64_t ad = smem_desc(base + g.fq + 4096u * t, 128, 256, 0);
+          for (int n0 = 0; n0 < g.skp;) {
+            const int rem = g.skp - n0;
+            const int n = rem >= 256 ? 256 : (rem >= 128 ? 128 : 64);
+            const uint64_t bd = smem_desc(base + g.fk + (uint32_t)(n0 / 8) * 256u, 128, 256, 0);
+            mma_mxf4nvf4(tmem + kFusedTmemS + n0, ad, bd, idesc_mxf4nvf4((uint32_t)n), t_qsf, t_ksf + (n0 / 128) * 4,
+                         0u);
+            n0 += n;
+          }
+          tc_commit(s_full);
+        }
+        __syncwarp();
+        if (!mbar_wait(p_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull) ||
+            (it > 0 && !mbar_wait(o_free, (uint32_t)(it - 1) & 1u, err, kDevErrTimeoutEmpty))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          for (int kb = 0; kb < nkb; ++kb) {
+            tmem_cp_32x128b_x4(t_psf + 4 * kb, smem_desc(base + g.sfp + 512 * kb, 0, 128, 0));
+            mma_mxf4nvf4(t_o, smem_desc(base + g.fp + 256u * kb, 128, sbo_kv, 0),
+                         smem_desc(base + g.fv + 256u * kb, 128, sbo_kv, 0), idesc_mxf4nvf4(64), t_psf + 4 * kb,
+                         t_vsf + 4 * kb, kb > 0 ? 1u : 0u);
+          }
+          tc_commit(o_full);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ prep, softmax, epilogue
+    const int cw = warp - 2;           // compute warp 0..15
+    const int qd = warp & 3;           // TMEM lane quadrant this warp may access
+    const int cs = cw >> 2;            // key slice 0..3
+    const int ct = threadIdx.x - 64;   // compute thread 0..511
+    const uint32_t qbar = 2u + (uint32_t)qd;
+    float* red = reinterpret_cast<float*>(gb + g.red);
+    float* red_kv = red;               // [2][16][64] column partial sums of k and v
+    float* red_m = red + 2048;         // [4][128] row max per key slice
+    float* red_l = red + 2560;         // [4][128] row sum per key slice
+    float* mu = red + 3072;            // [2][64] means of k and v
+    float* wmax = red + 3200;          // [3][16] per-warp amax of q, k~, v~
+    float* scal = red + 3248;          // gs_q, gs_k, gs_v, 1/gs_q, 1/gs_k, 1/gs_v
+    const uint8_t* rq = gb + g.raw_q;
+    const uint8_t* rk = gb + g.raw_k;
+    const uint8_t* rv = gb + g.raw_v;
+    const int S = g.S, D = g.D;
+    const int nvb = (S + 15) / 16;                      // key blocks holding real keys
+    const int b0 = cs * nvb / 4, b1 = (cs + 1) * nvb / 4;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const int r = qd * 32 + lane;                       // tile row == TMEM lane
+    bool ok = true;
+    int hi = 0, it = 0;
+    for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+      const int b = head / g.H, h = head - b * g.H;
+      if (ok) ok = mbar_wait(raw_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
+      if (g.stats) {
+        // tensor-wide globals: this head's means and the global maxima were computed beforehand
+        // (the first barrier: every warp has finished the previous head's epilogue, which reads mu)
+        named_bar_sync(1, 512);
+        if (ct < 128) mu[ct] = g.stats[(int64_t)head * 128 + ct];
+        if (ct < 3) {
+          const float gsv = __fdiv_rn(fmaxf(g.amax3[ct], 1e-12f), 2688.f);
+          scal[ct] = gsv;
+          scal[3 + ct] = __fdiv_rn(1.0f, gsv);
+        }
+        named_bar_sync(1, 512);
+      } else {
+      // ---- prep 1: column sums of k and v, amax of q (chunk j = ct % 8, rows ct/8 + 64i)
+      {
+        const int j = ct & 7;
+        float ks[8], vs[8], qm = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ks[e] = vs[e] = 0.f;
+        if (ok) {
+          for (int s = ct >> 3; s < S; s += 64) {
+            float a[8];
+            raw_load8(rq, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qm = fmaxf(qm, fabsf(a[e]));
+            raw_load8(rk, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ks[e] += a[e];
+            raw_load8(rv, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vs[e] += a[e];
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], 8);
+          ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], 16);
+          vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], 8);
+          vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], 16);
+        }
+        qm = warp_max(qm);
+        if (lane < 8) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            red_kv[cw * 64 + 8 * lane + e] = ks[e];
+            red_kv[(16 + cw) * 64 + 8 * lane + e] = vs[e];
+          }
+        }
+        if (lane == 0) wmax[cw] = qm;
+      }
+      named_bar_sync(1, 512);
+      if (ct < 128) {
+        const int which = ct >> 6, d = ct & 63;
+        float sum = 0.f;
+        for (int w = 0; w < kFusedCompute; ++w) sum += red_kv[(which * 16 + w) * 64 + d];   // fixed order
+        mu[which * 64 + d] = __fdiv_rn(sum, (float)S);
+      }
+      named_bar_sync(1, 512);
+      // ---- prep 2: amax of k - mean and v - mean
+      {
+        const int j = ct & 7;
+        float km = 0.f, vm = 0.f;
+        if (ok) {
+          for (int s = ct >> 3; s < S; s += 64) {
+            float a[8];
+            raw_load8(rk, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) km = fmaxf(km, fabsf(a[e] - mu[8 * j + e]));
+            raw_load8(rv, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vm = fmaxf(vm, fabsf(a[e] - mu[64 + 8 * j + e]));
+          }
+        }
+        km = warp_max(km);
+        vm = warp_max(vm);
+        if (lane == 0) {
+          wmax[16 + cw] = km;
+          wmax[32 + cw] = vm;
+        }
+      }
+      named_bar_sync(1, 512);
+      if (ct == 0) {
+        float am[3] = {0.f, 0.f, 0.f};
+        for (int w = 0; w < kFusedCompute; ++w)
+          for (int i = 0; i < 3; ++i) am[i] = fmaxf(am[i], wmax[16 * i + w]);
+        for (int i = 0; i < 3; ++i) {
+          const float gsv = __fdiv_rn(fmaxf(am[i], 1e-12f), 2688.f);
+          scal[i] = gsv;
+          scal[3 + i] = __fdiv_rn(1.0f, gsv);
+        }
+      }
+      named_bar_sync(1, 512);
+      }
+      const float gq = scal[0], gk = scal[1], gv = scal[2];
+      // ---- prep 3: NVFP4 operands.  Q rows [0, 128 nq) and K~ rows [0, skp): 4 column blocks
+      // per row, lane quads = one row (their 4 scale bytes merge into one word)
+      for (int i = ct; i < g.nq * 512; i += 512) {
+        const int s = i >> 2, cb = i & 3;
+        uint64_t codes = 0;
+        uint32_t sf = 0;
+        if (ok && s < S && cb * 16 < D) {
+          float x[16];
+          raw_load8(rq, s, 2 * cb, x);
+          raw_load8(rq, s, 2 * cb + 1, x + 8);
+          const BlockQ z = quantize_block<false>(x, gq, scal[3], 0x1p17f);   // raw bf16 values
+          codes = z.packed;
+          sf = z.sf;
+        }
+        *reinterpret_cast<uint64_t*>(gb + g.fq + cm_off(s, cb, 256)) = codes;
+        uint32_t w = sf << (8 * cb);
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        if (cb == 0) *reinterpret_cast<uint32_t*>(gb + g.sfq + sf_atom_off(s, 0)) = w;
+      }
+      for (int i = ct; i < g.skp * 4; i += 512) {
+        const int s = i >> 2, cb = i & 3;
+        uint64_t codes = 0;
+        uint32_t sf = 0;
+        if (ok && s < S && cb * 16 < D) {
+          float x[16];
+          raw_load8(rk, s, 2 * cb, x);
+          raw_load8(rk, s, 2 * cb + 1, x + 8);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[e] -= mu[16 * cb + e];
+          const BlockQ z = quantize_block<false>(x, gk, scal[4]);
+          codes = z.packed;
+          sf = z.sf;
+        }
+        *reinterpret_cast<uint64_t*>(gb + g.fk + cm_off(s, cb, 256)) = codes;
+        uint32_t w = sf << (8 * cb);
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        if (cb == 0) *reinterpret_cast<uint32_t*>(gb + g.sfk + sf_atom_off(s, 0)) = w;
+      }
+      // V~^T rows d in [0, 64), token blocks tb in [0, skp/16); a warp covers 32 consecutive d of one
+      // token block, so its raw reads of a token row are 64 contiguous bytes (no bank conflicts)
+      {
+        const int ntb = g.skp / 16;
+        for (int i = ct; i < 64 * ntb; i += 512) {
+          const int tb = i >> 6, d = i & 63;
+          uint64_t codes = 0;
+          uint32_t sf = 0;
+          if (ok && d < D && tb * 16 < S) {
+            float x[16];
+            const float m = mu[64 + d];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int s = tb * 16 + e;
+              x[e] = s < S ? raw_elem(rv, s, d) - m : 0.f;
+            }
+            const BlockQ z = quantize_block<false>(x, gv, scal[5]);
+            codes = z.packed;
+            sf = z.sf;
+          }
+          *reinterpret_cast<uint64_t*>(gb + g.fv + cm_off(d, tb, sbo_kv)) = codes;
+          gb[g.sfv + (uint32_t)(tb >> 2) * 512u + sf_atom_off(d, tb & 3)] = (uint8_t)sf;
+        }
+      }
+      fence_async_shared();   // operand writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(ops_ready);
+        mbar_arrive(raw_free);
+      }
+      const float cexp = gq * gk * g.scale * 1.4426950408889634f;
+      const float ofac = gv * kInv2688;
+      // ---- query tiles
+      for (int t = 0; t < g.nq; ++t, ++it) {
+        const bool active = ok && t * 128 + qd * 32 < S;
+        if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
+        tc_fence_after();
+        // pass 1: row max over this warp's key blocks
+        float m = -INFINITY;
+        if (active && ok) {
+          for (int bk = b0; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemS + 16 * bk, v);
+            tmem_wait_ld();
+            if (bk == nvb - 1) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                if (16 * bk + e < S) m = fmaxf(m, __uint_as_float(v[e]));
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) m = fmaxf(m, __uint_as_float(v[e]));
+            }
+          }
+        }
+        red_m[cs * 128 + r] = m;
+        named_bar_sync(qbar, 128);
+        m = fmaxf(fmaxf(red_m[r], red_m[128 + r]), fmaxf(red_m[256 + r], red_m[384 + r]));
+        // pass 2: P = 2^((s - m) * c) in [0, 1], row sums, NVFP4 P into shared memory
+        const float mc = m * cexp;
+        float lsum = 0.f;
+        if (active && ok) {
+          for (int bk = b0; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemS + 16 * bk, v);
+            tmem_wait_ld();
+            float p[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) p[e] = ex2_approx(__fmaf_rn(__uint_as_float(v[e]), cexp, -mc));
+            if (bk == nvb - 1) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                if (16 * bk + e >= S) p[e] = 0.f;
+            }
+            float am = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              lsum += p[e];
+              am = fmaxf(am, p[e]);
+            }
+            float dec;
+            const uint32_t sf = six_scale(am, 2688.f, kInv2688, &dec);
+            *reinterpret_cast<uint64_t*>(gb + g.fp + cm_off(r, bk, sbo_kv)) = encode16_fast(p, dec);
+            gb[g.sfp + (uint32_t)(bk >> 2) * 512u + sf_atom_off(r, bk & 3)] = (uint8_t)sf;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        red_l[cs * 128 + r] = lsum;
+        fence_async_shared();   // P writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        // epilogue: O rows of this quadrant, head-dim columns [16 cs, 16 cs + 16)
+        if (ok) ok = mbar_wait(o_full, (uint32_t)it & 1u, err, kDevErrTimeoutTmem);
+        tc_fence_after();
+        uint32_t ov[16];
+        if (active && ok) {
+          tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemO + 16 * cs, ov);
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free);
+        if (cs == 0 && lane == 0) bulk_wait_read();   // this quadrant's previous store left the staging
+        named_bar_sync(qbar, 128);                     // also publishes red_l
+        uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
+        if (active && ok) {
+          const float f = ofac / (red_l[r] + red_l[128 + r] + red_l[256 + r] + red_l[384 + r]);
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int d = 16 * cs + 2 * i;
+            __nv_bfloat162 hv = __floats2bfloat162_rn(__fmaf_rn(__uint_as_float(ov[2 * i]), f, mu[64 + d]),
+                                                      __fmaf_rn(__uint_as_float(ov[2 * i + 1]), f, mu[64 + d + 1]));
+            w[i] = *reinterpret_cast<uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(stg + (((2 * cs) ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(stg + (((2 * cs + 1) ^ (lane & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        fence_async_shared();
+        named_bar_sync(qbar, 128);
+        if (active && ok && cs == 0 && lane == 0) {
+          const int row = t * 128 + qd * 32;
+          tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
+          bulk_commit();
+        }
+      }
+    }
+    if (cs == 0 && lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// bf16 4-D view of (b, h, s, d) element strides (sb, sh, ss, 1) with boxes of 64 x rows x one head,
+// 128-byte swizzle; the s and h dimensions are ordered by increasing stride (hs = h first).
+static int make_head_map(CUtensorMap* m, const void* ptr, const FusedGeom& g, int64_t sb, int64_t sh, int64_t ss,
+                         int box_rows, bool hs) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {(cuuint64_t)g.D, (cuuint64_t)(hs ? g.H : g.S), (cuuint64_t)(hs ? g.S : g.H), (cuuint64_t)g.B};
+  cuuint64_t strides[3] = {(cuuint64_t)(hs ? sh : ss) * 2, (cuuint64_t)(hs ? ss : sh) * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64u, hs ? 1u : (cuuint32_t)box_rows, hs ? (cuuint32_t)box_rows : 1u, 1u};
+  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled (attention head view) failed (%d)", (int)r);
+  return VF4_OK;
+}
+
+static int launch_fused(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                        int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
+                        int64_t oss, const float* stats, const float* amax3, cudaStream_t s) {
+  FusedGeom g = make_fused_geom(B, H, S, D, scale);
+  g.stats = stats;
+  g.amax3 = amax3;
+  g.qkv_hs = sh < ss;
+  g.out_hs = osh < oss;
+  CUtensorMap tq, tk, tv, to;
+  if (int st = make_head_map(&tq, q, g, sb, sh, ss, g.box_rows, g.qkv_hs)) return st;
+  if (int st = make_head_map(&tk, k, g, sb, sh, ss, g.box_rows, g.qkv_hs)) return st;
+  if (int st = make_head_map(&tv, v, g, sb, sh, ss, g.box_rows, g.qkv_hs)) return st;
+  if (int st = make_head_map(&to, out, g, osb, osh, oss, 32, g.out_hs)) return st;
+  cudaError_t e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = g.heads < num_sms() ? g.heads : num_sms();
+  attn_fused_kernel<<<grid, kFusedWarps * 32, g.total, s>>>(tq, tk, tv, to, g);
+  return launch_status("vf4_attn_nvfp4 (fused)");
+}
+
 static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t rowbytes, int box_x, int box_y,
                     CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_tiled();
@@ -571,6 +1263,26 @@ static int launch_fwd(const AttnGeom& g, const uint8_t* ws, float scale, void* o
   return launch_status("vf4_attn_nvfp4 (forward)");
 }
 
+// Workspace of one call: [global maxima (256 B)][per-head means][long-sequence path buffers].
+// The first two exist only with tensor-wide globals; the last only off the fused path.
+struct AttnWs {
+  int64_t off_amax, off_stats, off_gen, total;
+};
+
+static AttnWs attn_ws_layout(int64_t B, int64_t H, int64_t S, int64_t D, bool tensor) {
+  AttnWs w{};
+  const int64_t Dp = D <= 64 ? 64 : 128;
+  int64_t o = 0;
+  w.off_amax = 0;
+  if (tensor) o = 256;
+  w.off_stats = o;
+  if (tensor) o = align_up(o + B * H * 2 * Dp * 4, 1024);
+  w.off_gen = o;
+  if (!fused_ok(S, D)) o += make_geom(B, H, S, D).total;
+  w.total = o;
+  return w;
+}
+
 }  // namespace vf4
 
 using namespace vf4;
@@ -578,35 +1290,69 @@ using namespace vf4;
 extern "C" {
 
 int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D) {
-  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
-  return make_geom(B, H, S, D).total;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0 || D % 16 != 0 || D > 128) return 0;
+  return attn_ws_layout(B, H, S, D, true).total;
+}
+
+int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                      int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
+                      int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, int flags, void* workspace,
+                      int64_t workspace_bytes, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: bad sizes");
+  if (D % 16 != 0 || D > 128) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim must be a multiple of 16, <= 128");
+  if (flags & ~VF4_ATTN_HEAD_GLOBALS) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: unknown flags %d", flags);
+  if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
+    return fail(VF4_ERR_ALIGN, "vf4_attn_nvfp4: 16-byte aligned pointers and strides (multiples of 8) needed");
+  if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H too large");
+  const bool tensor = !(flags & VF4_ATTN_HEAD_GLOBALS);
+  const bool fused = fused_ok(S, D);
+  if (!fused && B * H > 65535) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H must be <= 65535 for S=%lld D=%lld",
+                                           (long long)S, (long long)D);
+  const AttnWs w = attn_ws_layout(B, H, S, D, tensor);
+  if (w.total > 0 && (!workspace || !aligned16(workspace)))
+    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: a 16-byte aligned workspace of %lld bytes is needed", (long long)w.total);
+  if (workspace_bytes < w.total)
+    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                (long long)w.total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const auto* Q = static_cast<const __nv_bfloat16*>(q);
+  const auto* K = static_cast<const __nv_bfloat16*>(k);
+  const auto* V = static_cast<const __nv_bfloat16*>(v);
+  float* stats = nullptr;
+  float* amax3 = nullptr;
+  if (tensor) {
+    stats = reinterpret_cast<float*>(ws + w.off_stats);
+    amax3 = reinterpret_cast<float*>(ws + w.off_amax);
+    if (cudaMemsetAsync(amax3, 0, 16, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4: memset failed");
+    const int D8 = (int)D / 8, rpi = 256 / D8;
+    const int smem = 6 * rpi * (int)D * 4;
+    cudaError_t e = cudaFuncSetAttribute(attn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
+                                                           (int)D, D <= 64 ? 64 : 128, stats, amax3);
+    if (int st = launch_status("vf4_attn_nvfp4 (statistics)")) return st;
+  }
+  if (fused)
+    return launch_fused(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                        out_stride_s, stats, amax3, s);
+  AttnGeom g = make_geom(B, H, S, D);
+  uint8_t* gws = ws + w.off_gen;
+  attn_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(Q, K, V, stride_b, stride_h, stride_s, g, gws, stats, amax3);
+  if (int st = launch_status("vf4_attn_nvfp4 (prep)")) return st;
+  if (g.Dp == 64) return launch_fwd<64>(g, gws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
+  return launch_fwd<128>(g, gws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
 }
 
 int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                    int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
                    int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, void* workspace,
                    int64_t workspace_bytes, vf4_stream_t stream) {
-  if (int st = check_device()) return st;
-  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: bad sizes");
-  if (D % 16 != 0 || D > 128) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim must be a multiple of 16, <= 128");
-  if (!q || !k || !v || !out || !workspace) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: null pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(workspace) ||
-      stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
-    return fail(VF4_ERR_ALIGN, "vf4_attn_nvfp4: 16-byte aligned pointers and strides (multiples of 8) needed");
-  if (B * H > 65535) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H must be <= 65535");
-  AttnGeom g = make_geom(B, H, S, D);
-  if (workspace_bytes < g.total)
-    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: workspace %lld < %lld bytes", (long long)workspace_bytes,
-                (long long)g.total);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  attn_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(q),
-                                                   static_cast<const __nv_bfloat16*>(k),
-                                                   static_cast<const __nv_bfloat16*>(v), stride_b, stride_h, stride_s,
-                                                   g, ws);
-  if (int st = launch_status("vf4_attn_nvfp4 (prep)")) return st;
-  if (g.Dp == 64) return launch_fwd<64>(g, ws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
-  return launch_fwd<128>(g, ws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
+  return vf4_attn_nvfp4_ex(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                           out_stride_s, 0, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"
@@ -646,7 +1392,7 @@ extern "C" int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* 
                                       int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream) {
   if (int st = check_device()) return st;
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4_noalloc: bad sizes");
-  const int64_t need = (D % 16 == 0 && D <= 128) ? make_geom(B, H, S, D).total : 0;
+  const int64_t need = vf4_attn_workspace_size(B, H, S, D);
   if (need > kNoAllocScratchBytes)
     return fail(VF4_ERR_UNSUPPORTED,
                 "vf4_attn_nvfp4_noalloc: needs %lld bytes of scratch, the fixed device array holds %lld; "
