@@ -679,9 +679,14 @@ __global__ void __launch_bounds__(192, 1)
 // with the fixed P global both are quantizations of the same probabilities).
 // Named barriers: 1 = all 16 compute warps, 2 + q = the four warps of TMEM lane quadrant q.
 // ---------------------------------------------------------------------------------------
-constexpr int kFusedWarps = 18, kFusedCompute = 16;
-constexpr uint32_t kFusedTmemS = 0, kFusedTmemO = 384, kFusedTmemQsf = 448, kFusedTmemKsf = 452,
-                   kFusedTmemPsf = 464, kFusedTmemVsf = 488;
+#ifndef VF4_ATTN_SLICES
+#define VF4_ATTN_SLICES 3
+#endif
+constexpr int kSlices = VF4_ATTN_SLICES;                 // compute warps per TMEM lane quadrant
+constexpr int kFusedCompute = 4 * kSlices, kFusedWarps = kFusedCompute + 2, kCT = 32 * kFusedCompute;
+// TMEM columns: S (<= 320 keys), two O buffers (tile t's PV overlaps tile t+1's softmax), scales
+constexpr uint32_t kFusedTmemS = 0, kFusedTmemO = 320, kFusedTmemQsf = 448, kFusedTmemKsf = 452,
+                   kFusedTmemPsf = 464, kFusedTmemVsf = 484;
 
 struct FusedGeom {
   int B, H, S, D;
@@ -723,7 +728,7 @@ static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, flo
   g.zero_end = o;
   o = (uint32_t)align_up(o, 1024);
   g.stg = o; o += 4 * 4096;
-  g.red = o; o += 13312;
+  g.red = o; o += 15104;
   g.bar = o; o += 128;
   g.total = o + 1024;
   return g;
@@ -777,8 +782,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
   uint8_t* gb = smem_raw + (base - raw0);
   const uint32_t bar = base + g.bar;
   const uint32_t raw_full = bar, raw_free = bar + 8, ops_ready = bar + 16, s_full = bar + 24, s_free = bar + 32,
-                 p_full = bar + 40, o_full = bar + 48, o_free = bar + 56, drain = bar + 64;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 72);
+                 p_full = bar + 40, drain = bar + 80;
+  auto o_full = [&](int ob) { return bar + 48 + 8u * ob; };   // per O buffer
+  auto o_free = [&](int ob) { return bar + 64 + 8u * ob; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 88);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbo_kv = (uint32_t)(g.skp / 32) * 128u;   // bytes per 8-row group of P and V~^T
   int* err = &g_attn_err;
@@ -790,8 +797,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     mbar_init(s_full, 1);
     mbar_init(s_free, kFusedCompute);
     mbar_init(p_full, kFusedCompute);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, kFusedCompute);
+    for (int ob = 0; ob < 2; ++ob) {
+      mbar_init(o_full(ob), 1);
+      mbar_init(o_free(ob), kFusedCompute);
+    }
     mbar_init(drain, 1);
     fence_mbar_init();
     tma_prefetch(&tmQ);
@@ -805,7 +814,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
   }
   if (warp >= 2) {
     // scale atoms and P codes start at zero: padding keys, rows and head-dim columns stay zero
-    for (uint32_t o = g.sfq + 16u * (threadIdx.x - 64); o < g.zero_end; o += 16u * 32u * kFusedCompute)
+    for (uint32_t o = g.sfq + 16u * (threadIdx.x - 64); o < g.zero_end; o += 16u * kCT)
       *reinterpret_cast<uint4*>(gb + o) = make_uint4(0, 0, 0, 0);
   }
   fence_async_shared();
@@ -837,7 +846,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     // ------------------------------------------------------------ MMA issue
     bool ok = true;
     int hi = 0, it = 0;
-    const uint32_t t_o = tmem + kFusedTmemO, t_qsf = tmem + kFusedTmemQsf, t_ksf = tmem + kFusedTmemKsf;
+    const uint32_t t_qsf = tmem + kFusedTmemQsf, t_ksf = tmem + kFusedTmemKsf;
     const uint32_t t_psf = tmem + kFusedTmemPsf, t_vsf = tmem + kFusedTmemVsf;
     const int nkb = g.skp / 64;
     for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
@@ -870,20 +879,22 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           tc_commit(s_full);
         }
         __syncwarp();
+        const int ob = it & 1, use = it >> 1;
         if (!mbar_wait(p_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull) ||
-            (it > 0 && !mbar_wait(o_free, (uint32_t)(it - 1) & 1u, err, kDevErrTimeoutEmpty))) {
+            (use > 0 && !mbar_wait(o_free(ob), (uint32_t)(use - 1) & 1u, err, kDevErrTimeoutEmpty))) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
+          const uint32_t t_o = tmem + kFusedTmemO + 64u * ob;
           for (int kb = 0; kb < nkb; ++kb) {
             tmem_cp_32x128b_x4(t_psf + 4 * kb, smem_desc(base + g.sfp + 512 * kb, 0, 128, 0));
             mma_mxf4nvf4(t_o, smem_desc(base + g.fp + 256u * kb, 128, sbo_kv, 0),
                          smem_desc(base + g.fv + 256u * kb, 128, sbo_kv, 0), idesc_mxf4nvf4(64), t_psf + 4 * kb,
                          t_vsf + 4 * kb, kb > 0 ? 1u : 0u);
           }
-          tc_commit(o_full);
+          tc_commit(o_full(ob));
         }
         __syncwarp();
       }
@@ -903,16 +914,16 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     float* red = reinterpret_cast<float*>(gb + g.red);
     float* red_kv = red;               // [2][16][64] column partial sums of k and v
     float* red_m = red + 2048;         // [4][128] row max per key slice
-    float* red_l = red + 2560;         // [4][128] row sum per key slice
-    float* mu = red + 3072;            // [2][64] means of k and v
-    float* wmax = red + 3200;          // [3][16] per-warp amax of q, k~, v~
-    float* scal = red + 3248;          // gs_q, gs_k, gs_v, 1/gs_q, 1/gs_k, 1/gs_v
+    float* red_l = red + 2560;         // [2][4][128] row sum per key slice, per O buffer
+    float* mu = red + 3584;            // [2][64] means of k and v
+    float* wmax = red + 3712;          // [3][16] per-warp amax of q, k~, v~
+    float* scal = red + 3760;          // gs_q, gs_k, gs_v, 1/gs_q, 1/gs_k, 1/gs_v
     const uint8_t* rq = gb + g.raw_q;
     const uint8_t* rk = gb + g.raw_k;
     const uint8_t* rv = gb + g.raw_v;
     const int S = g.S, D = g.D;
     const int nvb = (S + 15) / 16;                      // key blocks holding real keys
-    const int b0 = cs * nvb / 4, b1 = (cs + 1) * nvb / 4;
+    const int b0 = cs * nvb / kSlices, b1 = (cs + 1) * nvb / kSlices;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int r = qd * 32 + lane;                       // tile row == TMEM lane
     bool ok = true;
@@ -923,14 +934,14 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       if (g.stats) {
         // tensor-wide globals: this head's means and the global maxima were computed beforehand
         // (the first barrier: every warp has finished the previous head's epilogue, which reads mu)
-        named_bar_sync(1, 512);
+        named_bar_sync(1, kCT);
         if (ct < 128) mu[ct] = g.stats[(int64_t)head * 128 + ct];
         if (ct < 3) {
           const float gsv = __fdiv_rn(fmaxf(g.amax3[ct], 1e-12f), 2688.f);
           scal[ct] = gsv;
           scal[3 + ct] = __fdiv_rn(1.0f, gsv);
         }
-        named_bar_sync(1, 512);
+        named_bar_sync(1, kCT);
       } else {
       // ---- prep 1: column sums of k and v, amax of q (chunk j = ct % 8, rows ct/8 + 64i)
       {
@@ -939,7 +950,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) ks[e] = vs[e] = 0.f;
         if (ok) {
-          for (int s = ct >> 3; s < S; s += 64) {
+          for (int s = ct >> 3; s < S; s += kCT / 8) {
             float a[8];
             raw_load8(rq, s, j, a);
 #pragma unroll
@@ -964,25 +975,25 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             red_kv[cw * 64 + 8 * lane + e] = ks[e];
-            red_kv[(16 + cw) * 64 + 8 * lane + e] = vs[e];
+            red_kv[(kFusedCompute + cw) * 64 + 8 * lane + e] = vs[e];
           }
         }
         if (lane == 0) wmax[cw] = qm;
       }
-      named_bar_sync(1, 512);
+      named_bar_sync(1, kCT);
       if (ct < 128) {
         const int which = ct >> 6, d = ct & 63;
         float sum = 0.f;
-        for (int w = 0; w < kFusedCompute; ++w) sum += red_kv[(which * 16 + w) * 64 + d];   // fixed order
+        for (int w = 0; w < kFusedCompute; ++w) sum += red_kv[(which * kFusedCompute + w) * 64 + d];   // fixed order
         mu[which * 64 + d] = __fdiv_rn(sum, (float)S);
       }
-      named_bar_sync(1, 512);
+      named_bar_sync(1, kCT);
       // ---- prep 2: amax of k - mean and v - mean
       {
         const int j = ct & 7;
         float km = 0.f, vm = 0.f;
         if (ok) {
-          for (int s = ct >> 3; s < S; s += 64) {
+          for (int s = ct >> 3; s < S; s += kCT / 8) {
             float a[8];
             raw_load8(rk, s, j, a);
 #pragma unroll
@@ -999,7 +1010,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           wmax[32 + cw] = vm;
         }
       }
-      named_bar_sync(1, 512);
+      named_bar_sync(1, kCT);
       if (ct == 0) {
         float am[3] = {0.f, 0.f, 0.f};
         for (int w = 0; w < kFusedCompute; ++w)
@@ -1010,12 +1021,12 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           scal[3 + i] = __fdiv_rn(1.0f, gsv);
         }
       }
-      named_bar_sync(1, 512);
+      named_bar_sync(1, kCT);
       }
       const float gq = scal[0], gk = scal[1], gv = scal[2];
       // ---- prep 3: NVFP4 operands.  Q rows [0, 128 nq) and K~ rows [0, skp): 4 column blocks
       // per row, lane quads = one row (their 4 scale bytes merge into one word)
-      for (int i = ct; i < g.nq * 512; i += 512) {
+      for (int i = ct; i < g.nq * 512; i += kCT) {
         const int s = i >> 2, cb = i & 3;
         uint64_t codes = 0;
         uint32_t sf = 0;
@@ -1033,7 +1044,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         w |= __shfl_xor_sync(0xffffffffu, w, 2);
         if (cb == 0) *reinterpret_cast<uint32_t*>(gb + g.sfq + sf_atom_off(s, 0)) = w;
       }
-      for (int i = ct; i < g.skp * 4; i += 512) {
+      for (int i = ct; i < g.skp * 4; i += kCT) {
         const int s = i >> 2, cb = i & 3;
         uint64_t codes = 0;
         uint32_t sf = 0;
@@ -1057,7 +1068,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       // token block, so its raw reads of a token row are 64 contiguous bytes (no bank conflicts)
       {
         const int ntb = g.skp / 16;
-        for (int i = ct; i < 64 * ntb; i += 512) {
+        for (int i = ct; i < 64 * ntb; i += kCT) {
           const int tb = i >> 6, d = i & 63;
           uint64_t codes = 0;
           uint32_t sf = 0;
@@ -1085,7 +1096,59 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       }
       const float cexp = gq * gk * g.scale * 1.4426950408889634f;
       const float ofac = gv * kInv2688;
-      // ---- query tiles
+      // epilogue of tile (global index itt, local index tl): O rows of this quadrant, the slice's
+      // 8-column chunks [c0, c1) of the head dim; O(itt) is complete (o_full waited by the caller)
+      const int c0 = cs * 8 / kSlices, c1 = (cs + 1) * 8 / kSlices;
+      auto epilogue = [&](int itt, int tl) {
+        const bool act = ok && tl * 128 + qd * 32 < S;
+        const int ob = itt & 1;
+        constexpr int kMaxChunks = (8 + kSlices - 1) / kSlices;
+        uint32_t ov[kMaxChunks][8];
+        if (act) {
+#pragma unroll
+          for (int k = 0; k < kMaxChunks; ++k)
+            if (c0 + k < c1) tmem_ld_32x32b_x8(tmem + lane_base + kFusedTmemO + 64u * ob + 8 * (c0 + k), ov[k]);
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free(ob));
+        if (cs == 0 && lane == 0) bulk_wait_read();   // this quadrant's previous store left the staging
+        named_bar_sync(qbar, 32 * kSlices);                     // also publishes red_l
+        uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
+        if (act) {
+          const float* rl = red_l + ob * (kSlices * 128);
+          float lsum = 0.f;
+#pragma unroll
+          for (int c = 0; c < kSlices; ++c) lsum += rl[c * 128 + r];
+          const float f = ofac / lsum;
+#pragma unroll
+          for (int k = 0; k < kMaxChunks; ++k) {
+            const int c = c0 + k;
+            if (c < c1) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int d = 8 * c + 2 * i;
+                __nv_bfloat162 hv = __floats2bfloat162_rn(__fmaf_rn(__uint_as_float(ov[k][2 * i]), f, mu[64 + d]),
+                                                          __fmaf_rn(__uint_as_float(ov[k][2 * i + 1]), f, mu[64 + d + 1]));
+                w[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+              *reinterpret_cast<uint4*>(stg + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        fence_async_shared();
+        named_bar_sync(qbar, 32 * kSlices);
+        if (act && cs == 0 && lane == 0) {
+          const int row = tl * 128 + qd * 32;
+          tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
+          bulk_commit();
+        }
+      };
+      // ---- query tiles: softmax of tile t overlaps the PV MMA of tile t - 1, whose epilogue
+      // follows (two O buffers); the head's last epilogue runs before the next head's prep
+      const unsigned long long c2 = f32x2_pack(cexp, cexp);
       for (int t = 0; t < g.nq; ++t, ++it) {
         const bool active = ok && t * 128 + qd * 32 < S;
         if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
@@ -1108,11 +1171,14 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           }
         }
         red_m[cs * 128 + r] = m;
-        named_bar_sync(qbar, 128);
-        m = fmaxf(fmaxf(red_m[r], red_m[128 + r]), fmaxf(red_m[256 + r], red_m[384 + r]));
+        named_bar_sync(qbar, 32 * kSlices);
+#pragma unroll
+        for (int c = 0; c < kSlices; ++c) m = fmaxf(m, red_m[c * 128 + r]);
+        // the P buffer is free once the previous tile's PV has completed
+        if (t > 0 && ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
         // pass 2: P = 2^((s - m) * c) in [0, 1], row sums, NVFP4 P into shared memory
-        const float mc = m * cexp;
-        float lsum = 0.f;
+        const unsigned long long nmc2 = f32x2_pack(-m * cexp, -m * cexp);
+        unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
         if (active && ok) {
           for (int bk = b0; bk < b1; ++bk) {
             uint32_t v[16];
@@ -1120,7 +1186,13 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
             tmem_wait_ld();
             float p[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) p[e] = ex2_approx(__fmaf_rn(__uint_as_float(v[e]), cexp, -mc));
+            for (int i = 0; i < 8; ++i) {
+              float x0, x1;
+              f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2, nmc2),
+                           &x0, &x1);
+              p[2 * i] = ex2_approx(x0);
+              p[2 * i + 1] = ex2_approx(x1);
+            }
             if (bk == nvb - 1) {
 #pragma unroll
               for (int e = 0; e < 16; ++e)
@@ -1128,9 +1200,9 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
             }
             float am = 0.f;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              lsum += p[e];
-              am = fmaxf(am, p[e]);
+            for (int i = 0; i < 8; ++i) {
+              lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * i], p[2 * i + 1]));
+              am = fmaxf(am, fmaxf(p[2 * i], p[2 * i + 1]));
             }
             float dec;
             const uint32_t sf = six_scale(am, 2688.f, kInv2688, &dec);
@@ -1141,45 +1213,18 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);
-        red_l[cs * 128 + r] = lsum;
+        float l0, l1;
+        f32x2_unpack(lsum2, &l0, &l1);
+        red_l[(it & 1) * (kSlices * 128) + cs * 128 + r] = l0 + l1;
         fence_async_shared();   // P writes -> visible to the tensor core
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
-        // epilogue: O rows of this quadrant, head-dim columns [16 cs, 16 cs + 16)
-        if (ok) ok = mbar_wait(o_full, (uint32_t)it & 1u, err, kDevErrTimeoutTmem);
-        tc_fence_after();
-        uint32_t ov[16];
-        if (active && ok) {
-          tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemO + 16 * cs, ov);
-          tmem_wait_ld();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
-        if (cs == 0 && lane == 0) bulk_wait_read();   // this quadrant's previous store left the staging
-        named_bar_sync(qbar, 128);                     // also publishes red_l
-        uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
-        if (active && ok) {
-          const float f = ofac / (red_l[r] + red_l[128 + r] + red_l[256 + r] + red_l[384 + r]);
-          uint32_t w[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int d = 16 * cs + 2 * i;
-            __nv_bfloat162 hv = __floats2bfloat162_rn(__fmaf_rn(__uint_as_float(ov[2 * i]), f, mu[64 + d]),
-                                                      __fmaf_rn(__uint_as_float(ov[2 * i + 1]), f, mu[64 + d + 1]));
-            w[i] = *reinterpret_cast<uint32_t*>(&hv);
-          }
-          *reinterpret_cast<uint4*>(stg + (((2 * cs) ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(stg + (((2 * cs + 1) ^ (lane & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
-        }
-        fence_async_shared();
-        named_bar_sync(qbar, 128);
-        if (active && ok && cs == 0 && lane == 0) {
-          const int row = t * 128 + qd * 32;
-          tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
-          bulk_commit();
-        }
+        if (t > 0) epilogue(it - 1, t - 1);
       }
+      // the head's last tile
+      if (ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
+      tc_fence_after();
+      epilogue(it - 1, g.nq - 1);
     }
     if (cs == 0 && lane == 0) bulk_wait_all();
   }
