@@ -180,13 +180,15 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
   } else {
     // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
     // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).
-    // Packed codes (NC/2 bytes per row) are staged in shared memory and stored by TMA;
-    // the 4-byte scale words go straight to the 128x4-tiled layout.
+    // Packed codes (NC/2 bytes per row) are staged in shared memory with the 64-byte (NC = 128)
+    // or 32-byte (NC = 64) swizzle, so a warp's 16-byte stores spread over all banks, and stored
+    // by TMA; the 4-byte scale words go straight to the 128x4-tiled layout.
     if (lane == 0) bulk_wait_read();
     __syncwarp();
 #pragma unroll
     for (int g4 = 0; g4 < NC / 64; ++g4) {
       uint32_t sfw = 0;
+      uint64_t pk[4];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const int blk = g4 * 4 + b;
@@ -222,7 +224,15 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
           packed = encode16_fast(h, dec);
           if (row < p.M) sfw |= sf << (8 * b);
         }
-        *reinterpret_cast<uint64_t*>(ebuf_g + lane * (NC / 2) + blk * 8) = packed;
+        pk[b] = packed;
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c = g4 * 2 + hh;   // 16-byte chunk of the row
+        const int cs = NC == 128 ? (c ^ ((lane >> 1) & 3)) : (c ^ ((lane >> 2) & 1));
+        *reinterpret_cast<uint4*>(ebuf_g + lane * (NC / 2) + (cs << 4)) =
+            make_uint4((uint32_t)pk[2 * hh], (uint32_t)(pk[2 * hh] >> 32), (uint32_t)pk[2 * hh + 1],
+                       (uint32_t)(pk[2 * hh + 1] >> 32));
       }
       const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
       if (col0 + g4 * 64 < p.N && row < (((int64_t)p.M + 127) & ~int64_t(127))) {
@@ -659,7 +669,7 @@ static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_
 }
 
 // Output map for the TMA-store epilogue: bf16 (M, N) with 64x32 boxes and the 128-byte swizzle,
-// or packed FP4 codes (M, N/2) bytes with (BN/4)x32 boxes, no swizzle.
+// or packed FP4 codes (M, N/2) bytes with (BN/4)x32 boxes and the BN/4-byte swizzle.
 static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, bool fp4, int bn) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -670,7 +680,9 @@ static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, b
   cuuint32_t es[2] = {1u, 1u};
   CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   fp4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   fp4 ? (bn == 256 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
+                       : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
   return VF4_OK;
