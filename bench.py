@@ -137,7 +137,7 @@ def run_reference(args, rank: int, world: int):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "images/s", "n_gpus": world,
         "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": round(1000 * statistics.median(times), 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": f"{MODEL} W4A4 forward (attention {args.attn})",
                                         "global_batch": args.batch, "seq_len": 257, "parallelism": "cpu"},
         "cpu_baseline": {"value": round(rate, 4), "unit": "images/s", "cores": cores, "kind": "port",
@@ -259,7 +259,7 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
     line = {
         "metric": METRIC, "value": round(img_per_step * steps / (ms * 1e-3), 2), "unit": "images/s",
         "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms / steps, 3),
-        "higher_is_better": True, "scaling": "weak" if world > 1 else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "nvfp4 W4A4 (fp32 accumulate, bf16 activations)", "data": "synthetic",
         "config": {"workload": f"{MODEL} W4A4 forward, attention {args.attn}", "model": "ViT-L/14",
                    "global_batch": img_per_step, "per_gpu_batch": per_rank, "seq_len": 257,

@@ -176,3 +176,26 @@ def test_gemm_residual_epilogue(M, K, N, gamma, tile, monkeypatch):
     inplace = res.clone()
     ops.gemm_residual(ap, asf, ag, bp, bsf, bg, bias, inplace, gamma=gam, out=inplace)
     assert torch.equal(inplace, ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(1152, 1024, 4096), (4736, 512, 832), (1300, 768, 2304)])
+def test_gemm_resident_b_scales_kernel(M, K, N, monkeypatch):
+    """The K <= 1024 kernel that keeps B's scale factors in TMEM (one N tile per CTA, M tiles
+    strided) against the emulation, and bit-equal to the streaming kernel on bf16 + bias and
+    GELU-NVFP4 outputs (same MMAs, same epilogue)."""
+    ops = _ops()
+    A, B = _operands(M, N, K, seed=M + N)
+    out = _gemm_cuda(A, B)
+    ref = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    assert np.abs(out - ref).max() <= 1e-3 * np.abs(ref).max() and cos(out, ref) >= 0.9999
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(1)) * 0.1).cuda().bfloat16()
+    gh = torch.tensor(float(np.abs(ref).max()) / 2688.0, device="cuda")
+    ws = [ops.gemm(ap, asf, ag, bp, bsf, bg, bias=bias, out_dtype=torch.bfloat16),
+          *ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, bias, gh)]
+    monkeypatch.setenv("VF4_GEMM_TILE", "stream")
+    st = [ops.gemm(ap, asf, ag, bp, bsf, bg, bias=bias, out_dtype=torch.bfloat16),
+          *ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, bias, gh)]
+    for a, b in zip(ws, st):
+        assert torch.equal(a, b)

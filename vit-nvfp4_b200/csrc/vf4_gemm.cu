@@ -433,6 +433,205 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---------------------------------------------------------------------------------------
+// Variant for K <= 1024 (n_kb <= 16) with the B operand's scale factors resident in TMEM.
+// Each CTA keeps one 256-wide N tile (nb = blockIdx.x % tiles_n) and walks M tiles
+// mb = blockIdx.x / tiles_n + k * (gridDim.x / tiles_n), so B's scales for the whole K are
+// copied into TMEM once per CTA and every K64 step issues one scale copy (A's) instead of three.
+// At any moment the CTAs of one "mb group" share their A row block through L2.
+// TMEM: accumulator [0, 256), resident SFB [256, 256 + 8 n_kb), SFA slots [384, 416).
+// ---------------------------------------------------------------------------------------
+struct GemmWsCfg {
+  static constexpr int BN = 256, BM = 128, KB_PER_STAGE = 4, STAGES = 3;
+  static constexpr int A_BYTES = BM * 128, B_BYTES = BN * 128, SFA_BYTES = KB_PER_STAGE * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES;
+  static constexpr int MAX_KB = 16;
+  static constexpr int SFB_RES_BYTES = 2 * MAX_KB * 512;
+  static constexpr int SFB_TCOL = 256, SFA_TCOL = 384, SFA_SLOT = KB_PER_STAGE * 4;
+  static constexpr int TMEM_COLS = 512, THREADS = 320;
+  static constexpr int EPI_WARP_BYTES = 4096, EPI_BYTES = 8 * EPI_WARP_BYTES;
+  static constexpr int NBAR = 2 * STAGES + 2 + 1 + 1;   // full/empty, tfull/tempty, drain, sfb
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SFB_RES_BYTES + EPI_BYTES + 8 * NBAR + 16;
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  static_assert(SFA_TCOL + 2 * SFA_SLOT <= TMEM_COLS, "TMEM overflow");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+template <int EPI, bool kF32>
+__global__ void __launch_bounds__(320, 1)
+    gemm_nvfp4_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
+  using C = GemmWsCfg;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sfb_res = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t epi0 = sfb_res + C::SFB_RES_BYTES;
+  const uint32_t bar0 = epi0 + C::EPI_BYTES;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+  const uint32_t tfull_bar = bar0 + 8u * (2 * C::STAGES), tempty_bar = tfull_bar + 8, drain_bar = tfull_bar + 16,
+                 sfb_bar = tfull_bar + 24;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bar0 - base) + 8 * C::NBAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = &g_gemm_err;
+  const int nb = blockIdx.x % p.tiles_n;
+  const int mb0 = blockIdx.x / p.tiles_n, mstep = gridDim.x / p.tiles_n;
+  const int n_st = (p.n_kb + C::KB_PER_STAGE - 1) / C::KB_PER_STAGE;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, 8);
+    mbar_init(drain_bar, 1);
+    mbar_init(sfb_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+    if (!kF32) tma_prefetch(&tmOut);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      // this CTA's B scales for all of K, once: row blocks 2 nb and 2 nb + 1 (N tail: stand-in)
+      const uint32_t sfb_bytes = (uint32_t)p.n_kb * 512u;
+      mbar_arrive_expect_tx(sfb_bar, 2 * sfb_bytes);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        int rb = nb * 2 + j;
+        if (rb >= p.n_rb_b) rb = nb * 2;
+        bulk_load(sfb_res + j * sfb_bytes, p.b_sf + (int64_t)rb * p.n_kb * 512, sfb_bytes, sfb_bar);
+      }
+      int it = 0;
+      bool ok = true;
+      for (int mb = mb0; mb < p.tiles_m && ok; mb += mstep) {
+        for (int st = 0; st < n_st; ++st, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int kb0 = st * C::KB_PER_STAGE;
+          const int nkb = min(C::KB_PER_STAGE, p.n_kb - kb0);
+          const uint32_t sf_bytes = (uint32_t)nkb * 512u;
+          mbar_arrive_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES + sf_bytes);
+          const uint32_t sa = base + s * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t ssfa = sb + C::B_BYTES;
+          tma_load_2d(sa, &tmA, st * 128, mb * 128, full_bar(s));
+          tma_load_2d(sb, &tmB, st * 128, nb * BN, full_bar(s));
+          bulk_load(ssfa, p.a_sf + ((int64_t)mb * p.n_kb + kb0) * 512, sf_bytes, full_bar(s));
+        }
+      }
+      for (int k = it - C::STAGES < 0 ? 0 : it - C::STAGES; k < it; ++k)
+        mbar_wait(full_bar(k % C::STAGES), (uint32_t)(k / C::STAGES) & 1u, err, kDevErrTimeoutFull);
+      mbar_wait(sfb_bar, 0, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_mxf4nvf4(BN);
+    const uint32_t sfb_t = tmem + C::SFB_TCOL;
+    bool ok = mbar_wait(sfb_bar, 0, err, kDevErrTimeoutFull);
+    tc_fence_after();
+    if (ok && lane == 0) {
+      for (int kb = 0; kb < p.n_kb; ++kb)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          tmem_cp_32x128b_x4(sfb_t + kb * 8 + j * 4,
+                             smem_desc(sfb_res + (uint32_t)(j * p.n_kb + kb) * 512u, 0, 128, 0));
+    }
+    __syncwarp();
+    int it = 0, lt = 0;
+    for (int mb = mb0; mb < p.tiles_m && ok; mb += mstep, ++lt) {
+      if (!mbar_wait(tempty_bar, ((uint32_t)lt & 1u) ^ 1u, err, kDevErrTimeoutTmem)) break;
+      tc_fence_after();
+      for (int st = 0; st < n_st; ++st, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+        if (!mbar_wait(full_bar(s), ph, err, kDevErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const int kb0 = st * C::KB_PER_STAGE;
+          const int nkb = min(C::KB_PER_STAGE, p.n_kb - kb0);
+          const uint32_t sfa_t = tmem + C::SFA_TCOL + (uint32_t)(it & 1) * C::SFA_SLOT;
+          const uint32_t sa = base + s * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t ssfa = sb + C::B_BYTES;
+          for (int kb = 0; kb < nkb; ++kb) {
+            tmem_cp_32x128b_x4(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
+            const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
+            mma_mxf4nvf4(tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + (kb0 + kb) * 8, (st > 0 || kb > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(s));
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(tfull_bar);
+      __syncwarp();
+    }
+    if (lane == 0) {
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    constexpr int NC = BN / 2;
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
+    float egs = 1.f, esenc = 1.f;
+    if constexpr (epi_gelu(EPI)) {
+      egs = __ldg(p.epi_gs);
+      esenc = __fdiv_rn(1.0f, egs);
+    }
+    int lt = 0;
+    for (int mb = mb0; mb < p.tiles_m; mb += mstep, ++lt) {
+      if (!mbar_wait(tfull_bar, (uint32_t)lt & 1u, err, kDevErrTimeoutTmem)) break;
+      tc_fence_after();
+      uint32_t v[NC];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * NC);
+#pragma unroll
+      for (int c = 0; c < NC / 32; ++c) tmem_ld_32x32b_x32(taddr + c * 32, v + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar);
+      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha, egs, esenc,
+                                   epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
+                                   gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
 
 // ---------------------------------------------------------------------------------------
 // CTA-pair variant: a cluster of 2 CTAs computes a 256 x 256 tile with cta_group::2 MMAs.
@@ -744,6 +943,37 @@ static int dispatch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p,
   return f32 ? launch_gemm_pair<VF4_EPI_NONE, true>(a, b, p, s) : launch_gemm_pair<VF4_EPI_NONE, false>(a, b, p, s);
 }
 
+template <int EPI, bool kF32>
+static int launch_gemm_ws(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
+  using C = GemmWsCfg;
+  CUtensorMap ta, tb, to;
+  memset(&to, 0, sizeof(to));
+  if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
+  if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, C::BN)) return st;
+  if (epi_gelu(EPI)) {
+    if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, C::BN)) return st;
+  } else if (!kF32) {
+    if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
+  }
+  auto kern = gemm_nvfp4_ws_kernel<EPI, kF32>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  p.tiles_m = (p.M + 127) / 128;
+  p.tiles_n = (p.N + C::BN - 1) / C::BN;
+  const int groups = num_sms() / p.tiles_n;   // CTAs per N tile
+  kern<<<groups * p.tiles_n, C::THREADS, C::SMEM, s>>>(ta, tb, to, p);
+  return launch_status("vf4_gemm_nvfp4 (resident B scales)");
+}
+
+static int dispatch_gemm_ws(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32, cudaStream_t s) {
+  if (epi == VF4_EPI_GELU_NVFP4) return launch_gemm_ws<VF4_EPI_GELU_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_GELU_ERF_NVFP4) return launch_gemm_ws<VF4_EPI_GELU_ERF_NVFP4, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS_RESIDUAL) return launch_gemm_ws<VF4_EPI_BIAS_RESIDUAL, false>(a, b, p, s);
+  if (epi == VF4_EPI_BIAS)
+    return f32 ? launch_gemm_ws<VF4_EPI_BIAS, true>(a, b, p, s) : launch_gemm_ws<VF4_EPI_BIAS, false>(a, b, p, s);
+  return f32 ? launch_gemm_ws<VF4_EPI_NONE, true>(a, b, p, s) : launch_gemm_ws<VF4_EPI_NONE, false>(a, b, p, s);
+}
+
 template <int BN>
 static int dispatch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, int epi, int f32,
                          cudaStream_t s) {
@@ -820,6 +1050,11 @@ static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float*
   const char* mode = getenv("VF4_GEMM_TILE");   // "pair" selects the CTA-pair 256x256 kernel
   if (N >= 256 && M > 128 && mode && mode[0] == 'p')
     return dispatch_gemm_pair(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
+  // resident-B-scales kernel: K <= 1024, at least one CTA per N tile and one M tile per CTA
+  // (VF4_GEMM_TILE=stream selects the plain streaming kernel)
+  const bool ws_ok = N >= 256 && p.n_kb <= GemmWsCfg::MAX_KB && (N + 255) / 256 <= num_sms() &&
+                     (M + 127) / 128 >= num_sms() / ((N + 255) / 256) && !(mode && mode[0] == 's');
+  if (ws_ok) return dispatch_gemm_ws(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   return dispatch_gemm<128>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
 }
