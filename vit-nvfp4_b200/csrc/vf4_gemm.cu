@@ -441,6 +441,10 @@ __global__ void __launch_bounds__(320, 1)
 // At any moment the CTAs of one "mb group" share their A row block through L2.
 // TMEM: accumulator [0, 256), resident SFB [256, 256 + 8 n_kb), SFA slots [384, 416).
 // ---------------------------------------------------------------------------------------
+// EW epilogue warps: 8 (each 128 accumulator columns) for the bf16 / fp32 epilogues, 16 (each
+// 64 columns) for the GELU-NVFP4 epilogue, whose per-element work needs the extra warps to keep
+// up with the MMAs (its staging is 32 rows x 32 bytes of codes per warp).
+template <int EW, bool kGelu>
 struct GemmWsCfg {
   static constexpr int BN = 256, BM = 128, KB_PER_STAGE = 4, STAGES = 3;
   static constexpr int A_BYTES = BM * 128, B_BYTES = BN * 128, SFA_BYTES = KB_PER_STAGE * 512;
@@ -448,20 +452,23 @@ struct GemmWsCfg {
   static constexpr int MAX_KB = 16;
   static constexpr int SFB_RES_BYTES = 2 * MAX_KB * 512;
   static constexpr int SFB_TCOL = 256, SFA_TCOL = 384, SFA_SLOT = KB_PER_STAGE * 4;
-  static constexpr int TMEM_COLS = 512, THREADS = 320;
-  static constexpr int EPI_WARP_BYTES = 4096, EPI_BYTES = 8 * EPI_WARP_BYTES;
+  static constexpr int TMEM_COLS = 512, THREADS = 64 + 32 * EW;
+  static constexpr int NC = BN / (EW / 4);                  // accumulator columns per epilogue thread
+  static constexpr int EPI_WARP_BYTES = kGelu ? 32 * NC / 2 : 4096;
+  static constexpr int EPI_BYTES = EW * EPI_WARP_BYTES;
   static constexpr int NBAR = 2 * STAGES + 2 + 1 + 1;   // full/empty, tfull/tempty, drain, sfb
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SFB_RES_BYTES + EPI_BYTES + 8 * NBAR + 16;
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  static_assert(EPI_BYTES % 1024 == 0, "staging alignment");
   static_assert(SFA_TCOL + 2 * SFA_SLOT <= TMEM_COLS, "TMEM overflow");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <int EPI, bool kF32>
-__global__ void __launch_bounds__(320, 1)
+template <int EPI, bool kF32, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_nvfp4_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
-  using C = GemmWsCfg;
+  using C = GemmWsCfg<EW, epi_gelu(EPI)>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -488,7 +495,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, 8);
+    mbar_init(tempty_bar, EW);
     mbar_init(drain_bar, 1);
     mbar_init(sfb_bar, 1);
     fence_mbar_init();
@@ -597,9 +604,9 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
-    constexpr int NC = BN / 2;
+    constexpr int NC = C::NC;
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;   // which NC-column slice of the tile
     const float alpha = __ldg(p.a_gs) * __ldg(p.b_gs);
     float egs = 1.f, esenc = 1.f;
     if constexpr (epi_gelu(EPI)) {
@@ -611,14 +618,14 @@ __global__ void __launch_bounds__(320, 1)
       if (!mbar_wait(tfull_bar, (uint32_t)lt & 1u, err, kDevErrTimeoutTmem)) break;
       tc_fence_after();
       uint32_t v[NC];
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * NC);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(part * NC);
 #pragma unroll
       for (int c = 0; c < NC / 32; ++c) tmem_ld_32x32b_x32(taddr + c * 32, v + c * 32);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar);
-      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha, egs, esenc,
+      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, alpha, egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
                                    gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES);
     }
@@ -945,17 +952,18 @@ static int dispatch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p,
 
 template <int EPI, bool kF32>
 static int launch_gemm_ws(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
-  using C = GemmWsCfg;
+  constexpr int EW = epi_gelu(EPI) ? 16 : 8;
+  using C = GemmWsCfg<EW, epi_gelu(EPI)>;
   CUtensorMap ta, tb, to;
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
   if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, C::BN)) return st;
-  if (epi_gelu(EPI)) {
-    if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, C::BN)) return st;
+  if (epi_gelu(EPI)) {   // each warp stores 32 rows x NC/2 bytes of codes: the map of a 2*NC-wide tile
+    if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, 2 * C::NC)) return st;
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
   }
-  auto kern = gemm_nvfp4_ws_kernel<EPI, kF32>;
+  auto kern = gemm_nvfp4_ws_kernel<EPI, kF32, EW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   p.tiles_m = (p.M + 127) / 128;
@@ -1052,7 +1060,7 @@ static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float*
     return dispatch_gemm_pair(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   // resident-B-scales kernel: K <= 1024, at least one CTA per N tile and one M tile per CTA
   // (VF4_GEMM_TILE=stream selects the plain streaming kernel)
-  const bool ws_ok = N >= 256 && p.n_kb <= GemmWsCfg::MAX_KB && (N + 255) / 256 <= num_sms() &&
+  const bool ws_ok = N >= 256 && p.n_kb <= 16 && (N + 255) / 256 <= num_sms() &&
                      (M + 127) / 128 >= num_sms() / ((N + 255) / 256) && !(mode && mode[0] == 's');
   if (ws_ok) return dispatch_gemm_ws(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
