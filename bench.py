@@ -32,6 +32,10 @@ GLOBAL_BATCH = 1024
 MODEL = "vit_l14_dinov2_style"
 METRIC = "ViT-L/14 W4A4 images/s"
 FP4_NOMINAL_TFLOPS = 9000.0
+# DRAM bytes (read + write) per output row measured by ncu for the GEMM kinds that can dominate
+# (profiles/gemm_nvfp4_vitl14_b256.md: the fc1 launch at M = 65792 moved 40.5 + 99.2 MB; A and the
+# output grow with M while the 2.4 MB of weights do not, so bytes scale with the rows)
+NCU_TRAFFIC_PER_ROW = {"gemm_gelu_nvfp4_": 139.716352e6 / 65792}
 
 
 def _args():
@@ -254,6 +258,15 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
                     "peak_source": "4 x measured bf16 burst (MEASURED_PEAKS.json); FP4 itself not measured"
                     if bf16_tf else "nominal dense FP4 (no measured peak)",
                     "frac_of_nominal_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4), "traffic": None}
+        for prefix, per_row in NCU_TRAFFIC_PER_ROW.items():
+            if dom[0].startswith(prefix):
+                m_rows, n_cols, k_dim = (int(x) for x in dom[0][len(prefix):].split("x"))
+                roofline["traffic"] = round(per_row * m_rows)   # bytes per launch
+                roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
+                                              "M = 65792, scaled by rows (profiles/gemm_nvfp4_vitl14_b256.md)")
+                # A and B codes + scales in, NVFP4 codes + scales out
+                roofline["algorithmic_bytes"] = (m_rows + n_cols) * (k_dim // 2 + k_dim // 16) + \
+                    m_rows * (n_cols // 2 + n_cols // 16)
     steps = args.steps
     img_per_step = args.batch
     line = {

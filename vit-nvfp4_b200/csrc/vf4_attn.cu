@@ -1408,12 +1408,13 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
 // Some callers cannot call cudaMalloc at all: a host runtime that has handed the whole device
 // to its own memory pool, or a plugin loaded into an inference server that forbids library
 // allocations (and the implicit device synchronisation cudaMalloc/cudaFree can cause) while
-// requests run.  vf4_attn_nvfp4_noalloc serves them: it runs the same two kernels as
+// requests run.  vf4_attn_nvfp4_noalloc serves them: it runs the same kernels as
 // vf4_attn_nvfp4, but its workspace is this file-scope device array instead of caller memory.
 //
 // Limits and contract:
 //   * at most kNoAllocScratchBytes (16 MiB) of workspace, i.e. vf4_attn_workspace_size(B,H,S,D)
-//     must not exceed it (about 25 ViT-L/14 images per call); larger calls return
+//     must not exceed it (the fused route needs 512 bytes per head, about 2000 ViT-L/14 images;
+//     the long-sequence route about 4 ViT-H/14 @448 images); larger calls return
 //     VF4_ERR_UNSUPPORTED and launch nothing;
 //   * the array lives on every GPU that loads the library until the process exits;
 //   * the host name g_attn_scratch is only a host-side stand-in for the symbol, never a device
@@ -1421,7 +1422,8 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
 //     address with cudaGetSymbolAddress and caches it, so make that first call before any
 //     stream capture;
 //   * every call shares the one array and it keeps the last call's contents; nothing in it
-//     has to start at zero (the prep kernel rewrites every byte the forward kernel reads);
+//     has to start at zero (each call clears the three maxima itself, and the statistics and
+//     prep kernels rewrite every other byte the later kernels read);
 //   * calls whose kernels overlap on the GPU (different streams, no ordering) race on it.
 // ---------------------------------------------------------------------------------------
 namespace vf4 {
