@@ -1025,50 +1025,45 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       }
       const float gq = scal[0], gk = scal[1], gv = scal[2];
       // ---- prep 3: NVFP4 operands.  Q rows [0, 128 nq) and K~ rows [0, skp): 4 column blocks
-      // per row, lane quads = one row (their 4 scale bytes merge into one word)
-      for (int i = ct; i < g.nq * 512; i += kCT) {
+      // per row, lane quads = one row (their 4 scale bytes merge into one word).  Two items per
+      // loop trip so the two quantization chains interleave (the loop bounds are multiples of 32:
+      // whole warps take the same branch, as the lane-quad shuffles need).
+      auto qk_block = [&](int i, const uint8_t* raw, uint32_t fo, uint32_t so, bool centre, float gs, float se,
+                          float dec_max) {
         const int s = i >> 2, cb = i & 3;
         uint64_t codes = 0;
         uint32_t sf = 0;
         if (ok && s < S && cb * 16 < D) {
           float x[16];
-          raw_load8(rq, s, 2 * cb, x);
-          raw_load8(rq, s, 2 * cb + 1, x + 8);
-          const BlockQ z = quantize_block<false>(x, gq, scal[3], 0x1p17f);   // raw bf16 values
-          codes = z.packed;
-          sf = z.sf;
-        }
-        *reinterpret_cast<uint64_t*>(gb + g.fq + cm_off(s, cb, 256)) = codes;
-        uint32_t w = sf << (8 * cb);
-        w |= __shfl_xor_sync(0xffffffffu, w, 1);
-        w |= __shfl_xor_sync(0xffffffffu, w, 2);
-        if (cb == 0) *reinterpret_cast<uint32_t*>(gb + g.sfq + sf_atom_off(s, 0)) = w;
-      }
-      for (int i = ct; i < g.skp * 4; i += kCT) {
-        const int s = i >> 2, cb = i & 3;
-        uint64_t codes = 0;
-        uint32_t sf = 0;
-        if (ok && s < S && cb * 16 < D) {
-          float x[16];
-          raw_load8(rk, s, 2 * cb, x);
-          raw_load8(rk, s, 2 * cb + 1, x + 8);
+          raw_load8(raw, s, 2 * cb, x);
+          raw_load8(raw, s, 2 * cb + 1, x + 8);
+          if (centre) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) x[e] -= mu[16 * cb + e];
-          const BlockQ z = quantize_block<false>(x, gk, scal[4]);
+            for (int e = 0; e < 16; ++e) x[e] -= mu[16 * cb + e];
+          }
+          const BlockQ z = quantize_block<false>(x, gs, se, dec_max);
           codes = z.packed;
           sf = z.sf;
         }
-        *reinterpret_cast<uint64_t*>(gb + g.fk + cm_off(s, cb, 256)) = codes;
+        *reinterpret_cast<uint64_t*>(gb + fo + cm_off(s, cb, 256)) = codes;
         uint32_t w = sf << (8 * cb);
         w |= __shfl_xor_sync(0xffffffffu, w, 1);
         w |= __shfl_xor_sync(0xffffffffu, w, 2);
-        if (cb == 0) *reinterpret_cast<uint32_t*>(gb + g.sfk + sf_atom_off(s, 0)) = w;
+        if (cb == 0) *reinterpret_cast<uint32_t*>(gb + so + sf_atom_off(s, 0)) = w;
+      };
+      for (int i = ct; i < g.nq * 512; i += 2 * kCT) {
+        qk_block(i, rq, g.fq, g.sfq, false, gq, scal[3], 0x1p17f);   // raw bf16 values
+        if (i + kCT < g.nq * 512) qk_block(i + kCT, rq, g.fq, g.sfq, false, gq, scal[3], 0x1p17f);
+      }
+      for (int i = ct; i < g.skp * 4; i += 2 * kCT) {
+        qk_block(i, rk, g.fk, g.sfk, true, gk, scal[4], 2.0f);
+        if (i + kCT < g.skp * 4) qk_block(i + kCT, rk, g.fk, g.sfk, true, gk, scal[4], 2.0f);
       }
       // V~^T rows d in [0, 64), token blocks tb in [0, skp/16); a warp covers 32 consecutive d of one
       // token block, so its raw reads of a token row are 64 contiguous bytes (no bank conflicts)
       {
         const int ntb = g.skp / 16;
-        for (int i = ct; i < 64 * ntb; i += kCT) {
+        auto v_block = [&](int i) {
           const int tb = i >> 6, d = i & 63;
           uint64_t codes = 0;
           uint32_t sf = 0;
@@ -1086,6 +1081,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           }
           *reinterpret_cast<uint64_t*>(gb + g.fv + cm_off(d, tb, sbo_kv)) = codes;
           gb[g.sfv + (uint32_t)(tb >> 2) * 512u + sf_atom_off(d, tb & 3)] = (uint8_t)sf;
+        };
+        for (int i = ct; i < 64 * ntb; i += 2 * kCT) {
+          v_block(i);
+          if (i + kCT < 64 * ntb) v_block(i + kCT);
         }
       }
       fence_async_shared();   // operand writes -> visible to the tensor core
@@ -1153,21 +1152,28 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         const bool active = ok && t * 128 + qd * 32 < S;
         if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
         tc_fence_after();
+        // key blocks of this warp: [b0, bu) need no masking, block bu (if < b1) holds the last real
+        // key and padding; unmasked blocks go two per TMEM load so their chains interleave
+        const int bu = (b1 == nvb && (S & 15)) ? b1 - 1 : b1;
+        const uint32_t srow = tmem + lane_base + kFusedTmemS;
         // pass 1: row max over this warp's key blocks
         float m = -INFINITY;
         if (active && ok) {
-          for (int bk = b0; bk < b1; ++bk) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemS + 16 * bk, v);
+          int bk = b0;
+          for (; bk + 1 < bu; bk += 2) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(srow + 16 * bk, v);
             tmem_wait_ld();
-            if (bk == nvb - 1) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e)
-                if (16 * bk + e < S) m = fmaxf(m, __uint_as_float(v[e]));
-            } else {
+            for (int e = 0; e < 32; ++e) m = fmaxf(m, __uint_as_float(v[e]));
+          }
+          for (; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(srow + 16 * bk, v);
+            tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) m = fmaxf(m, __uint_as_float(v[e]));
-            }
+            for (int e = 0; e < 16; ++e)
+              if (bk < bu || 16 * bk + e < S) m = fmaxf(m, __uint_as_float(v[e]));
           }
         }
         red_m[cs * 128 + r] = m;
@@ -1179,35 +1185,47 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         // pass 2: P = 2^((s - m) * c) in [0, 1], row sums, NVFP4 P into shared memory
         const unsigned long long nmc2 = f32x2_pack(-m * cexp, -m * cexp);
         unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
+        // one 16-key block: exp, masking of keys >= S (limit = S - 16 bk), sum, scale, codes
+        auto p_block = [&](const uint32_t* v, int bk, int limit) {
+          float p[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float x0, x1;
+            f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2, nmc2),
+                         &x0, &x1);
+            p[2 * i] = ex2_approx(x0);
+            p[2 * i + 1] = ex2_approx(x1);
+          }
+          if (limit < 16) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (e >= limit) p[e] = 0.f;
+          }
+          float am = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * i], p[2 * i + 1]));
+            am = fmaxf(am, fmaxf(p[2 * i], p[2 * i + 1]));
+          }
+          float dec;
+          const uint32_t sf = six_scale(am, 2688.f, kInv2688, &dec);
+          *reinterpret_cast<uint64_t*>(gb + g.fp + cm_off(r, bk, sbo_kv)) = encode16_fast(p, dec);
+          gb[g.sfp + (uint32_t)(bk >> 2) * 512u + sf_atom_off(r, bk & 3)] = (uint8_t)sf;
+        };
         if (active && ok) {
-          for (int bk = b0; bk < b1; ++bk) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(tmem + lane_base + kFusedTmemS + 16 * bk, v);
+          int bk = b0;
+          for (; bk + 1 < bu; bk += 2) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(srow + 16 * bk, v);
             tmem_wait_ld();
-            float p[16];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float x0, x1;
-              f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2, nmc2),
-                           &x0, &x1);
-              p[2 * i] = ex2_approx(x0);
-              p[2 * i + 1] = ex2_approx(x1);
-            }
-            if (bk == nvb - 1) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e)
-                if (16 * bk + e >= S) p[e] = 0.f;
-            }
-            float am = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * i], p[2 * i + 1]));
-              am = fmaxf(am, fmaxf(p[2 * i], p[2 * i + 1]));
-            }
-            float dec;
-            const uint32_t sf = six_scale(am, 2688.f, kInv2688, &dec);
-            *reinterpret_cast<uint64_t*>(gb + g.fp + cm_off(r, bk, sbo_kv)) = encode16_fast(p, dec);
-            gb[g.sfp + (uint32_t)(bk >> 2) * 512u + sf_atom_off(r, bk & 3)] = (uint8_t)sf;
+            p_block(v, bk, 16);
+            p_block(v + 16, bk + 1, 16);
+          }
+          for (; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(srow + 16 * bk, v);
+            tmem_wait_ld();
+            p_block(v, bk, bk < bu ? 16 : S - 16 * bk);
           }
         }
         tc_fence_before();
