@@ -90,7 +90,7 @@ VF4_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
 // [col0, col0 + NC) of row row0 + lane; ebuf is the warp's 4 KB staging buffer.
-template <int NC, int EPI, bool kF32>
+template <int NC, int EPI, bool kF32, int CW = 64>
 VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtensorMap* tmOut, int row0,
                            int col0, int lane, float alpha, float egs, float esenc, uint32_t ebuf,
                            uint8_t* ebuf_g) {
@@ -120,20 +120,21 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
       }
     }
   } else if constexpr (!epi_gelu(EPI)) {
-    // bf16 out: each 64-column chunk of the warp's 32x(NC) slab is staged in shared memory with
-    // the 128-byte swizzle (16-byte piece j of row r at (j ^ r%8)) and written by one TMA store
+    // bf16 out: each CW-column chunk of the warp's 32x(NC) slab is staged in shared memory with
+    // the 2*CW-byte swizzle (16-byte piece j of row r at j ^ (r%8) for 128-byte rows, j ^ ((r/2)%4)
+    // for 64-byte rows) and written by one TMA store
 #pragma unroll
-    for (int c = 0; c < NC / 64; ++c) {
-      const int colc = col0 + c * 64;
+    for (int c = 0; c < NC / CW; ++c) {
+      const int colc = col0 + c * CW;
       if (colc < p.N) {
         if (lane == 0) bulk_wait_read();      // the previous store has left the buffer
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < CW / 8; ++j) {
           const int col = colc + j * 8;
           float y[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * 64 + j * 8 + i]) * alpha;
+          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * CW + j * 8 + i]) * alpha;
           if (EPI != VF4_EPI_NONE && p.bias && col < p.N) {
             // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
             uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
@@ -167,7 +168,8 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
             __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
             w[i] = *reinterpret_cast<uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(ebuf_g + lane * 128 + ((j ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+          const int js = CW == 64 ? (j ^ (lane & 7)) : (j ^ ((lane >> 1) & 3));
+          *reinterpret_cast<uint4*>(ebuf_g + lane * (2 * CW) + js * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_async_shared();
         __syncwarp();
@@ -444,20 +446,28 @@ __global__ void __launch_bounds__(320, 1)
 // EW epilogue warps: 8 (each 128 accumulator columns) for the bf16 / fp32 epilogues, 16 (each
 // 64 columns) for the GELU-NVFP4 epilogue, whose per-element work needs the extra warps to keep
 // up with the MMAs (its staging is 32 rows x 32 bytes of codes per warp).
+// Four pipeline stages of 4 K64 blocks.  To fit them, the epilogue staging is 2 KB per warp (bf16
+// chunks of 32 columns, 64-byte swizzle) and shares its shared memory with the B-scale staging,
+// which tcgen05.cp reads before the first MMA: the staging is first written after the first
+// tile's MMAs (and so those copies) have completed.
 template <int EW, bool kGelu>
 struct GemmWsCfg {
-  static constexpr int BN = 256, BM = 128, KB_PER_STAGE = 4, STAGES = 3;
-  static constexpr int A_BYTES = BM * 128, B_BYTES = BN * 128, SFA_BYTES = KB_PER_STAGE * 512;
+  static constexpr int BN = 256, BM = 128, KB_PER_STAGE = 4, STAGES = 4;
+  static constexpr int ROWB = 32 * KB_PER_STAGE;                 // bytes of K per row and stage
+  static constexpr uint32_t LAYOUT = ROWB == 64 ? 4u : 2u;       // SWIZZLE_64B / SWIZZLE_128B
+  static constexpr int A_BYTES = BM * ROWB, B_BYTES = BN * ROWB, SFA_BYTES = KB_PER_STAGE * 512;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES;
   static constexpr int MAX_KB = 16;
   static constexpr int SFB_RES_BYTES = 2 * MAX_KB * 512;
   static constexpr int SFB_TCOL = 256, SFA_TCOL = 384, SFA_SLOT = KB_PER_STAGE * 4;
   static constexpr int TMEM_COLS = 512, THREADS = 64 + 32 * EW;
   static constexpr int NC = BN / (EW / 4);                  // accumulator columns per epilogue thread
-  static constexpr int EPI_WARP_BYTES = kGelu ? 32 * NC / 2 : 4096;
+  static constexpr int EPI_CW = 32;                          // bf16 staging chunk (columns)
+  static constexpr int EPI_WARP_BYTES = kGelu ? 32 * NC / 2 : 32 * EPI_CW * 2;
   static constexpr int EPI_BYTES = EW * EPI_WARP_BYTES;
+  static constexpr int SHARED_BYTES = EPI_BYTES > SFB_RES_BYTES ? EPI_BYTES : SFB_RES_BYTES;
   static constexpr int NBAR = 2 * STAGES + 2 + 1 + 1;   // full/empty, tfull/tempty, drain, sfb
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SFB_RES_BYTES + EPI_BYTES + 8 * NBAR + 16;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SHARED_BYTES + 8 * NBAR + 16;
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(EPI_BYTES % 1024 == 0, "staging alignment");
   static_assert(SFA_TCOL + 2 * SFA_SLOT <= TMEM_COLS, "TMEM overflow");
@@ -475,8 +485,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t sfb_res = base + C::STAGES * C::STAGE_BYTES;
-  const uint32_t epi0 = sfb_res + C::SFB_RES_BYTES;
-  const uint32_t bar0 = epi0 + C::EPI_BYTES;
+  const uint32_t epi0 = sfb_res;   // shared with the B-scale staging (see GemmWsCfg)
+  const uint32_t bar0 = epi0 + C::SHARED_BYTES;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   const uint32_t tfull_bar = bar0 + 8u * (2 * C::STAGES), tempty_bar = tfull_bar + 8, drain_bar = tfull_bar + 16,
@@ -541,8 +551,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const uint32_t sa = base + s * C::STAGE_BYTES;
           const uint32_t sb = sa + C::A_BYTES;
           const uint32_t ssfa = sb + C::B_BYTES;
-          tma_load_2d(sa, &tmA, st * 128, mb * 128, full_bar(s));
-          tma_load_2d(sb, &tmB, st * 128, nb * BN, full_bar(s));
+          tma_load_2d(sa, &tmA, st * C::ROWB, mb * 128, full_bar(s));
+          tma_load_2d(sb, &tmB, st * C::ROWB, nb * BN, full_bar(s));
           bulk_load(ssfa, p.a_sf + ((int64_t)mb * p.n_kb + kb0) * 512, sf_bytes, full_bar(s));
         }
       }
@@ -585,8 +595,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const uint32_t ssfa = sb + C::B_BYTES;
           for (int kb = 0; kb < nkb; ++kb) {
             tmem_cp_32x128b_x4(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
-            const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
-            const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
+            const uint64_t ad = smem_desc(sa + kb * 32, 16, 8 * C::ROWB, C::LAYOUT);
+            const uint64_t bd = smem_desc(sb + kb * 32, 16, 8 * C::ROWB, C::LAYOUT);
             mma_mxf4nvf4(tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + (kb0 + kb) * 8, (st > 0 || kb > 0) ? 1u : 0u);
           }
           tc_commit(empty_bar(s));
@@ -625,7 +635,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar);
-      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, alpha, egs, esenc,
+      epilogue_slab<NC, EPI, kF32, C::EPI_CW>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, alpha,
+                                               egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
                                    gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES);
     }
@@ -860,15 +871,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
   if (warp == 1) tmem_dealloc_pair(tmem, C::TMEM_COLS);
 }
 
-static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t kbytes, int box_rows) {
+static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t kbytes, int box_rows,
+                           int box_bytes = 128) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kbytes};
-  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1u, 1u};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return VF4_OK;
@@ -876,18 +889,18 @@ static int make_kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_
 
 // Output map for the TMA-store epilogue: bf16 (M, N) with 64x32 boxes and the 128-byte swizzle,
 // or packed FP4 codes (M, N/2) bytes with (BN/4)x32 boxes and the BN/4-byte swizzle.
-static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, bool fp4, int bn) {
+static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, bool fp4, int bn, int cw = 64) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const int64_t rowbytes = fp4 ? cols / 2 : cols * 2;
   cuuint64_t dims[2] = {(cuuint64_t)(fp4 ? cols / 2 : cols), (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
-  cuuint32_t box[2] = {(cuuint32_t)(fp4 ? bn / 4 : 64), 32u};
+  cuuint32_t box[2] = {(cuuint32_t)(fp4 ? bn / 4 : cw), 32u};
   cuuint32_t es[2] = {1u, 1u};
   CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    fp4 ? (bn == 256 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
-                       : CU_TENSOR_MAP_SWIZZLE_128B,
+                       : (cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B),
                    CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
@@ -956,12 +969,12 @@ static int launch_gemm_ws(const uint8_t* a, const uint8_t* b, GemmParams& p, cud
   using C = GemmWsCfg<EW, epi_gelu(EPI)>;
   CUtensorMap ta, tb, to;
   memset(&to, 0, sizeof(to));
-  if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
-  if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, C::BN)) return st;
+  if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128, C::ROWB)) return st;
+  if (int st = make_kmajor_map(&tb, b, p.N, p.K / 2, C::BN, C::ROWB)) return st;
   if (epi_gelu(EPI)) {   // each warp stores 32 rows x NC/2 bytes of codes: the map of a 2*NC-wide tile
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, 2 * C::NC)) return st;
   } else if (!kF32) {
-    if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
+    if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN, C::EPI_CW)) return st;
   }
   auto kern = gemm_nvfp4_ws_kernel<EPI, kF32, EW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
