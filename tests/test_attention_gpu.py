@@ -162,3 +162,18 @@ def test_quant_attention_adapter_returns_bshd():
     assert F.cosine_similarity(out.flatten().float(), ref.flatten().float(), dim=0) > 0.95
     out2, _ = _quant_attention(FakeAttention(), q, k, v, None, scaling=0.125)
     assert torch.equal(out2, F.scaled_dot_product_attention(q, k, v, scale=0.125).transpose(1, 2).contiguous())
+
+
+@pytest.mark.parametrize("qk,pv", [("fp8", "fp8"), ("nvfp4", "fp8"), ("fp8", "nvfp4"), ("bf16", "fp8"), ("fp8", "bf16")])
+def test_fp8_and_mixed_routes_match_reference(qk, pv):
+    """The reference's default route (fp8 / fp8) and the mixed ones run its own arithmetic on the GPU:
+    equal to the CPU restatement up to fp32 summation order."""
+    from vitfp4.nvfp4 import quant_sdpa
+    B, H, S, D = 2, 3, 197, 64
+    q, k, v = _qkv(B, H, S, D, seed=31)
+    out = quant_sdpa(q.cuda(), k.cuda(), v.cuda(), qk=qk, pv=pv).float().cpu().numpy()
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref = oracle.quant_sdpa(qn, kn, vn, qk=qk, pv=pv)
+    exact = oracle.quant_sdpa(qn, kn, vn, qk="bf16", pv="bf16", smooth_k=False, smooth_v=False)
+    assert cos(out, ref) >= 0.9999, cos(out, ref)
+    assert cos(out, exact) > 0.95

@@ -50,9 +50,11 @@ class FusedNVFP4Block(nn.Module):
         H, D = a.num_heads, a.head_dim
         if getattr(a, "_nvfp4_attn", False) and a._nvfp4_qk == "nvfp4" and a._nvfp4_pv == "nvfp4":
             return ops.attention_packed_qkv(qkv, H, a.scaling)
-        if getattr(a, "_nvfp4_attn", False):
-            raise NotImplementedError("fused block: only the nvfp4/nvfp4 and bf16 attention routes are built")
         q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+        if getattr(a, "_nvfp4_attn", False):   # the fp8 and mixed routes (GPU emulation)
+            from ..nvfp4.attention import quant_sdpa
+            o = quant_sdpa(q, k, v, scale=a.scaling, qk=a._nvfp4_qk, pv=a._nvfp4_pv)
+            return o.transpose(1, 2).reshape(B, S, H * D)
         return F.scaled_dot_product_attention(q, k, v, scale=a.scaling).transpose(1, 2).reshape(B, S, H * D)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
