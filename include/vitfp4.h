@@ -165,6 +165,16 @@ VF4_API int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t 
                            void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
                            void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
 
+/* FP8 attention, the reference's default route quant_sdpa(qk='fp8', pv='fp8') (attention.py:53-86,
+ * fp8.py:6-17, reached through ptq/qattention.py:20-30 with enable_quant_attention's defaults):
+ * smooth-K / smooth-V, then Q and K~ quantized to E4M3 per token (scale amax/448 of the row), P per
+ * query row and V~ per head-dim column along tokens; E4M3 MMAs with fp32 accumulation and the
+ * scales applied to scores and output.  Same operand / output layout and strides as
+ * vf4_attn_nvfp4; head dim 64 and S <= 320 (VF4_ERR_UNSUPPORTED otherwise); no workspace. */
+VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                         int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
+                         int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
+
 /* vf4_attn_nvfp4 with options.  flags: VF4_ATTN_HEAD_GLOBALS takes the Q / K~ / V~ global scales per
  * (image, head) instead of over the whole tensors as the reference does: no statistics pass and,
  * for head dim 64 and S <= 320, no workspace at all (workspace may then be NULL), at the cost of

@@ -1289,6 +1289,518 @@ static int launch_fused(const void* q, const void* k, const void* v, int64_t B, 
   return launch_status("vf4_attn_nvfp4 (fused)");
 }
 
+// ---------------------------------------------------------------------------------------
+// FP8 attention, the reference's default route quant_sdpa(qk='fp8', pv='fp8') (attention.py:53-86
+// with fp8.py:6-17): every operand row is quantized to E4M3 with its own scale amax/448 — Q and
+// K~ per token along d, P per query along keys, V~ per head-dim column along tokens.  The scales
+// factor out of the dot products, so QK^T and PV run as plain E4M3 x E4M3 -> fp32 MMAs
+// (tcgen05.mma kind::f8f6f4, K = 32 per instruction) and the scales are applied to the scores
+// (per row and column) and to the output (per row and column).  P = exp(s - max) is quantized as
+// e4m3(448 * P): the reference's per-row scale of the normalised P is max(P) / 448 = 1 / (448 rowsum),
+// so P / scale equals 448 * exp(s - max).  Head dim 64, S <= 320, one kernel, no workspace; the
+// same persistent structure as attn_fused_kernel (loader, MMA issuer, 12 compute warps), with q
+// read straight from global memory during prep (only k and v are staged, to fit 8-bit operands).
+// ---------------------------------------------------------------------------------------
+struct Fp8Geom {
+  int B, H, S, D;
+  int nq, skp, box_rows, nbox, heads;
+  int kv_hs, out_hs;
+  float scale;
+  const __nv_bfloat16* q;        // read directly: element (b, h, s, d) at q + b sb + h sh + s ss + d
+  int64_t sb, sh, ss;
+  uint32_t raw_k, raw_v, fq, fk, fv, fp, stg, scl, red, bar, total;
+};
+
+static Fp8Geom make_fp8_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
+  Fp8Geom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.nq = (int)((S + 127) / 128);
+  g.skp = (int)((S + 63) / 64 * 64);
+  g.nbox = S <= 256 ? 1 : 2;
+  g.box_rows = (int)align_up((S + g.nbox - 1) / g.nbox, 8);
+  g.heads = (int)(B * H);
+  g.scale = scale;
+  const uint32_t rawb = (uint32_t)(g.nbox * g.box_rows * 128);
+  uint32_t o = 0;
+  g.raw_k = o; o += rawb;
+  g.raw_v = o; o += rawb;
+  g.fq = o;  o += (uint32_t)g.nq * 128u * 64u;    // Q8: rows x 64 bytes
+  g.fk = o;  o += (uint32_t)g.skp * 64u;          // K8
+  g.fv = o;  o += 64u * (uint32_t)g.skp;          // V8^T: 64 rows x skp bytes
+  g.fp = o;  o += 128u * (uint32_t)g.skp;         // P8: 128 rows x skp bytes
+  o = (uint32_t)align_up(o, 1024);
+  g.stg = o; o += 4 * 4096;
+  g.scl = o; o += (uint32_t)(g.nq * 128 + g.skp + 64) * 4u;   // sq, sk, sv
+  o = (uint32_t)align_up(o, 16);
+  g.red = o; o += 15104;
+  g.bar = o; o += 128;
+  g.total = o + 1024;
+  return g;
+}
+
+static bool fp8_ok(int64_t S, int64_t D) {
+  if (D != 64 || S > 320) return false;
+  return make_fp8_geom(1, 1, S, D, 1.f).total <= 227u * 1024u;
+}
+
+// Instruction descriptor for kind::f8f6f4 with E4M3 A and B (K-major), fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_f8_e4m3(uint32_t n, uint32_t m = 128) {
+  return (1u << 4)            // D format: F32
+         | (0u << 7)          // A format: E4M3
+         | (0u << 10)         // B format: E4M3
+         | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+VF4_DEV void mma_f8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Two fp32 values -> two E4M3 bytes (low byte = first value), round-to-nearest-even, saturating.
+VF4_DEV uint32_t e4m3x2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+// 16 fp32 values times `mul` -> 16 E4M3 bytes
+VF4_DEV uint4 e4m3x16(const float* x, float mul) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = e4m3x2(x[4 * i] * mul, x[4 * i + 1] * mul) | (e4m3x2(x[4 * i + 2] * mul, x[4 * i + 3] * mul) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(kFusedWarps * 32, 1)
+    attn_fp8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                    const __grid_constant__ CUtensorMap tmO, const Fp8Geom g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (base - raw0);
+  const uint32_t bar = base + g.bar;
+  const uint32_t raw_full = bar, raw_free = bar + 8, ops_ready = bar + 16, s_full = bar + 24, s_free = bar + 32,
+                 p_full = bar + 40, drain = bar + 80;
+  auto o_full = [&](int ob) { return bar + 48 + 8u * ob; };
+  auto o_free = [&](int ob) { return bar + 64 + 8u * ob; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 88);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbo_q = 4u * 128u;                          // 64-byte rows: 4 chunks per 8-row group
+  const uint32_t sbo_kv = (uint32_t)(g.skp / 16) * 128u;     // skp-byte rows (P8, V8^T)
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(raw_full, 1);
+    mbar_init(raw_free, kFusedCompute);
+    mbar_init(ops_ready, kFusedCompute);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, kFusedCompute);
+    mbar_init(p_full, kFusedCompute);
+    for (int ob = 0; ob < 2; ++ob) {
+      mbar_init(o_full(ob), 1);
+      mbar_init(o_free(ob), kFusedCompute);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+    tma_prefetch(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp >= 2) {
+    // P8 starts at zero: keys >= S stay zero for the whole kernel
+    for (uint32_t o = g.fp + 16u * (threadIdx.x - 64); o < g.fp + 128u * (uint32_t)g.skp; o += 16u * kCT)
+      *reinterpret_cast<uint4*>(gb + o) = make_uint4(0, 0, 0, 0);
+  }
+  fence_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ raw k, v loads
+    if (lane == 0) {
+      const uint32_t bytes = 2u * (uint32_t)(g.nbox * g.box_rows) * 128u;
+      int hi = 0;
+      for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+        if (hi > 0 && !mbar_wait(raw_free, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutEmpty)) break;
+        const int b = head / g.H, h = head - b * g.H;
+        mbar_arrive_expect_tx(raw_full, bytes);
+        for (int j = 0; j < g.nbox; ++j) {
+          const uint32_t off = (uint32_t)(j * g.box_rows) * 128u;
+          const int c1 = g.kv_hs ? h : j * g.box_rows, c2 = g.kv_hs ? j * g.box_rows : h;
+          tma_load_4d(base + g.raw_k + off, &tmK, 0, c1, c2, b, raw_full);
+          tma_load_4d(base + g.raw_v + off, &tmV, 0, c1, c2, b, raw_full);
+        }
+      }
+      if (hi > 0) mbar_wait(raw_full, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    bool ok = true;
+    int hi = 0, it = 0;
+    const int nks = g.skp / 32;
+    for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
+      if (!mbar_wait(ops_ready, (uint32_t)hi & 1u, err, kDevErrTimeoutFull)) break;
+      tc_fence_after();
+      for (int t = 0; t < g.nq; ++t, ++it) {
+        if (it > 0 && !mbar_wait(s_free, (uint32_t)(it - 1) & 1u, err, kDevErrTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          for (int n0 = 0; n0 < g.skp;) {
+            const int rem = g.skp - n0;
+            const int n = rem >= 256 ? 256 : (rem >= 128 ? 128 : 64);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks) {   // K = 64 = two K32 steps
+              const uint64_t ad = smem_desc(base + g.fq + (uint32_t)t * 16u * sbo_q + 256u * ks, 128, sbo_q, 0);
+              const uint64_t bd = smem_desc(base + g.fk + (uint32_t)(n0 / 8) * sbo_q + 256u * ks, 128, sbo_q, 0);
+              mma_f8f6f4(tmem + kFusedTmemS + n0, ad, bd, idesc_f8_e4m3((uint32_t)n), ks > 0 ? 1u : 0u);
+            }
+            n0 += n;
+          }
+          tc_commit(s_full);
+        }
+        __syncwarp();
+        const int ob = it & 1, use = it >> 1;
+        if (!mbar_wait(p_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull) ||
+            (use > 0 && !mbar_wait(o_free(ob), (uint32_t)(use - 1) & 1u, err, kDevErrTimeoutEmpty))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t t_o = tmem + kFusedTmemO + 64u * ob;
+          for (int ks = 0; ks < nks; ++ks)
+            mma_f8f6f4(t_o, smem_desc(base + g.fp + 256u * ks, 128, sbo_kv, 0),
+                       smem_desc(base + g.fv + 256u * ks, 128, sbo_kv, 0), idesc_f8_e4m3(64), ks > 0 ? 1u : 0u);
+          tc_commit(o_full(ob));
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ prep, softmax, epilogue
+    const int cw = warp - 2;
+    const int qd = warp & 3;
+    const int cs = cw >> 2;
+    const int ct = threadIdx.x - 64;
+    const uint32_t qbar = 2u + (uint32_t)qd;
+    float* red = reinterpret_cast<float*>(gb + g.red);
+    float* red_kv = red;               // [2][kFusedCompute][64] column partial sums / maxima
+    float* red_m = red + 2048;         // [kSlices][128]
+    float* red_l = red + 2560;         // [2][kSlices][128]
+    float* mu = red + 3584;            // [2][64]
+    float* sq = reinterpret_cast<float*>(gb + g.scl);   // per query row scale amax / 448
+    float* sk = sq + g.nq * 128;                        // per key
+    float* sv = sk + g.skp;                             // per head-dim column
+    const uint8_t* rk = gb + g.raw_k;
+    const uint8_t* rv = gb + g.raw_v;
+    const int S = g.S, D = g.D;
+    const int nvb = (S + 15) / 16;
+    const int b0 = cs * nvb / kSlices, b1 = (cs + 1) * nvb / kSlices;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const int r = qd * 32 + lane;
+    bool ok = true;
+    int hi = 0, it = 0;
+    for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+      const int b = head / g.H, h = head - b * g.H;
+      // ---- Q8 straight from global memory (lane quads = one row, 16 values each)
+      {
+        const __nv_bfloat16* qh = g.q + (int64_t)b * g.sb + (int64_t)h * g.sh;
+        for (int i = ct; i < g.nq * 512; i += kCT) {
+          const int s = i >> 2, cb = i & 3;
+          float x[16];
+          float am = 0.f;
+          if (s < S) {
+            load8(qh + (int64_t)s * g.ss + 16 * cb, x);
+            load8(qh + (int64_t)s * g.ss + 16 * cb + 8, x + 8);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(x[e]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x[e] = 0.f;
+          }
+          am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+          am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+          const float scl = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
+          *reinterpret_cast<uint4*>(gb + g.fq + (uint32_t)(s >> 3) * sbo_q + (uint32_t)cb * 128u + (s & 7) * 16) =
+              e4m3x16(x, __fdiv_rn(1.f, scl));
+          if (cb == 0) sq[s] = s < S ? scl : 0.f;
+        }
+      }
+      if (ok) ok = mbar_wait(raw_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
+      // ---- column sums of k and v -> means (chunk j = ct % 8, rows ct/8 + (kCT/8) i)
+      {
+        const int j = ct & 7;
+        float ks[8], vs[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ks[e] = vs[e] = 0.f;
+        if (ok) {
+          for (int s = ct >> 3; s < S; s += kCT / 8) {
+            float a[8];
+            raw_load8(rk, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ks[e] += a[e];
+            raw_load8(rv, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vs[e] += a[e];
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], 8);
+          ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], 16);
+          vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], 8);
+          vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], 16);
+        }
+        if (lane < 8) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            red_kv[cw * 64 + 8 * lane + e] = ks[e];
+            red_kv[(kFusedCompute + cw) * 64 + 8 * lane + e] = vs[e];
+          }
+        }
+      }
+      named_bar_sync(1, kCT);
+      if (ct < 128) {
+        const int which = ct >> 6, d = ct & 63;
+        float sum = 0.f;
+        for (int w = 0; w < kFusedCompute; ++w) sum += red_kv[(which * kFusedCompute + w) * 64 + d];
+        mu[which * 64 + d] = __fdiv_rn(sum, (float)S);
+      }
+      named_bar_sync(1, kCT);
+      // ---- per-column amax of v - mean over the tokens -> sv
+      {
+        const int j = ct & 7;
+        float vm[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vm[e] = 0.f;
+        if (ok) {
+          for (int s = ct >> 3; s < S; s += kCT / 8) {
+            float a[8];
+            raw_load8(rv, s, j, a);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vm[e] = fmaxf(vm[e], fabsf(a[e] - mu[64 + 8 * j + e]));
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          vm[e] = fmaxf(vm[e], __shfl_xor_sync(0xffffffffu, vm[e], 8));
+          vm[e] = fmaxf(vm[e], __shfl_xor_sync(0xffffffffu, vm[e], 16));
+        }
+        if (lane < 8) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) red_kv[cw * 64 + 8 * lane + e] = vm[e];
+        }
+      }
+      named_bar_sync(1, kCT);
+      if (ct < 64) {
+        float m = 0.f;
+        for (int w = 0; w < kFusedCompute; ++w) m = fmaxf(m, red_kv[w * 64 + ct]);
+        sv[ct] = __fdiv_rn(fmaxf(m, 1e-12f), 448.f);
+      }
+      named_bar_sync(1, kCT);
+      // ---- K8: per key row (lane quads), k - mean
+      for (int i = ct; i < g.skp * 4; i += kCT) {
+        const int s = i >> 2, cb = i & 3;
+        float x[16];
+        float am = 0.f;
+        if (ok && s < S) {
+          raw_load8(rk, s, 2 * cb, x);
+          raw_load8(rk, s, 2 * cb + 1, x + 8);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            x[e] -= mu[16 * cb + e];
+            am = fmaxf(am, fabsf(x[e]));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[e] = 0.f;
+        }
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        const float scl = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
+        *reinterpret_cast<uint4*>(gb + g.fk + (uint32_t)(s >> 3) * sbo_q + (uint32_t)cb * 128u + (s & 7) * 16) =
+            e4m3x16(x, __fdiv_rn(1.f, scl));
+        if (cb == 0) sk[s] = s < S ? scl : 0.f;
+      }
+      // ---- V8^T: row d, 16-token blocks; a warp covers 32 consecutive d of one token block
+      {
+        const int ntb = g.skp / 16;
+        for (int i = ct; i < 64 * ntb; i += kCT) {
+          const int tb = i >> 6, d = i & 63;
+          float x[16];
+          const float m = mu[64 + d];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int s = tb * 16 + e;
+            x[e] = (ok && s < S) ? raw_elem(rv, s, d) - m : 0.f;
+          }
+          *reinterpret_cast<uint4*>(gb + g.fv + (uint32_t)(d >> 3) * sbo_kv + (uint32_t)tb * 128u + (d & 7) * 16) =
+              e4m3x16(x, __fdiv_rn(1.f, sv[d]));
+        }
+      }
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(ops_ready);
+        mbar_arrive(raw_free);
+      }
+      named_bar_sync(1, kCT);   // sq / sk / sv visible to every compute warp
+      const float cbase = g.scale * 1.4426950408889634f;
+      const int c0 = cs * 8 / kSlices, c1 = (cs + 1) * 8 / kSlices;
+      auto epilogue = [&](int itt, int tl) {
+        const bool act = ok && tl * 128 + qd * 32 < S;
+        const int ob = itt & 1;
+        constexpr int kMaxChunks = (8 + kSlices - 1) / kSlices;
+        uint32_t ov[kMaxChunks][8];
+        if (act) {
+#pragma unroll
+          for (int k = 0; k < kMaxChunks; ++k)
+            if (c0 + k < c1) tmem_ld_32x32b_x8(tmem + lane_base + kFusedTmemO + 64u * ob + 8 * (c0 + k), ov[k]);
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free(ob));
+        if (cs == 0 && lane == 0) bulk_wait_read();
+        named_bar_sync(qbar, 32 * kSlices);
+        uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
+        if (act) {
+          const float* rl = red_l + ob * (kSlices * 128);
+          float lsum = 0.f;
+#pragma unroll
+          for (int c = 0; c < kSlices; ++c) lsum += rl[c * 128 + r];
+          const float f = 1.0f / (448.f * lsum);
+#pragma unroll
+          for (int k = 0; k < kMaxChunks; ++k) {
+            const int c = c0 + k;
+            if (c < c1) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int d = 8 * c + 2 * i;
+                __nv_bfloat162 hv = __floats2bfloat162_rn(
+                    __fmaf_rn(__uint_as_float(ov[k][2 * i]), f * sv[d], mu[64 + d]),
+                    __fmaf_rn(__uint_as_float(ov[k][2 * i + 1]), f * sv[d + 1], mu[64 + d + 1]));
+                w[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+              *reinterpret_cast<uint4*>(stg + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        fence_async_shared();
+        named_bar_sync(qbar, 32 * kSlices);
+        if (act && cs == 0 && lane == 0) {
+          const int row = tl * 128 + qd * 32;
+          tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
+          bulk_commit();
+        }
+      };
+      for (int t = 0; t < g.nq; ++t, ++it) {
+        const bool active = ok && t * 128 + qd * 32 < S;
+        if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
+        tc_fence_after();
+        const uint32_t srow = tmem + lane_base + kFusedTmemS;
+        const float c = sq[t * 128 + r] * cbase;   // real score = acc * sq * sk * scale
+        // pass 1: max over keys of acc * sk (sq * scale > 0 is common to the row)
+        float m = -INFINITY;
+        if (active && ok) {
+          for (int bk = b0; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(srow + 16 * bk, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (16 * bk + e < S) m = fmaxf(m, __uint_as_float(v[e]) * sk[16 * bk + e]);
+          }
+        }
+        red_m[cs * 128 + r] = m;
+        named_bar_sync(qbar, 32 * kSlices);
+#pragma unroll
+        for (int k = 0; k < kSlices; ++k) m = fmaxf(m, red_m[k * 128 + r]);
+        if (t > 0 && ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
+        // pass 2: P = exp(s - max), row sums, P8 = e4m3(448 P)
+        const float nmc = -m * c;
+        float lsum = 0.f;
+        if (active && ok) {
+          for (int bk = b0; bk < b1; ++bk) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(srow + 16 * bk, v);
+            tmem_wait_ld();
+            float p[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              p[e] = 16 * bk + e < S ? ex2_approx(__fmaf_rn(__uint_as_float(v[e]) * sk[16 * bk + e], c, nmc)) : 0.f;
+              lsum += p[e];
+            }
+            *reinterpret_cast<uint4*>(gb + g.fp + (uint32_t)(r >> 3) * sbo_kv + (uint32_t)bk * 128u + (r & 7) * 16) =
+                e4m3x16(p, 448.f);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        red_l[(it & 1) * (kSlices * 128) + cs * 128 + r] = lsum;
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        if (t > 0) epilogue(it - 1, t - 1);
+      }
+      if (ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
+      tc_fence_after();
+      epilogue(it - 1, g.nq - 1);
+      named_bar_sync(1, kCT);   // every warp is done with this head's scales before the next head's prep
+    }
+    if ((warp - 2) < 4 && lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                      int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
+                      int64_t oss, cudaStream_t s) {
+  Fp8Geom g = make_fp8_geom(B, H, S, D, scale);
+  g.q = static_cast<const __nv_bfloat16*>(q);
+  g.sb = sb;
+  g.sh = sh;
+  g.ss = ss;
+  g.kv_hs = sh < ss;
+  g.out_hs = osh < oss;
+  FusedGeom fg = make_fused_geom(B, H, S, D, scale);   // the head-view maps take D, S, H, B from it
+  CUtensorMap tk, tv, to;
+  if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (int st = make_head_map(&to, out, fg, osb, osh, oss, 32, g.out_hs)) return st;
+  cudaError_t e = cudaFuncSetAttribute(attn_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = g.heads < num_sms() ? g.heads : num_sms();
+  attn_fp8_kernel<<<grid, kFusedWarps * 32, g.total, s>>>(tk, tv, to, g);
+  return launch_status("vf4_attn_fp8");
+}
+
 static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t rowbytes, int box_x, int box_y,
                     CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_tiled();
@@ -1408,6 +1920,22 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   if (int st = launch_status("vf4_attn_nvfp4 (prep)")) return st;
   if (g.Dp == 64) return launch_fwd<64>(g, gws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
   return launch_fwd<128>(g, gws, scale, out, out_stride_b, out_stride_h, out_stride_s, s);
+}
+
+int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                 int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out, int64_t out_stride_b,
+                 int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_fp8: bad sizes");
+  if (!fp8_ok(S, D)) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_fp8: needs head dim 64 and S <= 320 (S=%lld D=%lld)",
+                                 (long long)S, (long long)D);
+  if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_fp8: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
+    return fail(VF4_ERR_ALIGN, "vf4_attn_fp8: 16-byte aligned pointers and strides (multiples of 8) needed");
+  if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_fp8: B*H too large");
+  return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                    out_stride_s, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,

@@ -6,6 +6,8 @@
                        in shared memory, smooth-K / smooth-V);
   qk = pv = 'bf16'  -> exact bf16 attention (torch SDPA), the route the reference keeps for
                        unquantised blocks;
+  qk = pv = 'fp8'   -> the sm_100a FP8 attention kernel (E4M3 MMAs, per-row scales) for head dim
+                       64 and S <= 320 without mask; other shapes take the emulation below;
   any other mix     -> the reference's own emulation (quantize-dequantize of the operands, fp32
                        matmuls and softmax) run on the GPU with torch ops, in chunks of heads; NVFP4
                        operands are quantized by the CUDA cast kernel (whole-tensor globals, the P
@@ -120,4 +122,9 @@ def quant_sdpa(query, key, value, attn_mask=None, is_causal=False, scale=None, q
         return ops.attention_bhsd(query, key, value, scale).to(query.dtype)
     if not query.is_cuda:
         raise RuntimeError("quant_sdpa runs on the GPU (CUDA tensors required)")
+    if qk == "fp8" and pv == "fp8" and attn_mask is None and not is_causal and smooth_k and smooth_v \
+            and query.dim() == 4:
+        from . import ops
+        if ops.fp8_kernel_ok(query.shape[-2], D):
+            return ops.attention_fp8_bhsd(query, key, value, scale).to(query.dtype)
     return _emulated_sdpa(query, key, value, attn_mask, is_causal, scale, qk, pv, smooth_k, smooth_v).to(query.dtype)

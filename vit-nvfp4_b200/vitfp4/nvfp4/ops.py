@@ -293,6 +293,45 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int,
     return out
 
 
+def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
+                  strides: tuple[int, int, int], scale: float, out: torch.Tensor,
+                  out_strides: tuple[int, int, int]) -> torch.Tensor:
+    """FP8 (E4M3, per-row scales) attention over bf16 q/k/v views sharing element strides."""
+    _need_cuda(q, k, v, out)
+    for t in (q, k, v, out):
+        if t.dtype != torch.bfloat16:
+            raise _lib.VitFp4Error("FP8 attention takes bf16 q/k/v/out")
+    _lib.call("vf4_attn_fp8", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
+    _launched(1)
+    return out
+
+
+def fp8_kernel_ok(S: int, D: int) -> bool:
+    return D == 64 and S <= 320
+
+
+def _bhsd_operands(q, k, v):
+    B, H, S, D = q.shape
+    qb, kb, vb = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
+    st = qb.stride()
+    shared = (kb.stride() == st and vb.stride() == st and st[3] == 1 and all(x % 8 == 0 for x in st[:3])
+              and all(t.data_ptr() % 16 == 0 for t in (qb, kb, vb)))
+    if shared:
+        return qb, kb, vb, (st[0], st[1], st[2])
+    qb, kb, vb = (t.contiguous() for t in (qb, kb, vb))
+    return qb, kb, vb, (H * S * D, S * D, D)
+
+
+def attention_fp8_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """(B, H, S, D) q/k/v -> (B, H, S, D) bf16 through the FP8 kernel."""
+    B, H, S, D = q.shape
+    qb, kb, vb, strides = _bhsd_operands(q, k, v)
+    out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
+    attention_fp8(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D))
+    return out.transpose(1, 2)
+
+
 def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
                    head_globals: bool = False) -> torch.Tensor:
     """(B, H, S, D) q/k/v (any dtype; cast to bf16) -> (B, H, S, D) bf16."""
