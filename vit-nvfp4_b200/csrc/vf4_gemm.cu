@@ -38,11 +38,16 @@ int gemm_device_error(int clear) {
 
 __host__ __device__ constexpr bool epi_gelu(int e) { return e == VF4_EPI_GELU_NVFP4 || e == VF4_EPI_GELU_ERF_NVFP4; }
 
-template <int BN>
+// The bf16 epilogues of the 128x256 tile stage 32 rows x 16 columns (1 KB) per warp so that a
+// fourth pipeline stage fits; the GELU epilogue keeps 3 stages (its staging is 2 KB per warp) and
+// the fp32 epilogue stores directly.
+template <int BN, int EPI = VF4_EPI_BIAS, bool kF32 = false>
 struct GemmCfg {
+  static constexpr bool kGeluEpi = EPI == VF4_EPI_GELU_NVFP4 || EPI == VF4_EPI_GELU_ERF_NVFP4;
   static constexpr int BM = 128;
   static constexpr int KB_PER_STAGE = 4;                   // 4 x K64 MMAs = 256 elements = 128 B
-  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int STAGES = BN == 256 ? (kGeluEpi ? 3 : 4) : 4;
+  static constexpr int EPI_CW = BN == 256 ? 16 : 64;        // bf16 staging chunk (columns)
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int SFA_BYTES = KB_PER_STAGE * 512;
@@ -56,13 +61,14 @@ struct GemmCfg {
   static constexpr int SFB_SLOT = KB_PER_STAGE * SFB_PER_KB;
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 320;
-  static constexpr int EPI_WARP_BYTES = 4096;               // per epilogue warp: 32 rows x 128 B
+  static constexpr int EPI_WARP_BYTES = kGeluEpi ? 32 * BN / 4 : (kF32 ? 0 : 32 * EPI_CW * 2);
   static constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 16;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(ACC_STAGES * BN <= SFA_TCOL, "accumulators overlap the scale slots");
   static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
   static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct GemmParams {
@@ -122,7 +128,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
   } else if constexpr (!epi_gelu(EPI)) {
     // bf16 out: each CW-column chunk of the warp's 32x(NC) slab is staged in shared memory with
     // the 2*CW-byte swizzle (16-byte piece j of row r at j ^ (r%8) for 128-byte rows, j ^ ((r/2)%4)
-    // for 64-byte rows) and written by one TMA store
+    // for 64-byte rows, j ^ ((r/4)%2) for 32-byte rows) and written by one TMA store
 #pragma unroll
     for (int c = 0; c < NC / CW; ++c) {
       const int colc = col0 + c * CW;
@@ -168,7 +174,7 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
             __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
             w[i] = *reinterpret_cast<uint32_t*>(&h);
           }
-          const int js = CW == 64 ? (j ^ (lane & 7)) : (j ^ ((lane >> 1) & 3));
+          const int js = CW == 64 ? (j ^ (lane & 7)) : CW == 32 ? (j ^ ((lane >> 1) & 3)) : (j ^ ((lane >> 2) & 1));
           *reinterpret_cast<uint4*>(ebuf_g + lane * (2 * CW) + js * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_async_shared();
@@ -255,7 +261,7 @@ template <int BN, int EPI, bool kF32>
 __global__ void __launch_bounds__(320, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, EPI, kF32>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -421,7 +427,8 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
 
-      epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha, egs, esenc,
+      epilogue_slab<NC, EPI, kF32, C::EPI_CW>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha,
+                                               egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
                                    gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES);
     }
@@ -900,7 +907,8 @@ static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, b
   CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    fp4 ? (bn == 256 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
-                       : (cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B),
+                       : (cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : cw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B),
                    CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(VF4_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
@@ -909,7 +917,7 @@ static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, b
 
 template <int BN, int EPI, bool kF32>
 static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, EPI, kF32>;
   CUtensorMap ta, tb, to;
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
@@ -917,7 +925,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   if (epi_gelu(EPI)) {
     if (int st = make_out_map(&to, p.out_packed, p.M, p.N, true, BN)) return st;
   } else if (!kF32) {
-    if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN)) return st;
+    if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN, C::EPI_CW)) return st;
   }
   auto kern = gemm_nvfp4_kernel<BN, EPI, kF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
