@@ -35,7 +35,25 @@ FP4_NOMINAL_TFLOPS = 9000.0
 # DRAM bytes (read + write) per output row measured by ncu for the GEMM kinds that can dominate
 # (profiles/gemm_nvfp4_vitl14_b256.md: the fc1 launch at M = 65792 moved 40.5 + 99.2 MB; A and the
 # output grow with M while the 2.4 MB of weights do not, so bytes scale with the rows)
-NCU_TRAFFIC_PER_ROW = {"gemm_gelu_nvfp4_": 139.716352e6 / 65792}
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792 (ViT-L/14, batch 256),
+# per row of A, keyed by (kernel kind, N, K): profiles/gemm_nvfp4_vitl14_b256.md
+NCU_TRAFFIC_PER_ROW = {
+    ("gemm_gelu_nvfp4", 4096, 1024): (40.415488e6 + 98.564096e6) / 65792,
+    ("gemm_residual", 1024, 4096): (288.748288e6 + 93.634816e6) / 65792,
+    ("gemm_bias", 3072, 1024): (39.713280e6 + 350.148864e6) / 65792,
+    ("gemm_bias", 1024, 1024): (38.528512e6 + 80.605952e6) / 65792,
+}
+
+
+def gemm_algorithmic_bytes(kind: str, m: int, n: int, k: int) -> int:
+    """HBM bytes a GEMM launch must move: A and B codes + E4M3 scales in, plus its output
+    (bf16; NVFP4 codes + scales for the GELU epilogue; residual read + bf16 write for fc2)."""
+    operands = (m + n) * (k // 2 + k // 16)
+    if kind == "gemm_gelu_nvfp4":
+        return operands + m * (n // 2 + n // 16)
+    if kind == "gemm_residual":
+        return operands + 2 * m * n * 2
+    return operands + m * n * 2
 
 
 def _args():
@@ -258,15 +276,14 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
                     "peak_source": "4 x measured bf16 burst (MEASURED_PEAKS.json); FP4 itself not measured"
                     if bf16_tf else "nominal dense FP4 (no measured peak)",
                     "frac_of_nominal_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4), "traffic": None}
-        for prefix, per_row in NCU_TRAFFIC_PER_ROW.items():
-            if dom[0].startswith(prefix):
-                m_rows, n_cols, k_dim = (int(x) for x in dom[0][len(prefix):].split("x"))
-                roofline["traffic"] = round(per_row * m_rows)   # bytes per launch
-                roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
-                                              "M = 65792, scaled by rows (profiles/gemm_nvfp4_vitl14_b256.md)")
-                # A and B codes + scales in, NVFP4 codes + scales out
-                roofline["algorithmic_bytes"] = (m_rows + n_cols) * (k_dim // 2 + k_dim // 16) + \
-                    m_rows * (n_cols // 2 + n_cols // 16)
+        kind, dims = dom[0].rsplit("_", 1)
+        m_rows, n_cols, k_dim = (int(x) for x in dims.split("x"))
+        roofline["algorithmic_bytes"] = gemm_algorithmic_bytes(kind, m_rows, n_cols, k_dim)
+        per_row = NCU_TRAFFIC_PER_ROW.get((kind, n_cols, k_dim))
+        if per_row is not None:
+            roofline["traffic"] = round(per_row * m_rows)   # bytes per launch
+            roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
+                                          "M = 65792, scaled by rows (profiles/gemm_nvfp4_vitl14_b256.md)")
     steps = args.steps
     img_per_step = args.batch
     line = {

@@ -306,6 +306,37 @@ VF4_DEV uint64_t encode16_fast(const float* v, float dec) {
   return (uint64_t)cvt_e2m1x8(q) | ((uint64_t)cvt_e2m1x8(q + 8) << 32);
 }
 
+// encode16_fast with the reciprocal of the decode scale given (inv = __frcp_rn(dec)) and the
+// products formed by packed multiplies; zero_scale selects the dec == 0 codes of encode16_fast.
+VF4_DEV uint64_t encode16_inv(const float* v, float inv, bool zero_scale) {
+  if (zero_scale) {
+    uint64_t p = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p |= (uint64_t)(v[i] < 0.f ? 15u : 7u) << (4 * i);
+    return p;
+  }
+  const unsigned long long inv2 = f32x2_pack(inv, inv);
+  float q[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f32x2_unpack(mul_f32x2(f32x2_pack(v[2 * i], v[2 * i + 1]), inv2), &q[2 * i], &q[2 * i + 1]);
+  return (uint64_t)cvt_e2m1x8(q) | ((uint64_t)cvt_e2m1x8(q + 8) << 32);
+}
+
+// max(a, b, c) in one instruction (three-operand max.f32, sm_100)
+VF4_DEV float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// max |v_i| over 16 values
+VF4_DEV float amax16(const float* v) {
+  float m = max3f(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
+#pragma unroll
+  for (int i = 3; i < 15; i += 2) m = max3f(m, fabsf(v[i]), fabsf(v[i + 1]));
+  return fmaxf(m, fabsf(v[15]));
+}
+
 // E4M3 block scale (six rule) and its decode value: bs = e4m3(min((amax/6)*s_enc, 448)).
 // RN(a / 6) for normal a by one Markstein correction step (q0 = a*y, r = a - 6*q0 exact by FMA,
 // q = q0 + r*y with y = RN(1/6)); checked against IEEE division for every significand in
@@ -377,6 +408,19 @@ VF4_DEV float gelu_tanh(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(v));
   const float hx = 0.5f * x;
   return __fmaf_rn(hx, t, hx);
+}
+
+// gelu_tanh on an element pair with the packed fp32 ops (the same roundings, op for op)
+VF4_DEV unsigned long long gelu_tanh_x2(unsigned long long x2) {
+  const unsigned long long c1 = f32x2_pack(0.0356774081f, 0.0356774081f);
+  const unsigned long long c0 = f32x2_pack(0.7978845608f, 0.7978845608f);
+  const unsigned long long half2 = f32x2_pack(0.5f, 0.5f);
+  float u0, u1, t0, t1;
+  f32x2_unpack(mul_f32x2(x2, fma_f32x2(mul_f32x2(x2, x2), c1, c0)), &u0, &u1);
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(u0));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(u1));
+  const unsigned long long hx = mul_f32x2(x2, half2);
+  return fma_f32x2(hx, f32x2_pack(t0, t1), hx);
 }
 
 // Offset of scale factor (row r, column c) inside the 128x4-tiled ("to_blocked") layout.

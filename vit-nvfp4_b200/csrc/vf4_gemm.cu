@@ -64,7 +64,9 @@ struct GemmCfg {
   static constexpr int EPI_WARP_BYTES = kGeluEpi ? 32 * BN / 4 : (kF32 ? 0 : 32 * EPI_CW * 2);
   static constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * ACC_STAGES + 1) + 16;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int CONST_OFF = (STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 15) / 16 * 16;
+  static constexpr int CONST_BYTES = kGeluEpi ? 512 : 0;   // GELU: the scale reciprocal table
+  static constexpr int SMEM = 1024 + CONST_OFF + CONST_BYTES;
   static_assert(ACC_STAGES * BN <= SFA_TCOL, "accumulators overlap the scale slots");
   static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
   static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment");
@@ -94,12 +96,18 @@ struct GemmParams {
 VF4_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 VF4_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// 1/dec for every E4M3 scale byte b of the GELU-NVFP4 epilogue (dec = e4m3(b) * gs, rounded to
+// nearest as __frcp_rn): filled by the epilogue threads et = 0..127 before their first tile.
+VF4_DEV void fill_rcp_tab(float* tab, int et, float gs) {
+  if (et >= 0 && et < 128) tab[et] = __frcp_rn(__fmul_rn(e4m3_to_f32((uint32_t)et), gs));
+}
+
 // Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
 // [col0, col0 + NC) of row row0 + lane; ebuf is the warp's 4 KB staging buffer.
 template <int NC, int EPI, bool kF32, int CW = 64>
 VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtensorMap* tmOut, int row0,
                            int col0, int lane, float alpha, float egs, float esenc, uint32_t ebuf,
-                           uint8_t* ebuf_g) {
+                           uint8_t* ebuf_g, const float* rcp_tab = nullptr, const float* bias_f = nullptr) {
   const int64_t row = (int64_t)row0 + lane;
   if constexpr (!epi_gelu(EPI) && kF32) {
     if (row < p.M) {
@@ -186,13 +194,17 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
       }
     }
   } else {
-    // fp32 (acc * gs_a * gs_b + b1) -> GELU (A&S 7.1.26 erf) -> NVFP4 "six" cast
-    // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).
+    // fp32 (acc * gs_a * gs_b + b1) -> GELU (tanh form, or A&S 7.1.26 erf) -> NVFP4 "six" cast
+    // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).  Element
+    // pairs go through the packed fp32 ops (fma / mul.rn.f32x2, the scalar ops' roundings); the
+    // reciprocal of a block's decode scale is rcp_tab[scale byte] (= __frcp_rn(e4m3 * gs), filled
+    // per CTA) and the bias comes from bias_f (fp32 in shared memory) when the caller staged it.
     // Packed codes (NC/2 bytes per row) are staged in shared memory with the 64-byte (NC = 128)
     // or 32-byte (NC = 64) swizzle, so a warp's 16-byte stores spread over all banks, and stored
     // by TMA; the 4-byte scale words go straight to the 128x4-tiled layout.
     if (lane == 0) bulk_wait_read();
     __syncwarp();
+    const unsigned long long alpha2 = f32x2_pack(alpha, alpha);
 #pragma unroll
     for (int g4 = 0; g4 < NC / 64; ++g4) {
       uint32_t sfw = 0;
@@ -201,35 +213,45 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
       for (int b = 0; b < 4; ++b) {
         const int blk = g4 * 4 + b;
         const int col = col0 + blk * 16;
-        float h[16];
         uint64_t packed = 0;
         if (col < p.N) {
-          float bb[16];
-          if (p.bias) {
+          unsigned long long t2[8];
+          if (bias_f) {
+            const float4* bp = reinterpret_cast<const float4*>(bias_f + blk * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float4 bb = bp[i];
+              t2[2 * i] = f32x2_pack(bb.x, bb.y);
+              t2[2 * i + 1] = f32x2_pack(bb.z, bb.w);
+            }
+          } else if (p.bias) {
             const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
             uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
             const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              bb[2 * i] = __uint_as_float(bw[i] << 16);
-              bb[2 * i + 1] = __uint_as_float(bw[i] & 0xFFFF0000u);
-            }
+            for (int i = 0; i < 8; ++i) t2[i] = bf16x2_to_f32x2(bw[i]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) bb[i] = 0.f;
+            for (int i = 0; i < 8; ++i) t2[i] = 0ull;
           }
+          float h[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            {
-              const float t = __fmaf_rn(__uint_as_float(v[blk * 16 + i]), alpha, bb[i]);
-              h[i] = EPI == VF4_EPI_GELU_ERF_NVFP4 ? gelu_as(t) : gelu_tanh(t);
+          for (int i = 0; i < 8; ++i) {
+            const unsigned long long a2 =
+                fma_f32x2(f32x2_pack(__uint_as_float(v[blk * 16 + 2 * i]), __uint_as_float(v[blk * 16 + 2 * i + 1])),
+                          alpha2, t2[i]);
+            if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {
+              float x0, x1;
+              f32x2_unpack(a2, &x0, &x1);
+              h[2 * i] = gelu_as(x0);
+              h[2 * i + 1] = gelu_as(x1);
+            } else {
+              f32x2_unpack(gelu_tanh_x2(a2), &h[2 * i], &h[2 * i + 1]);
             }
-          float amax = 0.f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
-          float dec;
-          const uint32_t sf = six_scale(amax, esenc, egs, &dec);
-          packed = encode16_fast(h, dec);
+          }
+          const float bs_f = fminf(__fmul_rn(div6_rn(fmaxf(amax16(h), 1e-12f)), esenc), 448.f);
+          const uint32_t sf = f32_to_e4m3(bs_f);
+          packed = encode16_inv(h, rcp_tab[sf], sf == 0u);
           if (row < p.M) sfw |= sf << (8 * b);
         }
         pk[b] = packed;
@@ -411,6 +433,11 @@ __global__ void __launch_bounds__(320, 1)
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
+    float* rcp_tab = reinterpret_cast<float*>(gbase + C::CONST_OFF);
+    if constexpr (epi_gelu(EPI)) {
+      fill_rcp_tab(rcp_tab, threadIdx.x - 64, egs);
+      named_bar_sync(1, 256);
+    }
     int lt = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
       const int mb = tile / p.tiles_n, nb = tile - mb * p.tiles_n;
@@ -430,7 +457,7 @@ __global__ void __launch_bounds__(320, 1)
       epilogue_slab<NC, EPI, kF32, C::EPI_CW>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + half * NC, lane, alpha,
                                                egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
-                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES);
+                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES, rcp_tab);
     }
     if (lane == 0) bulk_wait_all();   // stores issued by this warp complete before the CTA retires
     __syncwarp();
@@ -477,7 +504,10 @@ struct GemmWsCfg {
   static constexpr int EPI_BYTES = EW * EPI_WARP_BYTES;
   static constexpr int SHARED_BYTES = EPI_BYTES > SFB_RES_BYTES ? EPI_BYTES : SFB_RES_BYTES;
   static constexpr int NBAR = 2 * STAGES + 2 + 1 + 1;   // full/empty, tfull/tempty, drain, sfb
-  static constexpr int SMEM = 1024 + B_RES_BYTES + STAGES * STAGE_BYTES + SHARED_BYTES + 8 * NBAR + 16;
+  static constexpr int CONST_OFF = B_RES_BYTES + STAGES * STAGE_BYTES + SHARED_BYTES + 8 * NBAR + 16;
+  static constexpr int CONST_BYTES = kGelu ? 512 + 4 * BN : 0;   // GELU: reciprocal table + fp32 bias
+  static constexpr int SMEM = 1024 + CONST_OFF + CONST_BYTES;
+  static_assert(CONST_OFF % 16 == 0, "table alignment");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(EPI_BYTES % 1024 == 0, "staging alignment");
   static_assert(SFA_TCOL + 2 * SFA_SLOT <= TMEM_COLS, "TMEM overflow");
@@ -636,6 +666,18 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
+    // GELU: the scale reciprocal table and this CTA's bias columns (one N tile for all its tiles)
+    float* rcp_tab = reinterpret_cast<float*>(gbase + C::CONST_OFF);
+    float* bias_f = rcp_tab + 128;
+    if constexpr (epi_gelu(EPI)) {
+      const int et = threadIdx.x - 64;
+      fill_rcp_tab(rcp_tab, et, egs);
+      if (et < BN) {
+        const int col = nb * BN + et;
+        bias_f[et] = (p.bias && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
+      }
+      named_bar_sync(1, 32 * EW);
+    }
     int lt = 0;
     for (int mb = mb0; mb < p.tiles_m; mb += mstep, ++lt) {
       if (!mbar_wait(tfull_bar, (uint32_t)lt & 1u, err, kDevErrTimeoutTmem)) break;
@@ -651,7 +693,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       epilogue_slab<NC, EPI, kF32, C::EPI_CW>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, alpha,
                                                egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
-                                   gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES);
+                                   gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES, rcp_tab,
+                                   epi_gelu(EPI) ? bias_f + part * NC : nullptr);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -690,7 +733,9 @@ struct Gemm2Cfg {
   static constexpr int THREADS = 352;
   static constexpr int EPI_WARP_BYTES = 4096, EPI_BYTES = 8 * EPI_WARP_BYTES;
   static constexpr int NBAR = 3 * STAGES + 3;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 8 * NBAR + 16;
+  static constexpr int CONST_OFF = STAGES * STAGE_BYTES + EPI_BYTES + 8 * NBAR + 16;
+  static constexpr int SMEM = 1024 + CONST_OFF + 512;   // + the GELU scale reciprocal table
+  static_assert(CONST_OFF % 16 == 0, "table alignment");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(SFB_TCOL + 2 * SFB_SLOT <= TMEM_COLS, "TMEM overflow");
 };
@@ -856,6 +901,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       egs = __ldg(p.epi_gs);
       esenc = __fdiv_rn(1.0f, egs);
     }
+    float* rcp_tab = reinterpret_cast<float*>(gbase + C::CONST_OFF);
+    if constexpr (epi_gelu(EPI)) {
+      fill_rcp_tab(rcp_tab, threadIdx.x - 96, egs);
+      named_bar_sync(1, 256);
+    }
     const uint32_t tempty_leader = mapa_shared(tempty_bar, 0);
     int lt = 0;
     for (int tile = pair; tile < tiles; tile += npairs, ++lt) {
@@ -872,7 +922,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       if (lane == 0) mbar_arrive_remote(tempty_leader);
       epilogue_slab<NC, EPI, kF32>(v, p, &tmOut, pm * 256 + (int)rank * 128 + q * 32, nb * BN + half * NC, lane,
                                    alpha, egs, esenc, epi0 + (uint32_t)(warp - 3) * C::EPI_WARP_BYTES,
-                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 3) * C::EPI_WARP_BYTES);
+                                   gbase + C::STAGES * C::STAGE_BYTES + (warp - 3) * C::EPI_WARP_BYTES, rcp_tab);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
