@@ -181,6 +181,13 @@ VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B,
  * differing from the reference's quantization by independent FP4 noise (cos ~0.98 instead of
  * ~0.9999 against quant_sdpa).  0 = vf4_attn_nvfp4. */
 #define VF4_ATTN_HEAD_GLOBALS 1
+/* flags: VF4_ATTN_PACKED (head dim 64, S <= 320; ignored otherwise) quantizes the operands of every
+ * head in a separate high-occupancy pass into per-head operand images in the workspace, which the
+ * fused kernel then bulk-copies: same results as the default route (identical bits with tensor-wide
+ * globals), faster, but the workspace grows by ~38 KB per (image, head) -- size it with
+ * vf4_attn_workspace_size_ex(B, H, S, D, flags). */
+#define VF4_ATTN_PACKED 2
+VF4_API int64_t vf4_attn_workspace_size_ex(int64_t B, int64_t H, int64_t S, int64_t D, int flags);
 VF4_API int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
                               int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
                               void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,

@@ -101,20 +101,52 @@ def test_attention_matches_oracles(B, H, S, D):
     assert c1 >= 0.999 and c2 >= 0.995 and c3 > 0.95 and c3 >= c_ref - 0.005, (c1, c2, c3, c_ref)
 
 
+@pytest.mark.parametrize("packed", [True, False])
 @pytest.mark.parametrize("B,H,S,D", [(2, 3, 257, 64), (16, 12, 197, 64), (1, 2, 1025, 80)])
-def test_attention_head_globals_mode(B, H, S, D):
+def test_attention_head_globals_mode(B, H, S, D, packed):
     """Per-head global scales (VF4_ATTN_HEAD_GLOBALS): exact to its own semantics, and as accurate
     as the reference on average over many heads (each head is an independent FP4 noise draw)."""
     from vitfp4.nvfp4 import ops
     q, k, v = _qkv(B, H, S, D, seed=7 + S)
     scale = 1.0 / math.sqrt(D)
-    out = ops.attention_bhsd(q.cuda(), k.cuda(), v.cuda(), scale, head_globals=True).float().cpu().numpy()
+    out = ops.attention_bhsd(q.cuda(), k.cuda(), v.cuda(), scale, head_globals=True,
+                             packed=packed).float().cpu().numpy()
     qn, kn, vn = (t.float().numpy() for t in (q, k, v))
     ref_kernel = _oracle_kernel_semantics(qn, kn, vn, scale, head_globals=True)
     exact = oracle.quant_sdpa(qn, kn, vn, qk="bf16", pv="bf16", smooth_k=False, smooth_v=False)
     ref_sdpa = oracle.quant_sdpa(qn, kn, vn, qk="nvfp4", pv="nvfp4")
     assert cos(out, ref_kernel) >= 0.999
     assert cos(out, exact) >= cos(ref_sdpa, exact) - 0.005 and cos(out, exact) > 0.95
+
+
+@pytest.mark.parametrize("B,H,S,D", [(2, 3, 257, 64), (1, 1, 1, 64), (1, 2, 48, 64), (2, 3, 320, 64),
+                                     (8, 40, 197, 64), (3, 16, 129, 64)])
+def test_packed_operand_route_equals_inline_route(B, H, S, D):
+    """VF4_ATTN_PACKED quantizes the operands in a separate pass into per-head images; with the
+    reference's tensor-wide globals the result is the in-kernel route's, bit for bit."""
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import ops
+    q, k, v = (t.cuda() for t in _qkv(B, H, S, D, seed=11 + S))
+    a = ops.attention_bhsd(q, k, v, D ** -0.5, packed=True)
+    b = ops.attention_bhsd(q, k, v, D ** -0.5, packed=False)
+    qkv = torch.stack([q, k, v], 0).permute(1, 3, 0, 2, 4).reshape(B, S, 3 * H * D).contiguous()
+    c = ops.attention_packed_qkv(qkv, H, D ** -0.5, packed=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(c.reshape(B, S, H, D), b.transpose(1, 2))
+    assert _lib.device_error() == 0
+
+
+def test_packed_workspace_size():
+    from vitfp4 import _lib
+    lib = _lib.lib()
+    plain = lib.vf4_attn_workspace_size(4, 16, 257, 64)
+    packed = lib.vf4_attn_workspace_size_ex(4, 16, 257, 64, _lib.VF4_ATTN_PACKED)
+    assert lib.vf4_attn_workspace_size_ex(4, 16, 257, 64, 0) == plain
+    assert packed >= plain + 4 * 16 * 38 * 1024
+    # the long-sequence route ignores the flag
+    assert lib.vf4_attn_workspace_size_ex(1, 2, 1025, 80, _lib.VF4_ATTN_PACKED) == lib.vf4_attn_workspace_size(1, 2, 1025, 80)
+    assert lib.vf4_attn_workspace_size_ex(1, 2, 257, 64, 4) == 0
 
 
 def test_attention_packed_qkv_path_equals_bhsd():

@@ -119,12 +119,13 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
                                                          const __nv_bfloat16* __restrict__ v, int64_t sb,
                                                          int64_t sh, int64_t ss, int H, int S, int D, int Dp,
                                                          float* __restrict__ stats, float* __restrict__ amax3) {
-  extern __shared__ float part[];   // [6][rpi][D]: k sum/max/min, v sum/max/min per row group
+  extern __shared__ float part[];   // [8 warps][6][D] (or [6][rpi][D]): k sum/max/min, v sum/max/min
   __shared__ float red[3][8];
   const int head = blockIdx.x;
   const int b = head / H, h = head - b * H;
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int D8 = D / 8, rpi = 256 / D8, active = rpi * D8;
+  const bool lanes_share = 32 % D8 == 0;   // every lane of a warp on whole rows (D = 16, 32, 64, 128)
   const int j = t % D8, r0 = t / D8;
   const int64_t off = (int64_t)b * sb + (int64_t)h * sh + 8 * j;
   float ks[8], kx[8], kn[8], vs[8], vx[8], vn[8], qm = 0.f;
@@ -162,16 +163,45 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
         }
       }
     }
-    const int RD = rpi * D;
+    if (!lanes_share) {
+      const int RD = rpi * D;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = r0 * D + 8 * j + e;
+        part[i] = ks[e];
+        part[RD + i] = kx[e];
+        part[2 * RD + i] = kn[e];
+        part[3 * RD + i] = vs[e];
+        part[4 * RD + i] = vx[e];
+        part[5 * RD + i] = vn[e];
+      }
+    }
+  }
+  if (lanes_share) {
+    // the lanes of a warp holding chunk j (lane % D8 == j) combine by shuffles, then lanes
+    // [0, D8) write the warp's partials part[w][6][D]: a fixed order, deterministic means
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int i = r0 * D + 8 * j + e;
-      part[i] = ks[e];
-      part[RD + i] = kx[e];
-      part[2 * RD + i] = kn[e];
-      part[3 * RD + i] = vs[e];
-      part[4 * RD + i] = vx[e];
-      part[5 * RD + i] = vn[e];
+      for (int o = D8; o < 32; o <<= 1) {
+        ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
+        vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
+        kx[e] = fmaxf(kx[e], __shfl_xor_sync(0xffffffffu, kx[e], o));
+        kn[e] = fminf(kn[e], __shfl_xor_sync(0xffffffffu, kn[e], o));
+        vx[e] = fmaxf(vx[e], __shfl_xor_sync(0xffffffffu, vx[e], o));
+        vn[e] = fminf(vn[e], __shfl_xor_sync(0xffffffffu, vn[e], o));
+      }
+    }
+    if (lane < D8) {
+      float* pw = part + w * 6 * D;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        pw[8 * lane + e] = ks[e];
+        pw[D + 8 * lane + e] = kx[e];
+        pw[2 * D + 8 * lane + e] = kn[e];
+        pw[3 * D + 8 * lane + e] = vs[e];
+        pw[4 * D + 8 * lane + e] = vx[e];
+        pw[5 * D + 8 * lane + e] = vn[e];
+      }
     }
   }
   qm = warp_max(qm);
@@ -179,16 +209,28 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
   __syncthreads();
   float ak = 0.f, av = 0.f;
   if (t < D) {
-    const int RD = rpi * D;
     float sk = 0.f, xk = -INFINITY, nk = INFINITY, sv = 0.f, xv = -INFINITY, nv = INFINITY;
-    for (int r = 0; r < rpi; ++r) {   // fixed order: deterministic means
-      const int i = r * D + t;
-      sk += part[i];
-      xk = fmaxf(xk, part[RD + i]);
-      nk = fminf(nk, part[2 * RD + i]);
-      sv += part[3 * RD + i];
-      xv = fmaxf(xv, part[4 * RD + i]);
-      nv = fminf(nv, part[5 * RD + i]);
+    if (lanes_share) {
+      for (int ww = 0; ww < 8; ++ww) {
+        const float* pw = part + ww * 6 * D;
+        sk += pw[t];
+        xk = fmaxf(xk, pw[D + t]);
+        nk = fminf(nk, pw[2 * D + t]);
+        sv += pw[3 * D + t];
+        xv = fmaxf(xv, pw[4 * D + t]);
+        nv = fminf(nv, pw[5 * D + t]);
+      }
+    } else {
+      const int RD = rpi * D;
+      for (int r = 0; r < rpi; ++r) {   // fixed order: deterministic means
+        const int i = r * D + t;
+        sk += part[i];
+        xk = fmaxf(xk, part[RD + i]);
+        nk = fminf(nk, part[2 * RD + i]);
+        sv += part[3 * RD + i];
+        xv = fmaxf(xv, part[4 * RD + i]);
+        nv = fminf(nv, part[5 * RD + i]);
+      }
     }
     const float mk = __fdiv_rn(sk, (float)S), mv = __fdiv_rn(sv, (float)S);
     stats[(int64_t)head * 2 * Dp + t] = mk;
@@ -697,10 +739,15 @@ struct FusedGeom {
   float scale;
   const float* stats;   // per-head means (tensor-wide globals) or NULL (per-head globals)
   const float* amax3;
+  const uint8_t* images;   // packed route: per-head operand images written by attn_pack_kernel
+  // In the packed route fq .. sfv are offsets inside an operand image (two image buffers at
+  // img[0], img[1]; the image's last 512 bytes hold gs_q, gs_k, gs_v and mean(v)); otherwise they
+  // are offsets from the shared-memory base after the raw q / k / v buffers.
   uint32_t raw_q, raw_k, raw_v, fq, fk, fv, sfq, sfk, sfv, fp, sfp, zero_end, stg, red, bar, total;
+  uint32_t img[2], img_bytes, img_scal;
 };
 
-static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
+static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale, bool packed = false) {
   FusedGeom g{};
   g.B = (int)B;
   g.H = (int)H;
@@ -712,17 +759,26 @@ static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, flo
   g.box_rows = (int)align_up((S + g.nbox - 1) / g.nbox, 8);
   g.heads = (int)(B * H);
   g.scale = scale;
-  const uint32_t rawb = (uint32_t)(g.nbox * g.box_rows * 128);
+  const uint32_t rawb = packed ? 0u : (uint32_t)(g.nbox * g.box_rows * 128);
   uint32_t o = 0;
   g.raw_q = o; o += rawb;
   g.raw_k = o; o += rawb;
   g.raw_v = o; o += rawb;
+  const uint32_t ops0 = o;
   g.fq = o;  o += (uint32_t)g.nq * 4096u;
   g.fk = o;  o += (uint32_t)g.skp * 32u;
   g.fv = o;  o += (uint32_t)g.skp * 32u;
   g.sfq = o; o += (uint32_t)g.nq * 512u;
   g.sfk = o; o += (uint32_t)((g.skp + 127) / 128) * 512u;
   g.sfv = o; o += (uint32_t)(g.skp / 64) * 512u;
+  if (packed) {   // operand offsets become image-relative; two images, then the P buffers
+    g.img_scal = o - ops0;
+    g.img_bytes = (uint32_t)align_up(g.img_scal + 512u, 1024);
+    for (uint32_t* f : {&g.fq, &g.fk, &g.fv, &g.sfq, &g.sfk, &g.sfv}) *f -= ops0;
+    g.img[0] = ops0;
+    g.img[1] = ops0 + g.img_bytes;
+    o = ops0 + 2 * g.img_bytes;
+  }
   g.fp = o;  o += (uint32_t)g.skp * 64u;
   g.sfp = o; o += (uint32_t)(g.skp / 64) * 512u;
   g.zero_end = o;
@@ -737,6 +793,10 @@ static FusedGeom make_fused_geom(int64_t B, int64_t H, int64_t S, int64_t D, flo
 static bool fused_ok(int64_t S, int64_t D) {
   if (D != 64 || S > 320) return false;
   return make_fused_geom(1, 1, S, D, 1.f).total <= 227u * 1024u;
+}
+
+static bool packed_ok(int64_t S, int64_t D) {
+  return fused_ok(S, D) && make_fused_geom(1, 1, S, D, 1.f, true).total <= 227u * 1024u;
 }
 
 // 8 bf16 of row s, 16-byte chunk j (elements 8j..8j+7) of a 128-byte-swizzled raw tile, as fp32.
@@ -772,6 +832,7 @@ VF4_DEV uint32_t sf_atom_off(int row, int c) {
   return (uint32_t)(row >> 7) * 512u + (uint32_t)(row & 31) * 16u + (uint32_t)((row >> 5) & 3) * 4u + (uint32_t)c;
 }
 
+template <bool kPacked>
 __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -785,6 +846,8 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
                  p_full = bar + 40, drain = bar + 80;
   auto o_full = [&](int ob) { return bar + 48 + 8u * ob; };   // per O buffer
   auto o_free = [&](int ob) { return bar + 64 + 8u * ob; };
+  auto img_full = [&](int i) { return bar + 96 + 8u * i; };    // packed route: operand image i landed
+  auto img_free = [&](int i) { return bar + 112 + 8u * i; };   // packed route: image i no longer read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 88);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbo_kv = (uint32_t)(g.skp / 32) * 128u;   // bytes per 8-row group of P and V~^T
@@ -802,6 +865,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       mbar_init(o_free(ob), kFusedCompute);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(img_full(i), 1);
+      mbar_init(img_free(i), kFusedCompute);
+    }
     fence_mbar_init();
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
@@ -814,7 +881,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
   }
   if (warp >= 2) {
     // scale atoms and P codes start at zero: padding keys, rows and head-dim columns stay zero
-    for (uint32_t o = g.sfq + 16u * (threadIdx.x - 64); o < g.zero_end; o += 16u * kCT)
+    for (uint32_t o = (kPacked ? g.fp : g.sfq) + 16u * (threadIdx.x - 64); o < g.zero_end; o += 16u * kCT)
       *reinterpret_cast<uint4*>(gb + o) = make_uint4(0, 0, 0, 0);
   }
   fence_async_shared();
@@ -824,8 +891,25 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ raw loads
-    if (lane == 0) {
+    if constexpr (kPacked) {
+      // ---------------------------------------------------------- operand images (packed route)
+      if (lane == 0) {
+        int hi = 0;
+        for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+          const int ib = hi & 1;
+          if (hi >= 2 && !mbar_wait(img_free(ib), (uint32_t)((hi >> 1) - 1) & 1u, err, kDevErrTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(img_full(ib), g.img_bytes);
+          const uint8_t* src = g.images + (int64_t)head * g.img_bytes;
+          for (uint32_t o = 0; o < g.img_bytes; o += 8192u) {
+            const uint32_t n = g.img_bytes - o < 8192u ? g.img_bytes - o : 8192u;
+            bulk_load(base + g.img[ib] + o, src + o, n, img_full(ib));
+          }
+        }
+        for (int k = hi - 2 < 0 ? 0 : hi - 2; k < hi; ++k)   // own copies landed
+          mbar_wait(img_full(k & 1), (uint32_t)(k >> 1) & 1u, err, kDevErrTimeoutFull);
+      }
+    } else if (lane == 0) {
+      // ---------------------------------------------------------- raw loads
       const uint32_t bytes = 3u * (uint32_t)(g.nbox * g.box_rows) * 128u;
       int hi = 0;
       for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
@@ -850,13 +934,16 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     const uint32_t t_psf = tmem + kFusedTmemPsf, t_vsf = tmem + kFusedTmemVsf;
     const int nkb = g.skp / 64;
     for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
-      if (!mbar_wait(ops_ready, (uint32_t)hi & 1u, err, kDevErrTimeoutFull)) break;
+      if (kPacked ? !mbar_wait(img_full(hi & 1), (uint32_t)(hi >> 1) & 1u, err, kDevErrTimeoutFull)
+                  : !mbar_wait(ops_ready, (uint32_t)hi & 1u, err, kDevErrTimeoutFull))
+        break;
       tc_fence_after();
+      const uint32_t opb = kPacked ? base + g.img[hi & 1] : base;   // operand base of this head
       if (lane == 0) {
         for (int a = 0; a < (g.skp + 127) / 128; ++a)
-          tmem_cp_32x128b_x4(t_ksf + 4 * a, smem_desc(base + g.sfk + 512 * a, 0, 128, 0));
+          tmem_cp_32x128b_x4(t_ksf + 4 * a, smem_desc(opb + g.sfk + 512 * a, 0, 128, 0));
         for (int kb = 0; kb < nkb; ++kb)
-          tmem_cp_32x128b_x4(t_vsf + 4 * kb, smem_desc(base + g.sfv + 512 * kb, 0, 128, 0));
+          tmem_cp_32x128b_x4(t_vsf + 4 * kb, smem_desc(opb + g.sfv + 512 * kb, 0, 128, 0));
       }
       __syncwarp();
       for (int t = 0; t < g.nq; ++t, ++it) {
@@ -866,12 +953,12 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          tmem_cp_32x128b_x4(t_qsf, smem_desc(base + g.sfq + 512 * t, 0, 128, 0));
-          const uint64_t ad = smem_desc(base + g.fq + 4096u * t, 128, 256, 0);
+          tmem_cp_32x128b_x4(t_qsf, smem_desc(opb + g.sfq + 512 * t, 0, 128, 0));
+          const uint64_t ad = smem_desc(opb + g.fq + 4096u * t, 128, 256, 0);
           for (int n0 = 0; n0 < g.skp;) {
             const int rem = g.skp - n0;
             const int n = rem >= 256 ? 256 : (rem >= 128 ? 128 : 64);
-            const uint64_t bd = smem_desc(base + g.fk + (uint32_t)(n0 / 8) * 256u, 128, 256, 0);
+            const uint64_t bd = smem_desc(opb + g.fk + (uint32_t)(n0 / 8) * 256u, 128, 256, 0);
             mma_mxf4nvf4(tmem + kFusedTmemS + n0, ad, bd, idesc_mxf4nvf4((uint32_t)n), t_qsf, t_ksf + (n0 / 128) * 4,
                          0u);
             n0 += n;
@@ -891,7 +978,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
           for (int kb = 0; kb < nkb; ++kb) {
             tmem_cp_32x128b_x4(t_psf + 4 * kb, smem_desc(base + g.sfp + 512 * kb, 0, 128, 0));
             mma_mxf4nvf4(t_o, smem_desc(base + g.fp + 256u * kb, 128, sbo_kv, 0),
-                         smem_desc(base + g.fv + 256u * kb, 128, sbo_kv, 0), idesc_mxf4nvf4(64), t_psf + 4 * kb,
+                         smem_desc(opb + g.fv + 256u * kb, 128, sbo_kv, 0), idesc_mxf4nvf4(64), t_psf + 4 * kb,
                          t_vsf + 4 * kb, kb > 0 ? 1u : 0u);
           }
           tc_commit(o_full(ob));
@@ -930,6 +1017,16 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     int hi = 0, it = 0;
     for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
       const int b = head / g.H, h = head - b * g.H;
+      float gq, gk, gv;
+      const float* muv;   // mean(v) of this head
+      if constexpr (kPacked) {
+        if (ok) ok = mbar_wait(img_full(hi & 1), (uint32_t)(hi >> 1) & 1u, err, kDevErrTimeoutFull);
+        const float* sc = reinterpret_cast<const float*>(gb + g.img[hi & 1] + g.img_scal);
+        gq = sc[0];
+        gk = sc[1];
+        gv = sc[2];
+        muv = sc + 64;
+      } else {
       if (ok) ok = mbar_wait(raw_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
       if (g.stats) {
         // tensor-wide globals: this head's means and the global maxima were computed beforehand
@@ -1023,7 +1120,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       }
       named_bar_sync(1, kCT);
       }
-      const float gq = scal[0], gk = scal[1], gv = scal[2];
+      gq = scal[0];
+      gk = scal[1];
+      gv = scal[2];
+      muv = mu + 64;
       // ---- prep 3: NVFP4 operands.  Q rows [0, 128 nq) and K~ rows [0, skp): 4 column blocks
       // per row, lane quads = one row (their 4 scale bytes merge into one word).  Two items per
       // loop trip so the two quantization chains interleave (the loop bounds are multiples of 32:
@@ -1093,6 +1193,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         mbar_arrive(ops_ready);
         mbar_arrive(raw_free);
       }
+      }
       const float cexp = gq * gk * g.scale * 1.4426950408889634f;
       const float ofac = gv * kInv2688;
       // epilogue of tile (global index itt, local index tl): O rows of this quadrant, the slice's
@@ -1129,8 +1230,8 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const int d = 8 * c + 2 * i;
-                __nv_bfloat162 hv = __floats2bfloat162_rn(__fmaf_rn(__uint_as_float(ov[k][2 * i]), f, mu[64 + d]),
-                                                          __fmaf_rn(__uint_as_float(ov[k][2 * i + 1]), f, mu[64 + d + 1]));
+                __nv_bfloat162 hv = __floats2bfloat162_rn(__fmaf_rn(__uint_as_float(ov[k][2 * i]), f, muv[d]),
+                                                          __fmaf_rn(__uint_as_float(ov[k][2 * i + 1]), f, muv[d + 1]));
                 w[i] = *reinterpret_cast<uint32_t*>(&hv);
               }
               *reinterpret_cast<uint4*>(stg + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -1243,6 +1344,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
       if (ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
       tc_fence_after();
       epilogue(it - 1, g.nq - 1);
+      if constexpr (kPacked) {   // every MMA of this head completed (o_full above); scalars read
+        __syncwarp();
+        if (lane == 0) mbar_arrive(img_free(hi & 1));
+      }
     }
     if (cs == 0 && lane == 0) bulk_wait_all();
   }
@@ -1269,12 +1374,204 @@ static int make_head_map(CUtensorMap* m, const void* ptr, const FusedGeom& g, in
   return VF4_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// Operand packing for the packed fused route: one CTA per (b, h) quantizes Q, K~ = K - mean(K) and
+// V~^T = (V - mean(V))^T with the arithmetic of the fused kernel's own preparation and writes the
+// head's operand image -- codes in the MMA's K-major core-matrix layout, scale atoms in the
+// tcgen05.cp layout, then gs_q, gs_k, gs_v and mean(v) -- to global memory; the packed fused kernel
+// bulk-copies it into shared memory unchanged.  The image is assembled in shared memory (its
+// padding rows and scale-atom tails stay zero) and stored with 16-byte writes.  With tensor-wide
+// globals the means and maxima come from attn_stats_kernel; otherwise this CTA computes the head's
+// own (means in a fixed summation order, centred maxima from column max / min).
+// Many small CTAs per SM (about 50 KB of shared memory each) keep the loads and the quantizer
+// latency overlapped, which the fused kernel's 12 compute warps could not.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256, 3) attn_pack_kernel(const __nv_bfloat16* __restrict__ q,
+                                                        const __nv_bfloat16* __restrict__ k,
+                                                        const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                        int64_t sh, int64_t ss, const FusedGeom g,
+                                                        uint8_t* __restrict__ images) {
+  extern __shared__ __align__(16) uint8_t img[];
+  __shared__ float mu[128];          // mean(k) [0, 64), mean(v) [64, 128)
+  __shared__ float scal[8];          // gs_q, gs_k, gs_v, 1/gs_q, 1/gs_k, 1/gs_v
+  __shared__ float part[8][6][64];   // per-warp column partials (per-head globals)
+  __shared__ __align__(16) uint32_t vstage[8][16 * 32];   // per-warp 16 v rows of 64 bf16
+  const int head = blockIdx.x;
+  const int b = head / g.H, h = head - b * g.H;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int S = g.S;
+  const int64_t hoff = (int64_t)b * sb + (int64_t)h * sh;
+  for (uint32_t o = 16u * t; o < g.img_bytes; o += 16u * 256u) *reinterpret_cast<uint4*>(img + o) = make_uint4(0, 0, 0, 0);
+  if (g.stats) {
+    if (t < 128) mu[t] = g.stats[(int64_t)head * 128 + t];
+    if (t < 3) {
+      const float gsv = __fdiv_rn(fmaxf(g.amax3[t], 1e-12f), 2688.f);
+      scal[t] = gsv;
+      scal[3 + t] = __fdiv_rn(1.0f, gsv);
+    }
+  } else {
+    // per-head globals: chunk j = t % 8 of rows t / 8 + 32 i
+    const int j = t & 7;
+    float ks[8], kx[8], kn[8], vs[8], vx[8], vn[8], qm = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ks[e] = vs[e] = 0.f;
+      kx[e] = vx[e] = -INFINITY;
+      kn[e] = vn[e] = INFINITY;
+    }
+    for (int r = t >> 3; r < S; r += 32) {
+      float a[8], c[8], u[8];
+      load8(q + hoff + (int64_t)r * ss + 8 * j, a);
+      load8(k + hoff + (int64_t)r * ss + 8 * j, c);
+      load8(v + hoff + (int64_t)r * ss + 8 * j, u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        qm = fmaxf(qm, fabsf(a[e]));
+        ks[e] += c[e];
+        kx[e] = fmaxf(kx[e], c[e]);
+        kn[e] = fminf(kn[e], c[e]);
+        vs[e] += u[e];
+        vx[e] = fmaxf(vx[e], u[e]);
+        vn[e] = fminf(vn[e], u[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {   // lanes j, j + 8, j + 16, j + 24 hold chunk j: fixed combination order
+#pragma unroll
+      for (int o = 8; o <= 16; o <<= 1) {
+        ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
+        vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
+        kx[e] = fmaxf(kx[e], __shfl_xor_sync(0xffffffffu, kx[e], o));
+        kn[e] = fminf(kn[e], __shfl_xor_sync(0xffffffffu, kn[e], o));
+        vx[e] = fmaxf(vx[e], __shfl_xor_sync(0xffffffffu, vx[e], o));
+        vn[e] = fminf(vn[e], __shfl_xor_sync(0xffffffffu, vn[e], o));
+      }
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        part[w][0][8 * j + e] = ks[e];
+        part[w][1][8 * j + e] = kx[e];
+        part[w][2][8 * j + e] = kn[e];
+        part[w][3][8 * j + e] = vs[e];
+        part[w][4][8 * j + e] = vx[e];
+        part[w][5][8 * j + e] = vn[e];
+      }
+    }
+    qm = warp_max(qm);
+    if (lane == 0) scal[6] = 0.f;
+    __syncthreads();
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(&scal[6]), __float_as_uint(qm));
+    float ak = 0.f, av = 0.f;
+    if (t < 64) {
+      float sk = 0.f, xk = -INFINITY, nk = INFINITY, sv = 0.f, xv = -INFINITY, nv = INFINITY;
+      for (int ww = 0; ww < 8; ++ww) {
+        sk += part[ww][0][t];
+        xk = fmaxf(xk, part[ww][1][t]);
+        nk = fminf(nk, part[ww][2][t]);
+        sv += part[ww][3][t];
+        xv = fmaxf(xv, part[ww][4][t]);
+        nv = fminf(nv, part[ww][5][t]);
+      }
+      const float mk = __fdiv_rn(sk, (float)S), mv = __fdiv_rn(sv, (float)S);
+      mu[t] = mk;
+      mu[64 + t] = mv;
+      ak = fmaxf(fabsf(xk - mk), fabsf(nk - mk));
+      av = fmaxf(fabsf(xv - mv), fabsf(nv - mv));
+    }
+    ak = warp_max(ak);
+    av = warp_max(av);
+    __shared__ float red2[2][2];   // centred maxima of k and v from warps 0, 1 (the 64 columns)
+    if (lane == 0 && w < 2) {
+      red2[w][0] = ak;
+      red2[w][1] = av;
+    }
+    __syncthreads();
+    if (t < 3) {
+      const float am = t == 0 ? scal[6] : fmaxf(red2[0][t - 1], red2[1][t - 1]);
+      const float gsv = __fdiv_rn(fmaxf(am, 1e-12f), 2688.f);
+      scal[t] = gsv;
+      scal[3 + t] = __fdiv_rn(1.0f, gsv);
+    }
+  }
+  __syncthreads();
+  const float gq = scal[0], gk = scal[1], gv = scal[2];
+  // Q rows [0, 128 nq) and K~ rows [0, skp): 4 column blocks per row, a lane quad per row (their
+  // scale bytes merge into one word); loop bounds are multiples of 256, so whole warps iterate
+  auto qk_block = [&](int i, const __nv_bfloat16* src, uint32_t fo, uint32_t so, bool centre, float gs, float se,
+                      float dec_max) {
+    const int r = i >> 2, cb = i & 3;
+    uint64_t codes = 0;
+    uint32_t sf = 0;
+    if (r < S) {
+      float x[16];
+      load8(src + hoff + (int64_t)r * ss + 16 * cb, x);
+      load8(src + hoff + (int64_t)r * ss + 16 * cb + 8, x + 8);
+      if (centre) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] -= mu[16 * cb + e];
+      }
+      const BlockQ z = quantize_block<false>(x, gs, se, dec_max);
+      codes = z.packed;
+      sf = z.sf;
+    }
+    *reinterpret_cast<uint64_t*>(img + fo + cm_off(r, cb, 256)) = codes;
+    uint32_t wd = sf << (8 * cb);
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
+    if (cb == 0) *reinterpret_cast<uint32_t*>(img + so + sf_atom_off(r, 0)) = wd;
+  };
+  for (int i = t; i < g.nq * 512; i += 256) qk_block(i, q, g.fq, g.sfq, false, gq, scal[3], 0x1p17f);
+  for (int i = t; i < g.skp * 4; i += 256) qk_block(i, k, g.fk, g.sfk, true, gk, scal[4], 2.0f);
+  // V~^T rows d in [0, 64), token blocks tb in [0, skp / 16): warp w stages the 16 v rows of its
+  // token blocks (2 KB, four 16-byte loads per lane) in shared memory, then lane l quantizes the
+  // columns d = 2l, 2l + 1 of the block (its reads of a row are one 4-byte word per lane)
+  const uint32_t sbo_kv = (uint32_t)(g.skp / 32) * 128u;
+  const int nvb = (S + 15) / 16;
+  uint4* vst = reinterpret_cast<uint4*>(vstage[w]);
+  for (int tb = w; tb < nvb; tb += 8) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int rr = 4 * p + (lane >> 3), r = tb * 16 + rr, c8 = lane & 7;
+      vst[rr * 8 + c8] = r < S ? __ldg(reinterpret_cast<const uint4*>(v + hoff + (int64_t)r * ss + 8 * c8))
+                               : make_uint4(0, 0, 0, 0);
+    }
+    __syncwarp();
+    float x0[16], x1[16];
+    const float m0 = mu[64 + 2 * lane], m1 = mu[64 + 2 * lane + 1];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const uint32_t wd = reinterpret_cast<const uint32_t*>(vstage[w])[e * 32 + lane];
+      const bool in = tb * 16 + e < S;
+      x0[e] = in ? __uint_as_float(wd << 16) - m0 : 0.f;
+      x1[e] = in ? __uint_as_float(wd & 0xFFFF0000u) - m1 : 0.f;
+    }
+    __syncwarp();   // the stage is refilled on the next trip
+    const BlockQ z0 = quantize_block<false>(x0, gv, scal[5]);
+    const BlockQ z1 = quantize_block<false>(x1, gv, scal[5]);
+    const int d0 = 2 * lane, d1 = 2 * lane + 1;
+    *reinterpret_cast<uint64_t*>(img + g.fv + cm_off(d0, tb, sbo_kv)) = z0.packed;
+    *reinterpret_cast<uint64_t*>(img + g.fv + cm_off(d1, tb, sbo_kv)) = z1.packed;
+    img[g.sfv + (uint32_t)(tb >> 2) * 512u + sf_atom_off(d0, tb & 3)] = (uint8_t)z0.sf;
+    img[g.sfv + (uint32_t)(tb >> 2) * 512u + sf_atom_off(d1, tb & 3)] = (uint8_t)z1.sf;
+  }
+  if (t < 3) reinterpret_cast<float*>(img + g.img_scal)[t] = scal[t];
+  if (t < 64) reinterpret_cast<float*>(img + g.img_scal)[64 + t] = mu[64 + t];
+  __syncthreads();
+  uint8_t* dst = images + (int64_t)head * g.img_bytes;
+  for (uint32_t o = 16u * t; o < g.img_bytes; o += 16u * 256u)
+    *reinterpret_cast<uint4*>(dst + o) = *reinterpret_cast<const uint4*>(img + o);
+}
+
 static int launch_fused(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                         int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
-                        int64_t oss, const float* stats, const float* amax3, cudaStream_t s) {
-  FusedGeom g = make_fused_geom(B, H, S, D, scale);
+                        int64_t oss, const float* stats, const float* amax3, cudaStream_t s,
+                        uint8_t* images = nullptr) {
+  const bool packed = images != nullptr;
+  FusedGeom g = make_fused_geom(B, H, S, D, scale, packed);
   g.stats = stats;
   g.amax3 = amax3;
+  g.images = images;
   g.qkv_hs = sh < ss;
   g.out_hs = osh < oss;
   CUtensorMap tq, tk, tv, to;
@@ -1282,11 +1579,21 @@ static int launch_fused(const void* q, const void* k, const void* v, int64_t B, 
   if (int st = make_head_map(&tk, k, g, sb, sh, ss, g.box_rows, g.qkv_hs)) return st;
   if (int st = make_head_map(&tv, v, g, sb, sh, ss, g.box_rows, g.qkv_hs)) return st;
   if (int st = make_head_map(&to, out, g, osb, osh, oss, 32, g.out_hs)) return st;
-  cudaError_t e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
+  if (packed) {
+    const int smem = (int)g.img_bytes;
+    cudaError_t e = cudaFuncSetAttribute(attn_pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attn_pack_kernel<<<(unsigned)g.heads, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
+                                                          static_cast<const __nv_bfloat16*>(k),
+                                                          static_cast<const __nv_bfloat16*>(v), sb, sh, ss, g, images);
+    if (int st = launch_status("vf4_attn_nvfp4 (pack)")) return st;
+  }
+  auto kern = packed ? attn_fused_kernel<true> : attn_fused_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
   if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
-  attn_fused_kernel<<<grid, kFusedWarps * 32, g.total, s>>>(tq, tk, tv, to, g);
-  return launch_status("vf4_attn_nvfp4 (fused)");
+  kern<<<grid, kFusedWarps * 32, g.total, s>>>(tq, tk, tv, to, g);
+  return launch_status(packed ? "vf4_attn_nvfp4 (fused, packed operands)" : "vf4_attn_nvfp4 (fused)");
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1841,10 +2148,11 @@ static int launch_fwd(const AttnGeom& g, const uint8_t* ws, float scale, void* o
 // Workspace of one call: [global maxima (256 B)][per-head means][long-sequence path buffers].
 // The first two exist only with tensor-wide globals; the last only off the fused path.
 struct AttnWs {
-  int64_t off_amax, off_stats, off_gen, total;
+  int64_t off_amax, off_stats, off_gen, off_img, total;
 };
 
-static AttnWs attn_ws_layout(int64_t B, int64_t H, int64_t S, int64_t D, bool tensor) {
+// packed: the packed fused route's per-head operand images follow (B*H images of img_bytes)
+static AttnWs attn_ws_layout(int64_t B, int64_t H, int64_t S, int64_t D, bool tensor, bool packed = false) {
   AttnWs w{};
   const int64_t Dp = D <= 64 ? 64 : 128;
   int64_t o = 0;
@@ -1854,6 +2162,11 @@ static AttnWs attn_ws_layout(int64_t B, int64_t H, int64_t S, int64_t D, bool te
   if (tensor) o = align_up(o + B * H * 2 * Dp * 4, 1024);
   w.off_gen = o;
   if (!fused_ok(S, D)) o += make_geom(B, H, S, D).total;
+  w.off_img = o;
+  if (packed && packed_ok(S, D)) {
+    w.off_img = align_up(o, 1024);
+    o = w.off_img + B * H * (int64_t)make_fused_geom(1, 1, S, D, 1.f, true).img_bytes;
+  }
   w.total = o;
   return w;
 }
@@ -1869,6 +2182,12 @@ int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D) {
   return attn_ws_layout(B, H, S, D, true).total;
 }
 
+int64_t vf4_attn_workspace_size_ex(int64_t B, int64_t H, int64_t S, int64_t D, int flags) {
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0 || D % 16 != 0 || D > 128) return 0;
+  if (flags & ~(VF4_ATTN_HEAD_GLOBALS | VF4_ATTN_PACKED)) return 0;
+  return attn_ws_layout(B, H, S, D, !(flags & VF4_ATTN_HEAD_GLOBALS), (flags & VF4_ATTN_PACKED) != 0).total;
+}
+
 int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                       int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
                       int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, int flags, void* workspace,
@@ -1876,7 +2195,8 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   if (int st = check_device()) return st;
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: bad sizes");
   if (D % 16 != 0 || D > 128) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim must be a multiple of 16, <= 128");
-  if (flags & ~VF4_ATTN_HEAD_GLOBALS) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: unknown flags %d", flags);
+  if (flags & ~(VF4_ATTN_HEAD_GLOBALS | VF4_ATTN_PACKED))
+    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: unknown flags %d", flags);
   if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: null pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
       stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
@@ -1886,7 +2206,8 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   const bool fused = fused_ok(S, D);
   if (!fused && B * H > 65535) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H must be <= 65535 for S=%lld D=%lld",
                                            (long long)S, (long long)D);
-  const AttnWs w = attn_ws_layout(B, H, S, D, tensor);
+  const bool packed = (flags & VF4_ATTN_PACKED) && packed_ok(S, D);
+  const AttnWs w = attn_ws_layout(B, H, S, D, tensor, packed);
   if (w.total > 0 && (!workspace || !aligned16(workspace)))
     return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: a 16-byte aligned workspace of %lld bytes is needed", (long long)w.total);
   if (workspace_bytes < w.total)
@@ -1904,7 +2225,7 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
     amax3 = reinterpret_cast<float*>(ws + w.off_amax);
     if (cudaMemsetAsync(amax3, 0, 16, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4: memset failed");
     const int D8 = (int)D / 8, rpi = 256 / D8;
-    const int smem = 6 * rpi * (int)D * 4;
+    const int smem = 32 % D8 == 0 ? 8 * 6 * (int)D * 4 : 6 * rpi * (int)D * 4;
     cudaError_t e = cudaFuncSetAttribute(attn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
@@ -1913,7 +2234,7 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   }
   if (fused)
     return launch_fused(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
-                        out_stride_s, stats, amax3, s);
+                        out_stride_s, stats, amax3, s, packed ? ws + w.off_img : nullptr);
   AttnGeom g = make_geom(B, H, S, D);
   uint8_t* gws = ws + w.off_gen;
   attn_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(Q, K, V, stride_b, stride_h, stride_s, g, gws, stats, amax3);

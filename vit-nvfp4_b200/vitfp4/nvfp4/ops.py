@@ -263,8 +263,8 @@ def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs, ex
 _ws_cache: dict = {}
 
 
-def _attn_workspace(B: int, H: int, S: int, D: int, device) -> torch.Tensor:
-    n = int(_lib.lib().vf4_attn_workspace_size(B, H, S, D))
+def _attn_workspace(B: int, H: int, S: int, D: int, device, flags: int = 0) -> torch.Tensor:
+    n = int(_lib.lib().vf4_attn_workspace_size_ex(B, H, S, D, flags))
     key = (device, torch.cuda.current_stream(device).cuda_stream)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < n:
@@ -275,21 +275,24 @@ def _attn_workspace(B: int, H: int, S: int, D: int, device) -> torch.Tensor:
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
               strides: tuple[int, int, int], scale: float, out: torch.Tensor,
-              out_strides: tuple[int, int, int], head_globals: bool = False) -> torch.Tensor:
+              out_strides: tuple[int, int, int], head_globals: bool = False, packed: bool = True) -> torch.Tensor:
     """NVFP4 attention over bf16 q/k/v views sharing (stride_b, stride_h, stride_s) element strides.
 
-    Global scales of Q, K~, V~ over the whole tensors (the reference's) unless ``head_globals``."""
+    Global scales of Q, K~, V~ over the whole tensors (the reference's) unless ``head_globals``.
+    ``packed`` (head dim 64, S <= 320): operands quantized by a separate pass into per-head images
+    in the workspace (~38 KB per image and head), the faster route; False keeps the quantization
+    inside the fused kernel (512 B of workspace per head)."""
     _need_cuda(q, k, v, out)
     for t in (q, k, v, out):
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("FP4 attention takes bf16 q/k/v/out")
-    ws = _attn_workspace(B, H, S, D, q.device)
-    flags = _lib.VF4_ATTN_HEAD_GLOBALS if head_globals else 0
+    flags = (_lib.VF4_ATTN_HEAD_GLOBALS if head_globals else 0) | (_lib.VF4_ATTN_PACKED if packed else 0)
+    ws = _attn_workspace(B, H, S, D, q.device, flags)
     _lib.call("vf4_attn_nvfp4_ex", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
               float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], flags,
               _ptr(ws) if ws.numel() else None, ws.numel(), _stream())
     fused = D == 64 and S <= 320
-    _launched((0 if head_globals else 1) + (1 if fused else 2))
+    _launched((0 if head_globals else 1) + (1 if fused else 2) + (1 if fused and packed else 0))
     return out
 
 
@@ -333,7 +336,7 @@ def attention_fp8_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale:
 
 
 def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-                   head_globals: bool = False) -> torch.Tensor:
+                   head_globals: bool = False, packed: bool = True) -> torch.Tensor:
     """(B, H, S, D) q/k/v (any dtype; cast to bf16) -> (B, H, S, D) bf16."""
     B, H, S, D = q.shape
     qb, kb, vb = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
@@ -346,11 +349,13 @@ def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
         qb, kb, vb = (t.contiguous() for t in (qb, kb, vb))
         strides = (H * S * D, S * D, D)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
-    attention(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D), head_globals=head_globals)
+    attention(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D), head_globals=head_globals,
+              packed=packed)
     return out.transpose(1, 2)
 
 
-def attention_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float, head_globals: bool = False) -> torch.Tensor:
+def attention_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float, head_globals: bool = False,
+                         packed: bool = True) -> torch.Tensor:
     """Packed (B, S, 3*H*D) projection output -> (B, S, H*D) bf16, read in place (no q/k/v copies)."""
     B, S, C3 = qkv.shape
     H = num_heads
@@ -359,7 +364,7 @@ def attention_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float, head_g
     out = torch.empty((B, S, H * D), dtype=torch.bfloat16, device=qkv.device)
     st = (S * C3, D, C3)
     attention(x, x[..., H * D:], x[..., 2 * H * D:], B, H, S, D, st, scale, out, (S * H * D, D, H * D),
-              head_globals=head_globals)
+              head_globals=head_globals, packed=packed)
     return out
 
 
