@@ -255,6 +255,95 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
   }
 }
 
+// Head dim 64 form of attn_stats_kernel (the fused route): threads 0-127 take k and |q|, threads
+// 128-255 take v, each thread 8 columns of rows t/8 + 16 i, two rows per trip; the lanes of a warp
+// that hold the same 8 columns combine by shuffles, the four warps of a tensor through shared
+// memory in a fixed order (deterministic means); three CTAs per SM.
+__global__ void __launch_bounds__(256, 3) attn_stats64_kernel(const __nv_bfloat16* __restrict__ q,
+                                                              const __nv_bfloat16* __restrict__ k,
+                                                              const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                              int64_t sh, int64_t ss, int H, int S,
+                                                              float* __restrict__ stats, float* __restrict__ amax3) {
+  __shared__ float part[8][3][64];   // per warp: sum, max, min of its tensor's 64 columns
+  __shared__ float qred[4], ared[4];
+  const int head = blockIdx.x;
+  const int b = head / H, h = head - b * H;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const bool is_v = t >= 128;
+  const int tt = t & 127, j = tt & 7;
+  const int64_t off = (int64_t)b * sb + (int64_t)h * sh + 8 * j;
+  const __nv_bfloat16* x = is_v ? v : k;
+  float sm[8], mx[8], mn[8], qm = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    sm[e] = 0.f;
+    mx[e] = -INFINITY;
+    mn[e] = INFINITY;
+  }
+  for (int r = tt >> 3; r < S; r += 32) {
+    const bool two = r + 16 < S;
+    float a[2][8], c[2][8];
+    load8(x + off + (int64_t)r * ss, c[0]);
+    if (two) load8(x + off + (int64_t)(r + 16) * ss, c[1]);
+    if (!is_v) {
+      load8(q + off + (int64_t)r * ss, a[0]);
+      if (two) load8(q + off + (int64_t)(r + 16) * ss, a[1]);
+    }
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (m == 1 && !two) break;   // fixed summation order per thread: row r, then r + 16
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (!is_v) qm = fmaxf(qm, fabsf(a[m][e]));
+        sm[e] += c[m][e];
+        mx[e] = fmaxf(mx[e], c[m][e]);
+        mn[e] = fminf(mn[e], c[m][e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+      sm[e] += __shfl_xor_sync(0xffffffffu, sm[e], o);
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], o));
+      mn[e] = fminf(mn[e], __shfl_xor_sync(0xffffffffu, mn[e], o));
+    }
+  }
+  if (lane < 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      part[w][0][8 * lane + e] = sm[e];
+      part[w][1][8 * lane + e] = mx[e];
+      part[w][2][8 * lane + e] = mn[e];
+    }
+  }
+  qm = warp_max(qm);
+  if (lane == 0 && w < 4) qred[w] = qm;
+  __syncthreads();
+  float am = 0.f;
+  if (t < 128) {   // t < 64: column t of k; 64 <= t < 128: column t - 64 of v
+    const int c = t & 63, w0 = t < 64 ? 0 : 4;
+    float su = 0.f, xx = -INFINITY, nn = INFINITY;
+    for (int ww = w0; ww < w0 + 4; ++ww) {
+      su += part[ww][0][c];
+      xx = fmaxf(xx, part[ww][1][c]);
+      nn = fminf(nn, part[ww][2][c]);
+    }
+    const float mean = __fdiv_rn(su, (float)S);
+    stats[(int64_t)head * 128 + t] = mean;
+    am = fmaxf(fabsf(xx - mean), fabsf(nn - mean));
+  }
+  am = warp_max(am);
+  if (lane == 0 && w < 4) ared[w] = am;   // warps 0-1: k columns, 2-3: v columns
+  __syncthreads();
+  if (t < 3) {
+    const float m = t == 0 ? fmaxf(fmaxf(qred[0], qred[1]), fmaxf(qred[2], qred[3]))
+                           : fmaxf(ared[2 * (t - 1)], ared[2 * (t - 1) + 1]);
+    atomicMax(reinterpret_cast<unsigned int*>(amax3) + t, __float_as_uint(m));
+  }
+}
+
 __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __restrict__ q,
                                                         const __nv_bfloat16* __restrict__ k,
                                                         const __nv_bfloat16* __restrict__ v, int64_t sb,
@@ -1529,13 +1618,20 @@ __global__ void __launch_bounds__(256, 3) attn_pack_kernel(const __nv_bfloat16* 
   const uint32_t sbo_kv = (uint32_t)(g.skp / 32) * 128u;
   const int nvb = (S + 15) / 16;
   uint4* vst = reinterpret_cast<uint4*>(vstage[w]);
-  for (int tb = w; tb < nvb; tb += 8) {
+  uint4 vnext[4];   // the next token block's rows, loaded while this one is quantized
+  auto vload = [&](int tb) {
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const int rr = 4 * p + (lane >> 3), r = tb * 16 + rr, c8 = lane & 7;
-      vst[rr * 8 + c8] = r < S ? __ldg(reinterpret_cast<const uint4*>(v + hoff + (int64_t)r * ss + 8 * c8))
-                               : make_uint4(0, 0, 0, 0);
+      vnext[p] = (tb < nvb && r < S) ? __ldg(reinterpret_cast<const uint4*>(v + hoff + (int64_t)r * ss + 8 * c8))
+                                     : make_uint4(0, 0, 0, 0);
     }
+  };
+  vload(w);
+  for (int tb = w; tb < nvb; tb += 8) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) vst[(4 * p + (lane >> 3)) * 8 + (lane & 7)] = vnext[p];
+    vload(tb + 8);
     __syncwarp();
     float x0[16], x1[16];
     const float m0 = mu[64 + 2 * lane], m1 = mu[64 + 2 * lane + 1];
@@ -2224,12 +2320,17 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
     stats = reinterpret_cast<float*>(ws + w.off_stats);
     amax3 = reinterpret_cast<float*>(ws + w.off_amax);
     if (cudaMemsetAsync(amax3, 0, 16, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4: memset failed");
-    const int D8 = (int)D / 8, rpi = 256 / D8;
-    const int smem = 32 % D8 == 0 ? 8 * 6 * (int)D * 4 : 6 * rpi * (int)D * 4;
-    cudaError_t e = cudaFuncSetAttribute(attn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
-                                                           (int)D, D <= 64 ? 64 : 128, stats, amax3);
+    if (D == 64) {
+      attn_stats64_kernel<<<(unsigned)(B * H), 256, 0, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
+                                                            stats, amax3);
+    } else {
+      const int D8 = (int)D / 8, rpi = 256 / D8;
+      const int smem = 32 % D8 == 0 ? 8 * 6 * (int)D * 4 : 6 * rpi * (int)D * 4;
+      cudaError_t e = cudaFuncSetAttribute(attn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
+                                                             (int)D, D <= 64 ? 64 : 128, stats, amax3);
+    }
     if (int st = launch_status("vf4_attn_nvfp4 (statistics)")) return st;
   }
   if (fused)
