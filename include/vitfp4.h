@@ -206,6 +206,19 @@ VF4_API int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* v, 
                                    int64_t stride_s, float scale, void* out, int64_t out_stride_b,
                                    int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
 
+/* Token embedding of the ViT forward around the (bf16) patch-projection GEMM.  No kernel counterpart
+ * in the reference: timm's PatchEmbed runs a strided Conv2d, then the model does
+ * torch.cat([cls, patches]) + pos_embed (vit.py / timm VisionTransformer._pos_embed).
+ * vf4_patchify: images (B, C, H, W) bf16 contiguous (W % 8 == 0, H and W multiples of p) ->
+ *   out (B * (H/p) * (W/p), k_pad) bf16, row = one patch with its C*p*p values in (c, i, j) order
+ *   (the Conv2d weight's flattening) and zeros up to k_pad (>= C*p*p, a multiple of 8).
+ * vf4_embed_tokens: y (B, T-1, D) patch projections, cls (D,), pos (T, D) -> x (B, T, D) with
+ *   x[:, 0] = cls + pos[0] and x[:, 1:] = y + pos[1:], each sum rounded once to bf16 (as cat + add). */
+VF4_API int vf4_patchify(const void* images, int64_t B, int64_t C, int64_t H, int64_t W, int64_t p, int64_t k_pad,
+                         void* out, vf4_stream_t stream);
+VF4_API int vf4_embed_tokens(const void* y, const void* cls, const void* pos, int64_t B, int64_t T, int64_t D, void* x,
+                             vf4_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -390,3 +390,29 @@ def ln_cast(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float,
               _ptr(gs_in), _ptr(packed), _ptr(sf), _ptr(gs_out), _stream())
     _launched(1 if gs_in is not None else 3)
     return packed, sf, (gs_out if gs_in is None else gs_in), (x if y is None else x_out)
+
+
+def patchify(images: torch.Tensor, patch: int, k_pad: int) -> torch.Tensor:
+    """(B, C, H, W) bf16 images -> (B * H/p * W/p, k_pad) bf16 patch rows in the Conv2d weight's
+    (c, i, j) order, zero-padded from C*p*p to k_pad columns (16-byte rows for the GEMM)."""
+    _need_cuda(images)
+    x = images.contiguous()
+    B, C, H, W = x.shape
+    out = torch.empty((B * (H // patch) * (W // patch), k_pad), dtype=torch.bfloat16, device=x.device)
+    _lib.call("vf4_patchify", _ptr(x), B, C, H, W, patch, k_pad, _ptr(out), _stream())
+    _launched()
+    return out
+
+
+def embed_tokens(y: torch.Tensor, cls: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    """(B, T-1, D) patch projections, (D,) class token, (T, D) position embedding -> (B, T, D)
+    = [cls + pos[0]; y + pos[1:]] in bf16 (torch.cat + add in one pass)."""
+    _need_cuda(y, cls, pos)
+    yb = y.contiguous()
+    B, P, D = yb.shape
+    c = cls.reshape(D).to(torch.bfloat16).contiguous()
+    p = pos.reshape(P + 1, D).to(torch.bfloat16).contiguous()
+    out = torch.empty((B, P + 1, D), dtype=torch.bfloat16, device=y.device)
+    _lib.call("vf4_embed_tokens", _ptr(yb), _ptr(c), _ptr(p), B, P + 1, D, _ptr(out), _stream())
+    _launched()
+    return out

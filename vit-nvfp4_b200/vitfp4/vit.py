@@ -143,9 +143,25 @@ class PatchEmbed(nn.Module):
         B, C, Hh, Ww = x.shape
         p = self.patch
         g_h, g_w = Hh // p, Ww // p
-        patches = x.reshape(B, C, g_h, p, g_w, p).permute(0, 2, 4, 1, 3, 5).reshape(B, g_h * g_w, C * p * p)
+        K = C * p * p
+        if x.is_cuda and x.dtype == torch.bfloat16 and Ww % 8 == 0:
+            # CUDA unfold into rows padded to a multiple of 8 values (16-byte rows keep cuBLAS on its
+            # sm_100 kernels; the zero columns meet zero weight columns)
+            from .nvfp4 import ops
+            kp = (K + 7) // 8 * 8
+            patches = ops.patchify(x, p, kp)
+            return F.linear(patches, self._weight_padded(kp), self.proj.bias).reshape(B, g_h * g_w, -1)
+        patches = x.reshape(B, C, g_h, p, g_w, p).permute(0, 2, 4, 1, 3, 5).reshape(B, g_h * g_w, K)
         w = self.proj.weight.reshape(self.proj.out_channels, -1)
         return F.linear(patches, w, self.proj.bias)
+
+    def _weight_padded(self, kp: int) -> torch.Tensor:
+        w = self.proj.weight
+        key = (w.data_ptr(), 0 if w.is_inference() else w._version, w.dtype, kp)
+        if getattr(self, "_wp_key", None) != key:
+            self._wp = F.pad(w.detach().reshape(w.shape[0], -1), (0, kp - w[0].numel())).contiguous()
+            self._wp_key = key
+        return self._wp
 
 
 class VisionTransformer(nn.Module):
@@ -162,8 +178,12 @@ class VisionTransformer(nn.Module):
 
     def forward_features(self, x):
         x = self.patch_embed(x)
-        x = torch.cat([self.cls_token.expand(x.shape[0], -1, -1).to(x.dtype), x], dim=1)
-        x = x + self.pos_embed.to(x.dtype)
+        if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0:
+            from .nvfp4 import ops
+            x = ops.embed_tokens(x, self.cls_token, self.pos_embed)   # cat + add, one pass
+        else:
+            x = torch.cat([self.cls_token.expand(x.shape[0], -1, -1).to(x.dtype), x], dim=1)
+            x = x + self.pos_embed.to(x.dtype)
         for blk in self.blocks:
             x = blk(x)
         return self.norm(x)
