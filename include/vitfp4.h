@@ -206,6 +206,19 @@ VF4_API int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* v, 
                                    int64_t stride_s, float scale, void* out, int64_t out_stride_b,
                                    int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
 
+/* vf4_cast_nvfp4 (six rule, bf16) of an operand whose rows arrive in two parts per image: x_main
+ * (n_img, rows_main, K) and x_tail (n_img, rows_tail, K), both contiguous; output row
+ * i * (rows_main + rows_tail) + t takes main row t, then the tail rows follow.  gs NULL: dynamic
+ * global over both parts into gs_out (the amax of the assembled tensor); otherwise gs is used.  Codes
+ * and scales equal vf4_cast_nvfp4 of the assembled (n_img * (rows_main + rows_tail), K) tensor.  The
+ * attention output of a query range split at a multiple of 128 (the bf16 route runs cuDNN on
+ * queries [0, 128 k) and on the few remaining ones separately) goes to the proj GEMM this way
+ * without being copied into one tensor.  No counterpart in the reference (its proj QuantLinear
+ * casts the one SDPA output: nvfp4/gemm.py:32-38). */
+VF4_API int vf4_cast_nvfp4_split(const void* x_main, int64_t rows_main, const void* x_tail, int64_t rows_tail,
+                                 int64_t n_img, int64_t K, const float* gs, float* gs_out, uint8_t* out_packed,
+                                 uint8_t* out_sf_swizzled, vf4_stream_t stream);
+
 /* Token embedding of the ViT forward around the (bf16) patch-projection GEMM.  No kernel counterpart
  * in the reference: timm's PatchEmbed runs a strided Conv2d, then the model does
  * torch.cat([cls, patches]) + pos_embed (vit.py / timm VisionTransformer._pos_embed).

@@ -223,6 +223,35 @@ def test_fused_block_matches_unfused_block(attn):
     assert _cos(a, b) >= 0.999, _cos(a, b)
 
 
+@pytest.mark.parametrize("S", [257, 264])
+def test_fused_block_split_query_attention(S):
+    """bf16 route with S = 128 k + (1..16): the fused block runs cuDNN on queries [0, 128 k) and on the
+    rest separately and casts both parts into one proj operand; it equals the per-module block."""
+    from vitfp4.ptq import FusedNVFP4Block
+    torch.manual_seed(6)
+    x = torch.randn(4, S, 384, device="cuda").bfloat16()
+    with torch.inference_mode():
+        model = _convert(_small_vit(depth=1), "bf16")
+        blk = model.blocks[0]
+        a = blk(x)
+        a = blk(x)
+        b = FusedNVFP4Block(blk)(x)
+    assert _cos(a, b) >= 0.999, _cos(a, b)
+
+
+@pytest.mark.parametrize("gs", [None, 0.003])
+def test_cast_split_equals_cast_of_concatenation(gs):
+    from vitfp4.nvfp4 import ops
+    torch.manual_seed(7)
+    main = (torch.randn(6, 256, 1024, device="cuda") * 3).bfloat16()
+    tail = (torch.randn(6, 1, 1024, device="cuda") * 5).bfloat16()
+    g = None if gs is None else torch.tensor(gs, device="cuda")
+    p1, s1, g1 = ops.cast_split(main, tail, gs=g)
+    p2, s2, _, g2 = ops.cast(torch.cat([main, tail], 1).reshape(-1, 1024), g, "six")
+    torch.cuda.synchronize()
+    assert torch.equal(g1, g2) and torch.equal(p1, p2) and torch.equal(s1, s2)
+
+
 @pytest.mark.parametrize("attn", ["bf16", "nvfp4"])
 def test_fused_model_accuracy_matches_unfused(attn):
     """Whole model: FP4 is discontinuous (a one-ulp LayerNorm difference can move an E4M3 block scale

@@ -188,6 +188,45 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
   }
 }
 
+// Cast of row groups into interleaved rows of one NVFP4 operand: input row t of group g
+// (x + (g * rows_in + t) * K, bf16, groups contiguous) becomes output row g * rows_out + row_off + t.
+// Same per-block arithmetic as cast_kernel (six rule, exact encoder); the scale bytes of an aligned
+// lane quad merge into one word of the to_blocked layout.  Padding rows are not touched here.
+__global__ void __launch_bounds__(256) cast_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows_total,
+                                                        int64_t rows_in, int64_t K, const float* __restrict__ gs_ptr,
+                                                        int64_t rows_out, int64_t row_off,
+                                                        uint8_t* __restrict__ out_packed, uint8_t* __restrict__ sf_swz) {
+  const int64_t nb = K / 16;
+  const int64_t nb4 = (nb + 3) & ~int64_t(3);
+  const int64_t ncb = nb4 >> 2;
+  const int64_t total = rows_total * nb4;
+  const float gs = *gs_ptr;
+  const float s_enc = __fdiv_rn(1.0f, gs);
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x - lane; t0 < total; t0 += stride) {
+    const int64_t t = t0 + lane;
+    const bool in_grid = t < total;
+    const int64_t r = t / nb4, blk = t - r * nb4;
+    const int64_t grp = r / rows_in;
+    const int64_t orow = grp * rows_out + row_off + (r - grp * rows_in);
+    uint32_t sf = 0;
+    if (in_grid && blk < nb) {
+      float v[16];
+      load16<__nv_bfloat16>(x + r * K + blk * 16, v);
+      BlockQ q = quantize_block<false>(v, gs, s_enc, 0x1p17f);
+      *reinterpret_cast<uint64_t*>(out_packed + orow * (K / 2) + blk * 8) = q.packed;
+      sf = q.sf;
+    }
+    uint32_t w = sf << (8 * (blk & 3));
+    w |= __shfl_xor_sync(0xffffffffu, w, 1);
+    w |= __shfl_xor_sync(0xffffffffu, w, 2);
+    if (in_grid && (blk & 3) == 0)
+      *reinterpret_cast<uint32_t*>(sf_swz + ((orow >> 7) * ncb + (blk >> 2)) * 512 + (orow & 31) * 16 +
+                                   ((orow >> 5) & 3) * 4) = w;
+  }
+}
+
 __global__ void pack_kernel(const uint8_t* __restrict__ codes, int64_t n_out,
                             uint8_t* __restrict__ out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_out;
@@ -636,6 +675,47 @@ int vf4_to_blocked(const uint8_t* sf, int64_t R, int64_t C, uint8_t* out, vf4_st
   int64_t total = ((R + 127) & ~int64_t(127)) * ((C + 3) / 4);
   to_blocked_kernel<<<grid_for(total), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(sf, R, C, out);
   return launch_status("vf4_to_blocked");
+}
+
+int vf4_cast_nvfp4_split(const void* x_main, int64_t rows_main, const void* x_tail, int64_t rows_tail,
+                         int64_t n_img, int64_t K, const float* gs, float* gs_out, uint8_t* out_packed,
+                         uint8_t* out_sf_swizzled, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (n_img <= 0 || rows_main <= 0 || rows_tail <= 0 || K <= 0 || K % 64 != 0)
+    return fail(VF4_ERR_ARG, "vf4_cast_nvfp4_split: bad sizes (n=%lld main=%lld tail=%lld K=%lld)", (long long)n_img,
+                (long long)rows_main, (long long)rows_tail, (long long)K);
+  if (!x_main || !x_tail || !out_packed || !out_sf_swizzled || (!gs && !gs_out))
+    return fail(VF4_ERR_ARG, "vf4_cast_nvfp4_split: null pointer");
+  if (!aligned16(x_main) || !aligned16(x_tail) || (reinterpret_cast<uintptr_t>(out_packed) & 7u) ||
+      (reinterpret_cast<uintptr_t>(out_sf_swizzled) & 3u))
+    return fail(VF4_ERR_ALIGN, "vf4_cast_nvfp4_split: misaligned pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float* use_gs = gs;
+  if (!gs) {   // dynamic global over both parts
+    if (cudaMemsetAsync(gs_out, 0, sizeof(float), s) != cudaSuccess)
+      return fail(VF4_ERR_CUDA, "vf4_cast_nvfp4_split: memset failed");
+    dispatch_amax<__nv_bfloat16>(x_main, n_img * rows_main, K, K, 0, nullptr, gs_out, s);
+    dispatch_amax<__nv_bfloat16>(x_tail, n_img * rows_tail, K, K, 0, nullptr, gs_out, s);
+    global_scale_kernel<<<1, 32, 0, s>>>(gs_out, 6.f * 448.f, gs_out);
+    use_gs = gs_out;
+  } else if (gs_out && gs_out != gs) {
+    if (cudaMemcpyAsync(gs_out, gs, sizeof(float), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return fail(VF4_ERR_CUDA, "vf4_cast_nvfp4_split: gs copy failed");
+  }
+  const int64_t rows_out = rows_main + rows_tail, M = n_img * rows_out;
+  const int64_t ncb = K / 64;
+  if (M % 128) {   // scale words of the last row block's padding rows stay zero
+    if (cudaMemsetAsync(out_sf_swizzled + (M / 128) * ncb * 512, 0, (size_t)ncb * 512, s) != cudaSuccess)
+      return fail(VF4_ERR_CUDA, "vf4_cast_nvfp4_split: memset failed");
+  }
+  const int64_t nb4 = K / 16;
+  cast_rows_kernel<<<grid_for(n_img * rows_main * nb4), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x_main), n_img * rows_main, rows_main, K, use_gs, rows_out, 0, out_packed,
+      out_sf_swizzled);
+  cast_rows_kernel<<<grid_for(n_img * rows_tail * nb4), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x_tail), n_img * rows_tail, rows_tail, K, use_gs, rows_out, rows_main,
+      out_packed, out_sf_swizzled);
+  return launch_status("vf4_cast_nvfp4_split");
 }
 
 }  // extern "C"

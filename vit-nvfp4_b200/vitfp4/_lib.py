@@ -41,6 +41,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_attn_workspace_size": [_L, _L, _L, _L],
     "vf4_attn_workspace_size_ex": [_L, _L, _L, _L, _I],
     "vf4_patchify": [_P, _L, _L, _L, _L, _L, _L, _P, _P],
+    "vf4_cast_nvfp4_split": [_P, _L, _P, _L, _L, _L, _P, _P, _P, _P, _P],
     "vf4_embed_tokens": [_P, _P, _P, _L, _L, _L, _P, _P],
     "vf4_attn_nvfp4": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _L, _P],
     "vf4_attn_nvfp4_ex": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _I, _P, _L, _P],

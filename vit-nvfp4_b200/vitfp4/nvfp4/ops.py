@@ -142,6 +142,26 @@ def cast(x: torch.Tensor, gs: torch.Tensor | None = None, block_select: str = "s
     return packed, sfs, sfl, (gs_out if gs_in is None else gs_in)
 
 
+def cast_split(x_main: torch.Tensor, x_tail: torch.Tensor, gs: torch.Tensor | None = None):
+    """NVFP4 cast (six) of an operand whose rows come in two parts per image: x_main (n, rows_main, K)
+    and x_tail (n, rows_tail, K) bf16; output row i * (rows_main + rows_tail) + t is main row t of
+    image i, the tail rows follow.  Same codes, scales and global as ``cast`` of the concatenated
+    (n, rows_main + rows_tail, K) tensor, without building it.  Returns (packed, sf_swizzled, gs)."""
+    _need_cuda(x_main, x_tail, gs)
+    a, b = x_main.contiguous(), x_tail.contiguous()
+    n, rm, K = a.shape
+    rt = b.shape[1]
+    M = n * (rm + rt)
+    packed = torch.empty((M, K // 2), dtype=torch.uint8, device=a.device)
+    sfs = torch.empty(sf_swizzled_numel(M, K), dtype=torch.uint8, device=a.device)
+    gs_in = None if gs is None else gs.reshape(()).to(torch.float32).contiguous()
+    gs_out = torch.empty((), dtype=torch.float32, device=a.device) if gs_in is None else None
+    _lib.call("vf4_cast_nvfp4_split", _ptr(a), rm, _ptr(b), rt, n, K, _ptr(gs_in), _ptr(gs_out), _ptr(packed),
+              _ptr(sfs), _stream())
+    _launched(2 if gs_in is not None else 5)
+    return packed, sfs, (gs_out if gs_in is None else gs_in)
+
+
 def pack_e2m1(codes: torch.Tensor) -> torch.Tensor:
     _need_cuda(codes)
     c = codes.contiguous()

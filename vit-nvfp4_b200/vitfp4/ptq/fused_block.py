@@ -55,6 +55,14 @@ class FusedNVFP4Block(nn.Module):
             from ..nvfp4.attention import quant_sdpa
             o = quant_sdpa(q, k, v, scale=a.scaling, qk=a._nvfp4_qk, pv=a._nvfp4_pv)
             return o.transpose(1, 2).reshape(B, S, H * D)
+        s_main = S // 128 * 128
+        if s_main >= 128 and 0 < S - s_main <= 16:
+            # cuDNN's SDPA pays for whole 128-query tiles (S = 257 costs 2.6x S = 256): run queries
+            # [0, s_main) and the few remaining ones as two calls over all keys -- each row's softmax
+            # is complete in either -- and hand both parts to the proj cast as they are
+            o1 = F.scaled_dot_product_attention(q[:, :, :s_main], k, v, scale=a.scaling)
+            o2 = F.scaled_dot_product_attention(q[:, :, s_main:], k, v, scale=a.scaling)
+            return o1.transpose(1, 2).reshape(B, s_main, H * D), o2.transpose(1, 2).reshape(B, S - s_main, H * D)
         return F.scaled_dot_product_attention(q, k, v, scale=a.scaling).transpose(1, 2).reshape(B, S, H * D)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -69,7 +77,12 @@ class FusedNVFP4Block(nn.Module):
         wp, wsf = qkv_l._packed_weight()
         qkv = ops.gemm(ap, asf, ag, wp, wsf, qkv_l.w_global_scale, bias=qkv_l.bias).reshape(B, S, -1)
         o = self._attention(qkv)
-        y = proj_l(o).reshape(B * S, C)
+        if isinstance(o, tuple):   # split query range: one NVFP4 operand from both parts, no concatenation
+            op, osf, og = ops.cast_split(o[0], o[1], gs=proj_l.x_global_scale)
+            wp2, wsf2 = proj_l._packed_weight()
+            y = ops.gemm(op, osf, og, wp2, wsf2, proj_l.w_global_scale, bias=proj_l.bias)
+        else:
+            y = proj_l(o).reshape(B * S, C)
         mlp: FusedNVFP4MLP = self.mlp
         if mlp.gx is None:   # first call: calibrate the MLP's static globals exactly as the module does
             x_mid = (x2 + self.ls1(y.reshape(B, S, C)).reshape(B * S, C))
