@@ -196,24 +196,27 @@ __global__ void __launch_bounds__(256) cast_rows_kernel(const __nv_bfloat16* __r
                                                         int64_t rows_in, int64_t K, const float* __restrict__ gs_ptr,
                                                         int64_t rows_out, int64_t row_off,
                                                         uint8_t* __restrict__ out_packed, uint8_t* __restrict__ sf_swz) {
-  const int64_t nb = K / 16;
-  const int64_t nb4 = (nb + 3) & ~int64_t(3);
-  const int64_t ncb = nb4 >> 2;
-  const int64_t total = rows_total * nb4;
+  // 32-bit indices (the entry point checks rows_total * K / 16 < 2^31); (row, blk) advanced by the
+  // grid stride without dividing, one 32-bit division per item for the row's group
+  const uint32_t nb = (uint32_t)(K / 16);
+  const uint32_t ncb = nb >> 2;
+  const uint32_t total = (uint32_t)rows_total * nb;
+  const uint32_t rin = (uint32_t)rows_in, rout = (uint32_t)rows_out, roff = (uint32_t)row_off;
   const float gs = *gs_ptr;
   const float s_enc = __fdiv_rn(1.0f, gs);
   const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x - lane; t0 < total; t0 += stride) {
-    const int64_t t = t0 + lane;
-    const bool in_grid = t < total;
-    const int64_t r = t / nb4, blk = t - r * nb4;
-    const int64_t grp = r / rows_in;
-    const int64_t orow = grp * rows_out + row_off + (r - grp * rows_in);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t t_first = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t d_row = stride / nb, d_blk = stride - d_row * nb;
+  uint32_t r = t_first / nb, blk = t_first - r * nb;
+  for (uint32_t t0 = t_first - lane; t0 < total; t0 += stride) {
+    const bool in_grid = t0 + lane < total;
+    const uint32_t grp = r / rin;
+    const int64_t orow = (int64_t)grp * rout + roff + (r - grp * rin);
     uint32_t sf = 0;
-    if (in_grid && blk < nb) {
+    if (in_grid) {
       float v[16];
-      load16<__nv_bfloat16>(x + r * K + blk * 16, v);
+      load16<__nv_bfloat16>(x + (int64_t)r * K + blk * 16, v);
       BlockQ q = quantize_block<false>(v, gs, s_enc, 0x1p17f);
       *reinterpret_cast<uint64_t*>(out_packed + orow * (K / 2) + blk * 8) = q.packed;
       sf = q.sf;
@@ -224,6 +227,12 @@ __global__ void __launch_bounds__(256) cast_rows_kernel(const __nv_bfloat16* __r
     if (in_grid && (blk & 3) == 0)
       *reinterpret_cast<uint32_t*>(sf_swz + ((orow >> 7) * ncb + (blk >> 2)) * 512 + (orow & 31) * 16 +
                                    ((orow >> 5) & 3) * 4) = w;
+    r += d_row;
+    blk += d_blk;
+    if (blk >= nb) {
+      blk -= nb;
+      ++r;
+    }
   }
 }
 
@@ -681,7 +690,8 @@ int vf4_cast_nvfp4_split(const void* x_main, int64_t rows_main, const void* x_ta
                          int64_t n_img, int64_t K, const float* gs, float* gs_out, uint8_t* out_packed,
                          uint8_t* out_sf_swizzled, vf4_stream_t stream) {
   if (int st = check_device()) return st;
-  if (n_img <= 0 || rows_main <= 0 || rows_tail <= 0 || K <= 0 || K % 64 != 0)
+  if (n_img <= 0 || rows_main <= 0 || rows_tail <= 0 || K <= 0 || K % 64 != 0 ||
+      n_img * (rows_main + rows_tail) * (K / 16) + 1024ll * 256 >= (1ll << 31))
     return fail(VF4_ERR_ARG, "vf4_cast_nvfp4_split: bad sizes (n=%lld main=%lld tail=%lld K=%lld)", (long long)n_img,
                 (long long)rows_main, (long long)rows_tail, (long long)K);
   if (!x_main || !x_tail || !out_packed || !out_sf_swizzled || (!gs && !gs_out))
