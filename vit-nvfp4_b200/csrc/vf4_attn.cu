@@ -280,26 +280,42 @@ __global__ void __launch_bounds__(256, 3) attn_stats64_kernel(const __nv_bfloat1
     mx[e] = -INFINITY;
     mn[e] = INFINITY;
   }
-  for (int r = tt >> 3; r < S; r += 32) {
-    const bool two = r + 16 < S;
-    float a[2][8], c[2][8];
-    load8(x + off + (int64_t)r * ss, c[0]);
-    if (two) load8(x + off + (int64_t)(r + 16) * ss, c[1]);
-    if (!is_v) {
-      load8(q + off + (int64_t)r * ss, a[0]);
-      if (two) load8(q + off + (int64_t)(r + 16) * ss, a[1]);
-    }
+  // rows tt/8 + 16 i; the raw 16-byte words of the next pair of rows are loaded before the current
+  // pair is accumulated (two pairs of loads in flight per thread), in the same summation order
+  auto fetch = [&](int r, uint4* cw, uint4* aw) {
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
-      if (m == 1 && !two) break;   // fixed summation order per thread: row r, then r + 16
+      const int rr = r + 16 * m;
+      const bool in = rr < S;
+      cw[m] = in ? __ldg(reinterpret_cast<const uint4*>(x + off + (int64_t)rr * ss)) : make_uint4(0, 0, 0, 0);
+      if (!is_v) aw[m] = in ? __ldg(reinterpret_cast<const uint4*>(q + off + (int64_t)rr * ss)) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 cw[2], aw[2], cn[2], an[2];
+  int r = tt >> 3;
+  fetch(r, cw, aw);
+  for (; r < S; r += 32) {
+    if (r + 32 < S) fetch(r + 32, cn, an);
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (r + 16 * m >= S) break;   // fixed summation order per thread: row r, then r + 16
+      const uint32_t cv[4] = {cw[m].x, cw[m].y, cw[m].z, cw[m].w}, av[4] = {aw[m].x, aw[m].y, aw[m].z, aw[m].w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        if (!is_v) qm = fmaxf(qm, fabsf(a[m][e]));
-        sm[e] += c[m][e];
-        mx[e] = fmaxf(mx[e], c[m][e]);
-        mn[e] = fminf(mn[e], c[m][e]);
+        const float c = (e & 1) ? __uint_as_float(cv[e >> 1] & 0xFFFF0000u) : __uint_as_float(cv[e >> 1] << 16);
+        if (!is_v) {
+          const float a = (e & 1) ? __uint_as_float(av[e >> 1] & 0xFFFF0000u) : __uint_as_float(av[e >> 1] << 16);
+          qm = fmaxf(qm, fabsf(a));
+        }
+        sm[e] += c;
+        mx[e] = fmaxf(mx[e], c);
+        mn[e] = fminf(mn[e], c);
       }
     }
+    cw[0] = cn[0];
+    cw[1] = cn[1];
+    aw[0] = an[0];
+    aw[1] = an[1];
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
