@@ -97,7 +97,9 @@ VF4_API int vf4_cast_nvfp4(const void* x, int dtype, int64_t M, int64_t K, int64
  * block runs around qlinear.py:42-47 / fused_mlp.py:47; the reference leaves it to torch):
  *   if y != NULL: x' = bf16(x + bf16(y * gamma)) (gamma NULL -> 1) is written to x_out (may be x)
  *   h = bf16(LayerNorm(x'; ln_w, ln_b, eps)) is cast to NVFP4 (six rule) with the static global gs,
- *   or, when gs == NULL, with the dynamic amax(|h|)/(6*448) written to gs_out (two passes).
+ *   or, when gs == NULL, with the dynamic amax(|h|)/(6*448) written to gs_out (two passes; the
+ *   first leaves each row's mean and rstd in the first 8 bytes of its out_packed row, which the
+ *   second reads and overwrites with the codes, so out_packed must not alias x or y).
  * x, y, x_out: (M, K) bf16 contiguous; gamma, ln_w, ln_b: (K,) bf16; K % 64 == 0, K <= 1280.
  * out_packed (M, K/2); out_sf swizzled (ceil128(M) x K/16, padding rows zeroed). */
 VF4_API int vf4_ln_cast_nvfp4(const void* x, const void* y, const void* gamma, void* x_out, const void* ln_w,

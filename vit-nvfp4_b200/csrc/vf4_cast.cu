@@ -331,32 +331,67 @@ static void dispatch_cast(const void* x, int64_t M, int64_t K, int64_t ld, const
 // One warp per row; lane l holds elements [256c + 8l, 256c + 8l + 8) of chunk c (16-byte
 // loads, coalesced), so an NVFP4 block of 16 is a lane pair.  Rounding points mirror the
 // unfused reference ops on bf16 tensors:  x' = bf16(x + bf16(y * gamma)),
-// h = bf16((x' - mean) * rstd * w + b), then the six-rule quantizer on h.
-//   kMode 0: write x' (if kRes) and atomically max |h| into amax_out (dynamic global scale)
+// h = bf16((x - mean) * rstd * w + b), then the six-rule quantizer on h.
+//   kMode 0: write x' (if kRes), atomically max |h| into amax_out (dynamic global scale) and
+//            leave the row's {mean, rstd} in the first 8 bytes of its code row, which the
+//            kMode 2 pass reads before it overwrites them with the row's codes
 //   kMode 1: write x' (if kRes) and quantize h with the global scale *gs
+//   kMode 2: quantize h with *gs and the row statistics left by a kMode 0 pass (no reductions)
+// The kernels are issue-bound, so the parameters sit in shared memory as fp32 (no per-row
+// unpacking) and the modes that reduce keep the row as fp32 pairs between the reductions.
 // ---------------------------------------------------------------------------------------
 VF4_DEV float bf16_bits_lo(uint32_t w) { return __uint_as_float(w << 16); }
 VF4_DEV float bf16_bits_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Resident CTAs per SM (launch bound and grid) and whether the row is kept as fp32 pairs between
+// the reductions; the modes that reduce keep it, at 16 warps per SM (measured at ViT-L/14 b1024:
+// 24 or 32 warps with spills or re-unpacking are 2-3% slower), except the residual form at
+// K > 1024, whose held row would not fit in 128 registers next to the prefetched x and y.
 template <int NC, bool kRes, int kMode>
-__global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_bfloat16* __restrict__ x,
-                                                      const __nv_bfloat16* __restrict__ y,
-                                                      const __nv_bfloat16* __restrict__ gamma,
-                                                      __nv_bfloat16* __restrict__ x_out,
-                                                      const __nv_bfloat16* __restrict__ ln_w,
-                                                      const __nv_bfloat16* __restrict__ ln_b, float eps,
-                                                      int64_t M, int K, const float* __restrict__ gs_ptr,
-                                                      float* __restrict__ amax_out,
-                                                      uint8_t* __restrict__ out_packed,
-                                                      uint8_t* __restrict__ out_sf) {
-  // LayerNorm weight, bias and LayerScale as bf16 pairs in shared memory (16-byte chunks)
-  __shared__ uint4 s_par[3][NC * 32];
-  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
-    s_par[0][i] = __ldg(reinterpret_cast<const uint4*>(ln_w) + i);
-    s_par[1][i] = __ldg(reinterpret_cast<const uint4*>(ln_b) + i);
-    if constexpr (kRes)
-      s_par[2][i] = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma) + i)
-                          : make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+struct LnCfg {
+  static constexpr int kMinBlocks = kMode == 2 ? 3 : 2;
+  static constexpr bool kHold = kMode != 2 && !(kRes && NC > 4);
+};
+
+// element pair i of a lane's chunk as fp32: held, or unpacked from the raw bf16 words
+template <bool kHold>
+VF4_DEV unsigned long long ln_x2(const unsigned long long* vc, const uint4& xc, int i) {
+  if constexpr (kHold) return vc[i];
+  else return bf16x2_to_f32x2(i == 0 ? xc.x : i == 1 ? xc.y : i == 2 ? xc.z : xc.w);
+}
+
+template <int NC, bool kRes, int kMode>
+__global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_cast_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ gamma,
+    __nv_bfloat16* __restrict__ x_out, const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
+    float eps, int64_t M, int K, const float* __restrict__ gs_ptr, float* __restrict__ amax_out,
+    uint8_t* out_packed, uint8_t* __restrict__ out_sf) {
+  static_assert(!(kRes && kMode == 2), "the statistics pass runs without the residual");
+  // s_wb[(4c + j) * 32 + l] = {w[e], w[e+1], b[e], b[e+1]}, e = 256c + 8l + 2j
+  // s_g [(2c + j) * 32 + l] = {g[e], .., g[e+3]},          e = 256c + 8l + 4j
+  // (consecutive lanes read consecutive 16 bytes: conflict-free)
+  __shared__ float4 s_wb[NC * 128];
+  __shared__ float4 s_g[kRes ? NC * 64 : 1];
+  for (int i = threadIdx.x; i < NC * 128; i += blockDim.x) {
+    const int e = 256 * (i >> 7) + 8 * (i & 31) + 2 * ((i >> 5) & 3);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < K) {
+      v.x = __bfloat162float(ln_w[e]);
+      v.y = __bfloat162float(ln_w[e + 1]);
+      v.z = __bfloat162float(ln_b[e]);
+      v.w = __bfloat162float(ln_b[e + 1]);
+    }
+    s_wb[i] = v;
+  }
+  if constexpr (kRes) {
+    for (int i = threadIdx.x; i < NC * 64; i += blockDim.x) {
+      const int e = 256 * (i >> 6) + 8 * (i & 31) + 4 * ((i >> 5) & 1);
+      float4 v = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (gamma && e < K)
+        v = make_float4(__bfloat162float(gamma[e]), __bfloat162float(gamma[e + 1]), __bfloat162float(gamma[e + 2]),
+                        __bfloat162float(gamma[e + 3]));
+      s_g[i] = v;
+    }
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -364,39 +399,44 @@ __global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_b
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t Mp = (M + 127) & ~int64_t(127);
   const int ncb = K / 64;
+  const int64_t code_ld = K / 2;
   float gs = 1.f, s_enc = 1.f;
-  if constexpr (kMode == 1) {
+  if constexpr (kMode != 0) {
     gs = *gs_ptr;
     s_enc = __fdiv_rn(1.0f, gs);
   }
-  // Raw bf16 words of the next row are loaded while the current row is processed.
-  constexpr int kAhead = 1;
-  uint4 nx[NC], ny[NC], nx2[NC];
-  auto fetch = [&](int64_t row, uint4* bx, uint4* by) {
+  // Raw bf16 words (and, in kMode 2, the row statistics) of the next row are loaded while the
+  // current row is processed.
+  uint4 nx[NC], ny[kRes ? NC : 1];
+  float2 nst = make_float2(0.f, 0.f);
+  auto fetch = [&](int64_t row) {
+    if (row < M) {
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int e0 = 256 * c + 8 * lane;
-      if (row < M && e0 < K) {
-        bx[c] = __ldg(reinterpret_cast<const uint4*>(x + row * K + e0));
-        if constexpr (kRes) by[c] = __ldg(reinterpret_cast<const uint4*>(y + row * K + e0));
+      for (int c = 0; c < NC; ++c) {
+        const int e0 = 256 * c + 8 * lane;
+        if (e0 < K) {
+          nx[c] = __ldg(reinterpret_cast<const uint4*>(x + row * K + e0));
+          if constexpr (kRes) ny[c] = __ldg(reinterpret_cast<const uint4*>(y + row * K + e0));
+        }
       }
+      // the statistics share their bytes with this row's codes, which this kernel writes:
+      // a coherent load, not the read-only path
+      if constexpr (kMode == 2) nst = __ldcg(reinterpret_cast<const float2*>(out_packed + row * code_ld));
     }
   };
   float lane_amax = 0.f;
-  fetch(warp_g, nx, ny);
-  if constexpr (kAhead == 2) fetch(warp_g + nwarps, nx2, ny);
+  fetch(warp_g);
   for (int64_t row = warp_g; row < Mp; row += nwarps) {
-    uint4 cx[NC], cy[NC];
+    uint4 cx[NC], cy[kRes ? NC : 1];
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       cx[c] = nx[c];
       if constexpr (kRes) cy[c] = ny[c];
-      if constexpr (kAhead == 2) nx[c] = nx2[c];
     }
-    if constexpr (kAhead == 2) fetch(row + 2 * nwarps, nx2, ny);
-    else fetch(row + nwarps, nx, ny);
+    const float2 cst = nst;
+    fetch(row + nwarps);
     if (row >= M) {  // zero the scale padding rows of the last 128-row tile
-      if constexpr (kMode == 1) {
+      if constexpr (kMode != 0) {
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
           const int e0 = 256 * c + 8 * lane;
@@ -409,58 +449,73 @@ __global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_b
       }
       continue;
     }
-    // r: this lane's 8*NC values as raw bf16 pairs (after the residual step when kRes); the
-    // fp32 pairs are re-derived from them in each pass, which keeps the register count low
-    // enough for 8 resident warps per scheduler
-    uint32_t r[NC][4];
-    unsigned long long sum2 = f32x2_pack(0.f, 0.f);
+    float mean, rstd;
+    // v: the row as fp32 pairs (after the residual step when kRes), kept between the reductions
+    constexpr bool kHold = LnCfg<NC, kRes, kMode>::kHold;
+    unsigned long long v[kHold ? NC : 1][4];
+    if constexpr (kMode == 2) {
+      mean = cst.x;
+      rstd = cst.y;
+      __syncwarp();   // every lane has read the statistics before any lane overwrites them
+    } else {
+      unsigned long long sum2 = f32x2_pack(0.f, 0.f);
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int e0 = 256 * c + 8 * lane;
-      if (e0 < K) {
-        const uint32_t xw[4] = {cx[c].x, cx[c].y, cx[c].z, cx[c].w};
-        if constexpr (kRes) {
-          const uint32_t yw[4] = {cy[c].x, cy[c].y, cy[c].z, cy[c].w};
-          const uint4 gv = s_par[2][e0 / 8];
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      for (int c = 0; c < NC; ++c) {
+        const int e0 = 256 * c + 8 * lane;
+        if (e0 < K) {
+          const uint32_t xw[4] = {cx[c].x, cx[c].y, cx[c].z, cx[c].w};
+          if constexpr (kRes) {
+            const uint32_t yw[4] = {cy[c].x, cy[c].y, cy[c].z, cy[c].w};
+            uint32_t rw[4];
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const float4 g4 = s_g[(2 * c + jj) * 32 + lane];
+              const unsigned long long g2[2] = {f32x2_pack(g4.x, g4.y), f32x2_pack(g4.z, g4.w)};
+#pragma unroll
+              for (int t = 0; t < 2; ++t) {
+                const int i = 2 * jj + t;
+                // x' = bf16(x + bf16(y * gamma))
+                const uint32_t yg = bf16x2_round(mul_f32x2(bf16x2_to_f32x2(yw[i]), g2[t]));
+                rw[i] = bf16x2_round(add_f32x2(bf16x2_to_f32x2(xw[i]), bf16x2_to_f32x2(yg)));
+                if constexpr (kHold) v[c][i] = bf16x2_to_f32x2(rw[i]);
+              }
+            }
+            *reinterpret_cast<uint4*>(x_out + row * K + e0) = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+            if constexpr (!kHold) cx[c] = make_uint4(rw[0], rw[1], rw[2], rw[3]);   // x' replaces x
+          } else if constexpr (kHold) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = bf16x2_to_f32x2(xw[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sum2 = add_f32x2(sum2, ln_x2<kHold>(v[kHold ? c : 0], cx[c], i));
+        }
+      }
+      float s0, s1;
+      f32x2_unpack(sum2, &s0, &s1);
+      float sum = s0 + s1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      mean = sum / (float)K;
+      const unsigned long long nm2 = f32x2_pack(-mean, -mean);
+      unsigned long long sq2 = f32x2_pack(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < NC; ++c)
+        if (256 * c + 8 * lane < K) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            // x' = bf16(x + bf16(y * gamma))
-            const uint32_t yg = bf16x2_round(mul_f32x2(bf16x2_to_f32x2(yw[i]), bf16x2_to_f32x2(gw[i])));
-            r[c][i] = bf16x2_round(add_f32x2(bf16x2_to_f32x2(xw[i]), bf16x2_to_f32x2(yg)));
+            const unsigned long long d2 = add_f32x2(ln_x2<kHold>(v[kHold ? c : 0], cx[c], i), nm2);
+            sq2 = fma_f32x2(d2, d2, sq2);
           }
-          *reinterpret_cast<uint4*>(x_out + row * K + e0) = make_uint4(r[c][0], r[c][1], r[c][2], r[c][3]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) r[c][i] = xw[i];
         }
+      f32x2_unpack(sq2, &s0, &s1);
+      float sq = s0 + s1;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sum2 = add_f32x2(sum2, bf16x2_to_f32x2(r[c][i]));
-      }
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      rstd = rsqrtf(sq / (float)K + eps);
+      if constexpr (kMode == 0)
+        if (lane == 0) *reinterpret_cast<float2*>(out_packed + row * code_ld) = make_float2(mean, rstd);
     }
-    float s0, s1;
-    f32x2_unpack(sum2, &s0, &s1);
-    float sum = s0 + s1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / (float)K;
-    const unsigned long long nmean2 = f32x2_pack(-mean, -mean);
-    unsigned long long sq2 = f32x2_pack(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < NC; ++c)
-      if (256 * c + 8 * lane < K) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const unsigned long long d2 = add_f32x2(bf16x2_to_f32x2(r[c][i]), nmean2);
-          sq2 = fma_f32x2(d2, d2, sq2);
-        }
-      }
-    f32x2_unpack(sq2, &s0, &s1);
-    float sq = s0 + s1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float rstd = rsqrtf(sq / (float)K + eps);
-    const unsigned long long rstd2 = f32x2_pack(rstd, rstd);
+    const unsigned long long nmean2 = f32x2_pack(-mean, -mean), rstd2 = f32x2_pack(rstd, rstd);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int e0 = 256 * c + 8 * lane;
@@ -468,19 +523,29 @@ __global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_b
       float h[8];
       float am = 0.f;
       if (in) {
-        const uint4 wv = s_par[0][e0 / 8], bv = s_par[1][e0 / 8];
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          // h = bf16((x - mean) * rstd * w + b)
-          const unsigned long long d2 = add_f32x2(bf16x2_to_f32x2(r[c][i]), nmean2);
-          const uint32_t hb = bf16x2_round(
-              fma_f32x2(mul_f32x2(d2, rstd2), bf16x2_to_f32x2(ww[i]), bf16x2_to_f32x2(bw[i])));
-          h[2 * i] = __uint_as_float(hb << 16);
-          h[2 * i + 1] = __uint_as_float(hb & 0xFFFF0000u);
+          const float4 wb = s_wb[(4 * c + i) * 32 + lane];
+          // h = (x - mean) * rstd * w + b, rounded to bf16 (kMode 0 rounds the maximum only:
+          // rounding is monotone, so max |bf16(h)| = bf16(max |h|))
+          const unsigned long long hf = fma_f32x2(mul_f32x2(add_f32x2(ln_x2<kHold>(v[kHold ? c : 0], cx[c], i), nmean2), rstd2), f32x2_pack(wb.x, wb.y),
+                                                  f32x2_pack(wb.z, wb.w));
+          if constexpr (kMode == 0) {
+            float h0, h1;
+            f32x2_unpack(hf, &h0, &h1);
+            am = max3f(am, fabsf(h0), fabsf(h1));
+          } else {
+            const uint32_t hb = bf16x2_round(hf);
+            h[2 * i] = __uint_as_float(hb << 16);
+            h[2 * i + 1] = __uint_as_float(hb & 0xFFFF0000u);
+          }
         }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(h[i]));
+        if constexpr (kMode != 0) {
+          am = max3f(fabsf(h[0]), fabsf(h[1]), fabsf(h[2]));
+          am = max3f(am, fabsf(h[3]), fabsf(h[4]));
+          am = max3f(am, fabsf(h[5]), fabsf(h[6]));
+          am = fmaxf(am, fabsf(h[7]));
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) h[i] = 0.f;
@@ -492,7 +557,7 @@ __global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_b
         float dec;
         const uint32_t sf = six_scale(bam, s_enc, gs, &dec);
         const uint32_t codes = encode8_bracket(h, dec, 0x1p17f);   // h is bf16-rounded
-        if (in) *reinterpret_cast<uint32_t*>(out_packed + row * (K / 2) + e0 / 2) = codes;
+        if (in) *reinterpret_cast<uint32_t*>(out_packed + row * code_ld + e0 / 2) = codes;
         // scale bytes of SF columns 16c + 4g .. +3 live in lanes 8g, 8g+2, 8g+4, 8g+6
         uint32_t b1 = __shfl_down_sync(0xffffffffu, sf, 2);
         uint32_t b2 = __shfl_down_sync(0xffffffffu, sf, 4);
@@ -508,26 +573,35 @@ __global__ void __launch_bounds__(256, kRes ? 2 : 4) ln_cast_kernel(const __nv_b
   if constexpr (kMode == 0) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lane_amax = fmaxf(lane_amax, __shfl_xor_sync(0xffffffffu, lane_amax, o));
+    lane_amax = __bfloat162float(__float2bfloat16_rn(lane_amax));
     if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), __float_as_uint(lane_amax));
   }
+}
+
+template <int NC, bool kRes, int kMode>
+static void launch_ln_one(const void* x, const void* y, const void* gamma, void* x_out, const void* w, const void* b,
+                          float eps, int64_t M, int K, const float* gs, float* amax, uint8_t* op, uint8_t* sf,
+                          cudaStream_t s) {
+  // one resident wave: every warp walks its rows with the next row's loads in flight
+  const int64_t Mp = (M + 127) & ~int64_t(127);
+  const int64_t per_wave = (int64_t)num_sms() * LnCfg<NC, kRes, kMode>::kMinBlocks;
+  const int64_t need = (Mp * 32 + 255) / 256;
+  const int grid = (int)(need < per_wave ? (need < 1 ? 1 : need) : per_wave);
+  ln_cast_kernel<NC, kRes, kMode><<<grid, 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y),
+      static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(x_out),
+      static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(b), eps, M, K, gs, amax, op, sf);
 }
 
 template <int NC>
 static void launch_ln(bool res, int mode, const void* x, const void* y, const void* gamma, void* x_out,
                       const void* w, const void* b, float eps, int64_t M, int K, const float* gs, float* amax,
                       uint8_t* op, uint8_t* sf, cudaStream_t s) {
-  const int64_t Mp = (M + 127) & ~int64_t(127);
-  int grid = grid_for(Mp * 32);
-  auto X = static_cast<const __nv_bfloat16*>(x);
-  auto Y = static_cast<const __nv_bfloat16*>(y);
-  auto G = static_cast<const __nv_bfloat16*>(gamma);
-  auto XO = static_cast<__nv_bfloat16*>(x_out);
-  auto W = static_cast<const __nv_bfloat16*>(w);
-  auto B = static_cast<const __nv_bfloat16*>(b);
-  if (res && mode == 0) ln_cast_kernel<NC, true, 0><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
-  else if (res) ln_cast_kernel<NC, true, 1><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
-  else if (mode == 0) ln_cast_kernel<NC, false, 0><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
-  else ln_cast_kernel<NC, false, 1><<<grid, 256, 0, s>>>(X, Y, G, XO, W, B, eps, M, K, gs, amax, op, sf);
+  if (res && mode == 0) launch_ln_one<NC, true, 0>(x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s);
+  else if (res) launch_ln_one<NC, true, 1>(x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s);
+  else if (mode == 0) launch_ln_one<NC, false, 0>(x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s);
+  else if (mode == 1) launch_ln_one<NC, false, 1>(x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s);
+  else launch_ln_one<NC, false, 2>(x, y, gamma, x_out, w, b, eps, M, K, gs, amax, op, sf, s);
 }
 
 static void dispatch_ln(int nc, bool res, int mode, const void* x, const void* y, const void* gamma, void* x_out,
@@ -648,9 +722,10 @@ int vf4_ln_cast_nvfp4(const void* x, const void* y, const void* gamma, void* x_o
   }
   // dynamic global scale: pass 1 (residual write + amax of the normalised rows), scale, pass 2
   if (cudaMemsetAsync(gs_out, 0, 4, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_ln_cast_nvfp4: memset");
-  dispatch_ln(nc, res, 0, x, y, gamma, x_out, ln_w, ln_b, eps, M, (int)K, nullptr, gs_out, nullptr, nullptr, s);
+  // (pass 1 leaves each row's mean and rstd in its code row for pass 2)
+  dispatch_ln(nc, res, 0, x, y, gamma, x_out, ln_w, ln_b, eps, M, (int)K, nullptr, gs_out, out_packed, nullptr, s);
   global_scale_kernel<<<1, 32, 0, s>>>(gs_out, 6.f * 448.f, gs_out);
-  dispatch_ln(nc, false, 1, res ? x_out : x, nullptr, nullptr, nullptr, ln_w, ln_b, eps, M, (int)K, gs_out, nullptr,
+  dispatch_ln(nc, false, 2, res ? x_out : x, nullptr, nullptr, nullptr, ln_w, ln_b, eps, M, (int)K, gs_out, nullptr,
               out_packed, out_sf, s);
   return launch_status("vf4_ln_cast_nvfp4");
 }
