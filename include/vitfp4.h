@@ -177,6 +177,16 @@ VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B,
                          int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
                          int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
 
+/* bf16 attention: softmax(q k^T * scale) v with bf16 operands, fp32 accumulation and an exact
+ * softmax -- the route the reference leaves to torch's scaled_dot_product_attention for blocks
+ * kept in bf16 (ptq/qattention.py:20-30 falls through to the model's own attention when quant
+ * attention is off; timm's Attention.forward calls F.scaled_dot_product_attention).  No
+ * counterpart kernel in the reference.  Same operand / output layout and strides as
+ * vf4_attn_nvfp4; head dim 64 and S <= 288 (VF4_ERR_UNSUPPORTED otherwise); no workspace. */
+VF4_API int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                          int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
+                          int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
+
 /* vf4_attn_nvfp4 with options.  flags: VF4_ATTN_HEAD_GLOBALS takes the Q / K~ / V~ global scales per
  * (image, head) instead of over the whole tensors as the reference does: no statistics pass and,
  * for head dim 64 and S <= 320, no workspace at all (workspace may then be NULL), at the cost of

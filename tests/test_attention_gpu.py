@@ -227,3 +227,46 @@ def test_fp8_kernel_matches_reference(B, H, S, D):
     assert np.isfinite(out).all()
     assert cos(out, ref) >= 0.999, cos(out, ref)
     assert cos(out, exact) >= cos(ref, exact) - 0.002
+
+
+# ----------------------------------------------------------------------------- bf16 kernel
+def _bf16_errors(q, k, v, scale, got):
+    """Max |error| of ``got`` and of torch's own bf16 SDPA against fp32 attention of the same bf16 inputs."""
+    import torch.nn.functional as F
+    ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=scale)
+    sdpa = F.scaled_dot_product_attention(q, k, v, scale=scale).float()
+    return (got.float() - ref).abs().max().item(), (sdpa - ref).abs().max().item()
+
+
+@pytest.mark.parametrize("B,H,S", [(2, 3, 257), (1, 4, 197), (1, 1, 1), (1, 2, 48), (2, 2, 256), (1, 3, 129),
+                                   (1, 2, 136), (1, 2, 288), (1, 1, 264), (4, 16, 257)])
+def test_bf16_kernel_matches_sdpa(B, H, S):
+    """The bf16 kernel (exact softmax, P rounded to bf16 for the PV MMA, like flash attention)
+    against fp32 attention of the same bf16 inputs: no worse than twice torch's own bf16 SDPA
+    error (and 4e-3 absolute), on (B, H, S, D) operands and on the strided views of a packed qkv
+    projection; S = 129 .. 136 and 257 .. 264 run the per-row tail."""
+    from vitfp4.nvfp4 import ops
+    D = 64
+    torch.manual_seed(S + 7 * H)
+    qkv = (torch.randn(B, S, 3 * H * D, device="cuda") * 1.5).bfloat16()
+    scale = D ** -0.5
+    got = ops.attention_bf16_packed_qkv(qkv, H, scale)
+    q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+    err, ref_err = _bf16_errors(q, k, v, scale, got.reshape(B, S, H, D).transpose(1, 2))
+    assert torch.isfinite(got).all()
+    assert err <= max(2 * ref_err, 4e-3), (err, ref_err)
+    # contiguous (B, H, S, D) operands, output in (B, H, S, D) strides
+    qc, kc, vc = (t.contiguous() for t in (q, k, v))
+    out = torch.empty(B, H, S, D, device="cuda", dtype=torch.bfloat16)
+    ops.attention_bf16(qc, kc, vc, B, H, S, D, (H * S * D, S * D, D), scale, out, (H * S * D, S * D, D))
+    assert torch.equal(out, got.reshape(B, S, H, D).transpose(1, 2))
+
+
+def test_bf16_kernel_rejects_unsupported_shapes():
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import ops
+    q = torch.zeros(1, 1, 300, 64, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    with pytest.raises(_lib.VitFp4Error):
+        ops.attention_bf16(q, q, q, 1, 1, 300, 64, (300 * 64, 300 * 64, 64), 0.125, out, (300 * 64, 300 * 64, 64))
+    assert not ops.bf16_kernel_ok(300, 64) and not ops.bf16_kernel_ok(257, 80) and ops.bf16_kernel_ok(257, 64)

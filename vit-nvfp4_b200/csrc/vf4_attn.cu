@@ -2220,6 +2220,585 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
   return launch_status("vf4_attn_fp8");
 }
 
+// ---------------------------------------------------------------------------------------
+// bf16 attention: the route the reference keeps for blocks left in bf16 (its qattention wrapper
+// and timm's Attention call torch's scaled_dot_product_attention): out = softmax(q k^T * scale) v
+// with bf16 q, k, v, fp32 accumulation and an exact (whole-row) softmax.  Head dim 64, S <= 288.
+// Persistent CTAs (one per SM, 16 warps) run one stream of 128-query tiles over the B*H heads:
+//   warp 0       TMA loads (128-byte swizzle): K (with the head's tail query rows) into one
+//                buffer, V into one of two (the next head's V lands while this head runs), Q
+//                one 128-row tile at a time
+//   warp 1       S = Q K^T (tcgen05.mma kind::f16; Q and K straight from the TMA tiles,
+//                K-major) into TMEM, keys padded to a multiple of 16 (chunks of <= 256); the
+//                next tile's S is issued as soon as the softmax has read this one, before this
+//                tile's O = P V (V straight from its TMA tile as an MN-major operand) into one
+//                of two O buffers; commits release Q, K and V the moment the MMAs are done
+//   warps 2-13   (TMEM lane quadrant x key slice) pass 1 row max, pass 2 P = 2^((s - max) c),
+//                row sums, P -> bf16 (K-major core matrices); the previous tile's epilogue
+//                (O / rowsum -> bf16 -> TMA store) follows, across head boundaries
+//   warps 14-15  query rows past the last full 128-row tile when there are at most 4 of them
+//                (S = 257: one): plain FMAs over the same shared-memory K and V, overlapped
+//                with the tiles (a 128-row MMA tile for one row costs a whole tile's MMA ->
+//                softmax -> PV chain)
+// ---------------------------------------------------------------------------------------
+// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; these
+// empty volatile statements keep the compiler from moving their first uses above the wait.
+VF4_DEV void reg_fence16(uint32_t* v) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+constexpr uint32_t kB16TmemS = 0, kB16TmemO = 320;
+constexpr int kB16TailWarps = 2, kB16Warps = kFusedWarps + kB16TailWarps, kB16TailMax = 4;
+
+struct Bf16Geom {
+  int B, H, S, D;
+  int nt, tail, skp;       // MMA query tiles, query rows left to the tail warps, keys padded to 16
+  int box_rows, nbox, heads;
+  int kv_hs, out_hs;
+  float scale;
+  __nv_bfloat16* out;      // tail rows: out element (b, h, s, d) at out + b osb + h osh + s oss + d
+  int64_t osb, osh, oss;
+  uint32_t qb, kb, vb[2], tqb, pb, stg, red, bar, total;
+};
+
+static Bf16Geom make_bf16_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
+  Bf16Geom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.skp = (int)align_up(S, 16);
+  g.tail = (S > 128 && S % 128 != 0 && S % 128 <= kB16TailMax) ? (int)(S % 128) : 0;
+  g.nt = (int)((S - g.tail + 127) / 128);
+  g.nbox = g.skp <= 256 ? 1 : 2;
+  g.box_rows = (int)align_up((g.skp + g.nbox - 1) / g.nbox, 8);
+  g.heads = (int)(B * H);
+  g.scale = scale;
+  const uint32_t rawb = (uint32_t)(g.nbox * g.box_rows) * 128u;   // a multiple of 1024
+  uint32_t o = 0;
+  g.qb = o;     o += 128u * 128u;
+  g.kb = o;     o += rawb;
+  g.vb[0] = o;  o += rawb;
+  g.vb[1] = o;  o += rawb;
+  g.tqb = o;    o += 1024u;                       // 8 query rows (tail rows, zero past S)
+  g.pb = o;     o += 256u * (uint32_t)g.skp;      // P: 128 rows x skp bf16, K-major core matrices
+  o = (uint32_t)align_up(o, 1024);
+  g.stg = o; o += 4 * 4096;
+  g.red = o; o += (uint32_t)(3 * kSlices * 128 + kB16TailMax * (g.skp + 2 * 64 + 4)) * 4u;
+  o = (uint32_t)align_up(o, 16);
+  g.bar = o; o += 128;
+  g.total = o + 1024;
+  return g;
+}
+
+static bool bf16_attn_ok(int64_t S, int64_t D) {
+  if (D != 64 || S < 1 || S > 288) return false;
+  return make_bf16_geom(1, 1, S, D, 1.f).total <= 227u * 1024u;
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B, fp32 accumulation, K-major A; B K-major
+// or (b_mn) MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t n, bool b_mn, uint32_t m = 128) {
+  return (1u << 4)            // D format: F32
+         | (1u << 7)          // A format: BF16
+         | (1u << 10)         // B format: BF16
+         | ((b_mn ? 1u : 0u) << 16)
+         | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+VF4_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kB16Warps * 32, 1)
+    attn_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                     const __grid_constant__ CUtensorMap tmT, const Bf16Geom g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (base - raw0);
+  const uint32_t bar = base + g.bar;
+  const uint32_t q_full = bar, q_free = bar + 8, k_full = bar + 16, k_free = bar + 24, s_full = bar + 32,
+                 p_full = bar + 40, drain = bar + 48;
+  auto v_full = [&](int sl) { return bar + 56 + 8u * sl; };
+  auto v_free = [&](int sl) { return bar + 72 + 8u * sl; };
+  auto o_full = [&](int ob) { return bar + 88 + 8u * ob; };
+  auto o_free = [&](int ob) { return bar + 104 + 8u * ob; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 120);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbo_p = 16u * (uint32_t)g.skp;   // bytes per 8-row group of P
+  const float c = g.scale * 1.4426950408889634f;
+  const uint32_t kv_release = g.tail > 0 ? 2u : 1u;   // MMA commit (+ the tail warps)
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_free, kv_release);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, kFusedCompute);
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(v_full(i), 1);
+      mbar_init(v_free(i), kv_release);
+      mbar_init(o_full(i), 1);
+      mbar_init(o_free(i), kFusedCompute);
+    }
+    fence_mbar_init();
+    tma_prefetch(&tmQ);
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+    tma_prefetch(&tmO);
+    if (g.tail > 0) tma_prefetch(&tmT);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  fence_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA loads
+    if (lane == 0) {
+      const uint32_t kv_bytes = (uint32_t)(g.nbox * g.box_rows) * 128u;
+      int hi = 0, qi = 0;
+      bool ok = true;
+      for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
+        const int b = head / g.H, h = head - b * g.H, sl = hi & 1;
+        if (hi >= 1 && !mbar_wait(k_free, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(k_full, kv_bytes + (g.tail > 0 ? 1024u : 0u));
+        for (int j = 0; j < g.nbox; ++j) {
+          const int row = j * g.box_rows;
+          tma_load_4d(base + g.kb + (uint32_t)row * 128u, &tmK, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, k_full);
+        }
+        if (g.tail > 0) {
+          const int row = g.S - g.tail;
+          tma_load_4d(base + g.tqb, &tmT, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, k_full);
+        }
+        for (int t = 0; t < g.nt; ++t, ++qi) {
+          if (qi > 0 && !mbar_wait(q_free, (uint32_t)(qi - 1) & 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int row = t * 128;
+          mbar_arrive_expect_tx(q_full, 128u * 128u);
+          tma_load_4d(base + g.qb, &tmQ, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, q_full);
+          if (t == 0) {   // V of this head after its first Q tile
+            if (hi >= 2 && !mbar_wait(v_free(sl), (uint32_t)((hi >> 1) - 1) & 1u, err, kDevErrTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(v_full(sl), kv_bytes);
+            for (int j = 0; j < g.nbox; ++j) {
+              const int vr = j * g.box_rows;
+              tma_load_4d(base + (sl ? g.vb[1] : g.vb[0]) + (uint32_t)vr * 128u, &tmV, 0, g.kv_hs ? h : vr, g.kv_hs ? vr : h, b,
+                          v_full(sl));
+            }
+          }
+        }
+      }
+      // no copy may still be writing shared memory when the CTA exits
+      if (qi > 0) mbar_wait(q_full, (uint32_t)(qi - 1) & 1u, err, kDevErrTimeoutFull);
+      if (hi > 0) {
+        mbar_wait(k_full, (uint32_t)(hi - 1) & 1u, err, kDevErrTimeoutFull);
+        mbar_wait(v_full((hi - 1) & 1), (uint32_t)((hi - 1) >> 1) & 1u, err, kDevErrTimeoutFull);
+        if (hi > 1) mbar_wait(v_full(hi & 1), (uint32_t)((hi - 2) >> 1) & 1u, err, kDevErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    bool ok = true;
+    int hi = 0, it = 0, qi = 0;
+    // S = Q K^T for the Q tile in the buffer; releases Q, and K after the head's last tile
+    auto issue_qk = [&](bool last) {
+      const uint32_t qa = base + g.qb, kbase = base + g.kb;
+      for (int n0 = 0; n0 < g.skp;) {
+        const int n = g.skp - n0 >= 256 ? 256 : g.skp - n0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16(tmem + kB16TmemS + (uint32_t)n0, smem_desc(qa + 32u * kk, 16, 1024, 2),
+                  smem_desc(kbase + (uint32_t)n0 * 128u + 32u * kk, 16, 1024, 2), idesc_bf16((uint32_t)n, false),
+                  kk > 0 ? 1u : 0u);
+        n0 += n;
+      }
+      tc_commit(s_full);
+      tc_commit(q_free);
+      if (last) tc_commit(k_free);
+    };
+    if ((int)blockIdx.x < g.heads) {
+      ok = mbar_wait(k_full, 0, err, kDevErrTimeoutFull) && mbar_wait(q_full, 0, err, kDevErrTimeoutFull);
+      tc_fence_after();
+      if (ok && lane == 0) issue_qk(g.nt == 1);
+      __syncwarp();
+      qi = 1;
+    }
+    for (int head = blockIdx.x; head < g.heads && ok; head += gridDim.x, ++hi) {
+      for (int t = 0; t < g.nt; ++t, ++it) {
+        // P of tile it written (and its S read) by every compute warp
+        if (!mbar_wait(p_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // the next tile's S first, so that its softmax overlaps this tile's PV
+        const bool same = t + 1 < g.nt;
+        if (same || head + (int)gridDim.x < g.heads) {
+          if ((!same && !mbar_wait(k_full, (uint32_t)(hi + 1) & 1u, err, kDevErrTimeoutFull)) ||
+              !mbar_wait(q_full, (uint32_t)qi & 1u, err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) issue_qk(same ? t + 1 == g.nt - 1 : g.nt == 1);
+          __syncwarp();
+          ++qi;
+        }
+        const int ob = it & 1, use = it >> 1;
+        if ((use > 0 && !mbar_wait(o_free(ob), (uint32_t)(use - 1) & 1u, err, kDevErrTimeoutEmpty)) ||
+            (t == 0 && !mbar_wait(v_full(hi & 1), (uint32_t)(hi >> 1) & 1u, err, kDevErrTimeoutFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t t_o = tmem + kB16TmemO + 64u * (uint32_t)ob, vbase = base + ((hi & 1) ? g.vb[1] : g.vb[0]);
+          for (int kk = 0; kk < g.skp / 16; ++kk)
+            mma_f16(t_o, smem_desc(base + g.pb + 256u * kk, 128, sbo_p, 0), smem_desc(vbase + 2048u * kk, 1024, 1024, 2),
+                    idesc_bf16(64, true), kk > 0 ? 1u : 0u);
+          tc_commit(o_full(ob));
+          if (t == g.nt - 1) tc_commit(v_free(hi & 1));
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp < kFusedWarps) {
+    // ------------------------------------------------------------ softmax and epilogue
+    const int cw = warp - 2;
+    const int qd = warp & 3;
+    const int cs = cw >> 2;
+    const uint32_t qbar = 2u + (uint32_t)qd;
+    float* red = reinterpret_cast<float*>(gb + g.red);
+    float* red_m = red;                         // [kSlices][128]
+    float* red_l = red_m + kSlices * 128;       // [2][kSlices][128]
+    const int S = g.S;
+    const int nkb = g.skp / 16;
+    const int b0 = cs * nkb / kSlices, b1 = (cs + 1) * nkb / kSlices;
+    const int c0 = cs * 8 / kSlices, c1 = (cs + 1) * 8 / kSlices;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const int r = qd * 32 + lane;
+    bool ok = true;
+    auto epilogue = [&](int itt, int head, int tl) {
+      const int b = head / g.H, h = head - b * g.H;
+      const bool act = ok && tl * 128 + qd * 32 < S;
+      const int ob = itt & 1;
+      constexpr int kMaxChunks = (8 + kSlices - 1) / kSlices;
+      uint32_t ov[kMaxChunks][8];
+      if (act) {
+#pragma unroll
+        for (int k = 0; k < kMaxChunks; ++k)
+          if (c0 + k < c1) tmem_ld_32x32b_x8(tmem + lane_base + kB16TmemO + 64u * ob + 8 * (c0 + k), ov[k]);
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free(ob));
+      if (cs == 0 && lane == 0) bulk_wait_read();
+      named_bar_sync(qbar, 32 * kSlices);
+      uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
+      if (act) {
+        const float* rl = red_l + ob * (kSlices * 128);
+        float lsum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kSlices; ++k) lsum += rl[k * 128 + r];
+        const float f = 1.0f / lsum;
+#pragma unroll
+        for (int k = 0; k < kMaxChunks; ++k) {
+          const int cc = c0 + k;
+          if (cc < c1) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[k][2 * i]) * f,
+                                                        __uint_as_float(ov[k][2 * i + 1]) * f);
+              w[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            *reinterpret_cast<uint4*>(stg + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      fence_async_shared();
+      named_bar_sync(qbar, 32 * kSlices);
+      if (act && cs == 0 && lane == 0) {
+        const int row = tl * 128 + qd * 32;
+        tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
+        bulk_commit();
+      }
+    };
+    int it = 0, prev_head = -1, prev_t = 0;
+    for (int head = blockIdx.x; head < g.heads; head += gridDim.x) {
+      for (int t = 0; t < g.nt; ++t, ++it) {
+        const bool active = ok && t * 128 + qd * 32 < S;
+        if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
+        tc_fence_after();
+        const uint32_t srow = tmem + lane_base + kB16TmemS;
+        // pass 1: row max over the valid keys; 16-column TMEM loads, the next one in flight while
+        // the current one is reduced
+        float m = -INFINITY;
+        auto max16 = [&](int u, const uint32_t* v) {
+          if (16 * u + 16 <= S) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) m = max3f(m, __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (16 * u + e < S) m = fmaxf(m, __uint_as_float(v[e]));
+          }
+        };
+        if (active && ok && b0 < b1) {
+          uint32_t va[16], vb[16];
+          tmem_ld_32x32b_x16(srow + 16 * b0, va);
+          tmem_wait_ld();
+          reg_fence16(va);
+          for (int u = b0; u < b1; u += 2) {
+            if (u + 1 < b1) tmem_ld_32x32b_x16(srow + 16 * (u + 1), vb);
+            max16(u, va);
+            tmem_wait_ld();
+            reg_fence16(vb);
+            if (u + 1 < b1) {
+              if (u + 2 < b1) tmem_ld_32x32b_x16(srow + 16 * (u + 2), va);
+              max16(u + 1, vb);
+              tmem_wait_ld();
+              reg_fence16(va);
+            }
+          }
+        }
+        red_m[cs * 128 + r] = m;
+        named_bar_sync(qbar, 32 * kSlices);
+#pragma unroll
+        for (int k = 0; k < kSlices; ++k) m = fmaxf(m, red_m[k * 128 + r]);
+        // P is single-buffered: the previous tile's PV must be done reading it
+        if (it > 0 && ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
+        // pass 2: P = 2^((s - max) c), row sums, P -> bf16
+        const float nmc = -m * c;
+        float lsum = 0.f;
+        uint8_t* prow = gb + g.pb + (uint32_t)(r >> 3) * sbo_p + (uint32_t)(r & 7) * 16u;
+        const unsigned long long c2 = f32x2_pack(c, c), nmc2 = f32x2_pack(nmc, nmc);
+        unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
+        auto exp16 = [&](int u, const uint32_t* v) {
+          float p[16];
+          // x = s c - m c by pairs, 2^x on the special-function unit; keys >= S give 0
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float x0, x1;
+            f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2, nmc2), &x0,
+                         &x1);
+            p[2 * i] = ex2_approx(x0);
+            p[2 * i + 1] = ex2_approx(x1);
+          }
+          if (16 * u + 16 > S) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (16 * u + e >= S) p[e] = 0.f;
+          }
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * i], p[2 * i + 1]));
+            __nv_bfloat162 pv = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&pv);
+          }
+          *reinterpret_cast<uint4*>(prow + (uint32_t)(2 * u) * 128u) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(prow + (uint32_t)(2 * u + 1) * 128u) = make_uint4(w[4], w[5], w[6], w[7]);
+        };
+        if (active && ok && b0 < b1) {
+          uint32_t va[16], vb[16];
+          tmem_ld_32x32b_x16(srow + 16 * b0, va);
+          tmem_wait_ld();
+          reg_fence16(va);
+          for (int u = b0; u < b1; u += 2) {
+            if (u + 1 < b1) tmem_ld_32x32b_x16(srow + 16 * (u + 1), vb);
+            exp16(u, va);
+            tmem_wait_ld();
+            reg_fence16(vb);
+            if (u + 1 < b1) {
+              if (u + 2 < b1) tmem_ld_32x32b_x16(srow + 16 * (u + 2), va);
+              exp16(u + 1, vb);
+              tmem_wait_ld();
+              reg_fence16(va);
+            }
+          }
+        }
+        {
+          float l0, l1;
+          f32x2_unpack(lsum2, &l0, &l1);
+          lsum = l0 + l1;
+        }
+        tc_fence_before();
+        red_l[(it & 1) * (kSlices * 128) + cs * 128 + r] = lsum;
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        if (it > 0) epilogue(it - 1, prev_head, prev_t);
+        prev_head = head;
+        prev_t = t;
+      }
+    }
+    if (it > 0) {
+      if (ok) ok = mbar_wait(o_full((it - 1) & 1), (uint32_t)((it - 1) >> 1) & 1u, err, kDevErrTimeoutTmem);
+      tc_fence_after();
+      epilogue(it - 1, prev_head, prev_t);
+    }
+    if (cw < 4 && lane == 0) bulk_wait_all();
+  } else if (g.tail > 0) {
+    // ------------------------------------------------------------ tail query rows
+    const int tw = warp - kFusedWarps, tid = threadIdx.x - 32 * kFusedWarps;
+    float* red = reinterpret_cast<float*>(gb + g.red) + 3 * kSlices * 128;
+    float* tp = red;                                   // [kB16TailMax][skp] probabilities
+    float* to = tp + kB16TailMax * g.skp;              // [2][kB16TailMax][64] partial outputs
+    float* tx = to + 2 * kB16TailMax * 64;             // [2 warps][2] maxima / sums exchange
+    const int S = g.S;
+    constexpr uint32_t kTailBar = 6;
+    constexpr int kKeys = (288 + 63) / 64;             // keys per thread
+    bool ok = true;
+    int hi = 0;
+    for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
+      const int b = head / g.H, h = head - b * g.H, sl = hi & 1;
+      if (ok) ok = mbar_wait(k_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
+      const uint8_t* kt = gb + g.kb;
+      const uint8_t* qt = gb + g.tqb;
+      float inv_l[kB16TailMax];
+      for (int rr = 0; rr < g.tail; ++rr) {
+        float qv[64];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) raw_load8(qt, rr, j, qv + 8 * j);
+        float s[kKeys];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kKeys; ++u) {
+          const int key = tid + 64 * u;
+          s[u] = -INFINITY;
+          if (ok && key < S) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float kv[8];
+              raw_load8(kt, key, j, kv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc = __fmaf_rn(kv[e], qv[8 * j + e], acc);
+            }
+            s[u] = acc * c;
+            mx = fmaxf(mx, s[u]);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) tx[tw] = mx;
+        named_bar_sync(kTailBar, 32 * kB16TailWarps);
+        mx = fmaxf(tx[0], tx[1]);
+        float l = 0.f;
+#pragma unroll
+        for (int u = 0; u < kKeys; ++u) {
+          const int key = tid + 64 * u;
+          const float p = (ok && key < S) ? ex2_approx(s[u] - mx) : 0.f;
+          if (key < g.skp) tp[rr * g.skp + key] = p;
+          l += p;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) tx[2 + tw] = l;
+        named_bar_sync(kTailBar, 32 * kB16TailWarps);
+        inv_l[rr] = 1.0f / (tx[2] + tx[3]);
+        named_bar_sync(kTailBar, 32 * kB16TailWarps);   // tx is reused by the next row
+      }
+      // K (and the tail query rows) no longer needed
+      if (tid == 0) mbar_arrive(k_free);
+      if (ok) ok = mbar_wait(v_full(sl), (uint32_t)(hi >> 1) & 1u, err, kDevErrTimeoutFull);
+      {
+        // thread: head-dim pair lane, key half tw
+        const int half = (S + 1) / 2;
+        const int j0 = tw * half, j1 = tw == 0 ? half : S;
+        float a[kB16TailMax][2];
+#pragma unroll
+        for (int rr = 0; rr < kB16TailMax; ++rr) a[rr][0] = a[rr][1] = 0.f;
+        if (ok) {
+          for (int j = j0; j < j1; ++j) {
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(gb + (sl ? g.vb[1] : g.vb[0]) + j * 128 +
+                                                                   (((lane >> 2) ^ (j & 7)) << 4) + (lane & 3) * 4);
+            const float v0 = __uint_as_float(w2 << 16), v1 = __uint_as_float(w2 & 0xFFFF0000u);
+#pragma unroll
+            for (int rr = 0; rr < kB16TailMax; ++rr)
+              if (rr < g.tail) {
+                a[rr][0] = __fmaf_rn(tp[rr * g.skp + j], v0, a[rr][0]);
+                a[rr][1] = __fmaf_rn(tp[rr * g.skp + j], v1, a[rr][1]);
+              }
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < kB16TailMax; ++rr)
+          if (rr < g.tail) {
+            to[(tw * kB16TailMax + rr) * 64 + 2 * lane] = a[rr][0];
+            to[(tw * kB16TailMax + rr) * 64 + 2 * lane + 1] = a[rr][1];
+          }
+      }
+      named_bar_sync(kTailBar, 32 * kB16TailWarps);
+      // V no longer needed
+      if (tid == 0) mbar_arrive(v_free(sl));
+      for (int i = tid; i < g.tail * 64; i += 32 * kB16TailWarps) {
+        const int rr = i >> 6, d = i & 63;
+        const int row = S - g.tail + rr;
+        if (ok)
+          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss + d] =
+              __float2bfloat16_rn((to[rr * 64 + d] + to[(kB16TailMax + rr) * 64 + d]) * inv_l[rr]);
+      }
+      named_bar_sync(kTailBar, 32 * kB16TailWarps);   // tp / to are reused by the next head
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                       int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
+                       int64_t oss, cudaStream_t s) {
+  Bf16Geom g = make_bf16_geom(B, H, S, D, scale);
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.osb = osb;
+  g.osh = osh;
+  g.oss = oss;
+  g.kv_hs = sh < ss;
+  g.out_hs = osh < oss;
+  FusedGeom fg = make_fused_geom(B, H, S, D, scale);   // the head-view maps take D, S, H, B from it
+  CUtensorMap tq, tk, tv, to, tt;
+  if (int st = make_head_map(&tq, q, fg, sb, sh, ss, 128, g.kv_hs)) return st;
+  if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (int st = make_head_map(&to, out, fg, osb, osh, oss, 32, g.out_hs)) return st;
+  if (int st = make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return st;
+  cudaError_t e = cudaFuncSetAttribute(attn_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
+  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = g.heads < num_sms() ? g.heads : num_sms();
+  attn_bf16_kernel<<<grid, kB16Warps * 32, g.total, s>>>(tq, tk, tv, to, tt, g);
+  return launch_status("vf4_attn_bf16");
+}
+
 static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t rowbytes, int box_x, int box_y,
                     CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_tiled();
@@ -2374,6 +2953,23 @@ int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_fp8: B*H too large");
   return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
                     out_stride_s, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                  int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out, int64_t out_stride_b,
+                  int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_bf16: bad sizes");
+  if (!bf16_attn_ok(S, D))
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: needs head dim 64 and S <= 288 (S=%lld D=%lld)", (long long)S,
+                (long long)D);
+  if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_bf16: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
+    return fail(VF4_ERR_ALIGN, "vf4_attn_bf16: 16-byte aligned pointers and strides (multiples of 8) needed");
+  if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: B*H too large");
+  return launch_bf16(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                     out_stride_s, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,

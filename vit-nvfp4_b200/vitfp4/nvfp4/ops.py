@@ -334,6 +334,36 @@ def fp8_kernel_ok(S: int, D: int) -> bool:
     return D == 64 and S <= 320
 
 
+def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
+                   strides: tuple[int, int, int], scale: float, out: torch.Tensor,
+                   out_strides: tuple[int, int, int]) -> torch.Tensor:
+    """Exact-softmax bf16 attention (tcgen05 kind::f16) over bf16 q/k/v views sharing element strides."""
+    _need_cuda(q, k, v, out)
+    for t in (q, k, v, out):
+        if t.dtype != torch.bfloat16:
+            raise _lib.VitFp4Error("bf16 attention takes bf16 q/k/v/out")
+    _lib.call("vf4_attn_bf16", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
+    _launched(1)
+    return out
+
+
+def bf16_kernel_ok(S: int, D: int) -> bool:
+    return D == 64 and 1 <= S <= 288
+
+
+def attention_bf16_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float) -> torch.Tensor:
+    """Packed (B, S, 3*H*D) bf16 projection output -> (B, S, H*D) bf16 through the bf16 kernel."""
+    B, S, C3 = qkv.shape
+    H = num_heads
+    D = C3 // (3 * H)
+    x = qkv if qkv.is_contiguous() else qkv.contiguous()
+    out = torch.empty((B, S, H * D), dtype=torch.bfloat16, device=qkv.device)
+    attention_bf16(x, x[..., H * D:], x[..., 2 * H * D:], B, H, S, D, (S * C3, D, C3), scale, out,
+                   (S * H * D, D, H * D))
+    return out
+
+
 def _bhsd_operands(q, k, v):
     B, H, S, D = q.shape
     qb, kb, vb = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
