@@ -228,10 +228,12 @@ def test_fused_block_matches_unfused_block(attn):
     assert _cos(a, b) >= 0.999, _cos(a, b)
 
 
-@pytest.mark.parametrize("S", [257, 264])
-def test_fused_block_split_query_attention(S):
-    """bf16 route with S = 128 k + (1..16): the fused block runs cuDNN on queries [0, 128 k) and on the
-    rest separately and casts both parts into one proj operand; it equals the per-module block."""
+@pytest.mark.parametrize("S", [257, 264, 385])
+def test_fused_block_bf16_attention_routes(S):
+    """bf16 attention in the fused block equals the per-module block (torch SDPA): S <= 288 runs the
+    tcgen05 bf16 kernel (S = 257 with its per-row tail, 264 with a partial 128-row tile); S = 385 =
+    3 * 128 + 1 runs cuDNN on queries [0, 384) and on the last one separately and casts both parts
+    into one proj operand."""
     from vitfp4.ptq import FusedNVFP4Block
     torch.manual_seed(6)
     x = torch.randn(4, S, 384, device="cuda").bfloat16()

@@ -2235,7 +2235,8 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
 //                of two O buffers; commits release Q, K and V the moment the MMAs are done
 //   warps 2-13   (TMEM lane quadrant x key slice) pass 1 row max, pass 2 P = 2^((s - max) c),
 //                row sums, P -> bf16 (K-major core matrices); the previous tile's epilogue
-//                (O / rowsum -> bf16 -> TMA store) follows, across head boundaries
+//                (O / rowsum -> bf16, each thread storing its row's 16-byte column chunks)
+//                follows, across head boundaries
 //   warps 14-15  query rows past the last full 128-row tile when there are at most 4 of them
 //                (S = 257: one): plain FMAs over the same shared-memory K and V, overlapped
 //                with the tiles (a 128-row MMA tile for one row costs a whole tile's MMA ->
@@ -2255,11 +2256,11 @@ struct Bf16Geom {
   int B, H, S, D;
   int nt, tail, skp;       // MMA query tiles, query rows left to the tail warps, keys padded to 16
   int box_rows, nbox, heads;
-  int kv_hs, out_hs;
+  int kv_hs;
   float scale;
-  __nv_bfloat16* out;      // tail rows: out element (b, h, s, d) at out + b osb + h osh + s oss + d
+  __nv_bfloat16* out;      // out element (b, h, s, d) at out + b osb + h osh + s oss + d
   int64_t osb, osh, oss;
-  uint32_t qb, kb, vb[2], tqb, pb, stg, red, bar, total;
+  uint32_t qb, kb, vb[2], tqb, pb, red, bar, total;
 };
 
 static Bf16Geom make_bf16_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
@@ -2283,8 +2284,7 @@ static Bf16Geom make_bf16_geom(int64_t B, int64_t H, int64_t S, int64_t D, float
   g.vb[1] = o;  o += rawb;
   g.tqb = o;    o += 1024u;                       // 8 query rows (tail rows, zero past S)
   g.pb = o;     o += 256u * (uint32_t)g.skp;      // P: 128 rows x skp bf16, K-major core matrices
-  o = (uint32_t)align_up(o, 1024);
-  g.stg = o; o += 4 * 4096;
+  o = (uint32_t)align_up(o, 16);
   g.red = o; o += (uint32_t)(3 * kSlices * 128 + kB16TailMax * (g.skp + 2 * 64 + 4)) * 4u;
   o = (uint32_t)align_up(o, 16);
   g.bar = o; o += 128;
@@ -2317,8 +2317,8 @@ VF4_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t i
 
 __global__ void __launch_bounds__(kB16Warps * 32, 1)
     attn_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                     const __grid_constant__ CUtensorMap tmT, const Bf16Geom g) {
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
+                     const Bf16Geom g) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
@@ -2355,7 +2355,6 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
-    tma_prefetch(&tmO);
     if (g.tail > 0) tma_prefetch(&tmT);
   }
   if (warp == 1) {
@@ -2503,8 +2502,12 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int r = qd * 32 + lane;
     bool ok = true;
+    // O / rowsum -> bf16, each thread storing its row's columns of this slice straight to global
+    // memory (the row sums of every slice were written before the quadrant barrier of the next
+    // tile's pass 1, which this warp has passed)
     auto epilogue = [&](int itt, int head, int tl) {
       const int b = head / g.H, h = head - b * g.H;
+      const int row = tl * 128 + r;
       const bool act = ok && tl * 128 + qd * 32 < S;
       const int ob = itt & 1;
       constexpr int kMaxChunks = (8 + kSlices - 1) / kSlices;
@@ -2518,15 +2521,13 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free(ob));
-      if (cs == 0 && lane == 0) bulk_wait_read();
-      named_bar_sync(qbar, 32 * kSlices);
-      uint8_t* stg = gb + g.stg + qd * 4096 + lane * 128;
-      if (act) {
+      if (act && row < S) {
         const float* rl = red_l + ob * (kSlices * 128);
         float lsum = 0.f;
 #pragma unroll
         for (int k = 0; k < kSlices; ++k) lsum += rl[k * 128 + r];
         const float f = 1.0f / lsum;
+        __nv_bfloat16* orow = g.out + (int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss;
 #pragma unroll
         for (int k = 0; k < kMaxChunks; ++k) {
           const int cc = c0 + k;
@@ -2538,16 +2539,9 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
                                                         __uint_as_float(ov[k][2 * i + 1]) * f);
               w[i] = *reinterpret_cast<uint32_t*>(&hv);
             }
-            *reinterpret_cast<uint4*>(stg + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(orow + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-      }
-      fence_async_shared();
-      named_bar_sync(qbar, 32 * kSlices);
-      if (act && cs == 0 && lane == 0) {
-        const int row = tl * 128 + qd * 32;
-        tma_store_4d(&tmO, base + g.stg + qd * 4096, 0, g.out_hs ? h : row, g.out_hs ? row : h, b);
-        bulk_commit();
       }
     };
     int it = 0, prev_head = -1, prev_t = 0;
@@ -2664,7 +2658,6 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       tc_fence_after();
       epilogue(it - 1, prev_head, prev_t);
     }
-    if (cw < 4 && lane == 0) bulk_wait_all();
   } else if (g.tail > 0) {
     // ------------------------------------------------------------ tail query rows
     const int tw = warp - kFusedWarps, tid = threadIdx.x - 32 * kFusedWarps;
@@ -2784,18 +2777,16 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
   g.osh = osh;
   g.oss = oss;
   g.kv_hs = sh < ss;
-  g.out_hs = osh < oss;
   FusedGeom fg = make_fused_geom(B, H, S, D, scale);   // the head-view maps take D, S, H, B from it
-  CUtensorMap tq, tk, tv, to, tt;
+  CUtensorMap tq, tk, tv, tt;
   if (int st = make_head_map(&tq, q, fg, sb, sh, ss, 128, g.kv_hs)) return st;
   if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
-  if (int st = make_head_map(&to, out, fg, osb, osh, oss, 32, g.out_hs)) return st;
   if (int st = make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return st;
   cudaError_t e = cudaFuncSetAttribute(attn_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
   if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
-  attn_bf16_kernel<<<grid, kB16Warps * 32, g.total, s>>>(tq, tk, tv, to, tt, g);
+  attn_bf16_kernel<<<grid, kB16Warps * 32, g.total, s>>>(tq, tk, tv, tt, g);
   return launch_status("vf4_attn_bf16");
 }
 

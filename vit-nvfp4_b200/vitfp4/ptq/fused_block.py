@@ -50,6 +50,10 @@ class FusedNVFP4Block(nn.Module):
         H, D = a.num_heads, a.head_dim
         if getattr(a, "_nvfp4_attn", False) and a._nvfp4_qk == "nvfp4" and a._nvfp4_pv == "nvfp4":
             return ops.attention_packed_qkv(qkv, H, a.scaling)
+        if not getattr(a, "_nvfp4_attn", False) and qkv.dtype == torch.bfloat16 and ops.bf16_kernel_ok(S, D):
+            # the reference's bf16 route (torch SDPA) on the tcgen05 kernel: exact softmax, fp32
+            # accumulation, output (B, S, H*D) read by the proj cast as it is
+            return ops.attention_bf16_packed_qkv(qkv, H, a.scaling)
         q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
         if getattr(a, "_nvfp4_attn", False):   # the fp8 and mixed routes (GPU emulation)
             from ..nvfp4.attention import quant_sdpa
