@@ -182,10 +182,14 @@ VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B,
  * kept in bf16 (ptq/qattention.py:20-30 falls through to the model's own attention when quant
  * attention is off; timm's Attention.forward calls F.scaled_dot_product_attention).  No
  * counterpart kernel in the reference.  Same operand / output layout and strides as
- * vf4_attn_nvfp4; head dim 64 and S <= 288 (VF4_ERR_UNSUPPORTED otherwise); no workspace. */
+ * vf4_attn_nvfp4; head dim 64 and S <= 288 (VF4_ERR_UNSUPPORTED otherwise); no workspace.
+ * out_amax (may be NULL): receives max |out| over the whole bf16 output -- the amax the next
+ * QuantLinear's dynamic activation cast would compute (quant.py:48-54), so the caller can cast
+ * with vf4_global_scale(out_amax) and skip that pass. */
 VF4_API int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                           int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out,
-                          int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
+                          int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, float* out_amax,
+                          vf4_stream_t stream);
 
 /* vf4_attn_nvfp4 with options.  flags: VF4_ATTN_HEAD_GLOBALS takes the Q / K~ / V~ global scales per
  * (image, head) instead of over the whole tensors as the reference does: no statistics pass and,

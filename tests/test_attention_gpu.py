@@ -260,6 +260,10 @@ def test_bf16_kernel_matches_sdpa(B, H, S):
     out = torch.empty(B, H, S, D, device="cuda", dtype=torch.bfloat16)
     ops.attention_bf16(qc, kc, vc, B, H, S, D, (H * S * D, S * D, D), scale, out, (H * S * D, S * D, D))
     assert torch.equal(out, got.reshape(B, S, H, D).transpose(1, 2))
+    # the output amax the kernel reports is the one the proj's dynamic cast computes
+    am = torch.empty((), dtype=torch.float32, device="cuda")
+    got2 = ops.attention_bf16_packed_qkv(qkv, H, scale, out_amax=am)
+    assert torch.equal(got2, got) and torch.equal(am, ops.amax(got))
 
 
 def test_bf16_kernel_rejects_unsupported_shapes():

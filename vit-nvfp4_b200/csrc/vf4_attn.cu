@@ -2260,6 +2260,7 @@ struct Bf16Geom {
   float scale;
   __nv_bfloat16* out;      // out element (b, h, s, d) at out + b osb + h osh + s oss + d
   int64_t osb, osh, oss;
+  float* amax;             // if set: max |out| over the whole output (atomic, as uint bits)
   uint32_t qb, kb, vb[2], tqb, pb, red, bar, total;
 };
 
@@ -2502,6 +2503,7 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int r = qd * 32 + lane;
     bool ok = true;
+    float out_max = 0.f;   // max |out| over this thread's stores (the amax of the proj input)
     // O / rowsum -> bf16, each thread storing its row's columns of this slice straight to global
     // memory (the row sums of every slice were written before the quadrant barrier of the next
     // tile's pass 1, which this warp has passed)
@@ -2538,6 +2540,7 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
               __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[k][2 * i]) * f,
                                                         __uint_as_float(ov[k][2 * i + 1]) * f);
               w[i] = *reinterpret_cast<uint32_t*>(&hv);
+              out_max = max3f(out_max, fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
             }
             *reinterpret_cast<uint4*>(orow + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
           }
@@ -2658,6 +2661,11 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       tc_fence_after();
       epilogue(it - 1, prev_head, prev_t);
     }
+    if (g.amax) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) out_max = fmaxf(out_max, __shfl_xor_sync(0xffffffffu, out_max, o));
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), __float_as_uint(out_max));
+    }
   } else if (g.tail > 0) {
     // ------------------------------------------------------------ tail query rows
     const int tw = warp - kFusedWarps, tid = threadIdx.x - 32 * kFusedWarps;
@@ -2670,6 +2678,7 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     constexpr int kKeys = (288 + 63) / 64;             // keys per thread
     bool ok = true;
     int hi = 0;
+    float tail_max = 0.f;
     for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
       const int b = head / g.H, h = head - b * g.H, sl = hi & 1;
       if (ok) ok = mbar_wait(k_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
@@ -2755,11 +2764,18 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       for (int i = tid; i < g.tail * 64; i += 32 * kB16TailWarps) {
         const int rr = i >> 6, d = i & 63;
         const int row = S - g.tail + rr;
-        if (ok)
-          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss + d] =
-              __float2bfloat16_rn((to[rr * 64 + d] + to[(kB16TailMax + rr) * 64 + d]) * inv_l[rr]);
+        if (ok) {
+          const __nv_bfloat16 ob = __float2bfloat16_rn((to[rr * 64 + d] + to[(kB16TailMax + rr) * 64 + d]) * inv_l[rr]);
+          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss + d] = ob;
+          tail_max = fmaxf(tail_max, fabsf(__bfloat162float(ob)));
+        }
       }
       named_bar_sync(kTailBar, 32 * kB16TailWarps);   // tp / to are reused by the next head
+    }
+    if (g.amax) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tail_max = fmaxf(tail_max, __shfl_xor_sync(0xffffffffu, tail_max, o));
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), __float_as_uint(tail_max));
     }
   }
   tc_fence_before();
@@ -2770,8 +2786,11 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
 
 static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                        int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
-                       int64_t oss, cudaStream_t s) {
+                       int64_t oss, float* amax, cudaStream_t s) {
   Bf16Geom g = make_bf16_geom(B, H, S, D, scale);
+  g.amax = amax;
+  if (amax && cudaMemsetAsync(amax, 0, sizeof(float), s) != cudaSuccess)
+    return fail(VF4_ERR_CUDA, "vf4_attn_bf16: amax reset failed");
   g.out = static_cast<__nv_bfloat16*>(out);
   g.osb = osb;
   g.osh = osh;
@@ -2948,7 +2967,7 @@ int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t
 
 int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                   int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, void* out, int64_t out_stride_b,
-                  int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream) {
+                  int64_t out_stride_h, int64_t out_stride_s, float* out_amax, vf4_stream_t stream) {
   if (int st = check_device()) return st;
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_bf16: bad sizes");
   if (!bf16_attn_ok(S, D))
@@ -2959,8 +2978,10 @@ int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_
       stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
     return fail(VF4_ERR_ALIGN, "vf4_attn_bf16: 16-byte aligned pointers and strides (multiples of 8) needed");
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: B*H too large");
+  if (out_amax && (reinterpret_cast<uintptr_t>(out_amax) & 3u))
+    return fail(VF4_ERR_ALIGN, "vf4_attn_bf16: out_amax must be 4-byte aligned");
   return launch_bf16(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
-                     out_stride_s, reinterpret_cast<cudaStream_t>(stream));
+                     out_stride_s, out_amax, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,

@@ -46,7 +46,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_attn_nvfp4": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _L, _P],
     "vf4_attn_nvfp4_ex": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _I, _P, _L, _P],
     "vf4_attn_fp8": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
-    "vf4_attn_bf16": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
+    "vf4_attn_bf16": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _P],
     "vf4_attn_nvfp4_noalloc": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
 }
 _RESTYPE = {"vf4_last_error_string": ctypes.c_char_p, "vf4_attn_workspace_size": ctypes.c_int64,

@@ -336,14 +336,17 @@ def fp8_kernel_ok(S: int, D: int) -> bool:
 
 def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
                    strides: tuple[int, int, int], scale: float, out: torch.Tensor,
-                   out_strides: tuple[int, int, int]) -> torch.Tensor:
-    """Exact-softmax bf16 attention (tcgen05 kind::f16) over bf16 q/k/v views sharing element strides."""
-    _need_cuda(q, k, v, out)
+                   out_strides: tuple[int, int, int], out_amax: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact-softmax bf16 attention (tcgen05 kind::f16) over bf16 q/k/v views sharing element strides;
+    ``out_amax`` (0-dim fp32) receives max |out| when given."""
+    _need_cuda(q, k, v, out, out_amax)
     for t in (q, k, v, out):
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("bf16 attention takes bf16 q/k/v/out")
+    if out_amax is not None and (out_amax.dtype != torch.float32 or out_amax.numel() != 1):
+        raise _lib.VitFp4Error("out_amax must be one fp32 value")
     _lib.call("vf4_attn_bf16", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
+              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _ptr(out_amax), _stream())
     _launched(1)
     return out
 
@@ -352,7 +355,8 @@ def bf16_kernel_ok(S: int, D: int) -> bool:
     return D == 64 and 1 <= S <= 288
 
 
-def attention_bf16_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float) -> torch.Tensor:
+def attention_bf16_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float,
+                              out_amax: torch.Tensor | None = None) -> torch.Tensor:
     """Packed (B, S, 3*H*D) bf16 projection output -> (B, S, H*D) bf16 through the bf16 kernel."""
     B, S, C3 = qkv.shape
     H = num_heads
@@ -360,7 +364,7 @@ def attention_bf16_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float) -
     x = qkv if qkv.is_contiguous() else qkv.contiguous()
     out = torch.empty((B, S, H * D), dtype=torch.bfloat16, device=qkv.device)
     attention_bf16(x, x[..., H * D:], x[..., 2 * H * D:], B, H, S, D, (S * C3, D, C3), scale, out,
-                   (S * H * D, D, H * D))
+                   (S * H * D, D, H * D), out_amax=out_amax)
     return out
 
 

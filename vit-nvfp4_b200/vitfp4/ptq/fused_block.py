@@ -52,8 +52,10 @@ class FusedNVFP4Block(nn.Module):
             return ops.attention_packed_qkv(qkv, H, a.scaling)
         if not getattr(a, "_nvfp4_attn", False) and qkv.dtype == torch.bfloat16 and ops.bf16_kernel_ok(S, D):
             # the reference's bf16 route (torch SDPA) on the tcgen05 kernel: exact softmax, fp32
-            # accumulation, output (B, S, H*D) read by the proj cast as it is
-            return ops.attention_bf16_packed_qkv(qkv, H, a.scaling)
+            # accumulation, output (B, S, H*D) read by the proj cast as it is; the kernel also
+            # returns max |out|, the amax of the proj's dynamic activation cast
+            am = torch.empty((), dtype=torch.float32, device=qkv.device)
+            return "amax", ops.attention_bf16_packed_qkv(qkv, H, a.scaling, out_amax=am), am
         q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
         if getattr(a, "_nvfp4_attn", False):   # the fp8 and mixed routes (GPU emulation)
             from ..nvfp4.attention import quant_sdpa
@@ -66,7 +68,7 @@ class FusedNVFP4Block(nn.Module):
             # is complete in either -- and hand both parts to the proj cast as they are
             o1 = F.scaled_dot_product_attention(q[:, :, :s_main], k, v, scale=a.scaling)
             o2 = F.scaled_dot_product_attention(q[:, :, s_main:], k, v, scale=a.scaling)
-            return o1.transpose(1, 2).reshape(B, s_main, H * D), o2.transpose(1, 2).reshape(B, S - s_main, H * D)
+            return "split", o1.transpose(1, 2).reshape(B, s_main, H * D), o2.transpose(1, 2).reshape(B, S - s_main, H * D)
         return F.scaled_dot_product_attention(q, k, v, scale=a.scaling).transpose(1, 2).reshape(B, S, H * D)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -81,8 +83,13 @@ class FusedNVFP4Block(nn.Module):
         wp, wsf = qkv_l._packed_weight()
         qkv = ops.gemm(ap, asf, ag, wp, wsf, qkv_l.w_global_scale, bias=qkv_l.bias).reshape(B, S, -1)
         o = self._attention(qkv)
-        if isinstance(o, tuple):   # split query range: one NVFP4 operand from both parts, no concatenation
-            op, osf, og = ops.cast_split(o[0], o[1], gs=proj_l.x_global_scale)
+        if isinstance(o, tuple) and o[0] == "split":   # one NVFP4 operand from both parts, no concatenation
+            op, osf, og = ops.cast_split(o[1], o[2], gs=proj_l.x_global_scale)
+            wp2, wsf2 = proj_l._packed_weight()
+            y = ops.gemm(op, osf, og, wp2, wsf2, proj_l.w_global_scale, bias=proj_l.bias)
+        elif isinstance(o, tuple):   # the attention kernel measured the amax: cast with its global
+            gs = proj_l.x_global_scale if proj_l.x_global_scale is not None else ops.global_scale(o[2])
+            op, osf, _, og = ops.cast(o[1].reshape(B * S, C), gs, "six")
             wp2, wsf2 = proj_l._packed_weight()
             y = ops.gemm(op, osf, og, wp2, wsf2, proj_l.w_global_scale, bias=proj_l.bias)
         else:
