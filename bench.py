@@ -45,12 +45,17 @@ NCU_TRAFFIC_PER_ROW = {
     ("gemm_residual", 1024, 4096): (288.748288e6 + 93.634816e6) / 65792,
     ("gemm_bias", 3072, 1024): (39.713280e6 + 350.148864e6) / 65792,
     ("gemm_bias", 1024, 1024): (38.528512e6 + 80.605952e6) / 65792,
+    # bf16 attention, per head of 257 x 64 (2048 heads, profiles/attn_bf16_vitl14_b128.md)
+    ("attn_bf16", 257, 64): (202.204160e6 + 42.473728e6) / 2048,
 }
 
 
 def gemm_algorithmic_bytes(kind: str, m: int, n: int, k: int) -> int:
     """HBM bytes a GEMM launch must move: A and B codes + E4M3 scales in, plus its output
-    (bf16; NVFP4 codes + scales for the GELU epilogue; residual read + bf16 write for fc2)."""
+    (bf16; NVFP4 codes + scales for the GELU epilogue; residual read + bf16 write for fc2).
+    For bf16 attention (m heads, n tokens, k head dim): q, k, v read and the output written once."""
+    if kind == "attn_bf16":
+        return m * n * k * 2 * 4
     operands = (m + n) * (k // 2 + k // 16)
     if kind == "gemm_gelu_nvfp4":
         return operands + m * (n // 2 + n // 16)
@@ -279,19 +284,26 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
     roofline = None
     if dom:
         achieved = dom[1][1] / (dom[1][2] * 1e-3) / 1e12
-        roofline = {"kernel": dom[0], "bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
-                    "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
-                    "peak_source": "4 x measured bf16 burst (MEASURED_PEAKS.json), of measured; FP4 itself not measured"
-                    if measured else "4 x fallback bf16 burst 1590 TFLOP/s (MEASURED_PEAKS.json absent), of fallback",
-                    "frac_of_nominal_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4), "traffic": None}
+        src = "measured bf16 burst (MEASURED_PEAKS.json), of measured" if measured else \
+            "fallback bf16 burst 1590 TFLOP/s (MEASURED_PEAKS.json absent), of fallback"
+        if dom[0].startswith("attn_bf16"):   # bf16 tensor-core kernel
+            peak, peak_source, nominal = bf16_tf, src, 2250.0
+        else:                                # FP4 GEMMs: FP4 itself is not measured
+            peak, peak_source, nominal = fp4_peak, "4 x " + src + "; FP4 itself not measured", FP4_NOMINAL_TFLOPS
+        roofline = {"kernel": dom[0], "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                    "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": peak_source,
+                    "frac_of_nominal": round(achieved / nominal, 4), "nominal_tflops": nominal, "traffic": None}
         kind, dims = dom[0].rsplit("_", 1)
         m_rows, n_cols, k_dim = (int(x) for x in dims.split("x"))
         roofline["algorithmic_bytes"] = gemm_algorithmic_bytes(kind, m_rows, n_cols, k_dim)
         per_row = NCU_TRAFFIC_PER_ROW.get((kind, n_cols, k_dim))
         if per_row is not None:
             roofline["traffic"] = round(per_row * m_rows)   # bytes per launch
-            roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
-                                          "M = 65792, scaled by rows (profiles/gemm_nvfp4_vitl14_b256.md)")
+            roofline["traffic_source"] = (
+                "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch 128, scaled by heads "
+                "(profiles/attn_bf16_vitl14_b128.md)" if kind == "attn_bf16" else
+                "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792, scaled by rows "
+                "(profiles/gemm_nvfp4_vitl14_b256.md)")
     steps = args.steps
     img_per_step = args.batch
     line = {

@@ -15,7 +15,8 @@ SF_TORCH_DTYPE = torch.uint8  # E4M3 bytes are carried as uint8 internally
 
 class Probe:
     """Launch accounting for the benchmark: counts libvitfp4 kernel launches and, when
-    ``timing`` is on, brackets every GEMM launch with CUDA events on the launching stream."""
+    ``timing`` is on, brackets every GEMM and bf16-attention launch with CUDA events on the
+    launching stream."""
 
     def __init__(self):
         self.launches = 0
@@ -345,8 +346,9 @@ def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
             raise _lib.VitFp4Error("bf16 attention takes bf16 q/k/v/out")
     if out_amax is not None and (out_amax.dtype != torch.float32 or out_amax.numel() != 1):
         raise _lib.VitFp4Error("out_amax must be one fp32 value")
-    _lib.call("vf4_attn_bf16", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _ptr(out_amax), _stream())
+    with _GemmTimer(f"attn_bf16_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
+        _lib.call("vf4_attn_bf16", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+                  float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _ptr(out_amax), _stream())
     _launched(1)
     return out
 
