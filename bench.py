@@ -64,6 +64,34 @@ def gemm_algorithmic_bytes(kind: str, m: int, n: int, k: int) -> int:
     return operands + m * n * 2
 
 
+def roofline_entry(name: str, flops: float, ms: float, bf16_tf: float, measured: bool) -> dict:
+    """Roofline object of one timed kernel kind ("<kind>_<m>x<n>x<k>"): its FLOPs over its summed
+    launch durations, against the bf16 peak for the bf16 attention kernel and 4 x the bf16 peak for
+    the FP4 GEMMs, with the algorithmic bytes of one launch and the ncu DRAM bytes where captured."""
+    achieved = flops / (ms * 1e-3) / 1e12
+    src = "measured bf16 burst (MEASURED_PEAKS.json), of measured" if measured else \
+        "fallback bf16 burst 1590 TFLOP/s (MEASURED_PEAKS.json absent), of fallback"
+    if name.startswith("attn_bf16"):     # bf16 tensor-core kernel
+        peak, peak_source, nominal = bf16_tf, src, 2250.0
+    else:                                # FP4 GEMMs: FP4 itself is not measured
+        peak, peak_source, nominal = 4 * bf16_tf, "4 x " + src + "; FP4 itself not measured", FP4_NOMINAL_TFLOPS
+    r = {"kernel": name, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": peak_source,
+         "frac_of_nominal": round(achieved / nominal, 4), "nominal_tflops": nominal, "traffic": None}
+    kind, dims = name.rsplit("_", 1)
+    m_rows, n_cols, k_dim = (int(x) for x in dims.split("x"))
+    r["algorithmic_bytes"] = gemm_algorithmic_bytes(kind, m_rows, n_cols, k_dim)
+    per_row = NCU_TRAFFIC_PER_ROW.get((kind, n_cols, k_dim))
+    if per_row is not None:
+        r["traffic"] = round(per_row * m_rows)   # bytes per launch
+        r["traffic_source"] = (
+            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch 128, scaled by heads "
+            "(profiles/attn_bf16_vitl14_b128.md)" if kind == "attn_bf16" else
+            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792, scaled by rows "
+            "(profiles/gemm_nvfp4_vitl14_b256.md)")
+    return r
+
+
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -277,41 +305,14 @@ def run_vitfp4(args, rank: int, world: int, local_rank: int):
     peaks = _peaks()
     measured = bool(peaks.get("bf16_tflops"))
     bf16_tf = peaks["bf16_tflops"] if measured else FALLBACK_PEAKS["bf16_tflops"]
-    fp4_peak = 4 * bf16_tf
     kernels = {k: {"launches": v[0], "ms_total": round(v[2], 3),
                    "tflops": round(v[1] / (v[2] * 1e-3) / 1e12, 1)} for k, v in sorted(by_kind.items())}
-    src = "measured bf16 burst (MEASURED_PEAKS.json), of measured" if measured else \
-        "fallback bf16 burst 1590 TFLOP/s (MEASURED_PEAKS.json absent), of fallback"
-
-    def kernel_roofline(name, rec):
-        """Roofline entry of one timed kernel kind: FLOPs over its summed launch durations."""
-        achieved = rec[1] / (rec[2] * 1e-3) / 1e12
-        if name.startswith("attn_bf16"):     # bf16 tensor-core kernel
-            peak, peak_source, nominal = bf16_tf, src, 2250.0
-        else:                                # FP4 GEMMs: FP4 itself is not measured
-            peak, peak_source, nominal = fp4_peak, "4 x " + src + "; FP4 itself not measured", FP4_NOMINAL_TFLOPS
-        r = {"kernel": name, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
-             "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": peak_source,
-             "frac_of_nominal": round(achieved / nominal, 4), "nominal_tflops": nominal, "traffic": None}
-        kind, dims = name.rsplit("_", 1)
-        m_rows, n_cols, k_dim = (int(x) for x in dims.split("x"))
-        r["algorithmic_bytes"] = gemm_algorithmic_bytes(kind, m_rows, n_cols, k_dim)
-        per_row = NCU_TRAFFIC_PER_ROW.get((kind, n_cols, k_dim))
-        if per_row is not None:
-            r["traffic"] = round(per_row * m_rows)   # bytes per launch
-            r["traffic_source"] = (
-                "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch 128, scaled by heads "
-                "(profiles/attn_bf16_vitl14_b128.md)" if kind == "attn_bf16" else
-                "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792, scaled by rows "
-                "(profiles/gemm_nvfp4_vitl14_b256.md)")
-        return r
-
     # the dominant kernel by device time, and (the metric's second figure) the dominant NVFP4 GEMM
     dom = max(by_kind.items(), key=lambda kv: kv[1][2]) if by_kind else None
     gemms = {k: v for k, v in by_kind.items() if k.startswith("gemm")}
     dom_gemm = max(gemms.items(), key=lambda kv: kv[1][2]) if gemms else None
-    roofline = kernel_roofline(*dom) if dom else None
-    gemm_roofline = kernel_roofline(*dom_gemm) if dom_gemm else None
+    roofline = roofline_entry(dom[0], dom[1][1], dom[1][2], bf16_tf, measured) if dom else None
+    gemm_roofline = roofline_entry(dom_gemm[0], dom_gemm[1][1], dom_gemm[1][2], bf16_tf, measured) if dom_gemm else None
     steps = args.steps
     img_per_step = args.batch
     line = {
