@@ -35,17 +35,16 @@ FP4_NOMINAL_TFLOPS = 9000.0
 # used when MEASURED_PEAKS.json is absent: an earlier measurement on the same B200 pool
 # (STREAM-style copy and cuBLAS bf16 burst)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-# DRAM bytes (read + write) per output row measured by ncu for the GEMM kinds that can dominate
-# (profiles/gemm_nvfp4_vitl14_b256.md: the fc1 launch at M = 65792 moved 40.5 + 99.2 MB; A and the
-# output grow with M while the 2.4 MB of weights do not, so bytes scale with the rows)
-# ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792 (ViT-L/14, batch 256),
-# per row of A, keyed by (kernel kind, N, K): profiles/gemm_nvfp4_vitl14_b256.md
+# DRAM bytes (read + write) per unit measured by ncu for the kernels that can dominate, keyed by
+# (kernel kind, N, K): ncu dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch at
+# M = 65792 (ViT-L/14, batch 256) per row of A -- the fc1 launch moved 40.5 + 99.2 MB; A and the
+# output grow with M while the 2.4 MB of weights do not, so bytes scale with the rows -- and of one
+# bf16 attention launch at batch 128 (2048 heads of 257 x 64) per head
 NCU_TRAFFIC_PER_ROW = {
     ("gemm_gelu_nvfp4", 4096, 1024): (40.415488e6 + 98.564096e6) / 65792,
     ("gemm_residual", 1024, 4096): (288.748288e6 + 93.634816e6) / 65792,
     ("gemm_bias", 3072, 1024): (39.713280e6 + 350.148864e6) / 65792,
     ("gemm_bias", 1024, 1024): (38.528512e6 + 80.605952e6) / 65792,
-    # bf16 attention, per head of 257 x 64 (2048 heads, profiles/attn_bf16_vitl14_b128.md)
     ("attn_bf16", 257, 64): (202.204160e6 + 42.473728e6) / 2048,
 }
 
@@ -85,10 +84,9 @@ def roofline_entry(name: str, flops: float, ms: float, bf16_tf: float, measured:
     if per_row is not None:
         r["traffic"] = round(per_row * m_rows)   # bytes per launch
         r["traffic_source"] = (
-            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch 128, scaled by heads "
-            "(profiles/attn_bf16_vitl14_b128.md)" if kind == "attn_bf16" else
-            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792, scaled by rows "
-            "(profiles/gemm_nvfp4_vitl14_b256.md)")
+            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch 128 (2048 heads), "
+            "scaled by heads" if kind == "attn_bf16" else
+            "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 65792, scaled by rows")
     return r
 
 
