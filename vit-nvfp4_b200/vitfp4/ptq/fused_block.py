@@ -44,7 +44,9 @@ class FusedNVFP4Block(nn.Module):
                 and block.norm1.weight is not None and block.norm1.bias is not None
                 and block.norm1.normalized_shape[0] % 64 == 0 and block.norm1.normalized_shape[0] <= 1280)
 
-    def _attention(self, qkv: torch.Tensor) -> torch.Tensor:
+    def _attention(self, qkv: torch.Tensor):
+        """Attention of the packed (B, S, 3*H*D) projection: a (B, S, H*D) tensor, ("amax", out,
+        max |out|) from the bf16 kernel, or ("split", out[:, :128k], out[:, 128k:]) from two cuDNN calls."""
         a = self.attn
         B, S, _ = qkv.shape
         H, D = a.num_heads, a.head_dim
