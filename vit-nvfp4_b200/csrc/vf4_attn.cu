@@ -2686,9 +2686,16 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       const uint8_t* qt = gb + g.tqb;
       float inv_l[kB16TailMax];
       for (int rr = 0; rr < g.tail; ++rr) {
-        float qv[64];
+        // the query row as fp32 pairs; each key's dot product by packed FMAs into two accumulators
+        unsigned long long q2[32];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) raw_load8(qt, rr, j, qv + 8 * j);
+        for (int j = 0; j < 8; ++j) {
+          const uint4 a = *reinterpret_cast<const uint4*>(qt + rr * 128 + ((j ^ (rr & 7)) << 4));
+          q2[4 * j] = bf16x2_to_f32x2(a.x);
+          q2[4 * j + 1] = bf16x2_to_f32x2(a.y);
+          q2[4 * j + 2] = bf16x2_to_f32x2(a.z);
+          q2[4 * j + 3] = bf16x2_to_f32x2(a.w);
+        }
         float s[kKeys];
         float mx = -INFINITY;
 #pragma unroll
@@ -2696,15 +2703,19 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
           const int key = tid + 64 * u;
           s[u] = -INFINITY;
           if (ok && key < S) {
-            float acc = 0.f;
+            unsigned long long acc0 = f32x2_pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              float kv[8];
-              raw_load8(kt, key, j, kv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc = __fmaf_rn(kv[e], qv[8 * j + e], acc);
+              const uint4 w = *reinterpret_cast<const uint4*>(kt + key * 128 + ((j ^ (key & 7)) << 4));
+              acc0 = fma_f32x2(bf16x2_to_f32x2(w.x), q2[4 * j], acc0);
+              acc1 = fma_f32x2(bf16x2_to_f32x2(w.y), q2[4 * j + 1], acc1);
+              acc0 = fma_f32x2(bf16x2_to_f32x2(w.z), q2[4 * j + 2], acc0);
+              acc1 = fma_f32x2(bf16x2_to_f32x2(w.w), q2[4 * j + 3], acc1);
             }
-            s[u] = acc * c;
+            float a0, a1, b0, b1;
+            f32x2_unpack(acc0, &a0, &a1);
+            f32x2_unpack(acc1, &b0, &b1);
+            s[u] = ((a0 + a1) + (b0 + b1)) * c;
             mx = fmaxf(mx, s[u]);
           }
         }
@@ -2732,30 +2743,41 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       if (tid == 0) mbar_arrive(k_free);
       if (ok) ok = mbar_wait(v_full(sl), (uint32_t)(hi >> 1) & 1u, err, kDevErrTimeoutFull);
       {
-        // thread: head-dim pair lane, key half tw
-        const int half = (S + 1) / 2;
-        const int j0 = tw * half, j1 = tw == 0 ? half : S;
-        float a[kB16TailMax][2];
+        // thread: head-dim quad dq = tid % 16 (dims 4 dq .. 4 dq + 3), key quarter tid / 16; the two
+        // quarters of a warp are merged by a shuffle, the two warps through shared memory
+        const int dq = tid & 15, kq = tid >> 4;
+        const int quarter = (S + 3) / 4;
+        const int j0 = kq * quarter, j1 = min(S, j0 + quarter);
+        const uint8_t* vt = gb + (sl ? g.vb[1] : g.vb[0]);
+        unsigned long long a[kB16TailMax][2];
 #pragma unroll
-        for (int rr = 0; rr < kB16TailMax; ++rr) a[rr][0] = a[rr][1] = 0.f;
+        for (int rr = 0; rr < kB16TailMax; ++rr) a[rr][0] = a[rr][1] = f32x2_pack(0.f, 0.f);
         if (ok) {
           for (int j = j0; j < j1; ++j) {
-            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(gb + (sl ? g.vb[1] : g.vb[0]) + j * 128 +
-                                                                   (((lane >> 2) ^ (j & 7)) << 4) + (lane & 3) * 4);
-            const float v0 = __uint_as_float(w2 << 16), v1 = __uint_as_float(w2 & 0xFFFF0000u);
+            const uint2 w = *reinterpret_cast<const uint2*>(vt + j * 128 + (((dq >> 1) ^ (j & 7)) << 4) + (dq & 1) * 8);
+            const unsigned long long v01 = bf16x2_to_f32x2(w.x), v23 = bf16x2_to_f32x2(w.y);
 #pragma unroll
             for (int rr = 0; rr < kB16TailMax; ++rr)
               if (rr < g.tail) {
-                a[rr][0] = __fmaf_rn(tp[rr * g.skp + j], v0, a[rr][0]);
-                a[rr][1] = __fmaf_rn(tp[rr * g.skp + j], v1, a[rr][1]);
+                const float p = tp[rr * g.skp + j];
+                const unsigned long long pp = f32x2_pack(p, p);
+                a[rr][0] = fma_f32x2(v01, pp, a[rr][0]);
+                a[rr][1] = fma_f32x2(v23, pp, a[rr][1]);
               }
           }
         }
 #pragma unroll
         for (int rr = 0; rr < kB16TailMax; ++rr)
           if (rr < g.tail) {
-            to[(tw * kB16TailMax + rr) * 64 + 2 * lane] = a[rr][0];
-            to[(tw * kB16TailMax + rr) * 64 + 2 * lane + 1] = a[rr][1];
+            float o[4];
+            f32x2_unpack(a[rr][0], &o[0], &o[1]);
+            f32x2_unpack(a[rr][1], &o[2], &o[3]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], 16);
+            if (lane < 16) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) to[(tw * kB16TailMax + rr) * 64 + 4 * dq + e] = o[e];
+            }
           }
       }
       named_bar_sync(kTailBar, 32 * kB16TailWarps);
