@@ -77,6 +77,12 @@ VF4_API int vf4_amax(const void* x, int dtype, int64_t n, int gelu, float* amax_
  * Replaces quant.py:48-53. amax and gs_out may alias. */
 VF4_API int vf4_global_scale(const float* amax, int block_select, float* gs_out, vf4_stream_t stream);
 
+/* out[i] = erf-GELU(x[i]) for n fp32 values, computed by the device function of the fc1
+ * GELU-NVFP4 epilogue (0.5 x (1 + erf(x / sqrt 2)) within 2.5e-7 |x|, one ex2 per element).
+ * The reference's GELU is torch's F.gelu / Triton's tl.erf in triton_cast.py:302-303; this
+ * elementwise form exists so the epilogue's function can be checked and reused on its own. */
+VF4_API int vf4_gelu_erf_f32(const float* x, int64_t n, float* out, vf4_stream_t stream);
+
 /* NVFP4 activation / weight cast, bit-exact to quantize_to_nvfp4 + pack_e2m1 + to_blocked
  * (quant.py:20-69, pack.py:4-9, pack.py:39-58) and the fused GELU cast of
  * triton_cast.py:138 (cast_nvfp4) with the quant.py arithmetic.

@@ -242,6 +242,44 @@ def gemm_reference(a_codes, a_bs, a_gs, b_codes, b_bs, b_gs):
 
 
 # --------------------------------------------------------------------------
+# The Triton cast (nvfp4/triton_cast.py:138-370): the reference's fused-MLP casts
+# --------------------------------------------------------------------------
+E4M3_EPS = F32(1.5258789e-05)      # triton_cast.py:247, the lower clamp of a block scale
+
+
+def e2m1_code_rne(q: np.ndarray) -> np.ndarray:
+    """E2M1 code of q with nearest-even rounding (the hardware fp32 -> fp4 conversion the Triton
+    cast uses, triton_cast.py:343): ties at 0.75, 1.75 and 3.5 go UP to the even code, the other
+    ties (0.25, 1.25, 2.5, 5.0) down; the sign bit is q's (so -0.0 -> code 8)."""
+    q = np.asarray(q, dtype=np.float32)
+    m = np.minimum(np.abs(q), E2M1_MAX)
+    idx = np.zeros(q.shape, dtype=np.uint8)
+    for mid in MID:
+        idx += (m > mid).astype(np.uint8)
+    idx += np.isin(m, np.array([0.75, 1.75, 3.5], np.float32)).astype(np.uint8)
+    return (np.signbit(q).astype(np.uint8) << 3) | idx
+
+
+def triton_cast_nvfp4(x, per_tensor_scale, apply_gelu: bool = False):
+    """cast_nvfp4 (triton_cast.py:138-233, kernel :235-370; E4M3 scales, precise math):
+    g = 1 / per_tensor_scale (:163); optional fp32 erf-GELU first (:302-303); per 16-block
+    scale = e4m3(clamp(RN(amax / 6) * g, 2^-16, 448)) (:318-322); q = x * RN(g / scale) (:327-331);
+    nearest-even E2M1.  Returns (codes (M, K) uint8, scale bytes (M, K/16) uint8)."""
+    xf = np.asarray(x, dtype=np.float32)
+    if apply_gelu:
+        xf = gelu(xf)
+    g = F32(1.0) / F32(per_tensor_scale)
+    blocks = xf.reshape(*xf.shape[:-1], xf.shape[-1] // 16, 16)
+    amax = np.abs(blocks).max(axis=-1)
+    sc = np.clip((amax / F32(6.0)).astype(np.float32) * g, E4M3_EPS, E4M3_MAX).astype(np.float32)
+    s8 = e4m3_encode(sc)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        total = (g / e4m3_decode(s8)).astype(np.float32)
+        q = (blocks * total[..., None]).astype(np.float32)
+    return e2m1_code_rne(q).reshape(xf.shape), s8
+
+
+# --------------------------------------------------------------------------
 # bf16 rounding, GELU, FP8 qdq, emulated SDPA
 # --------------------------------------------------------------------------
 def to_bf16(x) -> np.ndarray:

@@ -50,8 +50,11 @@ def _edge_block_matrix() -> torch.Tensor:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default=os.environ.get("VIT_NVFP4_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--reference-src", default=os.environ.get("VIT_NVFP4_REFERENCE_SRC"),
+                    help="the reference's src/ directory (or set VIT_NVFP4_REFERENCE_SRC)")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("pass --reference-src <vit-nvfp4>/src or set VIT_NVFP4_REFERENCE_SRC")
     sys.path.insert(0, args.reference_src)
     from vit_nvfp4.nvfp4 import format as fmt
     from vit_nvfp4.nvfp4 import gemm as G

@@ -276,3 +276,25 @@ def test_bf16_kernel_rejects_unsupported_shapes():
     with pytest.raises(_lib.VitFp4Error):
         ops.attention_bf16(q, q, q, 1, 1, 300, 64, (300 * 64, 300 * 64, 64), 0.125, out, (300 * 64, 300 * 64, 64))
     assert not ops.bf16_kernel_ok(300, 64) and not ops.bf16_kernel_ok(257, 80) and ops.bf16_kernel_ok(257, 64)
+
+
+@pytest.mark.parametrize("S,row", [(257, 5), (257, 256), (130, 129)])
+def test_bf16_kernel_amax_propagates_nan(S, row):
+    """A NaN in the attention output reaches the fused max |out| as NaN, as the reference's torch amax
+    of the SDPA output would give it (a float max would drop it and hand the proj cast a finite global).
+    One NaN in v makes every query row's output NaN in that head's column; row picks a tile row or a
+    tail row (S = 257 / 130 run the per-row tail for the last rows)."""
+    from vitfp4.nvfp4 import ops
+    B, H, D = 2, 3, 64
+    torch.manual_seed(S)
+    qkv = torch.randn(B, S, 3 * H * D, device="cuda").bfloat16()
+    qkv[1, row, 2 * H * D + D + 7] = float("nan")          # v of image 1, head 1, token `row`
+    am = torch.empty((), dtype=torch.float32, device="cuda")
+    got = ops.attention_bf16_packed_qkv(qkv, H, D ** -0.5, out_amax=am)
+    torch.cuda.synchronize()
+    assert got.isnan().any() and got.float().abs().amax().isnan()
+    assert am.isnan(), am
+    # and without a NaN the fused amax is finite and equals the output's
+    qkv[1, row, 2 * H * D + D + 7] = 0.5
+    got = ops.attention_bf16_packed_qkv(qkv, H, D ** -0.5, out_amax=am)
+    assert torch.equal(am, got.float().abs().amax())

@@ -87,35 +87,65 @@ def _gelu_tanh(x):
 @pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("M,K,N", [(256, 1024, 4096), (197, 768, 3072), (130, 512, 128)])
 def test_gemm_gelu_nvfp4_epilogue(M, K, N, exact):
-    """fc1 epilogue: NVFP4(GELU(gemm + b1)) with a static global scale; the intermediate stays fp32
-    (the unfused reference rounds it to bf16).  exact: erf-GELU via A&S 7.1.26 (|err| <= 1.5e-7),
-    compared with erf; default: the tanh form with the hardware tanh, compared with the tanh form."""
+    """fc1 epilogue NVFP4(GELU(gemm + b1)) with a static global scale, the reference's fused-MLP step
+    (fused_mlp.py:47-51).  exact (the default of FusedNVFP4MLP): the GEMM rounded to bf16, + b1 in bf16,
+    erf-GELU, the Triton cast's arithmetic -- compared with the oracle's restatement of exactly those
+    steps, so only fp32 summation order (which can move a bf16 rounding) and the kernel's erf (within
+    2.5e-7 |x|) separate them: codes and scales agree on all but < 2e-4 of the elements.  The tanh
+    form (no roundings, hardware tanh) is compared with its own function at < 2e-3."""
     ops = _ops()
     A, B = _operands(M, N, K, seed=7)
     bias = (np.random.default_rng(3).standard_normal(N) * 0.1).astype(np.float32)
     ref_y = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
-    h = (oracle.gelu if exact else _gelu_tanh)(ref_y + oracle.to_bf16(bias))
-    gh = np.float32(np.abs(h).max() / 2688.0)
+    b16 = oracle.to_bf16(bias)
+    y1 = oracle.to_bf16(oracle.to_bf16(ref_y) + b16)            # gemm_packed -> bf16, then y1 + b1
+    h = oracle.gelu(y1) if exact else _gelu_tanh(ref_y + b16)
+    gh = np.float32(np.abs(oracle.to_bf16(h)).max() / 2688.0)
     ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
     bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
     hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, torch.from_numpy(bias).cuda().bfloat16(),
                                   torch.tensor(gh, device="cuda"), exact=exact)
     torch.cuda.synchronize()
-    c, b, _ = oracle.quantize_to_nvfp4(h, 16, global_scale=gh)
+    if exact:
+        c, b = oracle.triton_cast_nvfp4(y1, gh, apply_gelu=True)
+    else:
+        c, b = oracle.triton_cast_nvfp4(h, gh)
     codes = oracle.unpack_e2m1(hp.cpu().numpy())
     sf = oracle.from_blocked(hsf.cpu().numpy(), M, N // 16)
-    # accumulation order can move a value across a rounding boundary: require near-identity
-    assert (codes != c).mean() < 2e-3, (codes != c).mean()
-    assert (sf != b).mean() < 2e-3, (sf != b).mean()
+    bar = 2e-4 if exact else 2e-3
+    assert (codes != c).mean() < bar, (codes != c).mean()
+    assert (sf != b).mean() < bar, (sf != b).mean()
     deq = oracle.dequantize_nvfp4(codes, sf, gh)
-    assert cos(deq, oracle.dequantize_nvfp4(c, b, gh)) >= 0.999
-    # either flavour stays within FP4 resolution of the erf-GELU quantization
-    ce, be, _ = oracle.quantize_to_nvfp4(oracle.gelu(ref_y + oracle.to_bf16(bias)), 16, global_scale=gh)
+    assert cos(deq, oracle.dequantize_nvfp4(c, b, gh)) >= 0.9999
+    # either flavour stays within FP4 resolution of the reference's erf-GELU quantization
+    ce, be = oracle.triton_cast_nvfp4(y1, gh, apply_gelu=True)
     assert cos(deq, oracle.dequantize_nvfp4(ce, be, gh)) >= 0.998
     # padded scale rows of the last 128-row tile are zero
     full = hsf.cpu().numpy()
     pad = oracle.from_blocked(full, (M + 127) // 128 * 128, N // 16)[M:]
     assert (pad == 0).all()
+
+
+def test_gelu_erf_matches_torch_exact_gelu():
+    """The fc1 epilogue's erf-GELU (vf4_gelu_erf_f32 runs the same device function elementwise)
+    against torch's exact F.gelu on the GPU (CUDA erff): |error| <= 3e-7 |x| + 1e-30 over a dense
+    sweep of [-12, 12] plus the saturation edge, +-inf, NaN and signed zeros."""
+    from vitfp4 import _lib
+    x = torch.cat([torch.linspace(-12, 12, 2_000_001, device="cuda"),
+                   torch.linspace(5.5, 5.6, 10001, device="cuda"), -torch.linspace(5.5, 5.6, 10001, device="cuda"),
+                   torch.tensor([0.0, -0.0, 1e-30, -1e-30, 1e4, -1e4], device="cuda")])
+    out = torch.empty_like(x)
+    _lib.call("vf4_gelu_erf_f32", x.data_ptr(), x.numel(), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    ref = torch.nn.functional.gelu(x.double())
+    err = (out.double() - ref).abs()
+    assert (err <= 3e-7 * x.double().abs() + 1e-30).all(), float((err / x.double().abs().clamp_min(1e-30)).max())
+    # where fp32 erf has rounded to +-1 the result is x itself or exactly zero
+    big = x.abs() >= 5.6
+    assert torch.equal(out[big & (x > 0)], x[big & (x > 0)]) and (out[big & (x < 0)] == 0).all()
+    special = torch.tensor([float("inf"), float("-inf"), float("nan")], device="cuda")
+    o2 = torch.empty_like(special)
+    _lib.call("vf4_gelu_erf_f32", special.data_ptr(), 3, o2.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert o2[0].item() == float("inf") and o2[1:].isnan().all()       # as 0.5 x (1 + erf(x / sqrt 2))
 
 
 def test_gemm_full_size_sampled_rows():

@@ -26,7 +26,8 @@ def _call(name, lib, q, k, v, B, H, S, D, out, ws=None):
     return getattr(lib, name)(*args, stream)
 
 
-@pytest.mark.parametrize("shapes", [[(2, 4, 257, 64), (1, 2, 1025, 80)]])
+@pytest.mark.parametrize("shapes", [[(2, 4, 257, 64), (1, 2, 1025, 80)],     # fused route, then long-sequence
+                                    [(1, 2, 1025, 80), (2, 4, 257, 64)]])    # and the reverse order
 def test_noalloc_matches_workspace_entry_point_twice(shapes):
     from vitfp4 import _lib
     lib = _lib.lib()

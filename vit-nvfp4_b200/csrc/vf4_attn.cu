@@ -1693,16 +1693,14 @@ static int launch_fused(const void* q, const void* k, const void* v, int64_t B, 
   if (int st = make_head_map(&to, out, g, osb, osh, oss, 32, g.out_hs)) return st;
   if (packed) {
     const int smem = (int)g.img_bytes;
-    cudaError_t e = cudaFuncSetAttribute(attn_pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (int st = smem_optin(attn_pack_kernel, smem)) return st;
     attn_pack_kernel<<<(unsigned)g.heads, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
                                                           static_cast<const __nv_bfloat16*>(k),
                                                           static_cast<const __nv_bfloat16*>(v), sb, sh, ss, g, images);
     if (int st = launch_status("vf4_attn_nvfp4 (pack)")) return st;
   }
   auto kern = packed ? attn_fused_kernel<true> : attn_fused_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(kern, (int)g.total)) return st;
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
   kern<<<grid, kFusedWarps * 32, g.total, s>>>(tq, tk, tv, to, g);
   return launch_status(packed ? "vf4_attn_nvfp4 (fused, packed operands)" : "vf4_attn_nvfp4 (fused)");
@@ -2213,8 +2211,7 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
   if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&to, out, fg, osb, osh, oss, 32, g.out_hs)) return st;
-  cudaError_t e = cudaFuncSetAttribute(attn_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(attn_fp8_kernel, (int)g.total)) return st;
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
   attn_fp8_kernel<<<grid, kFusedWarps * 32, g.total, s>>>(tk, tv, to, g);
   return launch_status("vf4_attn_fp8");
@@ -2503,7 +2500,11 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int r = qd * 32 + lane;
     bool ok = true;
-    float out_max = 0.f;   // max |out| over this thread's stores (the amax of the proj input)
+    // max |out| over this thread's stores (the amax of the proj input), kept as the bit patterns of
+    // the bf16 magnitudes in two 16-bit lanes: unsigned order of non-negative bf16 bits is their
+    // numeric order and a NaN (0x7FC0) sorts above +inf, so a NaN output reaches the amax as the
+    // reference's torch amax would give it, instead of being dropped by a float max
+    uint32_t out_max2 = 0;
     // O / rowsum -> bf16, each thread storing its row's columns of this slice straight to global
     // memory (the row sums of every slice were written before the quadrant barrier of the next
     // tile's pass 1, which this warp has passed)
@@ -2540,7 +2541,7 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
               __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[k][2 * i]) * f,
                                                         __uint_as_float(ov[k][2 * i + 1]) * f);
               w[i] = *reinterpret_cast<uint32_t*>(&hv);
-              out_max = max3f(out_max, fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
+              out_max2 = umax_u16x2(out_max2, w[i] & 0x7FFF7FFFu);
             }
             *reinterpret_cast<uint4*>(orow + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
           }
@@ -2663,8 +2664,8 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     }
     if (g.amax) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) out_max = fmaxf(out_max, __shfl_xor_sync(0xffffffffu, out_max, o));
-      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), __float_as_uint(out_max));
+      const uint32_t m = __reduce_max_sync(0xffffffffu, max(out_max2 & 0xFFFFu, out_max2 >> 16) << 16);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), m);
     }
   } else if (g.tail > 0) {
     // ------------------------------------------------------------ tail query rows
@@ -2678,7 +2679,7 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
     constexpr int kKeys = (288 + 63) / 64;             // keys per thread
     bool ok = true;
     int hi = 0;
-    float tail_max = 0.f;
+    uint32_t tail_max = 0;   // fp32 bits of max |out| of the tail rows (NaN propagates, as above)
     for (int head = blockIdx.x; head < g.heads; head += gridDim.x, ++hi) {
       const int b = head / g.H, h = head - b * g.H, sl = hi & 1;
       if (ok) ok = mbar_wait(k_full, (uint32_t)hi & 1u, err, kDevErrTimeoutFull);
@@ -2789,15 +2790,15 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
         if (ok) {
           const __nv_bfloat16 ob = __float2bfloat16_rn((to[rr * 64 + d] + to[(kB16TailMax + rr) * 64 + d]) * inv_l[rr]);
           g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss + d] = ob;
-          tail_max = fmaxf(tail_max, fabsf(__bfloat162float(ob)));
+          tail_max = max(tail_max, (uint32_t)(__bfloat16_as_ushort(ob) & 0x7FFFu) << 16);
         }
       }
       named_bar_sync(kTailBar, 32 * kB16TailWarps);   // tp / to are reused by the next head
     }
     if (g.amax) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tail_max = fmaxf(tail_max, __shfl_xor_sync(0xffffffffu, tail_max, o));
-      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), __float_as_uint(tail_max));
+      tail_max = __reduce_max_sync(0xffffffffu, tail_max);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), tail_max);
     }
   }
   tc_fence_before();
@@ -2824,8 +2825,7 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
   if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return st;
-  cudaError_t e = cudaFuncSetAttribute(attn_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(attn_bf16_kernel, (int)g.total)) return st;
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
   attn_bf16_kernel<<<grid, kB16Warps * 32, g.total, s>>>(tq, tk, tv, tt, g);
   return launch_status("vf4_attn_bf16");
@@ -2860,8 +2860,7 @@ static int launch_fwd(const AttnGeom& g, const uint8_t* ws, float scale, void* o
   if (int st = make_map(&tv, ws + g.off_v, g.BH * C::DV, g.S_pad / 2, 64, C::DV, CU_TENSOR_MAP_SWIZZLE_64B))
     return st;
   auto kern = attn_fwd_kernel<DP>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(kern, (int)L.total)) return st;
   dim3 grid(g.nc, (unsigned)g.BH);
   kern<<<grid, C::THREADS, L.total, s>>>(tq, tk, tv, g, ws, L, scale, static_cast<__nv_bfloat16*>(out), osb, osh,
                                          oss);
@@ -2953,8 +2952,7 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
     } else {
       const int D8 = (int)D / 8, rpi = 256 / D8;
       const int smem = 32 % D8 == 0 ? 8 * 6 * (int)D * 4 : 6 * rpi * (int)D * 4;
-      cudaError_t e = cudaFuncSetAttribute(attn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      if (int st = smem_optin(attn_stats_kernel, smem)) return st;
       attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
                                                              (int)D, D <= 64 ? 64 : 128, stats, amax3);
     }
@@ -3032,9 +3030,11 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
 //     VF4_ERR_UNSUPPORTED and launch nothing;
 //   * the array lives on every GPU that loads the library until the process exits;
 //   * the host name g_attn_scratch is only a host-side stand-in for the symbol, never a device
-//     address: the first call on each device (with that device current) resolves the real
-//     address with cudaGetSymbolAddress and caches it, so make that first call before any
-//     stream capture;
+//     address: the first call in each CUDA context (with its device current) resolves the real
+//     address with cudaGetSymbolAddress and caches it keyed by the context's ID, so make that
+//     first call before any stream capture; a new context on the device (after a device reset,
+//     or a caller's own driver-API context) resolves again, and a failed resolution caches
+//     nothing, so a later call retries;
 //   * every call shares the one array and it keeps the last call's contents; nothing in it
 //     has to start at zero (each call clears the three maxima itself, and the statistics and
 //     prep kernels rewrite every other byte the later kernels read);
@@ -3043,8 +3043,31 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
 namespace vf4 {
 constexpr int64_t kNoAllocScratchBytes = 16ll << 20;
 static __device__ __align__(256) uint8_t g_attn_scratch[kNoAllocScratchBytes];
-static uint8_t* g_scratch_ptr[64];
-static std::once_flag g_scratch_once[64];
+struct ScratchSlot {
+  unsigned long long ctx_id;   // CUDA context the address was resolved in (0: none yet)
+  uint8_t* ptr;
+};
+static ScratchSlot g_scratch[64];
+static std::mutex g_scratch_mu;
+
+// The device address of g_attn_scratch in the current context, resolved on first use there.
+static int scratch_address(int dev, uint8_t** out) {
+  unsigned long long id = 0;
+  if (current_context_id(&id) != VF4_OK)
+    return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: no current CUDA context");
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  ScratchSlot& slot = g_scratch[dev];
+  if (slot.ptr == nullptr || slot.ctx_id != id) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    slot.ptr = static_cast<uint8_t*>(p);
+    slot.ctx_id = id;
+  }
+  *out = slot.ptr;
+  return VF4_OK;
+}
 }  // namespace vf4
 
 extern "C" int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* v, int64_t B, int64_t H,
@@ -3062,18 +3085,8 @@ extern "C" int vf4_attn_nvfp4_noalloc(const void* q, const void* k, const void* 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: no current device");
-  int setup = VF4_OK;
-  std::call_once(g_scratch_once[dev], [&] {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
-    if (e != cudaSuccess) {
-      setup = fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-      return;
-    }
-    g_scratch_ptr[dev] = static_cast<uint8_t*>(p);
-  });
-  if (setup != VF4_OK) return setup;
-  if (!g_scratch_ptr[dev]) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4_noalloc: scratch address unavailable");
+  uint8_t* scratch = nullptr;
+  if (int st = scratch_address(dev, &scratch)) return st;
   return vf4_attn_nvfp4(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b,
-                        out_stride_h, out_stride_s, g_scratch_ptr[dev], kNoAllocScratchBytes, stream);
+                        out_stride_h, out_stride_s, scratch, kNoAllocScratchBytes, stream);
 }

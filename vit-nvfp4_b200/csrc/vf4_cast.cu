@@ -105,6 +105,9 @@ __global__ void __launch_bounds__(256) amax_rows_kernel(const T* __restrict__ x,
     m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // GELU of a bf16 tensor is a bf16 tensor in the reference (F.gelu keeps the dtype): round the
+    // maximum once (rounding is monotone, so this is the max of the rounded values)
+    if constexpr (kGelu && sizeof(T) == 2) m = bf16_round(m);
     if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(m));
   }
 }
@@ -122,6 +125,7 @@ __global__ void __launch_bounds__(256) amax_flat_kernel(const T* __restrict__ x,
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if constexpr (kGelu && sizeof(T) == 2) m = bf16_round(m);
   if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(m));
 }
 
@@ -644,6 +648,32 @@ int vf4_amax(const void* x, int dtype, int64_t n, int gelu, float* amax_out, vf4
     }
   }
   return launch_status("vf4_amax");
+}
+
+namespace vf4 {
+// Pairs of elements through the epilogue's packed erf-GELU; an odd tail element pairs with itself.
+__global__ void __launch_bounds__(256) gelu_erf_kernel(const float* __restrict__ x, int64_t n,
+                                                       float* __restrict__ out) {
+  const int64_t pairs = (n + 1) / 2;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < pairs; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = 2 * t;
+    const float a = x[i], b = i + 1 < n ? x[i + 1] : a;
+    float ga, gb;
+    f32x2_unpack(gelu_erf_x2(f32x2_pack(a, b)), &ga, &gb);
+    out[i] = ga;
+    if (i + 1 < n) out[i + 1] = gb;
+  }
+}
+}  // namespace vf4
+
+int vf4_gelu_erf_f32(const float* x, int64_t n, float* out, vf4_stream_t stream) {
+  if (int st = vf4::check_device()) return st;
+  if (n < 0 || (n > 0 && (!x || !out))) return vf4::fail(VF4_ERR_ARG, "vf4_gelu_erf_f32: bad arguments");
+  if (n == 0) return VF4_OK;
+  const int64_t pairs = (n + 1) / 2;
+  const int grid = (int)((pairs + 255) / 256 < 148 * 16 ? (pairs + 255) / 256 : 148 * 16);
+  vf4::gelu_erf_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, n, out);
+  return vf4::launch_status("vf4_gelu_erf_f32");
 }
 
 int vf4_global_scale(const float* amax, int block_select, float* gs_out, vf4_stream_t stream) {

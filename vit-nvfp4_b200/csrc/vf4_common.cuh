@@ -322,6 +322,13 @@ VF4_DEV uint64_t encode16_inv(const float* v, float inv, bool zero_scale) {
   return (uint64_t)cvt_e2m1x8(q) | ((uint64_t)cvt_e2m1x8(q + 8) << 32);
 }
 
+// per-16-bit-lane unsigned max of two pairs (max.u16x2)
+VF4_DEV uint32_t umax_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // max(a, b, c) in one instruction (three-operand max.f32, sm_100)
 VF4_DEV float max3f(float a, float b, float c) {
   float d;
@@ -352,24 +359,6 @@ VF4_DEV uint32_t six_scale(float amax, float s_enc, float gs, float* dec) {
   uint32_t b = f32_to_e4m3(bs_f);
   *dec = __fmul_rn(e4m3_to_f32(b), gs);
   return b;
-}
-
-// GELU with erf from Abramowitz & Stegun 7.1.26 (|error of erf| <= 1.5e-7):
-//   erf(y) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-y^2),  t = 1/(1 + p y),  y >= 0.
-// gelu(x) = x * (1 - E) for x >= 0 and x * E for x < 0, with E = 0.5 (1 - erf(|x|/sqrt 2)).
-VF4_DEV float gelu_as(float x) {
-  const float y = fabsf(x) * 0.70710678118654752f;
-  float t, e;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(0.3275911f, y, 1.0f)));
-  float p = 0.5f * 1.061405429f;
-  p = __fmaf_rn(p, t, 0.5f * -1.453152027f);
-  p = __fmaf_rn(p, t, 0.5f * 1.421413741f);
-  p = __fmaf_rn(p, t, 0.5f * -0.284496736f);
-  p = __fmaf_rn(p, t, 0.5f * 0.254829592f);
-  p = p * t;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-y * y * 1.4426950408889634f));
-  const float E = p * e;
-  return x * (x >= 0.f ? 1.0f - E : E);
 }
 
 // dec_max: the largest decode scale for which encode16_bracket may take its fast path for the
@@ -421,6 +410,49 @@ VF4_DEV unsigned long long gelu_tanh_x2(unsigned long long x2) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(u1));
   const unsigned long long hx = mul_f32x2(x2, half2);
   return fma_f32x2(hx, f32x2_pack(t0, t1), hx);
+}
+
+// RN(a + b) of two bf16 pairs.  For bf16 operands this equals torch's bf16 add (an fp32 add, then
+// one rounding to bf16): the fp32 sum of two bf16 values is exact unless their exponents differ by
+// more than 16, and then the sum lies within 2^-16 relative of the larger operand, far from any
+// bf16 rounding midpoint, so rounding once or twice gives the same bf16 value.
+VF4_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), on an element pair with one ex2 per element:
+//   gelu(x) = 0.5 x + |x| (0.5 - E(|x|)),   E(z) = 0.5 erfc(z / sqrt 2) = 2^(-z^2 log2(e) / 2) P(z).
+// P is a degree-10 polynomial in z, fitted for this kernel (weighted least squares on
+// Chebyshev-distributed points of [0, kGeluZmax], weight exp(-z^2 / 2), so that the error of E rather
+// than of P is levelled) to 0.5 erfc(z / sqrt 2) exp(z^2 / 2).  Evaluated in fp32 as below it is
+// within 2.5e-7 |x| of the exact erf-GELU (7.6e-7 at most on [-12, 12]).  From z = kGeluZmax on,
+// fp32 erf(z / sqrt 2) rounds to 1, and E is taken as 0, so the result is exactly x (x > 0) or +0
+// (x < 0) there, as the fp32 erf-GELU gives; NaN propagates.  Coefficients are stored negated
+// (Horner yields -P, and 0.5 - E is one FMA).
+constexpr float kGeluZmax = 5.542595f;
+
+VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
+  constexpr float kNegP[11] = {-1.631675673e-06f, 3.520753307e-05f, -3.397366090e-04f, 1.974620158e-03f,
+                               -7.939374074e-03f, 2.431390621e-02f,  -6.115486845e-02f, 1.325137913e-01f,
+                               -2.499167919e-01f, 3.989365101e-01f,  -4.999999404e-01f};
+  float x0, x1;
+  f32x2_unpack(x2, &x0, &x1);
+  const float z0 = fabsf(x0), z1 = fabsf(x1);
+  const unsigned long long zc = f32x2_pack(fminf(z0, kGeluZmax), fminf(z1, kGeluZmax));
+  unsigned long long p = f32x2_pack(kNegP[0], kNegP[0]);
+#pragma unroll
+  for (int i = 1; i < 11; ++i) p = fma_f32x2(p, zc, f32x2_pack(kNegP[i], kNegP[i]));
+  constexpr float kHalfLog2e = 0.72134752044448170368f;   // log2(e) / 2
+  float a0, a1;
+  f32x2_unpack(mul_f32x2(mul_f32x2(zc, zc), f32x2_pack(-kHalfLog2e, -kHalfLog2e)), &a0, &a1);
+  float e0, e1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(z0 < kGeluZmax ? a0 : -INFINITY));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(z1 < kGeluZmax ? a1 : -INFINITY));
+  const unsigned long long half2 = f32x2_pack(0.5f, 0.5f);
+  const unsigned long long t = fma_f32x2(f32x2_pack(e0, e1), p, half2);   // 0.5 - E
+  return fma_f32x2(f32x2_pack(z0, z1), t, mul_f32x2(x2, half2));
 }
 
 // Offset of scale factor (row r, column c) inside the 128x4-tiled ("to_blocked") layout.

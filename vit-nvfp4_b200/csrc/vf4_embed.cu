@@ -88,8 +88,7 @@ int vf4_patchify(const void* images, int64_t B, int64_t C, int64_t H, int64_t W,
   if (smem > 200 * 1024) return fail(VF4_ERR_UNSUPPORTED, "vf4_patchify: a row of patches needs %lld bytes", (long long)smem);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(patchify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (int st = smem_optin(patchify_kernel, (int)smem)) return st;
   }
   patchify_kernel<<<(unsigned)(B * (H / p)), 256, (size_t)smem, s>>>(static_cast<const __nv_bfloat16*>(images),
                                                                      (int)C, (int)H, (int)W, (int)p, (int)k_pad,

@@ -96,10 +96,12 @@ struct GemmParams {
 VF4_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 VF4_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// 1/dec for every E4M3 scale byte b of the GELU-NVFP4 epilogue (dec = e4m3(b) * gs, rounded to
-// nearest as __frcp_rn): filled by the epilogue threads et = 0..127 before their first tile.
-VF4_DEV void fill_rcp_tab(float* tab, int et, float gs) {
-  if (et >= 0 && et < 128) tab[et] = __frcp_rn(__fmul_rn(e4m3_to_f32((uint32_t)et), gs));
+// The multiplier that takes a GELU value to E2M1 units for every E4M3 scale byte b of the
+// GELU-NVFP4 epilogue: RN(s_enc / e4m3(b)) with s_enc = RN(1 / gs), the "total scale" of the
+// reference's fused Triton cast (nvfp4/triton_cast.py:327-330, global_scale = 1 / per_tensor_scale
+// at :163); filled by the epilogue threads et = 0..127 before their first tile.
+VF4_DEV void fill_rcp_tab(float* tab, int et, float s_enc) {
+  if (et >= 0 && et < 128) tab[et] = __fdiv_rn(s_enc, e4m3_to_f32((uint32_t)et));
 }
 
 // Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
@@ -194,11 +196,16 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
       }
     }
   } else {
-    // fp32 (acc * gs_a * gs_b + b1) -> GELU (tanh form, or A&S 7.1.26 erf) -> NVFP4 "six" cast
-    // (the unfused reference rounds the fc1 output to bf16 first; here it stays fp32).  Element
-    // pairs go through the packed fp32 ops (fma / mul.rn.f32x2, the scalar ops' roundings); the
-    // reciprocal of a block's decode scale is rcp_tab[scale byte] (= __frcp_rn(e4m3 * gs), filled
-    // per CTA) and the bias comes from bias_f (fp32 in shared memory) when the caller staged it.
+    // GELU -> NVFP4 "six" cast of the fc1 output (fused_mlp.py:47-51).
+    //  * VF4_EPI_GELU_ERF_NVFP4 follows the reference's steps: the GEMM result rounded to bf16,
+    //    + b1 in bf16 (gemm_packed's bf16 output, then y1 + b1), erf-GELU in fp32 on that bf16
+    //    value (the Triton cast's apply_gelu, triton_cast.py:302-303), then the cast.
+    //  * VF4_EPI_GELU_NVFP4: fp32 acc * gs_a * gs_b + b1 without roundings, tanh-form GELU.
+    // The cast is the Triton cast's arithmetic (triton_cast.py:318-340): block scale
+    // e4m3(min(RN(amax / 6) * s_enc, 448)), values times rcp_tab[scale byte] = RN(s_enc / scale),
+    // nearest-even E2M1.  Element pairs go through the packed fp32 ops (fma / mul.rn.f32x2, the
+    // scalar ops' roundings); bias_f, when the caller staged the bias in shared memory, holds fp32
+    // values (tanh form) or bf16 pairs (erf form).
     // Packed codes (NC/2 bytes per row) are staged in shared memory with the 64-byte (NC = 128)
     // or 32-byte (NC = 64) swizzle, so a warp's 16-byte stores spread over all banks, and stored
     // by TMA; the 4-byte scale words go straight to the 128x4-tiled layout.
@@ -215,37 +222,53 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
         const int col = col0 + blk * 16;
         uint64_t packed = 0;
         if (col < p.N) {
-          unsigned long long t2[8];
-          if (bias_f) {
-            const float4* bp = reinterpret_cast<const float4*>(bias_f + blk * 16);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float4 bb = bp[i];
-              t2[2 * i] = f32x2_pack(bb.x, bb.y);
-              t2[2 * i + 1] = f32x2_pack(bb.z, bb.w);
-            }
-          } else if (p.bias) {
-            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
-            uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-            const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) t2[i] = bf16x2_to_f32x2(bw[i]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) t2[i] = 0ull;
-          }
           float h[16];
+          if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {
+            uint32_t bw[8];
+            const bool has_bias = bias_f != nullptr || p.bias != nullptr;
+            if (bias_f) {
+              const uint4* bp = reinterpret_cast<const uint4*>(bias_f) + blk * 2;
+              const uint4 b0 = bp[0], b1 = bp[1];
+              bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
+              bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
+            } else if (p.bias) {
+              const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
+              const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+              bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
+              bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
+            }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const unsigned long long a2 =
-                fma_f32x2(f32x2_pack(__uint_as_float(v[blk * 16 + 2 * i]), __uint_as_float(v[blk * 16 + 2 * i + 1])),
-                          alpha2, t2[i]);
-            if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {
-              float x0, x1;
-              f32x2_unpack(a2, &x0, &x1);
-              h[2 * i] = gelu_as(x0);
-              h[2 * i + 1] = gelu_as(x1);
+            for (int i = 0; i < 8; ++i) {
+              uint32_t y1 = bf16x2_round(mul_f32x2(
+                  f32x2_pack(__uint_as_float(v[blk * 16 + 2 * i]), __uint_as_float(v[blk * 16 + 2 * i + 1])), alpha2));
+              if (has_bias) y1 = add_bf16x2(y1, bw[i]);
+              f32x2_unpack(gelu_erf_x2(bf16x2_to_f32x2(y1)), &h[2 * i], &h[2 * i + 1]);
+            }
+          } else {
+            unsigned long long t2[8];
+            if (bias_f) {
+              const float4* bp = reinterpret_cast<const float4*>(bias_f + blk * 16);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 bb = bp[i];
+                t2[2 * i] = f32x2_pack(bb.x, bb.y);
+                t2[2 * i + 1] = f32x2_pack(bb.z, bb.w);
+              }
+            } else if (p.bias) {
+              const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
+              uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+              const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+              for (int i = 0; i < 8; ++i) t2[i] = bf16x2_to_f32x2(bw[i]);
             } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) t2[i] = 0ull;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const unsigned long long a2 = fma_f32x2(
+                  f32x2_pack(__uint_as_float(v[blk * 16 + 2 * i]), __uint_as_float(v[blk * 16 + 2 * i + 1])), alpha2,
+                  t2[i]);
               f32x2_unpack(gelu_tanh_x2(a2), &h[2 * i], &h[2 * i + 1]);
             }
           }
@@ -435,7 +458,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     float* rcp_tab = reinterpret_cast<float*>(gbase + C::CONST_OFF);
     if constexpr (epi_gelu(EPI)) {
-      fill_rcp_tab(rcp_tab, threadIdx.x - 64, egs);
+      fill_rcp_tab(rcp_tab, threadIdx.x - 64, esenc);
       named_bar_sync(1, 256);
     }
     int lt = 0;
@@ -671,8 +694,15 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     float* bias_f = rcp_tab + 128;
     if constexpr (epi_gelu(EPI)) {
       const int et = threadIdx.x - 64;
-      fill_rcp_tab(rcp_tab, et, egs);
-      if (et < BN) {
+      fill_rcp_tab(rcp_tab, et, esenc);
+      if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {   // bf16 pairs (the erf form adds b1 in bf16)
+        if (et < BN / 2) {
+          const int col = nb * BN + 2 * et;
+          const uint32_t lo = (p.bias && col < p.N) ? (uint32_t)__bfloat16_as_ushort(p.bias[col]) : 0u;
+          const uint32_t hi = (p.bias && col + 1 < p.N) ? (uint32_t)__bfloat16_as_ushort(p.bias[col + 1]) : 0u;
+          reinterpret_cast<uint32_t*>(bias_f)[et] = lo | (hi << 16);
+        }
+      } else if (et < BN) {
         const int col = nb * BN + et;
         bias_f[et] = (p.bias && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
       }
@@ -694,7 +724,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
                                                egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
                                    gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES, rcp_tab,
-                                   epi_gelu(EPI) ? bias_f + part * NC : nullptr);
+                                   !epi_gelu(EPI) ? nullptr
+                                   : EPI == VF4_EPI_GELU_ERF_NVFP4 ? bias_f + part * NC / 2   // bf16 pairs
+                                                                   : bias_f + part * NC);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -903,7 +935,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     }
     float* rcp_tab = reinterpret_cast<float*>(gbase + C::CONST_OFF);
     if constexpr (epi_gelu(EPI)) {
-      fill_rcp_tab(rcp_tab, threadIdx.x - 96, egs);
+      fill_rcp_tab(rcp_tab, threadIdx.x - 96, esenc);
       named_bar_sync(1, 256);
     }
     const uint32_t tempty_leader = mapa_shared(tempty_bar, 0);
@@ -984,8 +1016,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN, C::EPI_CW)) return st;
   }
   auto kern = gemm_nvfp4_kernel<BN, EPI, kF32>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(kern, C::SMEM)) return st;
   p.tiles_m = (p.M + 127) / 128;
   p.tiles_n = (p.N + BN - 1) / BN;
   int tiles = p.tiles_m * p.tiles_n;
@@ -1007,8 +1038,7 @@ static int launch_gemm_pair(const uint8_t* a, const uint8_t* b, GemmParams& p, c
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN)) return st;
   }
   auto kern = gemm_nvfp4_pair_kernel<EPI, kF32>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(kern, C::SMEM)) return st;
   p.tiles_m = (p.M + 255) / 256;
   p.tiles_n = (p.N + C::BN - 1) / C::BN;
   const int tiles = p.tiles_m * p.tiles_n;
@@ -1041,8 +1071,7 @@ static int launch_gemm_ws(const uint8_t* a, const uint8_t* b, GemmParams& p, cud
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, C::BN, C::EPI_CW)) return st;
   }
   auto kern = gemm_nvfp4_ws_kernel<EPI, kF32, EW>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return fail(VF4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_optin(kern, C::SMEM)) return st;
   p.tiles_m = (p.M + 127) / 128;
   p.tiles_n = (p.N + C::BN - 1) / C::BN;
   const int groups = num_sms() / p.tiles_n;   // CTAs per N tile

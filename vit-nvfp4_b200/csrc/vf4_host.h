@@ -29,11 +29,25 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled();
 
+// ID of the calling thread's current CUDA context (driver API, resolved through the runtime so
+// the library loads on hosts without a driver).
+int current_context_id(unsigned long long* id);
+
 // Per-family readers of the device error word (defined in each .cu).
 int cast_device_error(int clear);
 int gemm_device_error(int clear);
 int attn_device_error(int clear);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Opt kernel `kern` into `bytes` of dynamic shared memory on the current device.  The attribute
+// lives with the kernel in the device's context, so the driver call is made only when a kernel
+// needs more than it was last given on that device (a process that resets the device must not
+// rely on this cache).
+int smem_optin_raw(const void* kern, int bytes);
+template <typename Kern>
+inline int smem_optin(Kern kern, int bytes) {
+  return smem_optin_raw(reinterpret_cast<const void*>(kern), bytes);
+}
 
 }  // namespace vf4

@@ -30,6 +30,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_last_error_string": [],
     "vf4_device_error": [_I],
     "vf4_amax": [_P, _I, _L, _I, _P, _P],
+    "vf4_gelu_erf_f32": [_P, _L, _P, _P],
     "vf4_global_scale": [_P, _I, _P, _P],
     "vf4_cast_nvfp4": [_P, _I, _L, _L, _L, _P, _I, _I, _P, _P, _P, _P, _P, _P],
     "vf4_ln_cast_nvfp4": [_P, _P, _P, _P, _P, _P, ctypes.c_float, _L, _L, _P, _P, _P, _P, _P],

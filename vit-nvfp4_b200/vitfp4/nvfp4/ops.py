@@ -15,13 +15,15 @@ SF_TORCH_DTYPE = torch.uint8  # E4M3 bytes are carried as uint8 internally
 
 class Probe:
     """Launch accounting for the benchmark: counts libvitfp4 kernel launches and, when
-    ``timing`` is on, brackets every GEMM and bf16-attention launch with CUDA events on the
-    launching stream."""
+    ``timing`` is on, brackets every GEMM, attention and cast call with CUDA events on the
+    launching stream.  Each record is (kind, work, start, end): ``work`` is the call's FLOPs for
+    GEMM and attention kinds and its algorithmic HBM bytes for cast kinds (names starting with
+    "cast" or "ln_cast")."""
 
     def __init__(self):
         self.launches = 0
         self.timing = False
-        self.records: list = []   # (kind, flops, start_event, end_event)
+        self.records: list = []   # (kind, work, start_event, end_event)
 
     def reset(self):
         self.launches = 0
@@ -35,9 +37,9 @@ def _launched(n: int = 1) -> None:
     probe.launches += n
 
 
-class _GemmTimer:
-    def __init__(self, kind: str, flops: float):
-        self.kind, self.flops = kind, flops
+class _Timed:
+    def __init__(self, kind: str, work: float):
+        self.kind, self.work = kind, work
 
     def __enter__(self):
         if probe.timing:
@@ -49,7 +51,7 @@ class _GemmTimer:
     def __exit__(self, *a):
         if probe.timing:
             self.e.record()
-            probe.records.append((self.kind, self.flops, self.s, self.e))
+            probe.records.append((self.kind, self.work, self.s, self.e))
 
 
 def _stream() -> int:
@@ -136,9 +138,12 @@ def cast(x: torch.Tensor, gs: torch.Tensor | None = None, block_select: str = "s
     b = None
     if bias is not None:
         b = bias.to(x2.dtype).contiguous()
-    _lib.call("vf4_cast_nvfp4", _ptr(x2), _dtype_code(x2), M, K, ld, _ptr(gs_in),
-              1 if block_select == "mse" else 0, int(gelu), _ptr(b), _ptr(packed), _ptr(sfs), _ptr(sfl),
-              _ptr(gs_out), _stream())
+    esz = x2.element_size()
+    with _Timed(f"cast_{'static' if gs_in is not None else 'dynamic'}_{M}x{K}",
+                M * K * (esz + 0.5 + 1 / 16 + (0 if gs_in is not None else esz))):
+        _lib.call("vf4_cast_nvfp4", _ptr(x2), _dtype_code(x2), M, K, ld, _ptr(gs_in),
+                  1 if block_select == "mse" else 0, int(gelu), _ptr(b), _ptr(packed), _ptr(sfs), _ptr(sfl),
+                  _ptr(gs_out), _stream())
     _launched(1 if gs_in is not None else 3)
     return packed, sfs, sfl, (gs_out if gs_in is None else gs_in)
 
@@ -157,8 +162,10 @@ def cast_split(x_main: torch.Tensor, x_tail: torch.Tensor, gs: torch.Tensor | No
     sfs = torch.empty(sf_swizzled_numel(M, K), dtype=torch.uint8, device=a.device)
     gs_in = None if gs is None else gs.reshape(()).to(torch.float32).contiguous()
     gs_out = torch.empty((), dtype=torch.float32, device=a.device) if gs_in is None else None
-    _lib.call("vf4_cast_nvfp4_split", _ptr(a), rm, _ptr(b), rt, n, K, _ptr(gs_in), _ptr(gs_out), _ptr(packed),
-              _ptr(sfs), _stream())
+    with _Timed(f"cast_split_{'static' if gs_in is not None else 'dynamic'}_{M}x{K}",
+                M * K * (2.5625 + (0 if gs_in is not None else 2))):
+        _lib.call("vf4_cast_nvfp4_split", _ptr(a), rm, _ptr(b), rt, n, K, _ptr(gs_in), _ptr(gs_out), _ptr(packed),
+                  _ptr(sfs), _stream())
     _launched(2 if gs_in is not None else 5)
     return packed, sfs, (gs_out if gs_in is None else gs_in)
 
@@ -225,7 +232,7 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
         else:
             bb = bias.to(torch.bfloat16).contiguous()
             epi = _lib.VF4_EPI_BIAS
-    with _GemmTimer(f"gemm_{'bias' if epi else 'none'}_{M}x{N}x{K}", 2.0 * M * N * K):
+    with _Timed(f"gemm_{'bias' if epi else 'none'}_{M}x{N}x{K}", 2.0 * M * N * K):
         _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
                   _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
                   _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
@@ -251,7 +258,7 @@ def gemm_residual(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, residual: to
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
     gg = None if gamma is None else gamma.to(torch.bfloat16).contiguous()
-    with _GemmTimer(f"gemm_residual_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
+    with _Timed(f"gemm_residual_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
         _lib.call("vf4_gemm_nvfp4_residual", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
                   _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb), _ptr(residual),
                   _ptr(gg), _ptr(out), _stream())
@@ -271,7 +278,7 @@ def gemm_gelu_nvfp4(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, epi_gs, ex
     packed = torch.empty((M, N // 2), dtype=torch.uint8, device=a.device)
     sf = torch.empty(sf_swizzled_numel(M, N), dtype=torch.uint8, device=a.device)
     bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
-    with _GemmTimer(f"gemm_gelu_nvfp4_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
+    with _Timed(f"gemm_gelu_nvfp4_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
         _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
                   _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
                   _lib.VF4_EPI_GELU_ERF_NVFP4 if exact else _lib.VF4_EPI_GELU_NVFP4, None, _lib.VF4_BF16,
@@ -309,9 +316,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int,
             raise _lib.VitFp4Error("FP4 attention takes bf16 q/k/v/out")
     flags = (_lib.VF4_ATTN_HEAD_GLOBALS if head_globals else 0) | (_lib.VF4_ATTN_PACKED if packed else 0)
     ws = _attn_workspace(B, H, S, D, q.device, flags)
-    _lib.call("vf4_attn_nvfp4_ex", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], flags,
-              _ptr(ws) if ws.numel() else None, ws.numel(), _stream())
+    with _Timed(f"attn_nvfp4_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
+        _lib.call("vf4_attn_nvfp4_ex", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+                  float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], flags,
+                  _ptr(ws) if ws.numel() else None, ws.numel(), _stream())
     fused = D == 64 and S <= 320
     _launched((0 if head_globals else 1) + (1 if fused else 2) + (1 if fused and packed else 0))
     return out
@@ -325,8 +333,9 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: 
     for t in (q, k, v, out):
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("FP8 attention takes bf16 q/k/v/out")
-    _lib.call("vf4_attn_fp8", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-              float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
+    with _Timed(f"attn_fp8_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
+        _lib.call("vf4_attn_fp8", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+                  float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
     _launched(1)
     return out
 
@@ -346,7 +355,7 @@ def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
             raise _lib.VitFp4Error("bf16 attention takes bf16 q/k/v/out")
     if out_amax is not None and (out_amax.dtype != torch.float32 or out_amax.numel() != 1):
         raise _lib.VitFp4Error("out_amax must be one fp32 value")
-    with _GemmTimer(f"attn_bf16_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
+    with _Timed(f"attn_bf16_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
         _lib.call("vf4_attn_bf16", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
                   float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _ptr(out_amax), _stream())
     _launched(1)
@@ -442,8 +451,12 @@ def ln_cast(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float,
     w = ln_w.to(torch.bfloat16).contiguous()
     b = ln_b.to(torch.bfloat16).contiguous()
     g = None if gamma is None else gamma.to(torch.bfloat16).contiguous()
-    _lib.call("vf4_ln_cast_nvfp4", _ptr(x), _ptr(y), _ptr(g), _ptr(x_out), _ptr(w), _ptr(b), float(eps), M, K,
-              _ptr(gs_in), _ptr(packed), _ptr(sf), _ptr(gs_out), _stream())
+    # bytes: x (and y, x') in bf16, codes + scales out; the dynamic form reads x twice
+    kind = "ln_cast_residual" if y is not None else ("ln_cast_static" if gs_in is not None else "ln_cast_dynamic")
+    per = (6 if y is not None else 2) + 0.5 + 1 / 16 + (2 if gs_in is None else 0)
+    with _Timed(f"{kind}_{M}x{K}", M * K * per):
+        _lib.call("vf4_ln_cast_nvfp4", _ptr(x), _ptr(y), _ptr(g), _ptr(x_out), _ptr(w), _ptr(b), float(eps), M, K,
+                  _ptr(gs_in), _ptr(packed), _ptr(sf), _ptr(gs_out), _stream())
     _launched(1 if gs_in is not None else 3)
     return packed, sf, (gs_out if gs_in is None else gs_in), (x if y is None else x_out)
 

@@ -4,9 +4,12 @@ src/vit_nvfp4/ptq/fused_mlp.py:25-167).
 The fc1 GEMM's epilogue applies ``+b1 -> GELU -> NVFP4 cast`` straight from the TMEM
 accumulator, so the (M, 4d) intermediate never round-trips HBM in bf16; fc2 consumes the packed
 FP4 codes + swizzled scales directly and adds ``b2`` in its epilogue.  Three kernels per MLP:
-activation cast, fc1 GEMM (fused epilogue), fc2 GEMM (bias epilogue).  The epilogue's GELU is the tanh form evaluated with the hardware tanh by default (its
-deviation from erf-GELU, ~1e-3 at most, is below the bf16 rounding the reference applies to the fc1
-output before its GELU); ``exact_gelu=True`` selects an erf-GELU epilogue accurate to 1.5e-7.
+activation cast, fc1 GEMM (fused epilogue), fc2 GEMM (bias epilogue).
+
+The epilogue computes what the reference's unfused steps compute: the fc1 result rounded to bf16,
+``+ b1`` in bf16, then erf-GELU in fp32 on that bf16 value and the NVFP4 cast of the fp32 GELU
+(the reference's Triton cast with ``apply_gelu``).  ``exact_gelu=False`` selects the cheaper
+tanh-form GELU on the unrounded accumulator instead (within ~1e-3 of erf-GELU).
 
 Buffers and calibration follow the reference: weights are quantized once with the RTN "six"
 rule and stored packed (``float4_e2m1fn_x2``) with swizzled E4M3 scales; the activation globals
@@ -45,7 +48,7 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
 def fused_mlp_op(x: torch.Tensor, w1q: torch.Tensor, w1sf: torch.Tensor, w1g: torch.Tensor,
                  b1: torch.Tensor | None, w2q: torch.Tensor, w2sf: torch.Tensor, w2g: torch.Tensor,
                  b2: torch.Tensor | None, gx: torch.Tensor, gh: torch.Tensor, k1: int, n2: int,
-                 exact_gelu: bool = False) -> torch.Tensor:
+                 exact_gelu: bool = True) -> torch.Tensor:
     M = x.numel() // k1
     x2 = x.reshape(M, k1)
     ap, asf, _, _ = ops.cast(x2, gx, "six")
@@ -55,14 +58,14 @@ def fused_mlp_op(x: torch.Tensor, w1q: torch.Tensor, w1sf: torch.Tensor, w1g: to
 
 
 @fused_mlp_op.register_fake
-def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2, exact_gelu=False):
+def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2, exact_gelu=True):
     return x.new_empty(*x.shape[:-1], n2, dtype=torch.bfloat16)
 
 
 class FusedNVFP4MLP(nn.Module):
     """Drop-in replacement for a ``fc1 -> GELU -> fc2`` MLP with NVFP4 W4A4 and GELU fusion."""
 
-    def __init__(self, fc1: nn.Linear, fc2: nn.Linear, exact_gelu: bool = False):
+    def __init__(self, fc1: nn.Linear, fc2: nn.Linear, exact_gelu: bool = True):
         super().__init__()
         self.exact_gelu = exact_gelu
         assert fc1.out_features == fc2.in_features, "not an fc1->fc2 MLP pair"
@@ -104,54 +107,69 @@ class FusedNVFP4MLP(nn.Module):
         return f"in={self.k1}, hidden={self.w1q.shape[0]}, out={self.n2}, nvfp4=W4A4+gelu_fused"
 
 
-# activation class names: exact erf-GELU (fusable) vs approximations (never fused)
-_EXACT_GELU = {"GELUActivation"}
-_APPROX_GELU = {"PytorchGELUTanh", "NewGELUActivation", "QuickGELUActivation", "FastGELUActivation",
-                "GELUTanh", "ClippedGELUActivation"}
+# Activation modules by what they compute.  The fused epilogue applies erf-GELU, so only an MLP
+# whose activation is known to be erf-GELU computes the same function after fusion.
+_ERF_GELU_CLASSES = frozenset({"GELUActivation"})
+_APPROXIMATE_GELU_CLASSES = frozenset({"PytorchGELUTanh", "NewGELUActivation", "QuickGELUActivation",
+                                       "FastGELUActivation", "GELUTanh", "ClippedGELUActivation"})
 
 
-def _is_exact_gelu(module: nn.Module):
-    """True: exact GELU child; False: known approximation; None: no activation found."""
-    for child in module.children():
-        cname = type(child).__name__
-        if cname in _EXACT_GELU:
-            return True
-        if cname in _APPROX_GELU:
-            return False
+def _activation_kind(mlp: nn.Module) -> str:
+    """"erf", "approximate" or "unknown": the first direct child that is a recognised activation
+    decides (torch's nn.GELU by its ``approximate`` flag, HF activations by class name)."""
+    for child in mlp.children():
         if isinstance(child, nn.GELU):
-            return child.approximate == "none"
-    return None
+            return "erf" if child.approximate == "none" else "approximate"
+        tname = type(child).__name__
+        if tname in _ERF_GELU_CLASSES:
+            return "erf"
+        if tname in _APPROXIMATE_GELU_CLASSES:
+            return "approximate"
+    return "unknown"
 
 
-def _mlp_pair(module: nn.Module):
-    """(fc1, fc2) of a plain fc1->act->fc2 MLP, else None (gated MLPs are never pairs)."""
-    if getattr(module, "gate_proj", None) is not None:
+def _fc_pair(mlp: nn.Module):
+    """(fc1, fc2) of an ungated two-Linear MLP whose shapes chain and whose input width is a
+    multiple of 16 (timm ``fc1/fc2`` or HF ``up_proj/down_proj`` names), else None."""
+    if getattr(mlp, "gate_proj", None) is not None:     # gated (SwiGLU-style) MLPs have no fc1->act->fc2 form
         return None
-    for up, down in (("fc1", "fc2"), ("up_proj", "down_proj")):
-        f1, f2 = getattr(module, up, None), getattr(module, down, None)
-        if isinstance(f1, nn.Linear) and isinstance(f2, nn.Linear) and f1.out_features == f2.in_features \
-                and f1.in_features % 16 == 0:
-            return f1, f2
+    for up_name, down_name in (("fc1", "fc2"), ("up_proj", "down_proj")):
+        up, down = getattr(mlp, up_name, None), getattr(mlp, down_name, None)
+        if not (isinstance(up, nn.Linear) and isinstance(down, nn.Linear)):
+            continue
+        if up.out_features == down.in_features and up.in_features % 16 == 0:
+            return up, down
     return None
 
 
-def fuse_mlps(model: nn.Module, skip_ends: int = 2, require_gelu: bool = True) -> int:
-    """Swap each block's GELU MLP for FusedNVFP4MLP in place; returns the number fused.
+def plan_mlp_fusion(model: nn.Module, skip_ends: int = 2, require_gelu: bool = True) -> list:
+    """The MLPs ``fuse_mlps`` would replace, as (dotted name, fc1, fc2) in module order.
 
-    ``skip_ends`` leaves the first/last N fusible MLPs in bf16; ``require_gelu`` fuses only
-    MLPs whose activation is confirmed exact erf-GELU (others stay bf16 with a warning)."""
-    cands = [(n, m, p) for n, m in model.named_modules() if (p := _mlp_pair(m)) is not None]
+    Pure module-tree inspection (no CUDA): every ungated fc1->act->fc2 MLP is a candidate; with
+    ``require_gelu`` only those whose activation is known erf-GELU stay candidates (a warning names
+    the others); then ``skip_ends`` candidates are dropped from each end of the list."""
+    found = []
+    for name, mod in model.named_modules():
+        pair = _fc_pair(mod)
+        if pair is not None:
+            found.append((name, mod, pair))
     if require_gelu:
-        unsure = [n for n, m, _ in cands if _is_exact_gelu(m) is not True]
-        if unsure:
-            warnings.warn(f"fuse_mlps: leaving {len(unsure)} MLP(s) in BF16 — activation not confirmed "
-                          f"exact GELU (e.g. {unsure[:3]}). Pass require_gelu=False to force.")
-        cands = [(n, m, p) for n, m, p in cands if _is_exact_gelu(m) is True]
-    if skip_ends and 2 * skip_ends >= len(cands):
-        raise ValueError(f"skip_ends={skip_ends} too large for {len(cands)} fusible MLP block(s)")
-    keep = cands[skip_ends:len(cands) - skip_ends] if skip_ends else cands
-    for name, _m, pair in keep:
-        parent_name, _, attr = name.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        setattr(parent, attr, FusedNVFP4MLP(*pair))
-    return len(keep)
+        left_out = [name for name, mod, _ in found if _activation_kind(mod) != "erf"]
+        if left_out:
+            warnings.warn(f"fuse_mlps: {len(left_out)} MLP(s) stay in bf16 because their activation is not "
+                          f"known to be erf-GELU (first: {left_out[:3]}); require_gelu=False fuses them anyway")
+        found = [entry for entry in found if _activation_kind(entry[1]) == "erf"]
+    if skip_ends:
+        if 2 * skip_ends >= len(found):
+            raise ValueError(f"fuse_mlps: skip_ends={skip_ends} leaves nothing of {len(found)} fusible MLP(s)")
+        found = found[skip_ends:-skip_ends]
+    return [(name, pair[0], pair[1]) for name, _, pair in found]
+
+
+def fuse_mlps(model: nn.Module, skip_ends: int = 2, require_gelu: bool = True, exact_gelu: bool = True) -> int:
+    """Replace the MLPs chosen by ``plan_mlp_fusion`` with ``FusedNVFP4MLP`` in place; returns how
+    many were replaced (reference: src/vit_nvfp4/ptq/fused_mlp.py:143-167)."""
+    plan = plan_mlp_fusion(model, skip_ends, require_gelu)
+    for name, fc1, fc2 in plan:
+        model.set_submodule(name, FusedNVFP4MLP(fc1, fc2, exact_gelu=exact_gelu))
+    return len(plan)

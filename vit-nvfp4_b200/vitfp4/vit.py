@@ -193,8 +193,11 @@ class VisionTransformer(nn.Module):
 
 
 def init_weights(model: nn.Module, seed: int = 0, std: float = 0.02) -> nn.Module:
-    """N(0, std) weights, zero biases, LayerNorm (1, 0); LayerScale keeps its init value."""
-    g = torch.Generator().manual_seed(seed)
+    """N(0, std) weights, zero biases, LayerNorm (1, 0); LayerScale keeps its init value.  The random
+    stream is a generator on the model's device seeded with ``seed`` (the CPU generator for a CPU
+    model, so CPU-built models are the same on every machine)."""
+    dev = next(model.parameters()).device
+    g = torch.Generator(device=dev).manual_seed(seed)
     for name, p in model.named_parameters():
         with torch.no_grad():
             if name.endswith("gamma"):
@@ -204,10 +207,15 @@ def init_weights(model: nn.Module, seed: int = 0, std: float = 0.02) -> nn.Modul
             elif name.endswith("bias"):
                 p.zero_()
             else:
-                p.copy_(torch.randn(p.shape, generator=g) * std)
+                p.copy_(torch.randn(p.shape, generator=g, device=dev, dtype=p.dtype) * std)
     return model
 
 
-def build_vit(seed: int = 0, **overrides) -> VisionTransformer:
+def build_vit(seed: int = 0, device=None, **overrides) -> VisionTransformer:
+    """A randomly initialised ViT (``init_weights``); ``device`` builds and initialises it there."""
     cfg = ViTConfig(**overrides)
-    return init_weights(VisionTransformer(cfg), seed=seed)
+    if device is None:
+        return init_weights(VisionTransformer(cfg), seed=seed)
+    with torch.device(device):
+        model = VisionTransformer(cfg)
+    return init_weights(model, seed=seed)
