@@ -153,7 +153,7 @@ def test_fuse_mlps_skips_gated_and_non_gelu():
             super().__init__()
             self.blocks = nn.ModuleList([Gated(), _block(nn.GELU(approximate="tanh")), Gated()])
     model = Net().cuda().bfloat16()
-    with pytest.warns(UserWarning, match="not confirmed exact GELU"):
+    with pytest.warns(UserWarning, match="not known to be erf-GELU"):
         assert fuse_mlps(model, skip_ends=0) == 0
     assert not any(isinstance(b, FusedNVFP4MLP) for b in model.blocks)
 
