@@ -78,7 +78,8 @@ VF4_API int vf4_amax(const void* x, int dtype, int64_t n, int gelu, float* amax_
 VF4_API int vf4_global_scale(const float* amax, int block_select, float* gs_out, vf4_stream_t stream);
 
 /* out[i] = erf-GELU(x[i]) for n fp32 values, computed by the device function of the fc1
- * GELU-NVFP4 epilogue (0.5 x (1 + erf(x / sqrt 2)) within 2.5e-7 |x|, one ex2 per element).
+ * GELU-NVFP4 epilogue: 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun 7.1.26
+ * (|error| <= 1.5e-7), one reciprocal and one ex2 per element.
  * The reference's GELU is torch's F.gelu / Triton's tl.erf in triton_cast.py:302-303; this
  * elementwise form exists so the epilogue's function can be checked and reused on its own. */
 VF4_API int vf4_gelu_erf_f32(const float* x, int64_t n, float* out, vf4_stream_t stream);

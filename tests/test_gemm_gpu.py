@@ -128,8 +128,9 @@ def test_gemm_gelu_nvfp4_epilogue(M, K, N, exact):
 
 def test_gelu_erf_matches_torch_exact_gelu():
     """The fc1 epilogue's erf-GELU (vf4_gelu_erf_f32 runs the same device function elementwise)
-    against torch's exact F.gelu on the GPU (CUDA erff): |error| <= 3e-7 |x| + 1e-30 over a dense
-    sweep of [-12, 12] plus the saturation edge, +-inf, NaN and signed zeros."""
+    against torch's exact F.gelu on the GPU (CUDA erff): |error| <= 4e-7 |x| + 1e-30 over a dense
+    sweep of [-12, 12] (A&S 7.1.26 bounds erf's error by 1.5e-7, half of it reaches GELU, plus the
+    approximate reciprocal / ex2 and fp32 roundings), the tails, +-inf, NaN and signed zeros."""
     from vitfp4 import _lib
     x = torch.cat([torch.linspace(-12, 12, 2_000_001, device="cuda"),
                    torch.linspace(5.5, 5.6, 10001, device="cuda"), -torch.linspace(5.5, 5.6, 10001, device="cuda"),
@@ -138,10 +139,10 @@ def test_gelu_erf_matches_torch_exact_gelu():
     _lib.call("vf4_gelu_erf_f32", x.data_ptr(), x.numel(), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     ref = torch.nn.functional.gelu(x.double())
     err = (out.double() - ref).abs()
-    assert (err <= 3e-7 * x.double().abs() + 1e-30).all(), float((err / x.double().abs().clamp_min(1e-30)).max())
-    # where fp32 erf has rounded to +-1 the result is x itself or exactly zero
+    assert (err <= 4e-7 * x.double().abs() + 1e-30).all(), float((err / x.double().abs().clamp_min(1e-30)).max())
+    # far tails: x itself for large positive x, within 1e-7 of zero for large negative x
     big = x.abs() >= 5.6
-    assert torch.equal(out[big & (x > 0)], x[big & (x > 0)]) and (out[big & (x < 0)] == 0).all()
+    assert torch.equal(out[big & (x > 0)], x[big & (x > 0)]) and (out[big & (x < 0)].abs() <= 1e-7).all()
     special = torch.tensor([float("inf"), float("-inf"), float("nan")], device="cuda")
     o2 = torch.empty_like(special)
     _lib.call("vf4_gelu_erf_f32", special.data_ptr(), 3, o2.data_ptr(), torch.cuda.current_stream().cuda_stream)
