@@ -64,6 +64,43 @@ VF4_DEV void load16<float>(const float* p, float* v) {
   }
 }
 
+// 16 elements held as raw 16-byte words (2 for bf16, 4 for fp32): a block loaded one iteration
+// ahead of its use, so a thread's next load is in flight while it encodes the current block.
+template <typename T>
+struct Raw16 {
+  uint4 w[sizeof(T)];
+};
+
+template <typename T>
+VF4_DEV void load_raw16(const T* p, Raw16<T>& r) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < (int)sizeof(T); ++i) r.w[i] = __ldg(q + i);
+}
+
+template <typename T>
+VF4_DEV void raw16_to_f32(const Raw16<T>& r, float* v) {
+  if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t w[4] = {r.w[i].x, r.w[i].y, r.w[i].z, r.w[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[4 * i] = __uint_as_float(r.w[i].x);
+      v[4 * i + 1] = __uint_as_float(r.w[i].y);
+      v[4 * i + 2] = __uint_as_float(r.w[i].z);
+      v[4 * i + 3] = __uint_as_float(r.w[i].w);
+    }
+  }
+}
+
 template <typename T, bool kGelu, bool kBias>
 VF4_DEV void prologue16(float* v, const T* bias, int64_t col0) {
   if constexpr (kBias) {
@@ -86,13 +123,27 @@ __global__ void __launch_bounds__(256) amax_rows_kernel(const T* __restrict__ x,
                                                         float* __restrict__ out) {
   const int64_t nb = K / 16;
   const int64_t total = rows * nb;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   float m = 0.f;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = t / nb, b = t - r * nb;
+  int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  // (row, block) of t, advanced by the grid stride without dividing
+  const int64_t d_r = stride / nb, d_b = stride - d_r * nb;
+  int64_t r = t / nb, b = t - r * nb;
+  Raw16<T> raw;
+  if (t < total) load_raw16<T>(x + r * ld + b * 16, raw);
+  for (; t < total; t += stride) {   // each block's load is issued one iteration ahead
+    const Raw16<T> cur = raw;
+    const int64_t bc = b;
+    r += d_r;
+    b += d_b;
+    if (b >= nb) {
+      b -= nb;
+      ++r;
+    }
+    if (t + stride < total) load_raw16<T>(x + r * ld + b * 16, raw);
     float v[16];
-    load16<T>(x + r * ld + b * 16, v);
-    prologue16<T, kGelu, kBias>(v, bias, b * 16);
+    raw16_to_f32<T>(cur, v);
+    prologue16<T, kGelu, kBias>(v, bias, bc * 16);
 #pragma unroll
     for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
   }
@@ -160,14 +211,24 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
   const int64_t t_first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t d_row = stride / nb4, d_blk = stride - d_row * nb4;
   int64_t row = t_first / nb4, blk = t_first - row * nb4;
+  Raw16<T> raw;
+  if (t_first < total && row < M && blk < nb) load_raw16<T>(x + row * ld + blk * 16, raw);
   for (int64_t t0 = t_first - lane; t0 < total; t0 += stride) {
     const int64_t t = t0 + lane;
     const bool in_grid = t < total;
     const bool valid = in_grid && row < M && blk < nb;
+    const Raw16<T> cur = raw;
+    // the next item of this thread, loaded now and used in the next iteration
+    int64_t nrow = row + d_row, nblk = blk + d_blk;
+    if (nblk >= nb4) {
+      nblk -= nb4;
+      ++nrow;
+    }
+    if (t + stride < total && nrow < M && nblk < nb) load_raw16<T>(x + nrow * ld + nblk * 16, raw);
     uint32_t sf = 0;
     if (valid) {
       float v[16];
-      load16<T>(x + row * ld + blk * 16, v);
+      raw16_to_f32<T>(cur, v);
       prologue16<T, kGelu, kBias>(v, bias, blk * 16);
       // bf16 inputs are >= 2^-133 in magnitude when non-zero (see encode16_bracket)
       BlockQ q = quantize_block<kMse>(v, gs, s_enc, kBf16Exact<T, kGelu, kBias> ? 0x1p17f : 2.0f);
@@ -183,12 +244,8 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
       int64_t off = ((row >> 7) * ncb + (blk >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
       *reinterpret_cast<uint32_t*>(sf_swz + off) = w;
     }
-    row += d_row;
-    blk += d_blk;
-    if (blk >= nb4) {
-      blk -= nb4;
-      ++row;
-    }
+    row = nrow;
+    blk = nblk;
   }
 }
 

@@ -191,6 +191,29 @@ VF4_DEV uint32_t encode8_exact(const float* v, float dec) {
   return cvt_e2m1x8(q) - fix;
 }
 
+// Out-of-line entries to the exact encoders, for the rare blocks the bracketing encoders below
+// cannot settle.  Kept out of line so the compiler branches around them: inlined, their
+// correctly rounded reciprocal, Markstein quotients and tie tests were evaluated under a predicate
+// for every block, more than doubling the instructions of the common path.
+static __device__ __noinline__ uint64_t encode16_exact_ool(float4 a, float4 b, float4 c, float4 d, float dec) {
+  const float v[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+  return encode16_exact(v, dec);
+}
+
+static __device__ __noinline__ uint32_t encode8_exact_ool(float4 a, float4 b, float dec) {
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  return encode8_exact(v, dec);
+}
+
+VF4_DEV uint64_t encode16_exact_call(const float* v, float dec) {
+  return encode16_exact_ool(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                            make_float4(v[8], v[9], v[10], v[11]), make_float4(v[12], v[13], v[14], v[15]), dec);
+}
+
+VF4_DEV uint32_t encode8_exact_call(const float* v, float dec) {
+  return encode8_exact_ool(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]), dec);
+}
+
 // Bracketing encoder, bit-exact with encode16_exact at a fraction of its cost.
 //
 // The reference code of x is round_half_down(q) with q = RN(x / dec).  Instead of q, two
@@ -250,7 +273,7 @@ VF4_DEV uint32_t bf16x2_round(unsigned long long p) {
 }
 
 VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
-  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode16_exact(v, dec);
+  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode16_exact_call(v, dec);
   float inv;
   asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
   const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
@@ -268,13 +291,13 @@ VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
     wa[h] = cvt_e2m1x8(a);
     wb[h] = cvt_e2m1x8(b);
   }
-  if ((wa[0] != wb[0]) | (wa[1] != wb[1])) return encode16_exact(v, dec);
+  if ((wa[0] != wb[0]) | (wa[1] != wb[1])) return encode16_exact_call(v, dec);
   return (uint64_t)wa[0] | ((uint64_t)wa[1] << 32);
 }
 
 // Half a block (8 values) with the bracketing scheme of encode16_bracket.
 VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
-  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode8_exact(v, dec);
+  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode8_exact_call(v, dec);
   float inv;
   asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
   const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
@@ -287,7 +310,7 @@ VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
     f32x2_unpack(fma_f32x2(x2, hi2, z2), &b[2 * i], &b[2 * i + 1]);
   }
   const uint32_t wa = cvt_e2m1x8(a), wb = cvt_e2m1x8(b);
-  return wa == wb ? wa : encode8_exact(v, dec);
+  return wa == wb ? wa : encode8_exact_call(v, dec);
 }
 
 // Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
@@ -428,8 +451,8 @@ VF4_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
 //   E = 0.5 (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2 / 2),   t = 1 / (1 + p |x| / sqrt 2),
 // with exp(-x^2 / 2) = 2^(-(|x| s)^2), s = sqrt(log2(e) / 2): one reciprocal and one ex2 per element
 // and no comparison or select (measured in a throughput probe as the fastest of the erf forms tried,
-// 1.25x the single-ex2 polynomial).  For x -> -inf the result goes to -0 / +0 as E underflows; NaN
-// propagates; +inf gives +inf and -inf NaN, as 0.5 x (1 + erf(x / sqrt 2)) does.
+// 1.25x the single-ex2 polynomial).  For x -> -inf the result goes to 0 as E underflows (also at
+// x = -inf, where 0.5 x (1 + erf(x / sqrt 2)) is NaN); +inf gives +inf and NaN propagates.
 VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
   constexpr float kP = 0.3275911f * 0.70710678118654752f;   // p / sqrt 2
   constexpr float kS = 0.84932180028801904272f;              // sqrt(log2(e) / 2)
@@ -437,7 +460,8 @@ VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
                   kA4 = 0.5f * -1.453152027f, kA5 = 0.5f * 1.061405429f;
   float x0, x1;
   f32x2_unpack(x2, &x0, &x1);
-  const unsigned long long z = f32x2_pack(fabsf(x0), fabsf(x1));
+  // |x| capped below +inf, so that |x| * exp(-x^2 / 2) is 0 rather than inf * 0 for x = +-inf
+  const unsigned long long z = f32x2_pack(fminf(fabsf(x0), 0x1p126f), fminf(fabsf(x1), 0x1p126f));
   float d0, d1, t0, t1;
   f32x2_unpack(fma_f32x2(z, f32x2_pack(kP, kP), f32x2_pack(1.f, 1.f)), &d0, &d1);
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d0));
