@@ -210,11 +210,36 @@ VF4_API int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B
  * globals), faster, but the workspace grows by ~38 KB per (image, head) -- size it with
  * vf4_attn_workspace_size_ex(B, H, S, D, flags). */
 #define VF4_ATTN_PACKED 2
+/* flags: VF4_ATTN_NO_SMOOTH_K / VF4_ATTN_NO_SMOOTH_V switch off the reference's smooth-K (k minus its
+ * token mean) / smooth-V (v minus its token mean, added back to the output), i.e. quant_sdpa(...,
+ * smooth_k=False / smooth_v=False) of attention.py:53-54.  Only with the tensor-wide globals (not
+ * with VF4_ATTN_HEAD_GLOBALS, which returns VF4_ERR_UNSUPPORTED). */
+#define VF4_ATTN_NO_SMOOTH_K 4
+#define VF4_ATTN_NO_SMOOTH_V 8
+
+/* Operand precision of a route of vf4_attn (the reference's 'bf16' | 'fp8' | 'nvfp4'). */
+#define VF4_ATTN_MODE_BF16 0
+#define VF4_ATTN_MODE_FP8 1
+#define VF4_ATTN_MODE_NVFP4 2
 VF4_API int64_t vf4_attn_workspace_size_ex(int64_t B, int64_t H, int64_t S, int64_t D, int flags);
 VF4_API int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
                               int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
                               void* out, int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
                               int flags, void* workspace, int64_t workspace_bytes, vf4_stream_t stream);
+
+/* quant_sdpa(q, k, v, scale=scale, qk=qk_mode, pv=pv_mode, smooth_k, smooth_v) of attention.py:53-86
+ * (reached through _quant_attention, qattention.py:20-30) as one entry point: qk_mode / pv_mode are
+ * VF4_ATTN_MODE_*, flags VF4_ATTN_NO_SMOOTH_K / _V switch smooth-K / smooth-V off (and, for the NVFP4
+ * route, VF4_ATTN_HEAD_GLOBALS / VF4_ATTN_PACKED as vf4_attn_nvfp4_ex).  Kernel routes: nvfp4/nvfp4
+ * (vf4_attn_nvfp4_ex), fp8/fp8 (E4M3 kernel: head dim 64, S <= 320), bf16/bf16 (vf4_attn_bf16, where
+ * smoothing changes no result).  Mixed modes return VF4_ERR_UNSUPPORTED.  The workspace is needed by
+ * the NVFP4 route only: size it with vf4_attn_workspace_size_modes. */
+VF4_API int vf4_attn(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                     int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, int qk_mode, int pv_mode,
+                     int flags, void* workspace, int64_t workspace_bytes, void* out, int64_t out_stride_b,
+                     int64_t out_stride_h, int64_t out_stride_s, vf4_stream_t stream);
+VF4_API int64_t vf4_attn_workspace_size_modes(int64_t B, int64_t H, int64_t S, int64_t D, int qk_mode, int pv_mode,
+                                              int flags);
 
 /* vf4_attn_nvfp4 without a caller workspace, for callers that cannot allocate device memory
  * (a runtime that owns all device memory through its own pool, or a plugin that may not

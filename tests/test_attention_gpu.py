@@ -40,22 +40,22 @@ def _fused_path(S, D):
     return D == 64 and S <= 320
 
 
-def _oracle_kernel_semantics(q, k, v, scale, head_globals=False):
-    """The kernels' arithmetic: smooth-K/V, NVFP4 Q, K~ (along d) and V~ (along tokens) with global
-    scales over the whole tensors (or per head), P with the fixed global 1/2688 (unnormalised on the
-    fused route)."""
+def _oracle_kernel_semantics(q, k, v, scale, head_globals=False, smooth_k=True, smooth_v=True):
+    """The kernels' arithmetic: smooth-K/V (each switchable), NVFP4 Q, K~ (along d) and V~ (along
+    tokens) with global scales over the whole tensors (or per head), P with the fixed global 1/2688
+    (unnormalised on the fused route)."""
     B, H, S, D = q.shape
     unnormalised = _fused_path(S, D)
     out = np.empty((B, H, S, D), F32)
     g = lambda t: F32(max(np.abs(t).max(), 1e-12) / 2688.0)
-    ktt = k - k.mean(2, keepdims=True)
-    vtt = v - v.mean(2, keepdims=True)
+    ktt = k - k.mean(2, keepdims=True) if smooth_k else k
+    vtt = v - v.mean(2, keepdims=True) if smooth_v else v
     gq_all, gk_all, gv_all = g(q), g(ktt), g(vtt)
     for b in range(B):
         for h in range(H):
             qq, kk, vv = q[b, h], k[b, h], v[b, h]
-            kt = kk - kk.mean(0, keepdims=True)
-            mu = vv.mean(0, keepdims=True)
+            kt = kk - kk.mean(0, keepdims=True) if smooth_k else kk
+            mu = vv.mean(0, keepdims=True) if smooth_v else np.zeros((1, D), F32)
             vt = vv - mu
             gq, gk, gv = (g(qq), g(kt), g(vt)) if head_globals else (gq_all, gk_all, gv_all)
             s = _qdq(qq, gq) @ _qdq(kt, gk).T * F32(scale)
@@ -298,3 +298,85 @@ def test_bf16_kernel_amax_propagates_nan(S, row):
     qkv[1, row, 2 * H * D + D + 7] = 0.5
     got = ops.attention_bf16_packed_qkv(qkv, H, D ** -0.5, out_amax=am)
     assert torch.equal(am, got.float().abs().amax())
+
+
+
+@pytest.mark.parametrize("smooth_k,smooth_v", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("B,H,S,D", [(2, 3, 257, 64), (1, 2, 1025, 80)])
+def test_nvfp4_attention_smoothing_switches(B, H, S, D, smooth_k, smooth_v):
+    """quant_sdpa(..., smooth_k=False / smooth_v=False) on the FP4 kernels (VF4_ATTN_NO_SMOOTH_K / _V):
+    against the kernels' semantics with the same switches (cos >= 0.999) and the reference's
+    quant_sdpa with them (>= 0.995); k and v carry a token-constant offset, so the switches matter
+    (smoothing exists to take it out of the FP4 ranges, attention.py:57-58, 66-67)."""
+    from vitfp4.nvfp4 import quant_sdpa
+    q, k, v = _qkv(B, H, S, D, seed=S + 11)
+    k = (k.float() + 3.0).bfloat16()
+    v = (v.float() - 2.0).bfloat16()
+    out = quant_sdpa(q.cuda(), k.cuda(), v.cuda(), qk="nvfp4", pv="nvfp4", smooth_k=smooth_k,
+                     smooth_v=smooth_v).float().cpu().numpy()
+    on = quant_sdpa(q.cuda(), k.cuda(), v.cuda(), qk="nvfp4", pv="nvfp4").float().cpu().numpy()
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref_kernel = _oracle_kernel_semantics(qn, kn, vn, 1.0 / math.sqrt(D), smooth_k=smooth_k, smooth_v=smooth_v)
+    ref_sdpa = oracle.quant_sdpa(qn, kn, vn, qk="nvfp4", pv="nvfp4", smooth_k=smooth_k, smooth_v=smooth_v)
+    assert cos(out, ref_kernel) >= 0.999, cos(out, ref_kernel)
+    assert cos(out, ref_sdpa) >= 0.995, cos(out, ref_sdpa)
+    assert not np.array_equal(out, on)
+
+
+@pytest.mark.parametrize("smooth_k,smooth_v", [(False, False), (True, False), (False, True)])
+def test_fp8_attention_smoothing_switches(smooth_k, smooth_v):
+    """The FP8 kernel with smooth-K / smooth-V switched off, through quant_sdpa and the unified vf4_attn
+    entry: against the reference's quant_sdpa(qk=pv='fp8') with the same switches, cos >= 0.999."""
+    import ctypes
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import quant_sdpa
+    B, H, S, D = 2, 3, 257, 64
+    q, k, v = _qkv(B, H, S, D, seed=5)
+    k = (k.float() + 3.0).bfloat16()
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = quant_sdpa(qc, kc, vc, qk="fp8", pv="fp8", smooth_k=smooth_k, smooth_v=smooth_v)
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref = oracle.quant_sdpa(qn, kn, vn, qk="fp8", pv="fp8", smooth_k=smooth_k, smooth_v=smooth_v)
+    assert cos(out.float().cpu().numpy(), ref) >= 0.999
+    # the same through vf4_attn directly, (B, H, S, D) in and (B, S, H, D) out
+    o2 = torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    flags = (0 if smooth_k else _lib.VF4_ATTN_NO_SMOOTH_K) | (0 if smooth_v else _lib.VF4_ATTN_NO_SMOOTH_V)
+    m = _lib.VF4_ATTN_MODE["fp8"]
+    _lib.call("vf4_attn", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), B, H, S, D, H * S * D, S * D, D,
+              ctypes.c_float(D ** -0.5), m, m, flags, None, 0, o2.data_ptr(), S * H * D, D, H * D,
+              torch.cuda.current_stream().cuda_stream)
+    assert torch.equal(o2.transpose(1, 2), out)
+
+
+def test_unified_attention_entry_routes_and_refusals():
+    """vf4_attn: nvfp4/nvfp4 equals vf4_attn_nvfp4_ex, bf16/bf16 equals vf4_attn_bf16, mixed modes and
+    switches on the per-head-globals route are refused without launching."""
+    import ctypes
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import ops
+    lib = _lib.lib()
+    B, H, S, D = 2, 2, 197, 64
+    q, k, v = (t.cuda() for t in _qkv(B, H, S, D, seed=9))
+    st = (H * S * D, S * D, D)
+    ost = (S * H * D, D, H * D)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(qk, pv, flags):
+        n = int(lib.vf4_attn_workspace_size_modes(B, H, S, D, _lib.VF4_ATTN_MODE[qk], _lib.VF4_ATTN_MODE[pv], flags))
+        ws = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda")
+        out = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+        status = lib.vf4_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, S, D, *st, ctypes.c_float(D ** -0.5),
+                              _lib.VF4_ATTN_MODE[qk], _lib.VF4_ATTN_MODE[pv], flags, ws.data_ptr(), ws.numel(),
+                              out.data_ptr(), *ost, stream)
+        return status, out
+
+    s1, o1 = run("nvfp4", "nvfp4", 0)
+    assert s1 == 0 and torch.equal(o1, ops.attention_bhsd(q, k, v, D ** -0.5, packed=False).transpose(1, 2))
+    s2, o2 = run("bf16", "bf16", 0)
+    ref = torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    ops.attention_bf16(q, k, v, B, H, S, D, st, D ** -0.5, ref, ost)
+    assert s2 == 0 and torch.equal(o2, ref)
+    s3, o3 = run("nvfp4", "fp8", 0)
+    assert s3 == 6 and (o3 == 0).all()                                  # VF4_ERR_UNSUPPORTED
+    s4, _ = run("nvfp4", "nvfp4", _lib.VF4_ATTN_HEAD_GLOBALS | _lib.VF4_ATTN_NO_SMOOTH_K)
+    assert s4 == 6

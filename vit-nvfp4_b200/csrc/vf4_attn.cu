@@ -118,7 +118,8 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
                                                          const __nv_bfloat16* __restrict__ k,
                                                          const __nv_bfloat16* __restrict__ v, int64_t sb,
                                                          int64_t sh, int64_t ss, int H, int S, int D, int Dp,
-                                                         float* __restrict__ stats, float* __restrict__ amax3) {
+                                                         int smooth, float* __restrict__ stats,
+                                                         float* __restrict__ amax3) {
   extern __shared__ float part[];   // [8 warps][6][D] (or [6][rpi][D]): k sum/max/min, v sum/max/min
   __shared__ float red[3][8];
   const int head = blockIdx.x;
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
         nv = fminf(nv, part[5 * RD + i]);
       }
     }
-    const float mk = __fdiv_rn(sk, (float)S), mv = __fdiv_rn(sv, (float)S);
+    // smooth bit 0 / 1 off: that mean is 0 (no centring, and the maximum is of |k| / |v| itself)
+    const float mk = (smooth & 1) ? __fdiv_rn(sk, (float)S) : 0.f, mv = (smooth & 2) ? __fdiv_rn(sv, (float)S) : 0.f;
     stats[(int64_t)head * 2 * Dp + t] = mk;
     stats[(int64_t)head * 2 * Dp + Dp + t] = mv;
     ak = fmaxf(fabsf(xk - mk), fabsf(nk - mk));
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(256) attn_stats_kernel(const __nv_bfloat16* __
 __global__ void __launch_bounds__(256, 3) attn_stats64_kernel(const __nv_bfloat16* __restrict__ q,
                                                               const __nv_bfloat16* __restrict__ k,
                                                               const __nv_bfloat16* __restrict__ v, int64_t sb,
-                                                              int64_t sh, int64_t ss, int H, int S,
+                                                              int64_t sh, int64_t ss, int H, int S, int smooth,
                                                               float* __restrict__ stats, float* __restrict__ amax3) {
   __shared__ float part[8][3][64];   // per warp: sum, max, min of its tensor's 64 columns
   __shared__ float qred[4], ared[4];
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(256, 3) attn_stats64_kernel(const __nv_bfloat1
       xx = fmaxf(xx, part[ww][1][c]);
       nn = fminf(nn, part[ww][2][c]);
     }
-    const float mean = __fdiv_rn(su, (float)S);
+    const float mean = (smooth & (t < 64 ? 1 : 2)) ? __fdiv_rn(su, (float)S) : 0.f;   // smooth-K / smooth-V
     stats[(int64_t)head * 128 + t] = mean;
     am = fmaxf(fabsf(xx - mean), fabsf(nn - mean));
   }
@@ -1722,6 +1724,7 @@ struct Fp8Geom {
   int B, H, S, D;
   int nq, skp, box_rows, nbox, heads;
   int kv_hs, out_hs;
+  int smooth;                    // bit 0: subtract mean(k), bit 1: subtract mean(v) (and add it back)
   float scale;
   const __nv_bfloat16* q;        // read directly: element (b, h, s, d) at q + b sb + h sh + s ss + d
   int64_t sb, sh, ss;
@@ -2002,7 +2005,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         const int which = ct >> 6, d = ct & 63;
         float sum = 0.f;
         for (int w = 0; w < kFusedCompute; ++w) sum += red_kv[(which * kFusedCompute + w) * 64 + d];
-        mu[which * 64 + d] = __fdiv_rn(sum, (float)S);
+        mu[which * 64 + d] = (g.smooth & (which ? 2 : 1)) ? __fdiv_rn(sum, (float)S) : 0.f;
       }
       named_bar_sync(1, kCT);
       // ---- per-column amax of v - mean over the tokens -> sv
@@ -2198,8 +2201,9 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
 
 static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                       int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
-                      int64_t oss, cudaStream_t s) {
+                      int64_t oss, int smooth, cudaStream_t s) {
   Fp8Geom g = make_fp8_geom(B, H, S, D, scale);
+  g.smooth = smooth;
   g.q = static_cast<const __nv_bfloat16*>(q);
   g.sb = sb;
   g.sh = sh;
@@ -2904,9 +2908,11 @@ int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D) {
   return attn_ws_layout(B, H, S, D, true).total;
 }
 
+static constexpr int kAttnFlags = VF4_ATTN_HEAD_GLOBALS | VF4_ATTN_PACKED | VF4_ATTN_NO_SMOOTH_K | VF4_ATTN_NO_SMOOTH_V;
+
 int64_t vf4_attn_workspace_size_ex(int64_t B, int64_t H, int64_t S, int64_t D, int flags) {
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0 || D % 16 != 0 || D > 128) return 0;
-  if (flags & ~(VF4_ATTN_HEAD_GLOBALS | VF4_ATTN_PACKED)) return 0;
+  if (flags & ~kAttnFlags) return 0;
   return attn_ws_layout(B, H, S, D, !(flags & VF4_ATTN_HEAD_GLOBALS), (flags & VF4_ATTN_PACKED) != 0).total;
 }
 
@@ -2917,8 +2923,11 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   if (int st = check_device()) return st;
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: bad sizes");
   if (D % 16 != 0 || D > 128) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim must be a multiple of 16, <= 128");
-  if (flags & ~(VF4_ATTN_HEAD_GLOBALS | VF4_ATTN_PACKED))
-    return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: unknown flags %d", flags);
+  if (flags & ~kAttnFlags) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: unknown flags %d", flags);
+  const int smooth = ((flags & VF4_ATTN_NO_SMOOTH_K) ? 0 : 1) | ((flags & VF4_ATTN_NO_SMOOTH_V) ? 0 : 2);
+  if (smooth != 3 && (flags & VF4_ATTN_HEAD_GLOBALS))
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: smooth-K / smooth-V can be switched off only with the "
+                                     "tensor-wide global scales (no VF4_ATTN_HEAD_GLOBALS)");
   if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_nvfp4: null pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
       stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
@@ -2948,13 +2957,13 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
     if (cudaMemsetAsync(amax3, 0, 16, s) != cudaSuccess) return fail(VF4_ERR_CUDA, "vf4_attn_nvfp4: memset failed");
     if (D == 64) {
       attn_stats64_kernel<<<(unsigned)(B * H), 256, 0, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
-                                                            stats, amax3);
+                                                            smooth, stats, amax3);
     } else {
       const int D8 = (int)D / 8, rpi = 256 / D8;
       const int smem = 32 % D8 == 0 ? 8 * 6 * (int)D * 4 : 6 * rpi * (int)D * 4;
       if (int st = smem_optin(attn_stats_kernel, smem)) return st;
       attn_stats_kernel<<<(unsigned)(B * H), 256, smem, s>>>(Q, K, V, stride_b, stride_h, stride_s, (int)H, (int)S,
-                                                             (int)D, D <= 64 ? 64 : 128, stats, amax3);
+                                                             (int)D, D <= 64 ? 64 : 128, smooth, stats, amax3);
     }
     if (int st = launch_status("vf4_attn_nvfp4 (statistics)")) return st;
   }
@@ -2982,7 +2991,7 @@ int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B, int64_t
     return fail(VF4_ERR_ALIGN, "vf4_attn_fp8: 16-byte aligned pointers and strides (multiples of 8) needed");
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_fp8: B*H too large");
   return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
-                    out_stride_s, reinterpret_cast<cudaStream_t>(stream));
+                    out_stride_s, 3, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
@@ -3010,6 +3019,48 @@ int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64
                    int64_t workspace_bytes, vf4_stream_t stream) {
   return vf4_attn_nvfp4_ex(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
                            out_stride_s, 0, workspace, workspace_bytes, stream);
+}
+
+int64_t vf4_attn_workspace_size_modes(int64_t B, int64_t H, int64_t S, int64_t D, int qk_mode, int pv_mode,
+                                      int flags) {
+  if (qk_mode == VF4_ATTN_MODE_NVFP4 && pv_mode == VF4_ATTN_MODE_NVFP4)
+    return vf4_attn_workspace_size_ex(B, H, S, D, flags);
+  return 0;
+}
+
+int vf4_attn(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+             int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, int qk_mode, int pv_mode, int flags,
+             void* workspace, int64_t workspace_bytes, void* out, int64_t out_stride_b, int64_t out_stride_h,
+             int64_t out_stride_s, vf4_stream_t stream) {
+  const bool nvfp4 = qk_mode == VF4_ATTN_MODE_NVFP4 && pv_mode == VF4_ATTN_MODE_NVFP4;
+  const bool fp8 = qk_mode == VF4_ATTN_MODE_FP8 && pv_mode == VF4_ATTN_MODE_FP8;
+  const bool bf16 = qk_mode == VF4_ATTN_MODE_BF16 && pv_mode == VF4_ATTN_MODE_BF16;
+  if (nvfp4)
+    return vf4_attn_nvfp4_ex(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b,
+                             out_stride_h, out_stride_s, flags, workspace, workspace_bytes, stream);
+  if (fp8) {
+    if (flags & ~(VF4_ATTN_NO_SMOOTH_K | VF4_ATTN_NO_SMOOTH_V))
+      return fail(VF4_ERR_ARG, "vf4_attn: flags %d do not apply to the FP8 route", flags);
+    if (int st = check_device()) return st;
+    if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn: bad sizes");
+    if (!fp8_ok(S, D)) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: the FP8 kernel needs head dim 64 and S <= 320");
+    if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn: null pointer");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || stride_b % 8 || stride_h % 8 ||
+        stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
+      return fail(VF4_ERR_ALIGN, "vf4_attn: 16-byte aligned pointers and strides (multiples of 8) needed");
+    if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: B*H too large");
+    const int smooth = ((flags & VF4_ATTN_NO_SMOOTH_K) ? 0 : 1) | ((flags & VF4_ATTN_NO_SMOOTH_V) ? 0 : 2);
+    return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                      out_stride_s, smooth, reinterpret_cast<cudaStream_t>(stream));
+  }
+  if (bf16) {   // smoothing is exact under the softmax and the PV product: the flags change no result
+    if (flags & ~(VF4_ATTN_NO_SMOOTH_K | VF4_ATTN_NO_SMOOTH_V))
+      return fail(VF4_ERR_ARG, "vf4_attn: flags %d do not apply to the bf16 route", flags);
+    return vf4_attn_bf16(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                         out_stride_s, nullptr, stream);
+  }
+  return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: qk_mode %d / pv_mode %d is not a kernel route (the mixed routes run "
+              "the reference's emulation on the host side)", qk_mode, pv_mode);
 }
 
 }  // extern "C"

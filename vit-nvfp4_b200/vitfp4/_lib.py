@@ -18,6 +18,9 @@ VF4_BF16, VF4_F32 = 0, 1
 VF4_SIX, VF4_MSE = 0, 1
 VF4_ATTN_HEAD_GLOBALS = 1
 VF4_ATTN_PACKED = 2
+VF4_ATTN_NO_SMOOTH_K = 4
+VF4_ATTN_NO_SMOOTH_V = 8
+VF4_ATTN_MODE = {"bf16": 0, "fp8": 1, "nvfp4": 2}
 VF4_EPI_NONE, VF4_EPI_BIAS, VF4_EPI_GELU_NVFP4, VF4_EPI_GELU_ERF_NVFP4, VF4_EPI_BIAS_RESIDUAL = 0, 1, 2, 3, 4
 
 _P = ctypes.c_void_p
@@ -49,9 +52,11 @@ SIGNATURES: dict[str, list] = {
     "vf4_attn_fp8": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
     "vf4_attn_bf16": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P, _P],
     "vf4_attn_nvfp4_noalloc": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
+    "vf4_attn": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _I, _I, _I, _P, _L, _P, _L, _L, _L, _P],
+    "vf4_attn_workspace_size_modes": [_L, _L, _L, _L, _I, _I, _I],
 }
 _RESTYPE = {"vf4_last_error_string": ctypes.c_char_p, "vf4_attn_workspace_size": ctypes.c_int64,
-            "vf4_attn_workspace_size_ex": ctypes.c_int64}
+            "vf4_attn_workspace_size_ex": ctypes.c_int64, "vf4_attn_workspace_size_modes": ctypes.c_int64}
 
 
 class VitFp4Error(RuntimeError):

@@ -3,7 +3,7 @@
 ``quant_sdpa`` keeps the reference's signature.  Routes:
   qk = pv = 'nvfp4' -> the sm_100a FP4 attention kernels of libvitfp4.so (QK^T and PV as
                        block-scaled tcgen05 MMAs, exact two-pass softmax, P re-quantised to NVFP4
-                       in shared memory, smooth-K / smooth-V);
+                       in shared memory, smooth-K / smooth-V each on or off as asked);
   qk = pv = 'bf16'  -> exact bf16 attention (torch SDPA), the route the reference keeps for
                        unquantised blocks;
   qk = pv = 'fp8'   -> the sm_100a FP8 attention kernel (E4M3 MMAs, per-row scales) for head dim
@@ -116,15 +116,13 @@ def quant_sdpa(query, key, value, attn_mask=None, is_causal=False, scale=None, q
     if qk == "nvfp4" and pv == "nvfp4":
         if attn_mask is not None or is_causal:
             raise NotImplementedError("the FP4 attention kernel is for ViT (no mask, not causal)")
-        if not (smooth_k and smooth_v):
-            raise NotImplementedError("the FP4 attention kernel always applies smooth-K / smooth-V")
         from . import ops
-        return ops.attention_bhsd(query, key, value, scale).to(query.dtype)
+        return ops.attention_bhsd(query, key, value, scale, smooth_k=smooth_k, smooth_v=smooth_v).to(query.dtype)
     if not query.is_cuda:
         raise RuntimeError("quant_sdpa runs on the GPU (CUDA tensors required)")
-    if qk == "fp8" and pv == "fp8" and attn_mask is None and not is_causal and smooth_k and smooth_v \
-            and query.dim() == 4:
+    if qk == "fp8" and pv == "fp8" and attn_mask is None and not is_causal and query.dim() == 4:
         from . import ops
         if ops.fp8_kernel_ok(query.shape[-2], D):
-            return ops.attention_fp8_bhsd(query, key, value, scale).to(query.dtype)
+            return ops.attention_fp8_bhsd(query, key, value, scale, smooth_k=smooth_k,
+                                          smooth_v=smooth_v).to(query.dtype)
     return _emulated_sdpa(query, key, value, attn_mask, is_causal, scale, qk, pv, smooth_k, smooth_v).to(query.dtype)

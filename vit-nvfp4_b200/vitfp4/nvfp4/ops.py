@@ -301,20 +301,27 @@ def _attn_workspace(B: int, H: int, S: int, D: int, device, flags: int = 0) -> t
     return ws
 
 
+def _smooth_flags(smooth_k: bool, smooth_v: bool) -> int:
+    return (0 if smooth_k else _lib.VF4_ATTN_NO_SMOOTH_K) | (0 if smooth_v else _lib.VF4_ATTN_NO_SMOOTH_V)
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
               strides: tuple[int, int, int], scale: float, out: torch.Tensor,
-              out_strides: tuple[int, int, int], head_globals: bool = False, packed: bool = True) -> torch.Tensor:
+              out_strides: tuple[int, int, int], head_globals: bool = False, packed: bool = True,
+              smooth_k: bool = True, smooth_v: bool = True) -> torch.Tensor:
     """NVFP4 attention over bf16 q/k/v views sharing (stride_b, stride_h, stride_s) element strides.
 
     Global scales of Q, K~, V~ over the whole tensors (the reference's) unless ``head_globals``.
     ``packed`` (head dim 64, S <= 320): operands quantized by a separate pass into per-head images
     in the workspace (~38 KB per image and head), the faster route; False keeps the quantization
-    inside the fused kernel (512 B of workspace per head)."""
+    inside the fused kernel (512 B of workspace per head).  ``smooth_k`` / ``smooth_v`` False switch off
+    the reference's smooth-K / smooth-V (tensor-wide globals only)."""
     _need_cuda(q, k, v, out)
     for t in (q, k, v, out):
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("FP4 attention takes bf16 q/k/v/out")
-    flags = (_lib.VF4_ATTN_HEAD_GLOBALS if head_globals else 0) | (_lib.VF4_ATTN_PACKED if packed else 0)
+    flags = (_lib.VF4_ATTN_HEAD_GLOBALS if head_globals else 0) | (_lib.VF4_ATTN_PACKED if packed else 0) | \
+        _smooth_flags(smooth_k, smooth_v)
     ws = _attn_workspace(B, H, S, D, q.device, flags)
     with _Timed(f"attn_nvfp4_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
         _lib.call("vf4_attn_nvfp4_ex", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
@@ -327,15 +334,18 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int,
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
                   strides: tuple[int, int, int], scale: float, out: torch.Tensor,
-                  out_strides: tuple[int, int, int]) -> torch.Tensor:
-    """FP8 (E4M3, per-row scales) attention over bf16 q/k/v views sharing element strides."""
+                  out_strides: tuple[int, int, int], smooth_k: bool = True, smooth_v: bool = True) -> torch.Tensor:
+    """FP8 (E4M3, per-row scales) attention over bf16 q/k/v views sharing element strides (through the
+    unified vf4_attn entry with qk = pv = fp8)."""
     _need_cuda(q, k, v, out)
     for t in (q, k, v, out):
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("FP8 attention takes bf16 q/k/v/out")
+    fp8 = _lib.VF4_ATTN_MODE["fp8"]
     with _Timed(f"attn_fp8_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
-        _lib.call("vf4_attn_fp8", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-                  float(scale), _ptr(out), out_strides[0], out_strides[1], out_strides[2], _stream())
+        _lib.call("vf4_attn", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
+                  float(scale), fp8, fp8, _smooth_flags(smooth_k, smooth_v), None, 0, _ptr(out), out_strides[0],
+                  out_strides[1], out_strides[2], _stream())
     _launched(1)
     return out
 
@@ -391,17 +401,19 @@ def _bhsd_operands(q, k, v):
     return qb, kb, vb, (H * S * D, S * D, D)
 
 
-def attention_fp8_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+def attention_fp8_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, smooth_k: bool = True,
+                       smooth_v: bool = True) -> torch.Tensor:
     """(B, H, S, D) q/k/v -> (B, H, S, D) bf16 through the FP8 kernel."""
     B, H, S, D = q.shape
     qb, kb, vb, strides = _bhsd_operands(q, k, v)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
-    attention_fp8(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D))
+    attention_fp8(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D), smooth_k, smooth_v)
     return out.transpose(1, 2)
 
 
 def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-                   head_globals: bool = False, packed: bool = True) -> torch.Tensor:
+                   head_globals: bool = False, packed: bool = True, smooth_k: bool = True,
+                   smooth_v: bool = True) -> torch.Tensor:
     """(B, H, S, D) q/k/v (any dtype; cast to bf16) -> (B, H, S, D) bf16."""
     B, H, S, D = q.shape
     qb, kb, vb = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
@@ -415,7 +427,7 @@ def attention_bhsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
         strides = (H * S * D, S * D, D)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=q.device)
     attention(qb, kb, vb, B, H, S, D, strides, scale, out, (S * H * D, D, H * D), head_globals=head_globals,
-              packed=packed)
+              packed=packed, smooth_k=smooth_k, smooth_v=smooth_v)
     return out.transpose(1, 2)
 
 
