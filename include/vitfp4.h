@@ -69,6 +69,13 @@ VF4_API const char* vf4_last_error_string(void);
  * (0 = none; otherwise a kernel gave up on a bounded wait). Synchronizes the device. */
 VF4_API int vf4_device_error(int clear);
 
+/* Self-test of the failure detector: launches one kernel whose bounded mbarrier wait (the wait every
+ * kernel here uses, given limit_ns instead of the production 4 s) waits on a barrier nothing arrives
+ * on.  The kernel gives up after limit_ns (0 < limit_ns <= 1e9), records VF4 device error 1 (producer
+ * data never arrived) for vf4_device_error and returns; the context stays usable.  No reference
+ * counterpart (the reference has no device-side waits). */
+VF4_API int vf4_selftest_wait_timeout(uint64_t limit_ns, vf4_stream_t stream);
+
 /* max|x| (or max|GELU(x)| when gelu != 0) over n elements, written to *amax_out.
  * Replaces the amax pass inside quant.py:48-49 and fused_mlp.py:25-29. */
 VF4_API int vf4_amax(const void* x, int dtype, int64_t n, int gelu, float* amax_out, vf4_stream_t stream);

@@ -230,3 +230,31 @@ def test_gemm_resident_b_scales_kernel(M, K, N, monkeypatch):
           *ops.gemm_gelu_nvfp4(ap, asf, ag, bp, bsf, bg, bias, gh)]
     for a, b in zip(ws, st):
         assert torch.equal(a, b)
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """The failure detector in the allowed form: a kernel's bounded mbarrier wait, given a 2 ms limit
+    and a barrier nothing arrives on, gives up, records device error 1 (producer data never arrived)
+    and returns; the call finishes far below the production 4 s limit, the error word clears when
+    read, and the context still runs a GEMM correctly afterwards."""
+    import time
+    from vitfp4 import _lib
+    ops = _ops()
+    assert _lib.device_error() == 0                       # also clears anything left over
+    stream = torch.cuda.current_stream().cuda_stream
+    t0 = time.perf_counter()
+    _lib.call("vf4_selftest_wait_timeout", 2_000_000, stream)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert elapsed < 1.0, elapsed
+    assert _lib.device_error(clear=True) == 1
+    assert _lib.device_error() == 0
+    with pytest.raises(_lib.VitFp4Error):
+        _lib.call("vf4_selftest_wait_timeout", 0, stream)
+    A, B = _operands(130, 256, 512, seed=1)
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    y = ops.gemm(ap, asf, ag, bp, bsf, bg, out_dtype=torch.float32)
+    ref = oracle.gemm_reference(A[0], A[1], A[2], B[0], B[1], B[2])
+    assert np.abs(y.cpu().numpy() - ref).max() <= 1e-3 * np.abs(ref).max()
+    assert _lib.device_error() == 0

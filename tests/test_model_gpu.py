@@ -304,3 +304,48 @@ def test_model_logits_vs_oracle():
     ref = vit_oracle.forward(W, images.float().numpy())
     assert cos(logits, ref) >= 0.99, cos(logits, ref)
     print("logits cos vs oracle", cos(logits, ref))
+
+
+# ----------------------------------------------------------------------------- composed W4A4 linear
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("static", [False, True])
+@pytest.mark.parametrize("M,K,N", [(394, 768, 2304), (257, 3072, 768), (1, 1024, 1024)])
+def test_qlinear_forward_matches_oracle(M, K, N, static, dtype):
+    """QuantLinear.forward / nvfp4_linear (reference qlinear.py:42-47 -> gemm.py:32-38) against the oracle
+    composed from the reference's steps: activation cast (six, dynamic or the static global),
+    dequantize-and-matmul (backends/reference.py:6-10), output rounded to x.dtype, + bias in x.dtype.
+    The activation codes and scales are bit-exact (held elsewhere); the GEMM's fp32 summation order
+    differs, so the fp32 output is held to 1e-3 of max |ref| and cos >= 0.9999, the bf16 output to a
+    bf16 step."""
+    from vitfp4.nvfp4 import nvfp4_linear
+    from vitfp4.ptq import QuantLinear
+    torch.manual_seed(M + K)
+    lin = nn.Linear(K, N).cuda()
+    with torch.no_grad():
+        lin.bias.copy_(torch.randn(N) * 0.1)
+    lin = lin.to(dtype)
+    q = QuantLinear.from_linear(lin)
+    x = (torch.randn(M, K, device="cuda") * 2).to(dtype)
+    x[:, 3] *= 20.0                                         # an outlier channel
+    xn = x.float().cpu().numpy()
+    gs = None
+    if static:
+        gs = np.float32(np.abs(xn).max() / 2688.0 * 0.8)   # a calibrated global that clips the outliers a bit
+        q.set_activation_scale(torch.tensor(gs, device="cuda"))
+    y = q(x)
+    y2 = nvfp4_linear(x, q.w_codes, q.w_block_scale, q.w_global_scale, x_global_scale=q.x_global_scale,
+                      bias=q.bias)
+    assert y.dtype == dtype and torch.equal(y, y2)
+    c, b, g = oracle.quantize_to_nvfp4(xn, 16, global_scale=gs)
+    wc, wb, wg = (q.w_codes.cpu().numpy(), q.w_block_scale.view(torch.uint8).cpu().numpy(),
+                  np.float32(q.w_global_scale.item()))
+    acc = oracle.gemm_reference(c, b, g, wc, wb, wg)
+    bias = lin.bias.detach().float().cpu().numpy()
+    yn = y.float().cpu().numpy()
+    if dtype == torch.float32:
+        ref = acc + bias
+        assert np.abs(yn - ref).max() <= 1e-3 * np.abs(ref).max() and cos(yn, ref) >= 0.9999
+    else:
+        ref = oracle.to_bf16(oracle.to_bf16(acc) + bias)
+        step = np.abs(ref) * 2.0 ** -7 + 1e-6              # two bf16 roundings
+        assert (np.abs(yn - ref) <= step).mean() >= 0.999 and cos(yn, ref) >= 0.9999

@@ -521,20 +521,25 @@ VF4_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (after recording `code` in *err) if the phase never completes.
-VF4_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+// Bounded wait: returns false (after recording `code` in *err) if the phase does not complete
+// within limit_ns of %globaltimer (checked every 256 polls) or another role already gave up.
+VF4_DEV bool mbar_wait_limit(uint32_t bar, uint32_t parity, int* err, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*(volatile int*)err != 0) return false;  // another role already gave up
-      if (globaltimer() - t0 > VF4_WAIT_TIMEOUT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         return false;
       }
     }
   }
+}
+
+VF4_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, VF4_WAIT_TIMEOUT_NS);
 }
 
 VF4_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {

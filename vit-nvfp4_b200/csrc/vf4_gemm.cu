@@ -36,6 +36,19 @@ int gemm_device_error(int clear) {
   return v;
 }
 
+// Self-test of the bounded waits every kernel uses: one thread waits on an mbarrier of its own that
+// nothing ever arrives on, with the caller's limit instead of the production one.  The wait must
+// give up, record kDevErrTimeoutFull in this file's error word and let the kernel return.
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_limit(smem_u32(&bar), 0, &g_gemm_err, kDevErrTimeoutFull, limit_ns);
+}
+
 __host__ __device__ constexpr bool epi_gelu(int e) { return e == VF4_EPI_GELU_NVFP4 || e == VF4_EPI_GELU_ERF_NVFP4; }
 
 // The bf16 epilogues of the 128x256 tile stage 32 rows x 16 columns (1 KB) per warp so that a
@@ -1171,6 +1184,14 @@ static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float*
   if (ws_ok) return dispatch_gemm_ws(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   if (N >= 256) return dispatch_gemm<256>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
   return dispatch_gemm<128>(a_packed, b_packed, p, epilogue, out_dtype == VF4_F32, s);
+}
+
+extern "C" int vf4_selftest_wait_timeout(uint64_t limit_ns, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(VF4_ERR_ARG, "vf4_selftest_wait_timeout: limit must be in (0, 1 s]");
+  wait_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns);
+  return launch_status("vf4_selftest_wait_timeout");
 }
 
 extern "C" int vf4_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,

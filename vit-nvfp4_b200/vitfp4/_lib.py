@@ -32,6 +32,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_version": [],
     "vf4_last_error_string": [],
     "vf4_device_error": [_I],
+    "vf4_selftest_wait_timeout": [ctypes.c_uint64, _P],
     "vf4_amax": [_P, _I, _L, _I, _P, _P],
     "vf4_gelu_erf_f32": [_P, _L, _P, _P],
     "vf4_global_scale": [_P, _I, _P, _P],
