@@ -1,21 +1,16 @@
 """Attention routing of FusedNVFP4Block on the host (no GPU): which route a bf16 block takes for a
 given sequence length, head dim and dtype, with the CUDA kernel entry replaced by a recorder and the
 cuDNN routes run by torch's CPU SDPA."""
-import types
-
 import pytest
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
 
-def _block(H, D):
-    from vitfp4.ptq.fused_block import FusedNVFP4Block
-    attn = types.SimpleNamespace(num_heads=H, head_dim=D, scaling=D ** -0.5)
-    C = H * D
-    src = types.SimpleNamespace(norm1=nn.LayerNorm(C), attn=attn, ls1=nn.Identity(), norm2=nn.LayerNorm(C),
-                                mlp=nn.Identity(), ls2=nn.Identity())
-    return FusedNVFP4Block(src)
+def _route(qkv, H, D):
+    """The fused block's attention routing for an unflagged (bf16-route) block."""
+    from vitfp4.ptq.fused_block import _attention_route
+    return _attention_route(qkv, H, D ** -0.5, "none", "none")
 
 
 @pytest.fixture
@@ -42,7 +37,7 @@ def _sdpa(qkv, H, D):
 def test_bf16_kernel_route(kernel_calls, S):
     H, D = 2, 64
     qkv = torch.randn(2, S, 3 * H * D).bfloat16()
-    tag, out, am = _block(H, D)._attention(qkv)
+    tag, out, am = _route(qkv, H, D)
     assert tag == "amax" and out.shape == (2, S, H * D) and am.item() == 3.0
     assert kernel_calls == [((2, S, 3 * H * D), H, D ** -0.5)]
 
@@ -54,7 +49,7 @@ def test_split_query_route(kernel_calls, S, D, dtype):
     over all keys, queries [0, 128 k) and the rest, whose rows equal one call's."""
     H = 2
     qkv = torch.randn(1, S, 3 * H * D).to(dtype)
-    tag, o1, o2 = _block(H, D)._attention(qkv)
+    tag, o1, o2 = _route(qkv, H, D)
     s_main = S // 128 * 128
     assert tag == "split" and not kernel_calls
     assert o1.shape == (1, s_main, H * D) and o2.shape == (1, S - s_main, H * D)
@@ -67,5 +62,5 @@ def test_split_query_route(kernel_calls, S, D, dtype):
 def test_whole_call_route(kernel_calls):
     H, D, S = 2, 64, 420                       # S % 128 = 36: one SDPA call
     qkv = torch.randn(1, S, 3 * H * D).bfloat16()
-    out = _block(H, D)._attention(qkv)
+    out = _route(qkv, H, D)
     assert isinstance(out, torch.Tensor) and out.shape == (1, S, H * D) and not kernel_calls

@@ -349,3 +349,35 @@ def test_qlinear_forward_matches_oracle(M, K, N, static, dtype):
         ref = oracle.to_bf16(oracle.to_bf16(acc) + bias)
         step = np.abs(ref) * 2.0 ** -7 + 1e-6              # two bf16 roundings
         assert (np.abs(yn - ref) <= step).mean() >= 0.999 and cos(yn, ref) >= 0.9999
+
+
+# ----------------------------------------------------------------------------- torch.compile contract
+def test_custom_ops_trace_under_torch_compile_fullgraph():
+    """vitfp4::cast_nvfp4, vitfp4::attention_lowp and vitfp4::fused_block are torch.library custom ops
+    with fake implementations (the contract of the reference's fused MLP op, fused_mlp.py:38,58-61), so
+    torch.compile(fullgraph=True) traces them without a graph break and runs the same kernels."""
+    from vitfp4.nvfp4 import quant_sdpa
+    torch.manual_seed(11)
+    x = torch.randn(300, 256, device="cuda").bfloat16()
+    gs = torch.tensor(0.004, device="cuda")
+    cast = torch.compile(lambda t: torch.ops.vitfp4.cast_nvfp4(t, gs, False), fullgraph=True)
+    p1, s1 = cast(x)
+    p2, s2 = torch.ops.vitfp4.cast_nvfp4(x, gs, False)
+    assert torch.equal(p1, p2) and torch.equal(s1, s2)
+    q, k, v = (torch.randn(2, 3, 197, 64, device="cuda").bfloat16() for _ in range(3))
+    for qk in ("nvfp4", "fp8"):
+        att = torch.compile(lambda a, b, c: quant_sdpa(a, b, c, qk=qk, pv=qk), fullgraph=True)
+        assert torch.equal(att(q, k, v), quant_sdpa(q, k, v, qk=qk, pv=qk))
+
+
+def test_fused_model_under_torch_compile():
+    """A converted model of fused blocks compiled end to end gives the eager logits (the blocks are opaque
+    custom ops; the embedding, final LayerNorm and head are left to the compiler)."""
+    torch.manual_seed(12)
+    x = torch.randn(4, 3, 224, 224, device="cuda").bfloat16()
+    with torch.no_grad():
+        model = _convert(_small_vit(depth=2), fuse_blocks=True)
+        eager = model(x)                    # calibrates the MLP globals
+        eager = model(x)
+        compiled = torch.compile(model)(x)
+    assert _cos(eager, compiled) >= 0.9999, _cos(eager, compiled)

@@ -105,6 +105,23 @@ def _emulated_sdpa(q, k, v, attn_mask, is_causal, scale, qk, pv, smooth_k, smoot
     return out.reshape(*lead, S, D)
 
 
+@torch.library.custom_op("vitfp4::attention_lowp", mutates_args=())
+def attention_lowp_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, qk: str, pv: str,
+                      smooth_k: bool, smooth_v: bool) -> torch.Tensor:
+    """The kernel routes of quant_sdpa (nvfp4/nvfp4 and fp8/fp8 with head dim 64, S <= 320) on (B, H, S, D)
+    operands -> (B, H, S, D) bf16, laid out as a (B, S, H, D) tensor (the kernels' output layout)."""
+    from . import ops
+    if qk == "nvfp4":
+        return ops.attention_bhsd(q, k, v, scale, smooth_k=smooth_k, smooth_v=smooth_v)
+    return ops.attention_fp8_bhsd(q, k, v, scale, smooth_k=smooth_k, smooth_v=smooth_v)
+
+
+@attention_lowp_op.register_fake
+def _(q, k, v, scale, qk, pv, smooth_k, smooth_v):
+    B, H, S, D = q.shape
+    return q.new_empty((B, S, H, D), dtype=torch.bfloat16).transpose(1, 2)
+
+
 def quant_sdpa(query, key, value, attn_mask=None, is_causal=False, scale=None, qk="fp8", pv="fp8",
                smooth_k=True, smooth_v=True):
     """Drop-in low-precision attention: (..., S, D) operands -> (..., S, D) in query.dtype."""
@@ -116,6 +133,8 @@ def quant_sdpa(query, key, value, attn_mask=None, is_causal=False, scale=None, q
     if qk == "nvfp4" and pv == "nvfp4":
         if attn_mask is not None or is_causal:
             raise NotImplementedError("the FP4 attention kernel is for ViT (no mask, not causal)")
+        if query.dim() == 4:
+            return attention_lowp_op(query, key, value, float(scale), qk, pv, smooth_k, smooth_v).to(query.dtype)
         from . import ops
         return ops.attention_bhsd(query, key, value, scale, smooth_k=smooth_k, smooth_v=smooth_v).to(query.dtype)
     if not query.is_cuda:
@@ -123,6 +142,5 @@ def quant_sdpa(query, key, value, attn_mask=None, is_causal=False, scale=None, q
     if qk == "fp8" and pv == "fp8" and attn_mask is None and not is_causal and query.dim() == 4:
         from . import ops
         if ops.fp8_kernel_ok(query.shape[-2], D):
-            return ops.attention_fp8_bhsd(query, key, value, scale, smooth_k=smooth_k,
-                                          smooth_v=smooth_v).to(query.dtype)
+            return attention_lowp_op(query, key, value, float(scale), qk, pv, smooth_k, smooth_v).to(query.dtype)
     return _emulated_sdpa(query, key, value, attn_mask, is_causal, scale, qk, pv, smooth_k, smooth_v).to(query.dtype)

@@ -50,22 +50,37 @@ def gemm_packed(a_fp4, a_sf, a_g, w_fp4, w_sf, w_g, out_dtype=torch.bfloat16):
     return ops.gemm(a_fp4, a_sf, a_g, w_fp4, w_sf, w_g, out_dtype=out_dtype)
 
 
+@torch.library.custom_op("vitfp4::cast_nvfp4", mutates_args=())
+def cast_nvfp4_op(x: torch.Tensor, gs: torch.Tensor, apply_gelu: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(M, K) -> packed codes (M, K/2) uint8 and the 128x4-tiled scales (ceil128(M), ceil4(K/16)) uint8."""
+    K = x.shape[-1]
+    packed, sf, _, _ = ops.cast(x, gs, "six", gelu=apply_gelu)
+    return packed, sf.view(-1, ((K // 16) + 3) // 4 * 4)
+
+
+@cast_nvfp4_op.register_fake
+def _(x, gs, apply_gelu):
+    K = x.shape[-1]
+    M = x.numel() // K
+    return (x.new_empty((M, K // 2), dtype=torch.uint8),
+            x.new_empty(((M + 127) // 128 * 128, ((K // 16) + 3) // 4 * 4), dtype=torch.uint8))
+
+
 def cast_nvfp4(x: torch.Tensor, per_tensor_scale: torch.Tensor | None, apply_gelu: bool = False,
                use_e8m0_scale: bool = False, use_precise_math: bool = True):
     """Fused single-pass NVFP4 cast (optionally GELU first) -> (qdata float4_e2m1fn_x2, swizzled scale).
 
-    Same contract as the reference's Triton cast_nvfp4: ``per_tensor_scale`` is the decode
-    global (``amax/(6*448)``), None means 1.0; the scale comes back 2-D (ceil128(M), ceil4(K/16)).
-    The block arithmetic is the reference quantizer's (quant.py), not the Triton kernel's.
+    Same contract as the reference's Triton cast_nvfp4 (triton_cast.py:138-233): ``per_tensor_scale`` is
+    the decode global (``amax/(6*448)``), None means 1.0; the scale comes back 2-D (ceil128(M),
+    ceil4(K/16)).  The block arithmetic is the reference quantizer's (quant.py), not the Triton
+    kernel's.  A ``torch.library`` custom op (``vitfp4::cast_nvfp4``), so torch.compile traces around it.
     """
     if use_e8m0_scale:
         raise NotImplementedError("E8M0 scales are not part of the NVFP4 path")
     K = x.shape[-1]
-    M = x.numel() // K
     gs = per_tensor_scale if per_tensor_scale is not None else torch.ones((), device=x.device)
-    packed, sf, _, _ = ops.cast(x, gs, "six", gelu=apply_gelu)
-    sf2 = sf.view(torch.float8_e4m3fn).view(-1, ((K // 16) + 3) // 4 * 4)
-    return packed.view(*x.shape[:-1], K // 2).view(torch.float4_e2m1fn_x2), sf2
+    packed, sf = cast_nvfp4_op(x.reshape(-1, K), gs.reshape(()).float(), bool(apply_gelu))
+    return (packed.view(*x.shape[:-1], K // 2).view(torch.float4_e2m1fn_x2), sf.view(torch.float8_e4m3fn))
 
 
 def nvfp4_linear(x, w_codes, w_bs, w_gs, *, x_global_scale=None, bias=None, backend=None):
