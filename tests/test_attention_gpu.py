@@ -146,7 +146,7 @@ def test_packed_workspace_size():
     assert packed >= plain + 4 * 16 * 38 * 1024
     # the long-sequence route ignores the flag
     assert lib.vf4_attn_workspace_size_ex(1, 2, 1025, 80, _lib.VF4_ATTN_PACKED) == lib.vf4_attn_workspace_size(1, 2, 1025, 80)
-    assert lib.vf4_attn_workspace_size_ex(1, 2, 257, 64, 4) == 0
+    assert lib.vf4_attn_workspace_size_ex(1, 2, 257, 64, 16) == 0
 
 
 def test_attention_packed_qkv_path_equals_bhsd():

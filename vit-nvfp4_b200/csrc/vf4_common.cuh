@@ -460,8 +460,12 @@ VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
                   kA4 = 0.5f * -1.453152027f, kA5 = 0.5f * 1.061405429f;
   float x0, x1;
   f32x2_unpack(x2, &x0, &x1);
-  // |x| capped below +inf, so that |x| * exp(-x^2 / 2) is 0 rather than inf * 0 for x = +-inf
-  const unsigned long long z = f32x2_pack(fminf(fabsf(x0), 0x1p126f), fminf(fabsf(x1), 0x1p126f));
+  // |x| capped below +inf, so that |x| * exp(-x^2 / 2) is 0 rather than inf * 0 for x = +-inf; the
+  // NaN-propagating min keeps a NaN input NaN (through m below; the relu term drops it)
+  float z0, z1;
+  asm("min.NaN.f32 %0, %1, 0f7E800000;" : "=f"(z0) : "f"(fabsf(x0)));
+  asm("min.NaN.f32 %0, %1, 0f7E800000;" : "=f"(z1) : "f"(fabsf(x1)));
+  const unsigned long long z = f32x2_pack(z0, z1);
   float d0, d1, t0, t1;
   f32x2_unpack(fma_f32x2(z, f32x2_pack(kP, kP), f32x2_pack(1.f, 1.f)), &d0, &d1);
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d0));

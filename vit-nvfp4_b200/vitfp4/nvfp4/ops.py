@@ -473,6 +473,28 @@ def ln_cast(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float,
     return packed, sf, (gs_out if gs_in is None else gs_in), (x if y is None else x_out)
 
 
+@torch.library.custom_op("vitfp4::patchify", mutates_args=())
+def patchify_op(images: torch.Tensor, patch: int, k_pad: int) -> torch.Tensor:
+    return patchify(images, patch, k_pad)
+
+
+@patchify_op.register_fake
+def _(images, patch, k_pad):
+    B, C, H, W = images.shape
+    return images.new_empty((B * (H // patch) * (W // patch), k_pad), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("vitfp4::embed_tokens", mutates_args=())
+def embed_tokens_op(y: torch.Tensor, cls: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    return embed_tokens(y, cls, pos)
+
+
+@embed_tokens_op.register_fake
+def _(y, cls, pos):
+    B, P, D = y.shape
+    return y.new_empty((B, P + 1, D), dtype=torch.bfloat16)
+
+
 def patchify(images: torch.Tensor, patch: int, k_pad: int) -> torch.Tensor:
     """(B, C, H, W) bf16 images -> (B * H/p * W/p, k_pad) bf16 patch rows in the Conv2d weight's
     (c, i, j) order, zero-padded from C*p*p to k_pad columns (16-byte rows for the GEMM)."""

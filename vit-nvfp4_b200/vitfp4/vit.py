@@ -149,7 +149,7 @@ class PatchEmbed(nn.Module):
             # sm_100 kernels; the zero columns meet zero weight columns)
             from .nvfp4 import ops
             kp = (K + 7) // 8 * 8
-            patches = ops.patchify(x, p, kp)
+            patches = ops.patchify_op(x, p, kp)
             return F.linear(patches, self._weight_padded(kp), self.proj.bias).reshape(B, g_h * g_w, -1)
         patches = x.reshape(B, C, g_h, p, g_w, p).permute(0, 2, 4, 1, 3, 5).reshape(B, g_h * g_w, K)
         w = self.proj.weight.reshape(self.proj.out_channels, -1)
@@ -180,7 +180,7 @@ class VisionTransformer(nn.Module):
         x = self.patch_embed(x)
         if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0:
             from .nvfp4 import ops
-            x = ops.embed_tokens(x, self.cls_token, self.pos_embed)   # cat + add, one pass
+            x = ops.embed_tokens_op(x, self.cls_token, self.pos_embed)   # cat + add, one pass
         else:
             x = torch.cat([self.cls_token.expand(x.shape[0], -1, -1).to(x.dtype), x], dim=1)
             x = x + self.pos_embed.to(x.dtype)
