@@ -539,8 +539,27 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
 }
 
 // ---------------------------------------------------------------------------------------
-// Kernel 2: attention forward
+// Kernel 2: attention forward (long sequences).  Persistent: each CTA takes whole heads (the
+// B*H heads strided over the grid) and runs all query tiles of a head against that head's K~ and
+// V~^T, which are loaded into shared memory once per head.
+//   warp 0      loads: K~, V~^T and their scales once per head; Q and its scales per 128-query
+//               tile (the next tile's Q is loaded as soon as the current tile's last QK^T MMA has
+//               run)
+//   warp 1      TMEM allocation, then the MMAs: per 128-key chunk S = Q K~^T into one of two
+//               TMEM score buffers (pass 1, then again in pass 2), and O = P V~ per chunk
+//   warps 2-9   softmax: two warps per TMEM lane quadrant, each owning 64 of a chunk's 128 key
+//               columns.  Pass 1: running row max and row sum of exp; the two halves combine
+//               through shared memory.  Pass 2: P = exp(s - max) / sum, NVFP4 with the fixed
+//               global 1/2688 (each half writes its 64 keys' codes and one K64 scale word) into
+//               one of two P buffers.  Epilogue: O * gs_v / 2688 + mean(v) -> bf16.
+// Every wait is bounded; a give-up records the device error and unwinds.
 // ---------------------------------------------------------------------------------------
+VF4_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int DP>
 struct AttnCfg {
   static constexpr int DV = DP;
@@ -551,15 +570,17 @@ struct AttnCfg {
   static constexpr int PBYTES = 128 * 64;             // P chunk: 128 rows x 128 keys
   static constexpr uint32_t QK_LAYOUT = DP == 64 ? 6u : 4u;   // SWIZZLE_32B / SWIZZLE_64B
   static constexpr uint32_t QK_SBO = 8 * ROWB;
-  // TMEM columns
-  static constexpr int T_S = 0, T_O = 128, T_QSF = 128 + DV, T_KSF = T_QSF + 4 * KB;
+  // TMEM columns: two score buffers, O, and the scale slots
+  static constexpr int T_S = 0, T_O = 256, T_QSF = 256 + DV, T_KSF = T_QSF + 4 * KB;
   static constexpr int T_PSF = T_KSF + 4 * KB, T_VSF = T_PSF + 8;
-  static constexpr int TMEM_COLS = (T_VSF + 8) <= 256 ? 256 : 512;
-  static constexpr int THREADS = 192;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SOFTMAX_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
+  static_assert(T_VSF + 8 <= TMEM_COLS, "TMEM overflow");
 };
 
 struct AttnSmem {
-  uint32_t q, k, v, p, qsf, ksf, vsf, psf, bar, total;
+  uint32_t q, k, v, p, qsf, ksf, vsf, psf, red, bar, total;
 };
 
 template <int DP>
@@ -575,13 +596,14 @@ static AttnSmem attn_smem_layout(int nc, int S_pad) {
   s.ksf = o; o += nc * C::KB * 512;
   s.vsf = o; o += (S_pad / 64) * 512;
   s.psf = o; o += 2 * 1024;
-  s.bar = o; o += 128;
+  s.red = o; o += 128 * 2 * 8;           // per row and key half: running max and sum
+  s.bar = o; o += 256;
   s.total = o + 1024;  // slack for aligning the base to 1024
   return s;
 }
 
 template <int DP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(AttnCfg<DP>::THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnGeom g, const uint8_t* __restrict__ ws,
                     const AttnSmem L, float scale, __nv_bfloat16* __restrict__ out, int64_t osb, int64_t osh,
@@ -592,24 +614,31 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t bar = base + L.bar;
-  const uint32_t load_bar = bar, s_full = bar + 8, s_free = bar + 16, o_full = bar + 24, drain = bar + 32;
-  auto p_full = [&](int i) { return bar + 40 + 8u * i; };
-  auto p_free = [&](int i) { return bar + 56 + 8u * i; };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L.bar + 72);
+  const uint32_t kv_full = bar, kv_free = bar + 8, q_full = bar + 16, q_free = bar + 24, o_full = bar + 32,
+                 o_free = bar + 40, drain = bar + 48;
+  auto s_full = [&](int i) { return bar + 56 + 8u * i; };
+  auto s_free = [&](int i) { return bar + 72 + 8u * i; };
+  auto p_full = [&](int i) { return bar + 88 + 8u * i; };
+  auto p_free = [&](int i) { return bar + 104 + 8u * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L.bar + 128);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, bh = blockIdx.y;
   const int nc = g.nc, S = g.S;
   int* err = &g_attn_err;
+  constexpr int NSW = C::SOFTMAX_WARPS;
 
   if (warp == 0 && lane == 0) {
-    mbar_init(load_bar, 1);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
+    mbar_init(kv_full, 1);
+    mbar_init(kv_free, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
     mbar_init(o_full, 1);
+    mbar_init(o_free, NSW);
     mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(p_full(i), 4);
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), NSW);
+      mbar_init(p_full(i), NSW);
       mbar_init(p_free(i), 1);
     }
     fence_mbar_init();
@@ -625,179 +654,222 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-  const float* scal = reinterpret_cast<const float*>(ws + g.off_scal) + (int64_t)bh * kScalStride;
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ loads
       const uint32_t qsf_bytes = C::KB * 512, ksf_bytes = nc * C::KB * 512, vsf_bytes = (g.S_pad / 64) * 512;
-      const uint32_t tx = C::QBYTES + nc * (C::QBYTES + C::VBYTES) + qsf_bytes + ksf_bytes + vsf_bytes;
-      mbar_arrive_expect_tx(load_bar, tx);
-      tma_load_2d(base + L.q, &tmQ, 0, bh * g.S_pad + qt * 128, load_bar);
-      for (int j = 0; j < nc; ++j) {
-        tma_load_2d(base + L.k + j * C::QBYTES, &tmK, 0, bh * g.S_pad + j * 128, load_bar);
-        tma_load_2d(base + L.v + j * C::VBYTES, &tmV, j * 64, bh * C::DV, load_bar);
+      uint32_t hc = 0, tcnt = 0;
+      bool ok = true;
+      for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
+        if (!(ok = mbar_wait(kv_free, (hc & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+        mbar_arrive_expect_tx(kv_full, nc * (C::QBYTES + C::VBYTES) + ksf_bytes + vsf_bytes);
+        for (int j = 0; j < nc; ++j) {
+          tma_load_2d(base + L.k + j * C::QBYTES, &tmK, 0, (int)(bh * g.S_pad + j * 128), kv_full);
+          tma_load_2d(base + L.v + j * C::VBYTES, &tmV, j * 64, (int)(bh * C::DV), kv_full);
+        }
+        bulk_load(base + L.ksf, ws + g.off_ksf + bh * g.qsf_head, ksf_bytes, kv_full);
+        bulk_load(base + L.vsf, ws + g.off_vsf + bh * g.vsf_head, vsf_bytes, kv_full);
+        for (int qt = 0; qt < nc; ++qt, ++tcnt) {
+          if (!(ok = mbar_wait(q_free, (tcnt & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+          mbar_arrive_expect_tx(q_full, C::QBYTES + qsf_bytes);
+          tma_load_2d(base + L.q, &tmQ, 0, (int)(bh * g.S_pad + qt * 128), q_full);
+          bulk_load(base + L.qsf, ws + g.off_qsf + bh * g.qsf_head + (int64_t)qt * C::KB * 512, qsf_bytes, q_full);
+        }
       }
-      bulk_load(base + L.qsf, ws + g.off_qsf + (int64_t)bh * g.qsf_head + (int64_t)qt * C::KB * 512, qsf_bytes,
-                load_bar);
-      bulk_load(base + L.ksf, ws + g.off_ksf + (int64_t)bh * g.qsf_head, ksf_bytes, load_bar);
-      bulk_load(base + L.vsf, ws + g.off_vsf + (int64_t)bh * g.vsf_head, vsf_bytes, load_bar);
-
+      // our own copies still in flight complete before the CTA retires (bounded)
+      if (hc > 0) mbar_wait(kv_full, (hc - 1) & 1u, err, kDevErrTimeoutFull);
+      if (tcnt > 0) mbar_wait(q_full, (tcnt - 1) & 1u, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
       // ------------------------------------------------------------ MMA issue
-      bool ok = mbar_wait(load_bar, 0, err, kDevErrTimeoutFull);
-      tc_fence_after();
       constexpr uint32_t id_s = idesc_mxf4nvf4(128);
       constexpr uint32_t id_o = idesc_mxf4nvf4(C::DV);
-      const uint32_t t_s = tmem + C::T_S, t_o = tmem + C::T_O;
-      const uint32_t t_qsf = tmem + C::T_QSF, t_ksf = tmem + C::T_KSF;
+      const uint32_t t_o = tmem + C::T_O, t_qsf = tmem + C::T_QSF, t_ksf = tmem + C::T_KSF;
       const uint32_t t_psf = tmem + C::T_PSF, t_vsf = tmem + C::T_VSF;
-      uint32_t sfree_n = 0;
-      auto issue_s = [&](int j) {
+      uint32_t hc = 0, tcnt = 0, sc = 0, pc = 0;
+      bool ok = true;
+      auto issue_s = [&](int j) -> bool {   // S chunk j into score buffer sc & 1
+        const int b = (int)(sc & 1u);
+        if (!mbar_wait(s_free(b), ((sc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty)) return false;
+        tc_fence_after();
         for (int kb = 0; kb < C::KB; ++kb)
           tmem_cp_32x128b_x4(t_ksf + kb * 4, smem_desc(base + L.ksf + (j * C::KB + kb) * 512, 0, 128, 0));
         for (int kb = 0; kb < C::KB; ++kb) {
           const uint64_t ad = smem_desc(base + L.q + kb * 32, 16, C::QK_SBO, C::QK_LAYOUT);
           const uint64_t bd = smem_desc(base + L.k + j * C::QBYTES + kb * 32, 16, C::QK_SBO, C::QK_LAYOUT);
-          mma_mxf4nvf4(t_s, ad, bd, id_s, t_qsf + kb * 4, t_ksf + kb * 4, kb > 0 ? 1u : 0u);
+          mma_mxf4nvf4(tmem + C::T_S + 128 * b, ad, bd, id_s, t_qsf + kb * 4, t_ksf + kb * 4, kb > 0 ? 1u : 0u);
         }
-        tc_commit(s_full);
+        tc_commit(s_full(b));
+        ++sc;
+        return true;
       };
-      if (ok) {
-        for (int kb = 0; kb < C::KB; ++kb)
-          tmem_cp_32x128b_x4(t_qsf + kb * 4, smem_desc(base + L.qsf + kb * 512, 0, 128, 0));
-        // pass 1: scores for the row statistics
-        for (int j = 0; j < nc && ok; ++j) {
-          if (j > 0) ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
-          if (ok) issue_s(j);
-        }
-        // pass 2: recompute scores, PV
-        if (ok) ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
-        if (ok) issue_s(0);
-        for (int j = 0; j < nc && ok; ++j) {
-          if (j + 1 < nc) {
-            ok = mbar_wait(s_free, (sfree_n++) & 1u, err, kDevErrTimeoutEmpty);
-            if (!ok) break;
-            issue_s(j + 1);
-          }
-          ok = mbar_wait(p_full(j & 1), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
-          if (!ok) break;
+      for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
+        if (!(ok = mbar_wait(kv_full, hc & 1u, err, kDevErrTimeoutFull))) break;
+        for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
+          if (!(ok = mbar_wait(q_full, tcnt & 1u, err, kDevErrTimeoutFull))) break;
           tc_fence_after();
-          const uint32_t pb = base + L.p + (j & 1) * C::PBYTES;
-          for (int kb = 0; kb < 2; ++kb) {
-            tmem_cp_32x128b_x4(t_psf + kb * 4, smem_desc(base + L.psf + (j & 1) * 1024 + kb * 512, 0, 128, 0));
-            tmem_cp_32x128b_x4(t_vsf + kb * 4, smem_desc(base + L.vsf + (2 * j + kb) * 512, 0, 128, 0));
+          for (int kb = 0; kb < C::KB; ++kb)
+            tmem_cp_32x128b_x4(t_qsf + kb * 4, smem_desc(base + L.qsf + kb * 512, 0, 128, 0));
+          // pass 1: scores for the row statistics
+          for (int j = 0; j < nc && ok; ++j) ok = issue_s(j);
+          // pass 2: scores again, one chunk ahead of the PV products
+          if (ok) ok = issue_s(0);
+          // O of the previous tile has been read by the softmax warps before it is overwritten
+          if (ok) ok = mbar_wait(o_free, (tcnt & 1u) ^ 1u, err, kDevErrTimeoutTmem);
+          for (int j = 0; j < nc && ok; ++j) {
+            if (j + 1 < nc) {
+              if (!(ok = issue_s(j + 1))) break;
+            } else {
+              tc_commit(q_free);   // every QK^T of this tile issued: Q's buffers free once they ran
+            }
+            const int pb = (int)(pc & 1u);
+            if (!(ok = mbar_wait(p_full(pb), (pc >> 1) & 1u, err, kDevErrTimeoutFull))) break;
+            tc_fence_after();
+            for (int kb = 0; kb < 2; ++kb) {
+              tmem_cp_32x128b_x4(t_psf + kb * 4, smem_desc(base + L.psf + pb * 1024 + kb * 512, 0, 128, 0));
+              tmem_cp_32x128b_x4(t_vsf + kb * 4, smem_desc(base + L.vsf + (2 * j + kb) * 512, 0, 128, 0));
+            }
+            const uint32_t pbuf = base + L.p + pb * C::PBYTES;
+            for (int kb = 0; kb < 2; ++kb) {
+              const uint64_t ad = smem_desc(pbuf + kb * 256, 128, 512, 0);           // interleaved, no swizzle
+              const uint64_t bd = smem_desc(base + L.v + j * C::VBYTES + kb * 32, 16, 512, 4);  // SWIZZLE_64B
+              mma_mxf4nvf4(t_o, ad, bd, id_o, t_psf + kb * 4, t_vsf + kb * 4, (j > 0 || kb > 0) ? 1u : 0u);
+            }
+            tc_commit(p_free(pb));
+            ++pc;
           }
-          for (int kb = 0; kb < 2; ++kb) {
-            const uint64_t ad = smem_desc(pb + kb * 256, 128, 512, 0);           // interleaved, no swizzle
-            const uint64_t bd = smem_desc(base + L.v + j * C::VBYTES + kb * 32, 16, 512, 4);  // SWIZZLE_64B
-            mma_mxf4nvf4(t_o, ad, bd, id_o, t_psf + kb * 4, t_vsf + kb * 4, (j > 0 || kb > 0) ? 1u : 0u);
-          }
-          tc_commit(p_free(j & 1));
+          if (ok) tc_commit(o_full);
         }
-        if (ok) tc_commit(o_full);
+        if (ok) tc_commit(kv_free);   // this head's K~ / V~ no longer read once these MMAs ran
       }
       tc_commit(drain);
       mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
     }
-  } else if (warp >= 2) {
+  } else {
     // ------------------------------------------------------------ softmax / epilogue
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;               // key columns [64 half, 64 half + 64) of a chunk
     const int r = quad * 32 + lane;                 // row of the query tile == TMEM lane
-    const int tq = qt * 128 + r;                    // query token
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const float cexp = scal[0] * scal[1] * scale * 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
-    uint32_t sfull_n = 0;
+    float2* red = reinterpret_cast<float2*>(gbase + L.red);   // [half][128 rows]
+    uint32_t tcnt = 0, sc = 0, pc = 0;
     bool ok = true;
-    uint32_t v[128];
-    auto load_s = [&](int j, int ncols) -> bool {
-      if (!mbar_wait(s_full, (sfull_n++) & 1u, err, kDevErrTimeoutFull)) return false;
+    uint32_t v[64];
+    auto load_s = [&]() -> bool {   // this warp's 64 columns of the next score chunk
+      const int b = (int)(sc & 1u);
+      if (!mbar_wait(s_full(b), (sc >> 1) & 1u, err, kDevErrTimeoutFull)) return false;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (c * 32 < ncols) tmem_ld_32x32b_x32(tmem + lane_addr + C::T_S + c * 32, v + c * 32);
+      const uint32_t ta = tmem + lane_addr + C::T_S + 128 * b + 64 * half;
+      tmem_ld_32x32b_x32(ta, v);
+      tmem_ld_32x32b_x32(ta + 32, v + 32);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
+      if (lane == 0) mbar_arrive(s_free(b));
+      ++sc;
       return true;
     };
-    // pass 1
-    for (int j = 0; j < nc && ok; ++j) {
-      const int nvalid = min(128, S - j * 128);
-      if (!(ok = load_s(j, nvalid))) break;
-      float cm = -INFINITY;
+    for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x) {
+      const float* scal = reinterpret_cast<const float*>(ws + g.off_scal) + bh * kScalStride;
+      const float cexp = scal[0] * scal[1] * scale * 1.4426950408889634f;
+      for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
+        const int tq = qt * 128 + r;                // query token
+        // pass 1: running max and sum of exp over this warp's columns
+        float m = -INFINITY, l = 0.f;
+        for (int j = 0; j < nc && ok; ++j) {
+          if (!(ok = load_s())) break;
+          const int nvalid = min(64, S - j * 128 - 64 * half);   // may be <= 0 for the last chunk
+          float cm = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
-        if (i < nvalid) cm = fmaxf(cm, __uint_as_float(v[i]) * cexp);
-      const float mn = fmaxf(m, cm);
-      float sum = 0.f;
+          for (int i = 0; i < 64; ++i)
+            if (i < nvalid) cm = fmaxf(cm, __uint_as_float(v[i]) * cexp);
+          const float mn = fmaxf(m, cm);
+          if (mn > -INFINITY) {
+            float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
-        if (i < nvalid) sum += exp2f(__uint_as_float(v[i]) * cexp - mn);
-      l = l * exp2f(m - mn) + sum;
-      m = mn;
-    }
-    const float inv_l = 1.0f / l;
-    // pass 2
-    for (int j = 0; j < nc && ok; ++j) {
-      const int nvalid = min(128, S - j * 128);
-      if (!(ok = load_s(j, nvalid))) break;
-      if (j >= 2 && !(ok = mbar_wait(p_free(j & 1), (uint32_t)((j >> 1) - 1) & 1u, err, kDevErrTimeoutEmpty)))
-        break;
-      uint8_t* pbuf = gbase + L.p + (j & 1) * C::PBYTES;
-      uint32_t sfw[2] = {0u, 0u};
-#pragma unroll
-      for (int blk = 0; blk < 8; ++blk) {
-        uint64_t codes = 0;
-        if (blk * 16 < nvalid) {
-          float pv[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int i = blk * 16 + e;
-            pv[e] = i < nvalid ? exp2f(__uint_as_float(v[i]) * cexp - m) * inv_l : 0.f;
+            for (int i = 0; i < 64; ++i)
+              if (i < nvalid) sum += ex2_approx(__uint_as_float(v[i]) * cexp - mn);
+            l = l * ex2_approx(m - mn) + sum;
+            m = mn;
           }
-          float amax = 0.f;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) amax = fmaxf(amax, pv[e]);
-          float dec;
-          const uint32_t sf = six_scale(amax, 2688.f, kInv2688, &dec);
-          codes = encode16_fast(pv, dec);
-          sfw[blk >> 2] |= sf << (8 * (blk & 3));
         }
-        // interleaved K-major core matrices: (row group, 16-byte K chunk) at rg*512 + kc*128 + (r%8)*16
-        *reinterpret_cast<uint64_t*>(pbuf + (r >> 3) * 512 + (blk >> 1) * 128 + (r & 7) * 16 + (blk & 1) * 8) = codes;
-      }
-      uint8_t* psf = gbase + L.psf + (j & 1) * 1024;
-      const int so = (r & 31) * 16 + (r >> 5) * 4;
-      *reinterpret_cast<uint32_t*>(psf + so) = sfw[0];
-      *reinterpret_cast<uint32_t*>(psf + 512 + so) = sfw[1];
-      fence_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(j & 1));
-    }
-    // epilogue
-    if (ok && mbar_wait(o_full, 0, err, kDevErrTimeoutTmem)) {
-      tc_fence_after();
+        // combine the two halves of the row
+        red[half * 128 + r] = make_float2(m, l);
+        named_bar_sync(1 + quad, 64);
+        const float2 o2 = red[(1 - half) * 128 + r];
+        const float mr = fmaxf(m, o2.x);
+        const float lr = (m > -INFINITY ? l * ex2_approx(m - mr) : 0.f) + (o2.x > -INFINITY ? o2.y * ex2_approx(o2.x - mr) : 0.f);
+        const float inv_l = 1.0f / lr;
+        named_bar_sync(1 + quad, 64);               // both halves have read red before it is reused
+        // pass 2: P = exp(s - max) / sum -> NVFP4 into the P buffers
+        for (int j = 0; j < nc && ok; ++j) {
+          if (!(ok = load_s())) break;
+          const int nvalid = min(64, S - j * 128 - 64 * half);
+          const int pb = (int)(pc & 1u);
+          if (!(ok = mbar_wait(p_free(pb), ((pc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+          uint8_t* pbuf = gbase + L.p + pb * C::PBYTES;
+          uint32_t sfw = 0u;
 #pragma unroll
-      for (int c = 0; c < C::DV / 32; ++c) tmem_ld_32x32b_x32(tmem + lane_addr + C::T_O + c * 32, v + c * 32);
-      tmem_wait_ld();
-      if (tq < S) {
-        const float ao = kInv2688 * scal[2];
-        const int b = bh / g.H, h = bh - b * g.H;
-        __nv_bfloat16* o = out + b * osb + (int64_t)tq * oss + h * osh;
+          for (int blk = 0; blk < 4; ++blk) {
+            uint64_t codes = 0;
+            if (blk * 16 < nvalid) {
+              float pv[16];
 #pragma unroll
-        for (int d8 = 0; d8 < C::DV / 8; ++d8) {
-          if (d8 * 8 < g.D) {
-            uint32_t w[4];
+              for (int e = 0; e < 16; ++e) {
+                const int i = blk * 16 + e;
+                pv[e] = i < nvalid ? ex2_approx(__uint_as_float(v[i]) * cexp - mr) * inv_l : 0.f;
+              }
+              float amax = 0.f;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int d = d8 * 8 + 2 * e;
-              __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(v[d]) * ao + scal[4 + d],
-                                                        __uint_as_float(v[d + 1]) * ao + scal[4 + d + 1]);
-              w[e] = *reinterpret_cast<uint32_t*>(&hv);
+              for (int e = 0; e < 16; ++e) amax = fmaxf(amax, pv[e]);
+              float dec;
+              const uint32_t sf = six_scale(amax, 2688.f, kInv2688, &dec);
+              codes = encode16_fast(pv, dec);
+              sfw |= sf << (8 * blk);
             }
-            *reinterpret_cast<uint4*>(o + d8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            // interleaved K-major core matrices: (row group, 16-byte K chunk) at rg*512 + kc*128 + (r%8)*16
+            const int gb = 4 * half + blk;          // 16-key block within the 128-key chunk
+            *reinterpret_cast<uint64_t*>(pbuf + (r >> 3) * 512 + (gb >> 1) * 128 + (r & 7) * 16 + (gb & 1) * 8) = codes;
+          }
+          // this half's four blocks are the K64 block `half` of the chunk: one scale word
+          *reinterpret_cast<uint32_t*>(gbase + L.psf + pb * 1024 + half * 512 + (r & 31) * 16 + (r >> 5) * 4) = sfw;
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full(pb));
+          ++pc;
+        }
+        // epilogue: this warp's half of the head dim
+        if (ok && (ok = mbar_wait(o_full, tcnt & 1u, err, kDevErrTimeoutTmem))) {
+          tc_fence_after();
+          constexpr int DH = C::DV / 2;
+          uint32_t ov[DH];
+#pragma unroll
+          for (int c = 0; c < DH / 32; ++c)
+            tmem_ld_32x32b_x32(tmem + lane_addr + C::T_O + half * DH + c * 32, ov + c * 32);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+          if (tq < S) {
+            const float ao = kInv2688 * scal[2];
+            const int b = (int)(bh / g.H), h = (int)(bh - (int64_t)b * g.H);
+            __nv_bfloat16* o = out + b * osb + (int64_t)tq * oss + h * osh + half * DH;
+#pragma unroll
+            for (int d8 = 0; d8 < DH / 8; ++d8) {
+              if (half * DH + d8 * 8 < g.D) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int d = d8 * 8 + 2 * e;
+                  __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[d]) * ao + scal[4 + half * DH + d],
+                                                            __uint_as_float(ov[d + 1]) * ao + scal[4 + half * DH + d + 1]);
+                  w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                }
+                *reinterpret_cast<uint4*>(o + d8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
           }
         }
       }
@@ -920,12 +992,6 @@ VF4_DEV void raw_load8(const uint8_t* raw, int s, int j, float* v) {
 VF4_DEV float raw_elem(const uint8_t* raw, int s, int d) {
   const uint16_t b = *reinterpret_cast<const uint16_t*>(raw + s * 128 + (((d >> 3) ^ (s & 7)) << 4) + (d & 7) * 2);
   return __uint_as_float((uint32_t)b << 16);
-}
-
-VF4_DEV float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
 }
 
 // byte offset of (row, 8-byte half-chunk h) in a K-major core-matrix operand with sbo bytes per
@@ -2865,7 +2931,7 @@ static int launch_fwd(const AttnGeom& g, const uint8_t* ws, float scale, void* o
     return st;
   auto kern = attn_fwd_kernel<DP>;
   if (int st = smem_optin(kern, (int)L.total)) return st;
-  dim3 grid(g.nc, (unsigned)g.BH);
+  const int grid = (int)(g.BH < num_sms() ? g.BH : num_sms());   // persistent: whole heads per CTA
   kern<<<grid, C::THREADS, L.total, s>>>(tq, tk, tv, g, ws, L, scale, static_cast<__nv_bfloat16*>(out), osb, osh,
                                          oss);
   return launch_status("vf4_attn_nvfp4 (forward)");
