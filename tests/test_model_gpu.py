@@ -381,3 +381,35 @@ def test_fused_model_under_torch_compile():
         eager = model(x)
         compiled = torch.compile(model)(x)
     assert _cos(eager, compiled) >= 0.9999, _cos(eager, compiled)
+
+
+# ----------------------------------------------------------------------------- packed weight format
+def test_qlinear_packed_state_dict_round_trip():
+    """persist_packed(): the GEMM-ready bytes travel in state_dict and a loaded module uses them without
+    repacking (no pack / swizzle launch); from_packed(): a module built from those bytes alone has the
+    reference's codes and scales and computes the same output."""
+    from vitfp4.nvfp4 import ops
+    from vitfp4.ptq import QuantLinear
+    torch.manual_seed(21)
+    lin = nn.Linear(384, 1152).cuda().bfloat16()
+    q = QuantLinear.from_linear(lin).persist_packed()
+    x = torch.randn(197, 384, device="cuda").bfloat16()
+    y = q(x)
+    sd = q.state_dict()
+    assert {"w_packed", "w_sf", "w_codes", "w_block_scale", "w_global_scale", "bias"} <= set(sd)
+    q2 = QuantLinear(torch.zeros_like(q.w_codes), torch.zeros_like(q.w_block_scale), torch.zeros((), device="cuda"),
+                     torch.zeros_like(q.bias), 384, 1152).persist_packed()
+    q2.load_state_dict(sd)
+    ops.probe.reset()
+    q(x)                                    # packed already: the activation cast and the GEMM only
+    n_ready = ops.probe.launches
+    ops.probe.reset()
+    y2 = q2(x)
+    assert ops.probe.launches == n_ready    # nothing repacked after loading
+    assert torch.equal(y, y2)
+    q3 = QuantLinear.from_packed(sd["w_packed"], sd["w_sf"], sd["w_global_scale"], sd["bias"], 384, 1152)
+    assert torch.equal(q3.w_codes, q.w_codes)
+    assert torch.equal(q3.w_block_scale.view(torch.uint8), q.w_block_scale.view(torch.uint8))
+    assert torch.equal(q3(x), y)
+    # without persist_packed the state_dict keeps the reference's buffer names only
+    assert "w_packed" not in QuantLinear.from_linear(lin).state_dict()
