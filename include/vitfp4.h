@@ -238,9 +238,11 @@ VF4_API int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64
  * (reached through _quant_attention, qattention.py:20-30) as one entry point: qk_mode / pv_mode are
  * VF4_ATTN_MODE_*, flags VF4_ATTN_NO_SMOOTH_K / _V switch smooth-K / smooth-V off (and, for the NVFP4
  * route, VF4_ATTN_HEAD_GLOBALS / VF4_ATTN_PACKED as vf4_attn_nvfp4_ex).  Kernel routes: nvfp4/nvfp4
- * (vf4_attn_nvfp4_ex), fp8/fp8 (E4M3 kernel: head dim 64, S <= 320), bf16/bf16 (vf4_attn_bf16, where
- * smoothing changes no result).  Mixed modes return VF4_ERR_UNSUPPORTED.  The workspace is needed by
- * the NVFP4 route only: size it with vf4_attn_workspace_size_modes. */
+ * (vf4_attn_nvfp4_ex), fp8/fp8 (E4M3 kernels: one fused kernel for head dim 64 and S <= 320, else a
+ * prep kernel and a long-sequence kernel for head dims that are multiples of 16 up to 128 -- S up to
+ * 1408 at head dim 80, 2304 at 64, 896 at 128), bf16/bf16 (vf4_attn_bf16, where smoothing changes no
+ * result).  Mixed modes return VF4_ERR_UNSUPPORTED.  The NVFP4 route and the long-sequence FP8 route
+ * need a workspace: size it with vf4_attn_workspace_size_modes (0 = none needed). */
 VF4_API int vf4_attn(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
                      int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale, int qk_mode, int pv_mode,
                      int flags, void* workspace, int64_t workspace_bytes, void* out, int64_t out_stride_b,

@@ -229,6 +229,81 @@ def test_fp8_kernel_matches_reference(B, H, S, D):
     assert cos(out, exact) >= cos(ref, exact) - 0.002
 
 
+@pytest.mark.parametrize("B,H,S,D", [(1, 2, 1025, 80), (2, 3, 257, 80), (1, 2, 400, 64), (1, 1, 129, 128),
+                                     (2, 2, 60, 96), (1, 2, 33, 16), (1, 1, 1408, 80)])
+def test_fp8_long_route_matches_reference(B, H, S, D):
+    """The long-sequence FP8 route (prep + persistent kernel; ViT-H/14's head dim 80 at 224 and 448 px)
+    against the reference's quant_sdpa(qk = pv = 'fp8'): the same quantization of Q, K~, V~ and P, so only
+    rounding differs -- per head cos >= 0.999, accuracy vs exact attention within 0.002 of the reference's."""
+    from vitfp4.nvfp4 import ops, quant_sdpa
+    assert ops.fp8_kernel_ok(S, D)
+    q, k, v = _qkv(B, H, S, D, seed=70 + S)
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = ops.attention_fp8_bhsd(qc, kc, vc, D ** -0.5).float().cpu().numpy()
+    assert np.array_equal(out, quant_sdpa(qc, kc, vc, qk="fp8", pv="fp8").float().cpu().numpy())
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref = oracle.quant_sdpa(qn, kn, vn, qk="fp8", pv="fp8")
+    exact = oracle.quant_sdpa(qn, kn, vn, qk="bf16", pv="bf16", smooth_k=False, smooth_v=False)
+    assert np.isfinite(out).all()
+    for b in range(B):
+        for h in range(H):
+            assert cos(out[b, h], ref[b, h]) >= 0.999, (b, h, cos(out[b, h], ref[b, h]))
+    assert cos(out, exact) >= cos(ref, exact) - 0.002
+    from vitfp4 import _lib
+    assert _lib.device_error() == 0
+
+
+def test_fp8_long_route_many_heads_in_place():
+    """More heads than SMs (several heads per persistent CTA, several query tiles per head) read in place
+    from the (B, H, S, D) views of a packed qkv projection, as the fused block calls it: against the
+    reference's arithmetic run on the GPU (the emulation route), per head cos >= 0.999."""
+    from vitfp4.nvfp4 import ops
+    from vitfp4.nvfp4.attention import _emulated_sdpa
+    B, H, S, D = 16, 16, 1025, 80
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, S, 3 * H * D, device="cuda", generator=g).bfloat16()
+    qkv[:, :2] *= 6.0
+    q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+    out = ops.attention_fp8_bhsd(q, k, v, D ** -0.5).float()
+    ref = _emulated_sdpa(q, k, v, None, False, D ** -0.5, "fp8", "fp8", True, True)
+    c = torch.nn.functional.cosine_similarity(out.reshape(B * H, -1), ref.reshape(B * H, -1), dim=1)
+    assert torch.isfinite(out).all()
+    assert c.min().item() >= 0.999, c.min().item()
+
+
+@pytest.mark.parametrize("smooth_k,smooth_v", [(False, False), (True, False), (False, True)])
+def test_fp8_long_route_smoothing_switches(smooth_k, smooth_v):
+    """Smooth-K / smooth-V switched off on the long-sequence FP8 route, through quant_sdpa and through
+    vf4_attn with the workspace vf4_attn_workspace_size_modes asks for (none given: VF4_ERR_ARG, nothing
+    launched)."""
+    import ctypes
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import quant_sdpa
+    B, H, S, D = 2, 2, 300, 80
+    q, k, v = _qkv(B, H, S, D, seed=8)
+    k = (k.float() + 3.0).bfloat16()
+    v = (v.float() - 2.0).bfloat16()
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = quant_sdpa(qc, kc, vc, qk="fp8", pv="fp8", smooth_k=smooth_k, smooth_v=smooth_v)
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref = oracle.quant_sdpa(qn, kn, vn, qk="fp8", pv="fp8", smooth_k=smooth_k, smooth_v=smooth_v)
+    assert cos(out.float().cpu().numpy(), ref) >= 0.999
+    lib = _lib.lib()
+    m = _lib.VF4_ATTN_MODE["fp8"]
+    flags = (0 if smooth_k else _lib.VF4_ATTN_NO_SMOOTH_K) | (0 if smooth_v else _lib.VF4_ATTN_NO_SMOOTH_V)
+    n = int(lib.vf4_attn_workspace_size_modes(B, H, S, D, m, m, flags))
+    assert n > 0
+    stream = torch.cuda.current_stream().cuda_stream
+    o2 = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), B, H, S, D, H * S * D, S * D, D, ctypes.c_float(D ** -0.5),
+            m, m, flags)
+    assert lib.vf4_attn(*args, None, 0, o2.data_ptr(), S * H * D, D, H * D, stream) == 1
+    assert (o2 == 0).all()
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    assert lib.vf4_attn(*args, ws.data_ptr(), n, o2.data_ptr(), S * H * D, D, H * D, stream) == 0
+    assert torch.equal(o2.transpose(1, 2), out)
+
+
 # ----------------------------------------------------------------------------- bf16 kernel
 def _bf16_errors(q, k, v, scale, got):
     """Max |error| of ``got`` and of torch's own bf16 SDPA against fp32 attention of the same bf16 inputs."""

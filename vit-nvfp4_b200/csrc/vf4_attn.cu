@@ -2288,6 +2288,569 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
 }
 
 // ---------------------------------------------------------------------------------------
+// FP8 attention for long sequences and head dims other than 64 (ViT-H/14: head dim 80 with
+// S = 257 at 224 px and S = 1025 at 448 px).  The arithmetic of attn_fp8_kernel (per-row E4M3
+// Q and K~, per-column V~, P = e4m3(448 exp(s - max)), out = O sv / (448 rowsum) + mean(v)),
+// split into two kernels because the 8-bit operands of a long head do not fit shared memory
+// next to its scores:
+//   attn_fp8_prep_kernel   one CTA per head: column means of k and v, per-column amax of v - mean
+//                          (from the column max and min), then Q8, K~8 and V~8^T written to the
+//                          workspace in the MMA's K-major core-matrix layout (8 rows x 16 bytes, no
+//                          swizzle) so that a plain bulk copy of a contiguous range is an operand
+//                          tile; per-row scales of Q (sq) and of K~ (sk, pre-multiplied by
+//                          scale * log2 e), per-column scales of V~ (sv) and mean(v)
+//   attn_fp8_long_kernel   persistent, whole heads per CTA.  K~8 and sk stay in shared memory for
+//                          the head; per 128-query tile Q8 is loaded once and the V~8^T key chunks
+//                          stream through a 3-stage ring.  The scores of each tile are formed twice
+//                          (128-key chunks into three TMEM buffers): pass 1 takes the exact row max,
+//                          pass 2 forms P, its row sums and P8, so P is quantized against the final
+//                          max as the reference quantizes its normalised P.
+// Warps: 0 loads (cp.async.bulk), 1 MMAs (tcgen05.mma kind::f8f6f4), 2-17 softmax (TMEM lane
+// quadrant x 32-key quarter of each chunk) and the epilogue (8-column groups of the head dim).
+// Every wait is bounded; a give-up records the device error and unwinds.
+// ---------------------------------------------------------------------------------------
+constexpr int kF8LStages = 3;                       // V~8^T chunks in flight
+constexpr int kF8LSlices = 4;                       // softmax warps per TMEM lane quadrant
+constexpr int kF8LSoftmax = 4 * kF8LSlices;
+constexpr int kF8LWarps = 2 + kF8LSoftmax;
+constexpr uint32_t kF8LSBuf = 3;                    // 128-column score buffers in TMEM, then O
+constexpr uint32_t kF8LTmemS = 0, kF8LTmemO = 128 * kF8LSBuf;
+static_assert(kF8LTmemO + 128 <= 512, "O (up to 128 columns) follows the score buffers in 512 columns");
+
+struct F8LGeom {
+  int B, H, S, D;
+  int S_pad, nc, DK, DV;   // keys padded to 128-key chunks; QK^T contraction padded to K32 steps
+  int64_t BH;
+  int64_t qk_head, v_head;  // bytes per head of Q8 (= K~8) and of V~8^T
+  int64_t off_q, off_k, off_v, off_sq, off_sk, off_sv, off_mu, total;
+};
+
+static F8LGeom make_f8l_geom(int64_t B, int64_t H, int64_t S, int64_t D) {
+  F8LGeom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.S_pad = (int)align_up(S, 128);
+  g.nc = g.S_pad / 128;
+  g.DK = (int)align_up(D, 32);
+  g.DV = (int)D;
+  g.BH = B * H;
+  g.qk_head = (int64_t)g.S_pad * g.DK;
+  g.v_head = (int64_t)g.nc * g.DV * 128;
+  int64_t o = 0;
+  g.off_q = o;  o = align_up(o + g.BH * g.qk_head, 1024);
+  g.off_k = o;  o = align_up(o + g.BH * g.qk_head, 1024);
+  g.off_v = o;  o = align_up(o + g.BH * g.v_head, 1024);
+  g.off_sq = o; o = align_up(o + g.BH * g.S_pad * 4, 1024);
+  g.off_sk = o; o = align_up(o + g.BH * g.S_pad * 4, 1024);
+  g.off_sv = o; o = align_up(o + g.BH * g.DV * 4, 1024);
+  g.off_mu = o; o = align_up(o + g.BH * g.DV * 4, 1024);
+  g.total = o;
+  return g;
+}
+
+struct F8LSmem {
+  uint32_t k, sk, q, v, p, red_m, red_l, bar, total;
+};
+
+static F8LSmem f8l_smem_layout(const F8LGeom& g) {
+  F8LSmem s{};
+  uint32_t o = 0;
+  s.k = o;     o += (uint32_t)g.nc * 128u * (uint32_t)g.DK;
+  s.sk = o;    o += (uint32_t)g.S_pad * 4u;
+  s.q = o;     o += 128u * (uint32_t)g.DK;
+  s.v = o;     o += (uint32_t)kF8LStages * (uint32_t)g.DV * 128u;
+  s.p = o;     o += 2u * 128u * 128u;
+  s.red_m = o; o += (uint32_t)kF8LSlices * 128u * 4u;
+  s.red_l = o; o += (uint32_t)kF8LSlices * 128u * 4u;
+  s.bar = o;   o += 256;
+  s.total = o + 1024;   // slack for aligning the base to 1024
+  return s;
+}
+
+static bool f8l_ok(int64_t S, int64_t D) {
+  if (S < 1 || D < 16 || D > 128 || D % 16 != 0 || S > (1 << 20)) return false;
+  return f8l_smem_layout(make_f8l_geom(1, 1, S, D)).total <= 227u * 1024u;
+}
+
+// 16 fp32 values divided by `scl` -> E4M3 bytes.  The quotients are the correctly rounded x / scl of
+// the reference (Markstein's correction with inv = RN(1 / scl); quotients too small for it to hold
+// are far below E4M3's smallest subnormal and encode as zero either way).
+VF4_DEV uint4 e4m3x16_div(const float* x, float scl, float inv) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = e4m3x2(div_markstein(x[4 * i], scl, inv), div_markstein(x[4 * i + 1], scl, inv)) |
+           (e4m3x2(div_markstein(x[4 * i + 2], scl, inv), div_markstein(x[4 * i + 3], scl, inv)) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16* __restrict__ q,
+                                                            const __nv_bfloat16* __restrict__ k,
+                                                            const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                            int64_t sh, int64_t ss, const F8LGeom g, float scale,
+                                                            int smooth, uint8_t* __restrict__ ws) {
+  __shared__ __align__(16) float part[4][2048];   // pass A partials; pass C's v tile afterwards
+  __shared__ float mu[2][128];
+  __shared__ float svs[128];
+  const int bh = blockIdx.x;
+  const int b = bh / g.H, h = bh - b * g.H;
+  const __nv_bfloat16* qh = q + b * sb + h * sh;
+  const __nv_bfloat16* kh = k + b * sb + h * sh;
+  const __nv_bfloat16* vh = v + b * sb + h * sh;
+  const int S = g.S, D = g.D, D8 = D / 8;
+  const int rpi = 256 / D8, active = rpi * D8;
+  const int t = threadIdx.x, c8 = t % D8, r0 = t / D8;
+
+  // pass A: column sums of k and v, column max / min of v
+  {
+    float sk[8], sv[8], vmax[8], vmin[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sk[i] = sv[i] = 0.f;
+      vmax[i] = -INFINITY;
+      vmin[i] = INFINITY;
+    }
+    if (t < active) {
+      for (int r = r0; r < S; r += rpi) {
+        float bk[8], bv[8];
+        load8(kh + r * ss + c8 * 8, bk);
+        load8(vh + r * ss + c8 * 8, bv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          sk[i] += bk[i];
+          sv[i] += bv[i];
+          vmax[i] = fmaxf(vmax[i], bv[i]);
+          vmin[i] = fminf(vmin[i], bv[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        part[0][r0 * D + c8 * 8 + i] = sk[i];
+        part[1][r0 * D + c8 * 8 + i] = sv[i];
+        part[2][r0 * D + c8 * 8 + i] = vmax[i];
+        part[3][r0 * D + c8 * 8 + i] = vmin[i];
+      }
+    }
+  }
+  __syncthreads();
+  float* sv_g = reinterpret_cast<float*>(ws + g.off_sv) + (int64_t)bh * g.DV;
+  float* mu_g = reinterpret_cast<float*>(ws + g.off_mu) + (int64_t)bh * g.DV;
+  if (t < D) {
+    float a = 0.f, bb = 0.f, mx = -INFINITY, mn = INFINITY;
+    for (int r = 0; r < rpi && r < S; ++r) {   // fixed order: deterministic means
+      a += part[0][r * D + t];
+      bb += part[1][r * D + t];
+      mx = fmaxf(mx, part[2][r * D + t]);
+      mn = fminf(mn, part[3][r * D + t]);
+    }
+    const float mk = (smooth & 1) ? __fdiv_rn(a, (float)S) : 0.f;
+    const float mv = (smooth & 2) ? __fdiv_rn(bb, (float)S) : 0.f;
+    // rounding is monotone: max_s |v_s - m| = max(|max v - m|, |min v - m|) exactly
+    const float am = fmaxf(fabsf(mx - mv), fabsf(mn - mv));
+    const float s = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
+    mu[0][t] = mk;
+    mu[1][t] = mv;
+    svs[t] = s;
+    sv_g[t] = s;
+    mu_g[t] = mv;
+  }
+  __syncthreads();
+
+  // pass B: Q8 and K~8 rows, 8 lanes per row (lane & 7 = 16-element chunk along d), 4 rows per warp
+  {
+    const int lane = t & 31, kc = lane & 7, nkc = g.DK / 16, dkc = D / 16;
+    const float kmul = scale * 1.4426950408889634f;
+    uint8_t* qp = ws + g.off_q + (int64_t)bh * g.qk_head;
+    uint8_t* kp = ws + g.off_k + (int64_t)bh * g.qk_head;
+    float* sq_g = reinterpret_cast<float*>(ws + g.off_sq) + (int64_t)bh * g.S_pad;
+    float* sk_g = reinterpret_cast<float*>(ws + g.off_sk) + (int64_t)bh * g.S_pad;
+    for (int r = (t >> 5) * 4 + (lane >> 3); r < g.S_pad; r += 32) {
+      float xq[16], xk[16];
+      float aq = 0.f, ak = 0.f;
+      if (r < S && kc < dkc) {
+        load8(qh + r * ss + 16 * kc, xq);
+        load8(qh + r * ss + 16 * kc + 8, xq + 8);
+        load8(kh + r * ss + 16 * kc, xk);
+        load8(kh + r * ss + 16 * kc + 8, xk + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          xk[e] -= mu[0][16 * kc + e];
+          aq = fmaxf(aq, fabsf(xq[e]));
+          ak = fmaxf(ak, fabsf(xk[e]));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xq[e] = xk[e] = 0.f;
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        aq = fmaxf(aq, __shfl_xor_sync(0xffffffffu, aq, o));
+        ak = fmaxf(ak, __shfl_xor_sync(0xffffffffu, ak, o));
+      }
+      const float scq = __fdiv_rn(fmaxf(aq, 1e-12f), 448.f);
+      const float sck = __fdiv_rn(fmaxf(ak, 1e-12f), 448.f);
+      if (kc < nkc) {
+        const int rr = r & 127;
+        const int64_t off = (int64_t)(r >> 7) * 128 * g.DK + (rr >> 3) * 8 * g.DK + kc * 128 + (rr & 7) * 16;
+        *reinterpret_cast<uint4*>(qp + off) = e4m3x16_div(xq, scq, __frcp_rn(scq));
+        *reinterpret_cast<uint4*>(kp + off) = e4m3x16_div(xk, sck, __frcp_rn(sck));
+      }
+      if (kc == 0) {
+        sq_g[r] = r < S ? scq : 0.f;
+        sk_g[r] = r < S ? sck * kmul : 0.f;
+      }
+    }
+  }
+
+  // pass C: V~8^T per 128-key chunk: the chunk's v rows staged in shared memory (coalesced 16-byte
+  // loads; the pass-A partials are dead), then one (16-key block, column d) per thread, consecutive
+  // threads taking consecutive d
+  {
+    __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(&part[0][0]);   // [128][D]
+    uint8_t* vp = ws + g.off_v + (int64_t)bh * g.v_head;
+    for (int j = 0; j < g.nc; ++j) {
+      for (int i = t; i < 128 * D8; i += 256) {
+        const int rr = i / D8, cc = i - rr * D8, tok = j * 128 + rr;
+        const uint4 w = tok < S ? __ldg(reinterpret_cast<const uint4*>(vh + (int64_t)tok * ss + cc * 8))
+                                : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(tile + rr * D + cc * 8) = w;
+      }
+      __syncthreads();
+      for (int i = t; i < 8 * D; i += 256) {
+        const int kc = i / D, d = i - kc * D;
+        const float m = mu[1][d], sc = svs[d];
+        float x[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int rr = kc * 16 + e;
+          x[e] = j * 128 + rr < S ? __bfloat162float(tile[rr * D + d]) - m : 0.f;
+        }
+        *reinterpret_cast<uint4*>(vp + (int64_t)j * g.DV * 128 + (d >> 3) * 1024 + kc * 128 + (d & 7) * 16) =
+            e4m3x16_div(x, sc, __frcp_rn(sc));
+      }
+      __syncthreads();   // the tile is rewritten by the next chunk
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kF8LWarps * 32, 1)
+    attn_fp8_long_kernel(const F8LGeom g, const uint8_t* __restrict__ ws, const F8LSmem L,
+                         __nv_bfloat16* __restrict__ out, int64_t osb, int64_t osh, int64_t oss) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar = base + L.bar;
+  const uint32_t kv_full = bar, kv_free = bar + 8, q_full = bar + 16, q_free = bar + 24, o_full = bar + 32,
+                 o_free = bar + 40, drain = bar + 48;
+  auto s_full = [&](int i) { return bar + 56 + 8u * i; };    // [4]
+  auto s_free = [&](int i) { return bar + 88 + 8u * i; };    // [4]
+  auto p_full = [&](int i) { return bar + 120 + 8u * i; };   // [2]
+  auto p_free = [&](int i) { return bar + 136 + 8u * i; };   // [2]
+  auto v_full = [&](int i) { return bar + 152 + 8u * i; };   // [4]
+  auto v_free = [&](int i) { return bar + 184 + 8u * i; };   // [4]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L.bar + 224);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nc = g.nc, S = g.S, DK = g.DK, DV = g.DV;
+  const uint32_t qbytes = 128u * (uint32_t)DK, vbytes = (uint32_t)DV * 128u;
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_free, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, kF8LSoftmax);
+    mbar_init(drain, 1);
+    for (int i = 0; i < (int)kF8LSBuf; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), kF8LSoftmax);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(p_full(i), kF8LSoftmax);
+      mbar_init(p_free(i), 1);
+    }
+    for (int i = 0; i < kF8LStages; ++i) {
+      mbar_init(v_full(i), 1);
+      mbar_init(v_free(i), 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ loads
+      const uint32_t skbytes = (uint32_t)g.S_pad * 4u;
+      uint32_t hc = 0, tcnt = 0, vc = 0;
+      bool ok = true;
+      for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
+        if (!(ok = mbar_wait(kv_free, (hc & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+        mbar_arrive_expect_tx(kv_full, (uint32_t)nc * qbytes + skbytes);
+        for (int j = 0; j < nc; ++j)
+          bulk_load(base + L.k + (uint32_t)j * qbytes, ws + g.off_k + bh * g.qk_head + (int64_t)j * qbytes, qbytes,
+                    kv_full);
+        bulk_load(base + L.sk, ws + g.off_sk + bh * g.S_pad * 4, skbytes, kv_full);
+        for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
+          if (!(ok = mbar_wait(q_free, (tcnt & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+          mbar_arrive_expect_tx(q_full, qbytes);
+          bulk_load(base + L.q, ws + g.off_q + bh * g.qk_head + (int64_t)qt * qbytes, qbytes, q_full);
+          for (int j = 0; j < nc; ++j, ++vc) {
+            const int st = (int)(vc % kF8LStages);
+            if (!(ok = mbar_wait(v_free(st), ((vc / kF8LStages) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+            mbar_arrive_expect_tx(v_full(st), vbytes);
+            bulk_load(base + L.v + (uint32_t)st * vbytes, ws + g.off_v + bh * g.v_head + (int64_t)j * vbytes, vbytes,
+                      v_full(st));
+          }
+        }
+      }
+      // our own copies still in flight complete before the CTA retires (bounded)
+      if (hc > 0) mbar_wait(kv_full, (hc - 1) & 1u, err, kDevErrTimeoutFull);
+      if (tcnt > 0) mbar_wait(q_full, (tcnt - 1) & 1u, err, kDevErrTimeoutFull);
+      for (uint32_t n = vc > kF8LStages ? vc - kF8LStages : 0; n < vc; ++n)
+        mbar_wait(v_full((int)(n % kF8LStages)), (n / kF8LStages) & 1u, err, kDevErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issue
+      const uint32_t id_s = idesc_f8_e4m3(128), id_o = idesc_f8_e4m3((uint32_t)DV);
+      const uint32_t sbo_qk = 8u * (uint32_t)DK;   // bytes between 8-row core-matrix groups
+      const int nks = DK / 32;
+      uint32_t hc = 0, tcnt = 0, sc = 0, pc = 0, vc = 0;
+      bool ok = true;
+      auto issue_s = [&](int j) -> bool {   // scores of key chunk j into buffer sc % kF8LSBuf
+        const int b = (int)(sc % kF8LSBuf);
+        if (!mbar_wait(s_free(b), ((sc / kF8LSBuf) & 1u) ^ 1u, err, kDevErrTimeoutEmpty)) return false;
+        tc_fence_after();
+        for (int ks = 0; ks < nks; ++ks)
+          mma_f8f6f4(tmem + kF8LTmemS + 128u * b, smem_desc(base + L.q + 256u * ks, 128, sbo_qk, 0),
+                     smem_desc(base + L.k + (uint32_t)j * qbytes + 256u * ks, 128, sbo_qk, 0), id_s,
+                     ks > 0 ? 1u : 0u);
+        tc_commit(s_full(b));
+        ++sc;
+        return true;
+      };
+      for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
+        if (!(ok = mbar_wait(kv_full, hc & 1u, err, kDevErrTimeoutFull))) break;
+        for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
+          if (!(ok = mbar_wait(q_full, tcnt & 1u, err, kDevErrTimeoutFull))) break;
+          tc_fence_after();
+          for (int j = 0; j < nc && ok; ++j) ok = issue_s(j);          // pass 1
+          if (ok) ok = issue_s(0);                                      // pass 2, ahead of the PV products
+          if (ok) ok = mbar_wait(o_free, (tcnt & 1u) ^ 1u, err, kDevErrTimeoutTmem);
+          for (int j = 0; j < nc && ok; ++j) {
+            if (j + 1 < nc) {
+              if (!(ok = issue_s(j + 1))) break;
+            } else {
+              tc_commit(q_free);   // every QK^T of this tile issued: Q's buffer is free once they ran
+            }
+            const int pb = (int)(pc & 1u);
+            const int st = (int)(vc % kF8LStages);
+            if (!(ok = mbar_wait(p_full(pb), (pc >> 1) & 1u, err, kDevErrTimeoutFull))) break;
+            if (!(ok = mbar_wait(v_full(st), (vc / kF8LStages) & 1u, err, kDevErrTimeoutFull))) break;
+            tc_fence_after();
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f8f6f4(tmem + kF8LTmemO, smem_desc(base + L.p + (uint32_t)pb * 16384u + 256u * ks, 128, 1024, 0),
+                         smem_desc(base + L.v + (uint32_t)st * vbytes + 256u * ks, 128, 1024, 0), id_o,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+            tc_commit(p_free(pb));
+            tc_commit(v_free(st));
+            ++pc;
+            ++vc;
+          }
+          if (ok) tc_commit(o_full);
+        }
+        if (ok) tc_commit(kv_free);   // this head's K~8 and sk are no longer read once these MMAs ran
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int quad = warp & 3;
+    const int slice = (warp - 2) >> 2;            // key columns [32 slice, 32 slice + 32) of a chunk
+    const int r = quad * 32 + lane;               // row of the query tile == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    float* red_m = reinterpret_cast<float*>(gbase + L.red_m);   // [slice][128]
+    float* red_l = reinterpret_cast<float*>(gbase + L.red_l);
+    const float* sk = reinterpret_cast<const float*>(gbase + L.sk);
+    const int nlast = S - (nc - 1) * 128 - 32 * slice;   // this warp's valid keys in the last chunk
+    constexpr float kLog2_448 = 8.8073549220576041f;
+    uint32_t hc = 0, tcnt = 0, sc = 0, pc = 0;
+    bool ok = true;
+    uint32_t v[32];
+    auto load_s = [&]() -> bool {   // this warp's 32 columns of the next score chunk
+      const int b = (int)(sc % kF8LSBuf);
+      if (!mbar_wait(s_full(b), (sc / kF8LSBuf) & 1u, err, kDevErrTimeoutFull)) return false;
+      tc_fence_after();
+      tmem_ld_32x32b_x32(tmem + lane_addr + kF8LTmemS + 128u * b + 32u * slice, v);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free(b));
+      ++sc;
+      return true;
+    };
+    for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
+      if (!(ok = mbar_wait(kv_full, hc & 1u, err, kDevErrTimeoutFull))) break;
+      const float* sq_g = reinterpret_cast<const float*>(ws + g.off_sq) + bh * g.S_pad;
+      const float* sv_g = reinterpret_cast<const float*>(ws + g.off_sv) + bh * DV;
+      const float* mu_g = reinterpret_cast<const float*>(ws + g.off_mu) + bh * DV;
+      for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
+        const float sqr = sq_g[qt * 128 + r];
+        // pass 1: row max of acc * sk (scores in log2 units are acc * sk * sqr, sqr > 0 for real rows)
+        float m = -INFINITY;
+        for (int j = 0; j < nc && ok; ++j) {
+          if (!(ok = load_s())) break;
+          const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
+          const int nv = j + 1 < nc ? 32 : nlast;
+          float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 k4 = sk4[i];
+            float a0, a1, a2, a3;
+            f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                   f32x2_pack(k4.x, k4.y)), &a0, &a1);
+            f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                   f32x2_pack(k4.z, k4.w)), &a2, &a3);
+            if (nv < 32) {   // keys past S in the last chunk
+              a0 = 4 * i < nv ? a0 : -INFINITY;
+              a1 = 4 * i + 1 < nv ? a1 : -INFINITY;
+              a2 = 4 * i + 2 < nv ? a2 : -INFINITY;
+              a3 = 4 * i + 3 < nv ? a3 : -INFINITY;
+            }
+            ma = max3f(ma, a0, a1);
+            mb = max3f(mb, a2, a3);
+          }
+          m = max3f(m, ma, mb);
+        }
+        red_m[slice * 128 + r] = m;
+        named_bar_sync(1 + quad, 32 * kF8LSlices);
+        float mr = red_m[r];
+#pragma unroll
+        for (int s = 1; s < kF8LSlices; ++s) mr = fmaxf(mr, red_m[s * 128 + r]);
+        // fl(x * sqr) is monotone in x for sqr >= 0, so the row max of the scores is mr * sqr exactly
+        const float nmc = kLog2_448 - mr * sqr;
+        // pass 2: P' = 448 exp(s - max) = 2^(acc sk sqr - max + log2 448), row sums, P8 = e4m3(P')
+        const unsigned long long sq2 = f32x2_pack(sqr, sqr), nm2 = f32x2_pack(nmc, nmc);
+        unsigned long long l2a = f32x2_pack(0.f, 0.f), l2b = l2a;
+        for (int j = 0; j < nc && ok; ++j) {
+          if (!(ok = load_s())) break;
+          const int pb = (int)(pc & 1u);
+          if (!(ok = mbar_wait(p_free(pb), ((pc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+          const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
+          const int nv = j + 1 < nc ? 32 : nlast;
+          float p[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 k4 = sk4[i];
+            float e0, e1, e2, e3;
+            f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                             f32x2_pack(k4.x, k4.y)), sq2, nm2), &e0, &e1);
+            f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                             f32x2_pack(k4.z, k4.w)), sq2, nm2), &e2, &e3);
+            p[4 * i] = ex2_approx(e0);
+            p[4 * i + 1] = ex2_approx(e1);
+            p[4 * i + 2] = ex2_approx(e2);
+            p[4 * i + 3] = ex2_approx(e3);
+            if (nv < 32) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) p[4 * i + e] = 4 * i + e < nv ? p[4 * i + e] : 0.f;
+            }
+            l2a = add_f32x2(l2a, f32x2_pack(p[4 * i], p[4 * i + 1]));
+            l2b = add_f32x2(l2b, f32x2_pack(p[4 * i + 2], p[4 * i + 3]));
+          }
+          uint8_t* pbuf = gbase + L.p + pb * 16384;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)   // K-major core matrices: (row group, 16-key chunk) at rg*1024 + kc*128
+            *reinterpret_cast<uint4*>(pbuf + (r >> 3) * 1024 + (2 * slice + c) * 128 + (r & 7) * 16) =
+                e4m3x16(p + 16 * c, 1.f);
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full(pb));
+          ++pc;
+        }
+        float la0, la1, lb0, lb1;
+        f32x2_unpack(l2a, &la0, &la1);
+        f32x2_unpack(l2b, &lb0, &lb1);
+        red_l[slice * 128 + r] = (la0 + la1) + (lb0 + lb1);
+        named_bar_sync(1 + quad, 32 * kF8LSlices);
+        float lr = red_l[r];
+#pragma unroll
+        for (int s = 1; s < kF8LSlices; ++s) lr += red_l[s * 128 + r];
+        // epilogue: 8-column groups slice, slice + 4, ... of O
+        if (ok && (ok = mbar_wait(o_full, tcnt & 1u, err, kDevErrTimeoutTmem))) {
+          tc_fence_after();
+          const int ng = DV / 8;
+          uint32_t ov[4][8];
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq)
+            if (slice + 4 * kq < ng) tmem_ld_32x32b_x8(tmem + lane_addr + kF8LTmemO + 8u * (slice + 4 * kq), ov[kq]);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+          const int tq = qt * 128 + r;
+          if (tq < S) {
+            const float f = 1.0f / lr;
+            const int b = (int)(bh / g.H), h = (int)(bh - (int64_t)b * g.H);
+            __nv_bfloat16* o = out + b * osb + (int64_t)tq * oss + h * osh;
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              const int gi = slice + 4 * kq;
+              if (gi < ng) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int d = 8 * gi + 2 * e;
+                  __nv_bfloat162 hv = __floats2bfloat162_rn(
+                      __fmaf_rn(__uint_as_float(ov[kq][2 * e]), f * __ldg(sv_g + d), __ldg(mu_g + d)),
+                      __fmaf_rn(__uint_as_float(ov[kq][2 * e + 1]), f * __ldg(sv_g + d + 1), __ldg(mu_g + d + 1)));
+                  w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                }
+                *reinterpret_cast<uint4*>(o + 8 * gi) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static int launch_fp8_long(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                           int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
+                           int64_t oss, int smooth, uint8_t* ws, cudaStream_t s) {
+  const F8LGeom g = make_f8l_geom(B, H, S, D);
+  const F8LSmem L = f8l_smem_layout(g);
+  attn_fp8_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(q),
+                                                      static_cast<const __nv_bfloat16*>(k),
+                                                      static_cast<const __nv_bfloat16*>(v), sb, sh, ss, g, scale,
+                                                      smooth, ws);
+  if (int st = launch_status("vf4_attn fp8 (prep)")) return st;
+  if (int st = smem_optin(attn_fp8_long_kernel, (int)L.total)) return st;
+  const int grid = (int)(g.BH < num_sms() ? g.BH : num_sms());   // persistent: whole heads per CTA
+  attn_fp8_long_kernel<<<grid, kF8LWarps * 32, L.total, s>>>(g, ws, L, static_cast<__nv_bfloat16*>(out), osb, osh,
+                                                             oss);
+  return launch_status("vf4_attn fp8 (forward)");
+}
+
+// ---------------------------------------------------------------------------------------
 // bf16 attention: the route the reference keeps for blocks left in bf16 (its qattention wrapper
 // and timm's Attention call torch's scaled_dot_product_attention): out = softmax(q k^T * scale) v
 // with bf16 q, k, v, fp32 accumulation and an exact (whole-row) softmax.  Head dim 64, S <= 288.
@@ -3091,6 +3654,11 @@ int64_t vf4_attn_workspace_size_modes(int64_t B, int64_t H, int64_t S, int64_t D
                                       int flags) {
   if (qk_mode == VF4_ATTN_MODE_NVFP4 && pv_mode == VF4_ATTN_MODE_NVFP4)
     return vf4_attn_workspace_size_ex(B, H, S, D, flags);
+  if (qk_mode == VF4_ATTN_MODE_FP8 && pv_mode == VF4_ATTN_MODE_FP8) {
+    if (B <= 0 || H <= 0 || (flags & ~(VF4_ATTN_NO_SMOOTH_K | VF4_ATTN_NO_SMOOTH_V))) return 0;
+    if (fp8_ok(S, D) || !f8l_ok(S, D)) return 0;   // the short kernel needs none; unsupported shapes fail
+    return make_f8l_geom(B, H, S, D).total;
+  }
   return 0;
 }
 
@@ -3109,15 +3677,26 @@ int vf4_attn(const void* q, const void* k, const void* v, int64_t B, int64_t H, 
       return fail(VF4_ERR_ARG, "vf4_attn: flags %d do not apply to the FP8 route", flags);
     if (int st = check_device()) return st;
     if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(VF4_ERR_ARG, "vf4_attn: bad sizes");
-    if (!fp8_ok(S, D)) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: the FP8 kernel needs head dim 64 and S <= 320");
+    const bool short_route = fp8_ok(S, D);
+    if (!short_route && !f8l_ok(S, D))
+      return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: FP8 attention needs a head dim that is a multiple of 16 and <= 128, "
+                  "and a sequence whose keys fit shared memory (S=%lld D=%lld)", (long long)S, (long long)D);
     if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn: null pointer");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || stride_b % 8 || stride_h % 8 ||
         stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)
       return fail(VF4_ERR_ALIGN, "vf4_attn: 16-byte aligned pointers and strides (multiples of 8) needed");
     if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn: B*H too large");
     const int smooth = ((flags & VF4_ATTN_NO_SMOOTH_K) ? 0 : 1) | ((flags & VF4_ATTN_NO_SMOOTH_V) ? 0 : 2);
-    return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
-                      out_stride_s, smooth, reinterpret_cast<cudaStream_t>(stream));
+    if (short_route)
+      return launch_fp8(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                        out_stride_s, smooth, reinterpret_cast<cudaStream_t>(stream));
+    const int64_t need = make_f8l_geom(B, H, S, D).total;
+    if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+      return fail(VF4_ERR_ARG, "vf4_attn: the long-sequence FP8 route needs a 16-byte aligned workspace of %lld bytes "
+                  "(got %lld)", (long long)need, (long long)workspace_bytes);
+    return launch_fp8_long(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
+                           out_stride_s, smooth, static_cast<uint8_t*>(workspace),
+                           reinterpret_cast<cudaStream_t>(stream));
   }
   if (bf16) {   // smoothing is exact under the softmax and the PV product: the flags change no result
     if (flags & ~(VF4_ATTN_NO_SMOOTH_K | VF4_ATTN_NO_SMOOTH_V))

@@ -6,14 +6,16 @@
                        in shared memory, smooth-K / smooth-V each on or off as asked);
   qk = pv = 'bf16'  -> exact bf16 attention (torch SDPA), the route the reference keeps for
                        unquantised blocks;
-  qk = pv = 'fp8'   -> the sm_100a FP8 attention kernel (E4M3 MMAs, per-row scales) for head dim
-                       64 and S <= 320 without mask; other shapes take the emulation below;
+  qk = pv = 'fp8'   -> the sm_100a FP8 attention kernels (E4M3 MMAs, per-row scales, no mask): one
+                       fused kernel for head dim 64 and S <= 320, a prep kernel plus a long-sequence
+                       kernel for other head dims (multiples of 16 up to 128) and longer sequences
+                       (ViT-H/14: head dim 80, S = 257 or 1025); shapes beyond those take the
+                       emulation below;
   any other mix     -> the reference's own emulation (quantize-dequantize of the operands, fp32
                        matmuls and softmax) run on the GPU with torch ops, in chunks of heads; NVFP4
                        operands are quantized by the CUDA cast kernel (whole-tensor globals, the P
-                       global from a first pass over all chunks), FP8 ones per row as fp8.py.  This
-                       covers the reference's default 'fp8'/'fp8' route and the mixed ones; no
-                       dedicated kernel is built for them.
+                       global from a first pass over all chunks), FP8 ones per row as fp8.py.  No
+                       dedicated kernel is built for the mixed routes.
 """
 from __future__ import annotations
 
@@ -108,7 +110,7 @@ def _emulated_sdpa(q, k, v, attn_mask, is_causal, scale, qk, pv, smooth_k, smoot
 @torch.library.custom_op("vitfp4::attention_lowp", mutates_args=())
 def attention_lowp_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, qk: str, pv: str,
                       smooth_k: bool, smooth_v: bool) -> torch.Tensor:
-    """The kernel routes of quant_sdpa (nvfp4/nvfp4 and fp8/fp8 with head dim 64, S <= 320) on (B, H, S, D)
+    """The kernel routes of quant_sdpa (nvfp4/nvfp4, and fp8/fp8 where ops.fp8_kernel_ok) on (B, H, S, D)
     operands -> (B, H, S, D) bf16, laid out as a (B, S, H, D) tensor (the kernels' output layout)."""
     from . import ops
     if qk == "nvfp4":

@@ -292,7 +292,11 @@ _ws_cache: dict = {}
 
 
 def _attn_workspace(B: int, H: int, S: int, D: int, device, flags: int = 0) -> torch.Tensor:
-    n = int(_lib.lib().vf4_attn_workspace_size_ex(B, H, S, D, flags))
+    return _workspace(int(_lib.lib().vf4_attn_workspace_size_ex(B, H, S, D, flags)), device)
+
+
+def _workspace(n: int, device) -> torch.Tensor:
+    """An attention workspace of at least ``n`` bytes, kept per (device, stream) and grown on demand."""
     key = (device, torch.cuda.current_stream(device).cuda_stream)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < n:
@@ -342,16 +346,31 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: 
         if t.dtype != torch.bfloat16:
             raise _lib.VitFp4Error("FP8 attention takes bf16 q/k/v/out")
     fp8 = _lib.VF4_ATTN_MODE["fp8"]
+    flags = _smooth_flags(smooth_k, smooth_v)
+    n = int(_lib.lib().vf4_attn_workspace_size_modes(B, H, S, D, fp8, fp8, flags))
+    ws = _workspace(n, q.device) if n > 0 else None
     with _Timed(f"attn_fp8_{B * H}x{S}x{D}", 4.0 * B * H * S * S * D):
         _lib.call("vf4_attn", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
-                  float(scale), fp8, fp8, _smooth_flags(smooth_k, smooth_v), None, 0, _ptr(out), out_strides[0],
-                  out_strides[1], out_strides[2], _stream())
-    _launched(1)
+                  float(scale), fp8, fp8, flags, _ptr(ws) if ws is not None else None, n, _ptr(out),
+                  out_strides[0], out_strides[1], out_strides[2], _stream())
+    _launched(1 if ws is None else 2)
     return out
 
 
+def _fp8_long_smem(S: int, D: int) -> int:
+    """Shared memory of the long-sequence FP8 kernel (f8l_smem_layout in vf4_attn.cu): the head's K~8 and
+    key scales, one Q8 tile, three V~8^T chunks, two P8 chunks, row reductions, barriers, alignment slack."""
+    s_pad = -(-S // 128) * 128
+    dk = -(-D // 32) * 32
+    return s_pad * dk + s_pad * 4 + 128 * dk + 3 * D * 128 + 2 * 128 * 128 + 2 * 4 * 128 * 4 + 256 + 1024
+
+
 def fp8_kernel_ok(S: int, D: int) -> bool:
-    return D == 64 and S <= 320
+    """Shapes the FP8 kernels take: head dim 64 with S <= 320 (one fused kernel), else head dims that are
+    multiples of 16 up to 128 whose keys fit shared memory (prep + long-sequence kernel)."""
+    if S < 1 or D < 16 or D > 128 or D % 16:
+        return False
+    return (D == 64 and S <= 320) or _fp8_long_smem(S, D) <= 227 * 1024
 
 
 def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int, S: int, D: int,
