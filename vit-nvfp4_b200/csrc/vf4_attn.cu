@@ -2535,6 +2535,58 @@ __global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16*
   }
 }
 
+// Pass 1 of a score chunk: max over this warp's 32 columns of acc * sk (packed multiplies,
+// three-input max); kMask drops the columns >= nv (keys past S in the last chunk).
+template <bool kMask>
+VF4_DEV float f8l_chunk_max(const uint32_t* v, const float4* sk4, int nv) {
+  float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 k4 = sk4[i];
+    float a0, a1, a2, a3;
+    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), f32x2_pack(k4.x, k4.y)),
+                 &a0, &a1);
+    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                           f32x2_pack(k4.z, k4.w)), &a2, &a3);
+    if (kMask) {
+      a0 = 4 * i < nv ? a0 : -INFINITY;
+      a1 = 4 * i + 1 < nv ? a1 : -INFINITY;
+      a2 = 4 * i + 2 < nv ? a2 : -INFINITY;
+      a3 = 4 * i + 3 < nv ? a3 : -INFINITY;
+    }
+    ma = max3f(ma, a0, a1);
+    mb = max3f(mb, a2, a3);
+  }
+  return fmaxf(ma, mb);
+}
+
+// Pass 2 of a score chunk: p = 2^(acc sk sq - max + log2 448) for this warp's 32 columns (sq2, nm2:
+// sq and log2 448 - max in both halves), row sums accumulated in two packed pairs; kMask zeroes the
+// columns >= nv.
+template <bool kMask>
+VF4_DEV void f8l_chunk_exp(const uint32_t* v, const float4* sk4, int nv, unsigned long long sq2,
+                           unsigned long long nm2, float* p, unsigned long long& l2a, unsigned long long& l2b) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 k4 = sk4[i];
+    float e0, e1, e2, e3;
+    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                     f32x2_pack(k4.x, k4.y)), sq2, nm2), &e0, &e1);
+    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                     f32x2_pack(k4.z, k4.w)), sq2, nm2), &e2, &e3);
+    p[4 * i] = ex2_approx(e0);
+    p[4 * i + 1] = ex2_approx(e1);
+    p[4 * i + 2] = ex2_approx(e2);
+    p[4 * i + 3] = ex2_approx(e3);
+    if (kMask) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p[4 * i + e] = 4 * i + e < nv ? p[4 * i + e] : 0.f;
+    }
+    l2a = add_f32x2(l2a, f32x2_pack(p[4 * i], p[4 * i + 1]));
+    l2b = add_f32x2(l2b, f32x2_pack(p[4 * i + 2], p[4 * i + 3]));
+  }
+}
+
 __global__ void __launch_bounds__(kF8LWarps * 32, 1)
     attn_fp8_long_kernel(const F8LGeom g, const uint8_t* __restrict__ ws, const F8LSmem L,
                          __nv_bfloat16* __restrict__ out, int64_t osb, int64_t osh, int64_t oss) {
@@ -2714,26 +2766,7 @@ __global__ void __launch_bounds__(kF8LWarps * 32, 1)
         for (int j = 0; j < nc && ok; ++j) {
           if (!(ok = load_s())) break;
           const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
-          const int nv = j + 1 < nc ? 32 : nlast;
-          float ma = -INFINITY, mb = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 k4 = sk4[i];
-            float a0, a1, a2, a3;
-            f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
-                                   f32x2_pack(k4.x, k4.y)), &a0, &a1);
-            f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
-                                   f32x2_pack(k4.z, k4.w)), &a2, &a3);
-            if (nv < 32) {   // keys past S in the last chunk
-              a0 = 4 * i < nv ? a0 : -INFINITY;
-              a1 = 4 * i + 1 < nv ? a1 : -INFINITY;
-              a2 = 4 * i + 2 < nv ? a2 : -INFINITY;
-              a3 = 4 * i + 3 < nv ? a3 : -INFINITY;
-            }
-            ma = max3f(ma, a0, a1);
-            mb = max3f(mb, a2, a3);
-          }
-          m = max3f(m, ma, mb);
+          m = fmaxf(m, j + 1 < nc || nlast >= 32 ? f8l_chunk_max<false>(v, sk4, 32) : f8l_chunk_max<true>(v, sk4, nlast));
         }
         red_m[slice * 128 + r] = m;
         named_bar_sync(1 + quad, 32 * kF8LSlices);
@@ -2750,27 +2783,11 @@ __global__ void __launch_bounds__(kF8LWarps * 32, 1)
           const int pb = (int)(pc & 1u);
           if (!(ok = mbar_wait(p_free(pb), ((pc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
           const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
-          const int nv = j + 1 < nc ? 32 : nlast;
           float p[32];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 k4 = sk4[i];
-            float e0, e1, e2, e3;
-            f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
-                                             f32x2_pack(k4.x, k4.y)), sq2, nm2), &e0, &e1);
-            f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
-                                             f32x2_pack(k4.z, k4.w)), sq2, nm2), &e2, &e3);
-            p[4 * i] = ex2_approx(e0);
-            p[4 * i + 1] = ex2_approx(e1);
-            p[4 * i + 2] = ex2_approx(e2);
-            p[4 * i + 3] = ex2_approx(e3);
-            if (nv < 32) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) p[4 * i + e] = 4 * i + e < nv ? p[4 * i + e] : 0.f;
-            }
-            l2a = add_f32x2(l2a, f32x2_pack(p[4 * i], p[4 * i + 1]));
-            l2b = add_f32x2(l2b, f32x2_pack(p[4 * i + 2], p[4 * i + 3]));
-          }
+          if (j + 1 < nc || nlast >= 32)
+            f8l_chunk_exp<false>(v, sk4, 32, sq2, nm2, p, l2a, l2b);
+          else
+            f8l_chunk_exp<true>(v, sk4, nlast, sq2, nm2, p, l2a, l2b);
           uint8_t* pbuf = gbase + L.p + pb * 16384;
 #pragma unroll
           for (int c = 0; c < 2; ++c)   // K-major core matrices: (row group, 16-key chunk) at rg*1024 + kc*128
