@@ -289,6 +289,22 @@ VF4_API int vf4_patchify(const void* images, int64_t B, int64_t C, int64_t H, in
 VF4_API int vf4_embed_tokens(const void* y, const void* cls, const void* pos, int64_t B, int64_t T, int64_t D, void* x,
                              vf4_stream_t stream);
 
+/* GPTQ column loop of one block of input columns (replaces the inner loop of gptq_quantize_weight,
+ * src/vit_nvfp4/ptq/gptq.py:101-122; the caller keeps the Hessian preparation, gptq.py:79-94, and the
+ * cross-block update W[:, i2:] -= Err @ Hinv[i1:i2, i2:], gptq.py:124-126).  For each row n < N of
+ * the fp32 weight block w (columns col0 .. col0 + count of W, row stride ldw; read only) and the
+ * block's upper inverse-Cholesky factor hinv (count x count, row stride ldh), columns i = 0..count-1
+ * in order: code = E2M1 code of w_i / s, q = value(code) * s, err_i = (w_i - q) / hinv[i][i], and
+ * w_c -= err_i * hinv[i][c] for c > i, with s = e4m3(block_scale[n][(col0 + i) / 16]) * global_scale
+ * (block_scale: the frozen per-16 E4M3 bytes of the original weight, row stride ldb; global_scale one
+ * fp32 on the device).  Writes codes[n][col0 + i] (uint8 E2M1 code of q / s, the reference's final
+ * re-encoding; row stride ldc) and err[n][i] (fp32, row stride lde).  Divisions correctly rounded,
+ * products rounded before the subtraction, as the reference's torch ops.  16 <= count <= 128 and
+ * col0 multiples of 16. */
+VF4_API int vf4_gptq_block(const float* w, int64_t ldw, const float* hinv, int64_t ldh, const uint8_t* block_scale,
+                           int64_t ldb, const float* global_scale, int64_t N, int64_t col0, int64_t count,
+                           uint8_t* codes, int64_t ldc, float* err, int64_t lde, vf4_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, list] = {
     "vf4_attn_nvfp4_noalloc": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _P, _L, _L, _L, _P],
     "vf4_attn": [_P, _P, _P, _L, _L, _L, _L, _L, _L, _L, ctypes.c_float, _I, _I, _I, _P, _L, _P, _L, _L, _L, _P],
     "vf4_attn_workspace_size_modes": [_L, _L, _L, _L, _I, _I, _I],
+    "vf4_gptq_block": [_P, _L, _P, _L, _P, _L, _P, _L, _L, _L, _P, _L, _P, _L, _P],
 }
 _RESTYPE = {"vf4_last_error_string": ctypes.c_char_p, "vf4_attn_workspace_size": ctypes.c_int64,
             "vf4_attn_workspace_size_ex": ctypes.c_int64, "vf4_attn_workspace_size_modes": ctypes.c_int64}

@@ -193,6 +193,28 @@ def unpack_e2m1(packed: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def gptq_block(w: torch.Tensor, hinv: torch.Tensor, block_scale: torch.Tensor, global_scale: torch.Tensor,
+               col0: int, count: int, codes: torch.Tensor, err: torch.Tensor) -> None:
+    """GPTQ column loop over columns [col0, col0 + count) (vf4_gptq_block).
+
+    ``w``: fp32 (N, >= count) view whose column 0 is weight column col0 (unit column stride);
+    ``hinv``: fp32 (count, count) view (unit column stride); ``block_scale``: (N, K/16) E4M3 bytes of
+    the whole weight; ``global_scale``: one fp32; writes ``codes`` (N, K) uint8 columns
+    [col0, col0 + count) and ``err`` (N, count) fp32."""
+    _need_cuda(w, hinv, block_scale, global_scale, codes, err)
+    if w.dtype != torch.float32 or hinv.dtype != torch.float32 or err.dtype != torch.float32:
+        raise _lib.VitFp4Error("gptq_block takes fp32 w / hinv / err")
+    bs = block_scale if block_scale.dtype == torch.uint8 else block_scale.view(torch.uint8)
+    w, hinv, bs = (t if t.stride(-1) == 1 else t.contiguous() for t in (w, hinv, bs))   # read-only inputs
+    for t in (codes, err):
+        if t.stride(-1) != 1:
+            raise _lib.VitFp4Error("gptq_block writes codes / err with unit column strides")
+    gs = global_scale.reshape(()).to(torch.float32)
+    _lib.call("vf4_gptq_block", _ptr(w), w.stride(0), _ptr(hinv), hinv.stride(0), _ptr(bs), bs.stride(0), _ptr(gs),
+              w.shape[0], col0, count, _ptr(codes), codes.stride(0), _ptr(err), err.stride(0), _stream())
+    _launched()
+
+
 def to_blocked(sf: torch.Tensor) -> torch.Tensor:
     """(R, C) E4M3 scales (uint8 or float8_e4m3fn) -> flat 128x4-tiled uint8."""
     _need_cuda(sf)
