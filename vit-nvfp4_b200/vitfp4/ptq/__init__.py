@@ -6,7 +6,7 @@ from .fused_mlp import FusedNVFP4MLP, fuse_mlps
 from .fused_block import FusedNVFP4Block, fuse_norms
 from .convert import quantize_model
 from .models import ModelSpec, model_spec, find_block_container, quantize_vit
-from .diagnostics import tensor_cosine
+from .diagnostics import block_output_cosines, tensor_cosine
 from .gptq import HessianObserver, gptq_quantize_weight
 from .convert_gptq import quantize_model_gptq
 
@@ -14,5 +14,5 @@ __all__ = [
     "QuantLinear", "vit_block_policy", "block_index", "enable_quant_attention", "vit_attn_policy",
     "FusedNVFP4MLP", "fuse_mlps", "quantize_model", "ModelSpec", "model_spec", "find_block_container",
     "quantize_vit", "tensor_cosine", "FusedNVFP4Block", "fuse_norms", "HessianObserver", "gptq_quantize_weight",
-    "quantize_model_gptq",
+    "quantize_model_gptq", "block_output_cosines",
 ]
