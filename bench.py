@@ -235,7 +235,8 @@ def run_reference(args, rank: int, world: int):
 # ------------------------------------------------------------------------------- models
 def build_model(arch: dict, attn: str, device, fused: bool = True, exact_gelu: bool = True, seed: int = 0):
     """A W4A4 ViT as the benchmark runs it: all blocks converted (skip 0/0), Four-Over-Six weights,
-    fused MLPs (erf-GELU epilogue unless exact_gelu=False), fused blocks, attention bf16 or nvfp4."""
+    fused MLPs (erf-GELU epilogue unless exact_gelu=False), fused blocks, attention bf16, fp8 or nvfp4
+    (QK^T and PV operands; fp8 is the reference's enable_quant_attention default)."""
     import torch
     from vitfp4 import vit
     from vitfp4.ptq import enable_quant_attention, fuse_mlps, fuse_norms, quantize_vit, vit_attn_policy
@@ -244,10 +245,11 @@ def build_model(arch: dict, attn: str, device, fused: bool = True, exact_gelu: b
     n_mlp = fuse_mlps(model, skip_ends=0, exact_gelu=exact_gelu)
     n_lin, _ = quantize_vit(model, skip_first=0, skip_last=0, w_block_select="mse")
     n_att = 0
-    if attn == "nvfp4":
-        n_att = enable_quant_attention(model, vit_attn_policy(depth, 0, 0, "blocks"), qk="nvfp4", pv="nvfp4")
+    if attn in ("nvfp4", "fp8"):
+        n_att = enable_quant_attention(model, vit_attn_policy(depth, 0, 0, "blocks"), qk=attn, pv=attn)
     n_blk = fuse_norms(model) if fused else 0
-    return model, {"fused_mlps": n_mlp, "quant_linears": n_lin, "fp4_attention": n_att, "fused_blocks": n_blk}
+    return model, {"fused_mlps": n_mlp, "quant_linears": n_lin, "quant_attention": n_att, "attention_route": attn,
+                   "fused_blocks": n_blk}
 
 
 def _events():
@@ -488,6 +490,31 @@ def model_rate(arch: dict, batch: int, attn: str, steps: int, peaks: dict, seq: 
     return res
 
 
+def gptq_rate() -> dict:
+    """GPTQ weight conversion on the GPU for the headline model's Linear shapes (ViT-L/14: qkv, proj,
+    fc1, fc2): ms per layer of gptq_quantize_weight (block scales, Cholesky factors, the vf4_gptq_block
+    column loop and the cross-block GEMMs), Hessian from 4096 calibration rows."""
+    import torch
+    from vitfp4.ptq import gptq_quantize_weight
+    rows = []
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for name, (n, k) in {"qkv": (3072, 1024), "proj": (1024, 1024), "fc1": (4096, 1024), "fc2": (1024, 4096)}.items():
+        w = torch.randn(n, k, device="cuda", generator=g) * 0.02
+        x = torch.randn(4096, k, device="cuda", generator=g)
+        H = x.t() @ x
+        gptq_quantize_weight(w, H)
+        torch.cuda.synchronize()
+        t0, t1 = _events()
+        t0.record()
+        for _ in range(3):
+            gptq_quantize_weight(w, H)
+        t1.record()
+        torch.cuda.synchronize()
+        rows.append({"layer": name, "N": n, "K": k, "ms": round(t0.elapsed_time(t1) / 3, 2)})
+    return {"workload": "gptq_quantize_weight per Linear of ViT-L/14 (blocksize 128, percdamp 0.01)", "layers": rows,
+            "ms_per_block_of_4": round(sum(r["ms"] for r in rows), 2)}
+
+
 def secondary(args, peaks: dict) -> dict:
     from vitfp4 import vit
     out = {}
@@ -506,11 +533,14 @@ def secondary(args, peaks: dict) -> dict:
                                         "BASELINE config 3: ViT-B/16 W4A4, batch 256, FP4 QK^T/PV attention in all 12 blocks")
     out["config3_vit_b16_bf16_attention"] = model_rate(dict(vit.VIT_B16), 256, "bf16", 10, peaks, 197,
                                                        "config 3 model with the bf16 attention route, for comparison")
-    for attn in ("bf16", "nvfp4"):
+    for attn in ("bf16", "fp8", "nvfp4"):
         out[f"config5_vit_h14_448_{attn}_attention"] = model_rate(
             dict(vit.VIT_H14_448), 64, attn, 5, peaks, 1025,
             f"BASELINE config 5: ViT-H/14 @448 (1025 tokens, head dim 80) W4A4, the 64 images of one GPU of 8, "
-            f"{attn} attention" + (" (cuDNN SDPA: the bf16 kernel covers S <= 288)" if attn == "bf16" else ""))
+            f"{attn} attention" + {"bf16": " (cuDNN SDPA: the bf16 kernel covers S <= 288)",
+                                   "fp8": " (the reference's default route; long-sequence FP8 kernels)",
+                                   "nvfp4": " (long-sequence FP4 kernels)"}[attn])
+    out["gptq_column_loop"] = gptq_rate()
     out["seconds"] = round(time.time() - t, 1)
     return out
 
