@@ -2291,14 +2291,15 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
 // FP8 attention for long sequences and head dims other than 64 (ViT-H/14: head dim 80 with
 // S = 257 at 224 px and S = 1025 at 448 px).  The arithmetic of attn_fp8_kernel (per-row E4M3
 // Q and K~, per-column V~, P = e4m3(448 exp(s - max)), out = O sv / (448 rowsum) + mean(v)),
-// split into two kernels because the 8-bit operands of a long head do not fit shared memory
-// next to its scores:
-//   attn_fp8_prep_kernel   one CTA per head: column means of k and v, per-column amax of v - mean
-//                          (from the column max and min), then Q8, K~8 and V~8^T written to the
+// split into kernels because the 8-bit operands of a long head do not fit shared memory next to
+// its scores:
+//   attn_fp8_colstats_kernel  one CTA per head: column means of k and v, per-column scale of V~
+//                          (amax of v - mean from the column max and min)
+//   attn_fp8_pack_kernel   one CTA per (head, 128-token chunk): Q8, K~8 and V~8^T written to the
 //                          workspace in the MMA's K-major core-matrix layout (8 rows x 16 bytes, no
 //                          swizzle) so that a plain bulk copy of a contiguous range is an operand
 //                          tile; per-row scales of Q (sq) and of K~ (sk, pre-multiplied by
-//                          scale * log2 e), per-column scales of V~ (sv) and mean(v)
+//                          scale * log2 e)
 //   attn_fp8_long_kernel   persistent, whole heads per CTA.  K~8 and sk stay in shared memory for
 //                          the head; per 128-query tile Q8 is loaded once and the V~8^T key chunks
 //                          stream through a 3-stage ring.  The scores of each tile are formed twice
@@ -2309,6 +2310,13 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
 // quadrant x 32-key quarter of each chunk) and the epilogue (8-column groups of the head dim).
 // Every wait is bounded; a give-up records the device error and unwinds.
 // ---------------------------------------------------------------------------------------
+// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; these
+// empty volatile statements keep the compiler from moving their first uses above the wait.
+VF4_DEV void reg_fence16(uint32_t* v) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(v[i]));
+}
+
 constexpr int kF8LStages = 3;                       // V~8^T chunks in flight
 constexpr int kF8LSlices = 4;                       // softmax warps per TMEM lane quadrant
 constexpr int kF8LSoftmax = 4 * kF8LSlices;
@@ -2322,7 +2330,7 @@ struct F8LGeom {
   int S_pad, nc, DK, DV;   // keys padded to 128-key chunks; QK^T contraction padded to K32 steps
   int64_t BH;
   int64_t qk_head, v_head;  // bytes per head of Q8 (= K~8) and of V~8^T
-  int64_t off_q, off_k, off_v, off_sq, off_sk, off_sv, off_mu, total;
+  int64_t off_q, off_k, off_v, off_sq, off_sk, off_sv, off_mu, off_muk, total;
 };
 
 static F8LGeom make_f8l_geom(int64_t B, int64_t H, int64_t S, int64_t D) {
@@ -2346,6 +2354,7 @@ static F8LGeom make_f8l_geom(int64_t B, int64_t H, int64_t S, int64_t D) {
   g.off_sk = o; o = align_up(o + g.BH * g.S_pad * 4, 1024);
   g.off_sv = o; o = align_up(o + g.BH * g.DV * 4, 1024);
   g.off_mu = o; o = align_up(o + g.BH * g.DV * 4, 1024);
+  g.off_muk = o; o = align_up(o + g.BH * g.DV * 4, 1024);
   g.total = o;
   return g;
 }
@@ -2386,24 +2395,22 @@ VF4_DEV uint4 e4m3x16_div(const float* x, float scl, float inv) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16* __restrict__ q,
-                                                            const __nv_bfloat16* __restrict__ k,
-                                                            const __nv_bfloat16* __restrict__ v, int64_t sb,
-                                                            int64_t sh, int64_t ss, const F8LGeom g, float scale,
-                                                            int smooth, uint8_t* __restrict__ ws) {
-  __shared__ __align__(16) float part[4][2048];   // pass A partials; pass C's v tile afterwards
-  __shared__ float mu[2][128];
-  __shared__ float svs[128];
+// Column statistics of one head (one CTA per head): sums of k and v, max and min of v over the
+// tokens -> mean(k) (or 0 without smooth-K), mean(v) (or 0 without smooth-V) and the per-column
+// scale of V~ = max_s |v_s - mean| / 448 (rounding is monotone, so that max is
+// max(|max v - mean|, |min v - mean|) exactly).
+__global__ void __launch_bounds__(256) attn_fp8_colstats_kernel(const __nv_bfloat16* __restrict__ k,
+                                                                const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                                int64_t sh, int64_t ss, const F8LGeom g, int smooth,
+                                                                uint8_t* __restrict__ ws) {
+  __shared__ float part[4][2048];   // per thread row-slice: column sums of k and v, max and min of v
   const int bh = blockIdx.x;
   const int b = bh / g.H, h = bh - b * g.H;
-  const __nv_bfloat16* qh = q + b * sb + h * sh;
   const __nv_bfloat16* kh = k + b * sb + h * sh;
   const __nv_bfloat16* vh = v + b * sb + h * sh;
   const int S = g.S, D = g.D, D8 = D / 8;
   const int rpi = 256 / D8, active = rpi * D8;
   const int t = threadIdx.x, c8 = t % D8, r0 = t / D8;
-
-  // pass A: column sums of k and v, column max / min of v
   {
     float sk[8], sv[8], vmax[8], vmin[8];
 #pragma unroll
@@ -2435,8 +2442,6 @@ __global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16*
     }
   }
   __syncthreads();
-  float* sv_g = reinterpret_cast<float*>(ws + g.off_sv) + (int64_t)bh * g.DV;
-  float* mu_g = reinterpret_cast<float*>(ws + g.off_mu) + (int64_t)bh * g.DV;
   if (t < D) {
     float a = 0.f, bb = 0.f, mx = -INFINITY, mn = INFINITY;
     for (int r = 0; r < rpi && r < S; ++r) {   // fixed order: deterministic means
@@ -2445,28 +2450,54 @@ __global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16*
       mx = fmaxf(mx, part[2][r * D + t]);
       mn = fminf(mn, part[3][r * D + t]);
     }
-    const float mk = (smooth & 1) ? __fdiv_rn(a, (float)S) : 0.f;
     const float mv = (smooth & 2) ? __fdiv_rn(bb, (float)S) : 0.f;
-    // rounding is monotone: max_s |v_s - m| = max(|max v - m|, |min v - m|) exactly
     const float am = fmaxf(fabsf(mx - mv), fabsf(mn - mv));
-    const float s = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
-    mu[0][t] = mk;
-    mu[1][t] = mv;
-    svs[t] = s;
-    sv_g[t] = s;
-    mu_g[t] = mv;
+    reinterpret_cast<float*>(ws + g.off_muk)[(int64_t)bh * g.DV + t] = (smooth & 1) ? __fdiv_rn(a, (float)S) : 0.f;
+    reinterpret_cast<float*>(ws + g.off_mu)[(int64_t)bh * g.DV + t] = mv;
+    reinterpret_cast<float*>(ws + g.off_sv)[(int64_t)bh * g.DV + t] = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
+  }
+}
+
+// Operands of one 128-token chunk of one head (blockIdx.x = head * nc + chunk): Q8 and K~8 rows with
+// their per-row scales (sk pre-multiplied by scale * log2 e) and the chunk of V~8^T, all in the MMA's
+// K-major core-matrix layout.  Quotients x / scale correctly rounded, as the reference divides.
+__global__ void __launch_bounds__(256) attn_fp8_pack_kernel(const __nv_bfloat16* __restrict__ q,
+                                                            const __nv_bfloat16* __restrict__ k,
+                                                            const __nv_bfloat16* __restrict__ v, int64_t sb,
+                                                            int64_t sh, int64_t ss, const F8LGeom g, float scale,
+                                                            uint8_t* __restrict__ ws) {
+  __shared__ __align__(16) __nv_bfloat16 tile[128 * 128];   // the chunk's v rows [128][D]
+  __shared__ float muk[128], muv[128], svs[128];
+  const int bh = blockIdx.x / g.nc, j = blockIdx.x - bh * g.nc;
+  const int b = bh / g.H, h = bh - b * g.H;
+  const __nv_bfloat16* qh = q + b * sb + h * sh;
+  const __nv_bfloat16* kh = k + b * sb + h * sh;
+  const __nv_bfloat16* vh = v + b * sb + h * sh;
+  const int S = g.S, D = g.D, D8 = D / 8;
+  const int t = threadIdx.x, lane = t & 31;
+  if (t < D) {
+    muk[t] = reinterpret_cast<const float*>(ws + g.off_muk)[(int64_t)bh * g.DV + t];
+    muv[t] = reinterpret_cast<const float*>(ws + g.off_mu)[(int64_t)bh * g.DV + t];
+    svs[t] = reinterpret_cast<const float*>(ws + g.off_sv)[(int64_t)bh * g.DV + t];
+  }
+  // the chunk's v rows into shared memory (zeros past S)
+  for (int i = t; i < 128 * D8; i += 256) {
+    const int rr = i / D8, cc = i - rr * D8, tok = j * 128 + rr;
+    const uint4 w = tok < S ? __ldg(reinterpret_cast<const uint4*>(vh + (int64_t)tok * ss + cc * 8))
+                            : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(tile + rr * D + cc * 8) = w;
   }
   __syncthreads();
-
-  // pass B: Q8 and K~8 rows, 8 lanes per row (lane & 7 = 16-element chunk along d), 4 rows per warp
+  // Q8 and K~8: 8 lanes per row (lane & 7 = 16-element chunk along d), 4 rows per warp
   {
-    const int lane = t & 31, kc = lane & 7, nkc = g.DK / 16, dkc = D / 16;
+    const int kc = lane & 7, nkc = g.DK / 16, dkc = D / 16;
     const float kmul = scale * 1.4426950408889634f;
-    uint8_t* qp = ws + g.off_q + (int64_t)bh * g.qk_head;
-    uint8_t* kp = ws + g.off_k + (int64_t)bh * g.qk_head;
-    float* sq_g = reinterpret_cast<float*>(ws + g.off_sq) + (int64_t)bh * g.S_pad;
-    float* sk_g = reinterpret_cast<float*>(ws + g.off_sk) + (int64_t)bh * g.S_pad;
-    for (int r = (t >> 5) * 4 + (lane >> 3); r < g.S_pad; r += 32) {
+    uint8_t* qp = ws + g.off_q + (int64_t)bh * g.qk_head + (int64_t)j * 128 * g.DK;
+    uint8_t* kp = ws + g.off_k + (int64_t)bh * g.qk_head + (int64_t)j * 128 * g.DK;
+    float* sq_g = reinterpret_cast<float*>(ws + g.off_sq) + (int64_t)bh * g.S_pad + j * 128;
+    float* sk_g = reinterpret_cast<float*>(ws + g.off_sk) + (int64_t)bh * g.S_pad + j * 128;
+    for (int rr = (t >> 5) * 4 + (lane >> 3); rr < 128; rr += 32) {
+      const int r = j * 128 + rr;
       float xq[16], xk[16];
       float aq = 0.f, ak = 0.f;
       if (r < S && kc < dkc) {
@@ -2476,7 +2507,7 @@ __global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16*
         load8(kh + r * ss + 16 * kc + 8, xk + 8);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          xk[e] -= mu[0][16 * kc + e];
+          xk[e] -= muk[16 * kc + e];
           aq = fmaxf(aq, fabsf(xq[e]));
           ak = fmaxf(ak, fabsf(xk[e]));
         }
@@ -2492,56 +2523,40 @@ __global__ void __launch_bounds__(256) attn_fp8_prep_kernel(const __nv_bfloat16*
       const float scq = __fdiv_rn(fmaxf(aq, 1e-12f), 448.f);
       const float sck = __fdiv_rn(fmaxf(ak, 1e-12f), 448.f);
       if (kc < nkc) {
-        const int rr = r & 127;
-        const int64_t off = (int64_t)(r >> 7) * 128 * g.DK + (rr >> 3) * 8 * g.DK + kc * 128 + (rr & 7) * 16;
+        const int64_t off = (rr >> 3) * 8 * g.DK + kc * 128 + (rr & 7) * 16;
         *reinterpret_cast<uint4*>(qp + off) = e4m3x16_div(xq, scq, __frcp_rn(scq));
         *reinterpret_cast<uint4*>(kp + off) = e4m3x16_div(xk, sck, __frcp_rn(sck));
       }
       if (kc == 0) {
-        sq_g[r] = r < S ? scq : 0.f;
-        sk_g[r] = r < S ? sck * kmul : 0.f;
+        sq_g[rr] = r < S ? scq : 0.f;
+        sk_g[rr] = r < S ? sck * kmul : 0.f;
       }
     }
   }
-
-  // pass C: V~8^T per 128-key chunk: the chunk's v rows staged in shared memory (coalesced 16-byte
-  // loads; the pass-A partials are dead), then one (16-key block, column d) per thread, consecutive
-  // threads taking consecutive d
+  // V~8^T of the chunk: one (16-key block, column d) per thread, consecutive threads on consecutive d
   {
-    __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(&part[0][0]);   // [128][D]
-    uint8_t* vp = ws + g.off_v + (int64_t)bh * g.v_head;
-    for (int j = 0; j < g.nc; ++j) {
-      for (int i = t; i < 128 * D8; i += 256) {
-        const int rr = i / D8, cc = i - rr * D8, tok = j * 128 + rr;
-        const uint4 w = tok < S ? __ldg(reinterpret_cast<const uint4*>(vh + (int64_t)tok * ss + cc * 8))
-                                : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(tile + rr * D + cc * 8) = w;
-      }
-      __syncthreads();
-      for (int i = t; i < 8 * D; i += 256) {
-        const int kc = i / D, d = i - kc * D;
-        const float m = mu[1][d], sc = svs[d];
-        float x[16];
+    uint8_t* vp = ws + g.off_v + (int64_t)bh * g.v_head + (int64_t)j * g.DV * 128;
+    for (int i = t; i < 8 * D; i += 256) {
+      const int kc = i / D, d = i - kc * D;
+      const float m = muv[d], sc = svs[d];
+      float x[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int rr = kc * 16 + e;
-          x[e] = j * 128 + rr < S ? __bfloat162float(tile[rr * D + d]) - m : 0.f;
-        }
-        *reinterpret_cast<uint4*>(vp + (int64_t)j * g.DV * 128 + (d >> 3) * 1024 + kc * 128 + (d & 7) * 16) =
-            e4m3x16_div(x, sc, __frcp_rn(sc));
+      for (int e = 0; e < 16; ++e) {
+        const int rr = kc * 16 + e;
+        x[e] = j * 128 + rr < S ? __bfloat162float(tile[rr * D + d]) - m : 0.f;
       }
-      __syncthreads();   // the tile is rewritten by the next chunk
+      *reinterpret_cast<uint4*>(vp + (d >> 3) * 1024 + kc * 128 + (d & 7) * 16) = e4m3x16_div(x, sc, __frcp_rn(sc));
     }
   }
 }
 
-// Pass 1 of a score chunk: max over this warp's 32 columns of acc * sk (packed multiplies,
-// three-input max); kMask drops the columns >= nv (keys past S in the last chunk).
+// Pass 1 on 16 of this warp's score columns: max of acc * sk (packed multiplies, three-input max);
+// kMask drops the columns >= nv (keys past S in the last chunk).
 template <bool kMask>
-VF4_DEV float f8l_chunk_max(const uint32_t* v, const float4* sk4, int nv) {
+VF4_DEV float f8l_half_max(const uint32_t* v, const float4* sk4, int nv) {
   float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const float4 k4 = sk4[i];
     float a0, a1, a2, a3;
     f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), f32x2_pack(k4.x, k4.y)),
@@ -2560,14 +2575,14 @@ VF4_DEV float f8l_chunk_max(const uint32_t* v, const float4* sk4, int nv) {
   return fmaxf(ma, mb);
 }
 
-// Pass 2 of a score chunk: p = 2^(acc sk sq - max + log2 448) for this warp's 32 columns (sq2, nm2:
-// sq and log2 448 - max in both halves), row sums accumulated in two packed pairs; kMask zeroes the
-// columns >= nv.
+// Pass 2 on 16 of this warp's score columns: p = 2^(acc sk sq - max + log2 448) (sq2, nm2: sq and
+// log2 448 - max in both halves), row sums accumulated in two packed pairs; kMask zeroes the columns
+// >= nv.
 template <bool kMask>
-VF4_DEV void f8l_chunk_exp(const uint32_t* v, const float4* sk4, int nv, unsigned long long sq2,
-                           unsigned long long nm2, float* p, unsigned long long& l2a, unsigned long long& l2b) {
+VF4_DEV void f8l_half_exp(const uint32_t* v, const float4* sk4, int nv, unsigned long long sq2,
+                          unsigned long long nm2, float* p, unsigned long long& l2a, unsigned long long& l2b) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const float4 k4 = sk4[i];
     float e0, e1, e2, e3;
     f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
@@ -2741,18 +2756,27 @@ __global__ void __launch_bounds__(kF8LWarps * 32, 1)
     constexpr float kLog2_448 = 8.8073549220576041f;
     uint32_t hc = 0, tcnt = 0, sc = 0, pc = 0;
     bool ok = true;
-    uint32_t v[32];
-    auto load_s = [&]() -> bool {   // this warp's 32 columns of the next score chunk
+    uint32_t va[16], vb[16];
+    // this warp's 32 columns of the next score chunk: the first 16 loaded and waited for, the other
+    // 16 left in flight while the first are processed; finish_s waits for them and frees the buffer
+    auto start_s = [&]() -> bool {
       const int b = (int)(sc % kF8LSBuf);
       if (!mbar_wait(s_full(b), (sc / kF8LSBuf) & 1u, err, kDevErrTimeoutFull)) return false;
       tc_fence_after();
-      tmem_ld_32x32b_x32(tmem + lane_addr + kF8LTmemS + 128u * b + 32u * slice, v);
+      const uint32_t ta = tmem + lane_addr + kF8LTmemS + 128u * b + 32u * slice;
+      tmem_ld_32x32b_x16(ta, va);
       tmem_wait_ld();
+      reg_fence16(va);
+      tmem_ld_32x32b_x16(ta + 16, vb);
+      return true;
+    };
+    auto finish_s = [&]() {
+      tmem_wait_ld();
+      reg_fence16(vb);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free(b));
+      if (lane == 0) mbar_arrive(s_free((int)(sc % kF8LSBuf)));
       ++sc;
-      return true;
     };
     for (int64_t bh = blockIdx.x; bh < g.BH && ok; bh += gridDim.x, ++hc) {
       if (!(ok = mbar_wait(kv_full, hc & 1u, err, kDevErrTimeoutFull))) break;
@@ -2764,9 +2788,13 @@ __global__ void __launch_bounds__(kF8LWarps * 32, 1)
         // pass 1: row max of acc * sk (scores in log2 units are acc * sk * sqr, sqr > 0 for real rows)
         float m = -INFINITY;
         for (int j = 0; j < nc && ok; ++j) {
-          if (!(ok = load_s())) break;
+          if (!(ok = start_s())) break;
           const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
-          m = fmaxf(m, j + 1 < nc || nlast >= 32 ? f8l_chunk_max<false>(v, sk4, 32) : f8l_chunk_max<true>(v, sk4, nlast));
+          const bool full = j + 1 < nc || nlast >= 32;
+          const float m1 = full ? f8l_half_max<false>(va, sk4, 16) : f8l_half_max<true>(va, sk4, nlast);
+          finish_s();
+          const float m2 = full ? f8l_half_max<false>(vb, sk4 + 4, 16) : f8l_half_max<true>(vb, sk4 + 4, nlast - 16);
+          m = max3f(m, m1, m2);
         }
         red_m[slice * 128 + r] = m;
         named_bar_sync(1 + quad, 32 * kF8LSlices);
@@ -2779,20 +2807,28 @@ __global__ void __launch_bounds__(kF8LWarps * 32, 1)
         const unsigned long long sq2 = f32x2_pack(sqr, sqr), nm2 = f32x2_pack(nmc, nmc);
         unsigned long long l2a = f32x2_pack(0.f, 0.f), l2b = l2a;
         for (int j = 0; j < nc && ok; ++j) {
-          if (!(ok = load_s())) break;
+          if (!(ok = start_s())) break;
           const int pb = (int)(pc & 1u);
-          if (!(ok = mbar_wait(p_free(pb), ((pc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) break;
+          if (!(ok = mbar_wait(p_free(pb), ((pc >> 1) & 1u) ^ 1u, err, kDevErrTimeoutEmpty))) {
+            finish_s();
+            break;
+          }
           const float4* sk4 = reinterpret_cast<const float4*>(sk + j * 128 + 32 * slice);
-          float p[32];
-          if (j + 1 < nc || nlast >= 32)
-            f8l_chunk_exp<false>(v, sk4, 32, sq2, nm2, p, l2a, l2b);
+          const bool full = j + 1 < nc || nlast >= 32;
+          // K-major core matrices of P: (row group, 16-key chunk) at rg*1024 + kc*128
+          uint8_t* prow = gbase + L.p + pb * 16384 + (r >> 3) * 1024 + 2 * slice * 128 + (r & 7) * 16;
+          float p[16];
+          if (full)
+            f8l_half_exp<false>(va, sk4, 16, sq2, nm2, p, l2a, l2b);
           else
-            f8l_chunk_exp<true>(v, sk4, nlast, sq2, nm2, p, l2a, l2b);
-          uint8_t* pbuf = gbase + L.p + pb * 16384;
-#pragma unroll
-          for (int c = 0; c < 2; ++c)   // K-major core matrices: (row group, 16-key chunk) at rg*1024 + kc*128
-            *reinterpret_cast<uint4*>(pbuf + (r >> 3) * 1024 + (2 * slice + c) * 128 + (r & 7) * 16) =
-                e4m3x16(p + 16 * c, 1.f);
+            f8l_half_exp<true>(va, sk4, nlast, sq2, nm2, p, l2a, l2b);
+          *reinterpret_cast<uint4*>(prow) = e4m3x16(p, 1.f);
+          finish_s();
+          if (full)
+            f8l_half_exp<false>(vb, sk4 + 4, 16, sq2, nm2, p, l2a, l2b);
+          else
+            f8l_half_exp<true>(vb, sk4 + 4, nlast - 16, sq2, nm2, p, l2a, l2b);
+          *reinterpret_cast<uint4*>(prow + 128) = e4m3x16(p, 1.f);
           fence_async_shared();
           __syncwarp();
           if (lane == 0) mbar_arrive(p_full(pb));
@@ -2855,11 +2891,13 @@ static int launch_fp8_long(const void* q, const void* k, const void* v, int64_t 
                            int64_t oss, int smooth, uint8_t* ws, cudaStream_t s) {
   const F8LGeom g = make_f8l_geom(B, H, S, D);
   const F8LSmem L = f8l_smem_layout(g);
-  attn_fp8_prep_kernel<<<(unsigned)g.BH, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(q),
-                                                      static_cast<const __nv_bfloat16*>(k),
-                                                      static_cast<const __nv_bfloat16*>(v), sb, sh, ss, g, scale,
-                                                      smooth, ws);
-  if (int st = launch_status("vf4_attn fp8 (prep)")) return st;
+  const auto* Q = static_cast<const __nv_bfloat16*>(q);
+  const auto* K = static_cast<const __nv_bfloat16*>(k);
+  const auto* V = static_cast<const __nv_bfloat16*>(v);
+  attn_fp8_colstats_kernel<<<(unsigned)g.BH, 256, 0, s>>>(K, V, sb, sh, ss, g, smooth, ws);
+  if (int st = launch_status("vf4_attn fp8 (column statistics)")) return st;
+  attn_fp8_pack_kernel<<<(unsigned)(g.BH * g.nc), 256, 0, s>>>(Q, K, V, sb, sh, ss, g, scale, ws);
+  if (int st = launch_status("vf4_attn fp8 (operand pack)")) return st;
   if (int st = smem_optin(attn_fp8_long_kernel, (int)L.total)) return st;
   const int grid = (int)(g.BH < num_sms() ? g.BH : num_sms());   // persistent: whole heads per CTA
   attn_fp8_long_kernel<<<grid, kF8LWarps * 32, L.total, s>>>(g, ws, L, static_cast<__nv_bfloat16*>(out), osb, osh,
@@ -2889,13 +2927,6 @@ static int launch_fp8_long(const void* q, const void* k, const void* v, int64_t 
 //                with the tiles (a 128-row MMA tile for one row costs a whole tile's MMA ->
 //                softmax -> PV chain)
 // ---------------------------------------------------------------------------------------
-// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; these
-// empty volatile statements keep the compiler from moving their first uses above the wait.
-VF4_DEV void reg_fence16(uint32_t* v) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(v[i]));
-}
-
 constexpr uint32_t kB16TmemS = 0, kB16TmemO = 320;
 constexpr int kB16TailWarps = 2, kB16Warps = kFusedWarps + kB16TailWarps, kB16TailMax = 4;
 

@@ -375,7 +375,7 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: 
         _lib.call("vf4_attn", _ptr(q), _ptr(k), _ptr(v), B, H, S, D, strides[0], strides[1], strides[2],
                   float(scale), fp8, fp8, flags, _ptr(ws) if ws is not None else None, n, _ptr(out),
                   out_strides[0], out_strides[1], out_strides[2], _stream())
-    _launched(1 if ws is None else 2)
+    _launched(1 if ws is None else 3)   # short route: one kernel; long: statistics, pack, forward
     return out
 
 
