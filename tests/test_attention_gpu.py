@@ -1,7 +1,8 @@
 """GPU parity of the NVFP4 attention kernels.
 
-The kernels' deliberate difference from the reference's emulated quant_sdpa is the fixed
-1/(6*448) global for P (and, on the fused route, P quantized before the 1/rowsum).  Bars:
+The kernels' deliberate differences from the reference's emulated quant_sdpa: the fixed 1/(6*448)
+global for P, and P quantized before the 1/rowsum (P = exp(s - max) in [0, 1], exactly 1 at the row
+max; the output is divided by the row sum).  Bars:
   * vs a CPU restatement of exactly those semantics (``_oracle_kernel_semantics``): cos >= 0.999
   * vs the reference's quantized output (oracle.quant_sdpa, qk = pv = 'nvfp4'): cos >= 0.995
   * accuracy vs exact fp32 attention no worse than the reference's own minus 0.005, and > 0.95
@@ -35,17 +36,11 @@ def _qdq(x, gs, axis=-1):
     return np.moveaxis(d, -1, axis)
 
 
-def _fused_path(S, D):
-    """The single-kernel route (head dim 64, S <= 320) quantizes P unnormalised."""
-    return D == 64 and S <= 320
-
-
 def _oracle_kernel_semantics(q, k, v, scale, head_globals=False, smooth_k=True, smooth_v=True):
     """The kernels' arithmetic: smooth-K/V (each switchable), NVFP4 Q, K~ (along d) and V~ (along
     tokens) with global scales over the whole tensors (or per head), P with the fixed global 1/2688
-    (unnormalised on the fused route)."""
+    quantized unnormalised (P = exp(s - max) in [0, 1], the 1/rowsum applied to the output)."""
     B, H, S, D = q.shape
-    unnormalised = _fused_path(S, D)
     out = np.empty((B, H, S, D), F32)
     g = lambda t: F32(max(np.abs(t).max(), 1e-12) / 2688.0)
     ktt = k - k.mean(2, keepdims=True) if smooth_k else k
@@ -60,12 +55,8 @@ def _oracle_kernel_semantics(q, k, v, scale, head_globals=False, smooth_k=True, 
             gq, gk, gv = (g(qq), g(kt), g(vt)) if head_globals else (gq_all, gk_all, gv_all)
             s = _qdq(qq, gq) @ _qdq(kt, gk).T * F32(scale)
             vd = _qdq(vt, gv, axis=0)
-            if unnormalised:   # P = exp(s - max) in [0, 1] quantized, 1/rowsum applied to the output
-                p = np.exp(s - s.max(-1, keepdims=True)).astype(F32)
-                out[b, h] = (_qdq(p, F32(1.0 / 2688.0)) @ vd) / p.sum(-1, keepdims=True) + mu
-            else:
-                p = oracle.softmax(s)
-                out[b, h] = _qdq(p, F32(1.0 / 2688.0)) @ vd + mu
+            p = np.exp(s - s.max(-1, keepdims=True)).astype(F32)
+            out[b, h] = (_qdq(p, F32(1.0 / 2688.0)) @ vd) / p.sum(-1, keepdims=True) + mu
     return out
 
 

@@ -1,22 +1,18 @@
-// NVFP4 attention for ViT on sm_100a: QK^T and PV as block-scaled tcgen05 MMAs.
+// Low-precision attention for ViT on sm_100a: QK^T and PV as tcgen05 MMAs.
 //
-// Semantics follow the reference's emulated quant_sdpa(qk='nvfp4', pv='nvfp4', smooth_k,
+// NVFP4 routes follow the reference's emulated quant_sdpa(qk='nvfp4', pv='nvfp4', smooth_k,
 // smooth_v) (src/vit_nvfp4/nvfp4/attention.py:53-86):
 //   k~ = k - mean_S(k);  S = deq(Q) deq(K~)^T * scale;  P = softmax(S);
 //   v~ = v - mean_S(v);  out = deq(P) deq(V~) + mean_S(v)
 // with Q, K~ quantized along the head dim and V~ along tokens (16-element NVFP4 blocks, E4M3
-// block scales, "six" rule, ties-down codes).  Two deliberate differences, both forced by a
-// single-pass kernel: the fp32 global scale of Q, K~ and V~ is taken per (image, head) rather
-// than over the whole tensor, and P (exactly normalised, <= 1) uses the fixed global 1/(6*448)
-// instead of the amax of the whole P tensor.
-//
-// Kernel 1 (attn_prep, one CTA per (b, h)): means, per-head amax, and NVFP4 packing of Q, K~
-//   and V~^T into the MMA operand layouts (128x4-tiled scales) in a workspace.
-// Kernel 2 (attn_fwd, one CTA per (b, h, 128-query tile)): TMA loads Q tile, all K~ and V~^T
-//   of the head; warp 0 issues the MMAs, warps 2..5 (one query row per thread) run an exact
-//   two-pass softmax from TMEM (pass 1: row max / sum; pass 2: recompute S, P = exp(S-m)/l),
-//   re-quantize P to NVFP4 in shared memory (scales staged for tcgen05.cp), and the PV MMA
-//   accumulates O in TMEM; the epilogue adds mean(v) and writes bf16 (B, S, H, D).
+// block scales, "six" rule, ties-down codes) under the reference's tensor-wide global scales
+// (or, with VF4_ATTN_HEAD_GLOBALS, per (image, head)).  Two deliberate differences: P uses the
+// fixed global 1/(6*448) instead of the amax of the whole P tensor, and P is quantized before
+// the 1/rowsum (P = exp(S - max) lies in [0, 1] with the row max exactly 1; the output is
+// divided by the row sum), so a tile's probabilities need one pass over its scores for the
+// maximum and one for P.
+// The FP8 routes (quant_sdpa(qk='fp8', pv='fp8'), the reference's default arguments) and the
+// bf16 route of blocks the reference leaves unconverted are described at their kernels below.
 #include <mutex>
 
 #include "vf4_common.cuh"
@@ -548,10 +544,11 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __nv_bfloat16* __r
 //   warp 1      TMEM allocation, then the MMAs: per 128-key chunk S = Q K~^T into one of two
 //               TMEM score buffers (pass 1, then again in pass 2), and O = P V~ per chunk
 //   warps 2-9   softmax: two warps per TMEM lane quadrant, each owning 64 of a chunk's 128 key
-//               columns.  Pass 1: running row max and row sum of exp; the two halves combine
-//               through shared memory.  Pass 2: P = exp(s - max) / sum, NVFP4 with the fixed
-//               global 1/2688 (each half writes its 64 keys' codes and one K64 scale word) into
-//               one of two P buffers.  Epilogue: O * gs_v / 2688 + mean(v) -> bf16.
+//               columns.  Pass 1: row max (and min, for a negative scale); the two halves combine
+//               through shared memory.  Pass 2: P = exp(s - max) in [0, 1] and its row sums, NVFP4
+//               with the fixed global 1/2688 (each half writes its 64 keys' codes and one K64
+//               scale word) into one of two P buffers.  Epilogue: O * gs_v / (2688 rowsum) +
+//               mean(v) -> bf16.
 // Every wait is bounded; a give-up records the device error and unwinds.
 // ---------------------------------------------------------------------------------------
 VF4_DEV float ex2_approx(float x) {
@@ -776,34 +773,36 @@ __global__ void __launch_bounds__(AttnCfg<DP>::THREADS, 1)
       const float cexp = scal[0] * scal[1] * scale * 1.4426950408889634f;
       for (int qt = 0; qt < nc && ok; ++qt, ++tcnt) {
         const int tq = qt * 128 + r;                // query token
-        // pass 1: running max and sum of exp over this warp's columns
-        float m = -INFINITY, l = 0.f;
+        // pass 1: the row's largest and smallest raw score over this warp's columns; fl(x * cexp) is
+        // monotone in x, so the row max of the scaled scores is (cexp >= 0 ? max : min) * cexp exactly
+        float m = -INFINITY, mn = INFINITY;
         for (int j = 0; j < nc && ok; ++j) {
           if (!(ok = load_s())) break;
           const int nvalid = min(64, S - j * 128 - 64 * half);   // may be <= 0 for the last chunk
-          float cm = -INFINITY;
+          if (nvalid >= 64) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < nvalid) cm = fmaxf(cm, __uint_as_float(v[i]) * cexp);
-          const float mn = fmaxf(m, cm);
-          if (mn > -INFINITY) {
-            float sum = 0.f;
+            for (int i = 0; i < 64; i += 2) {
+              m = max3f(m, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+              mn = min3f(mn, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+            }
+          } else {
 #pragma unroll
             for (int i = 0; i < 64; ++i)
-              if (i < nvalid) sum += ex2_approx(__uint_as_float(v[i]) * cexp - mn);
-            l = l * ex2_approx(m - mn) + sum;
-            m = mn;
+              if (i < nvalid) {
+                m = fmaxf(m, __uint_as_float(v[i]));
+                mn = fminf(mn, __uint_as_float(v[i]));
+              }
           }
         }
         // combine the two halves of the row
-        red[half * 128 + r] = make_float2(m, l);
+        red[half * 128 + r] = make_float2(m, mn);
         named_bar_sync(1 + quad, 64);
         const float2 o2 = red[(1 - half) * 128 + r];
-        const float mr = fmaxf(m, o2.x);
-        const float lr = (m > -INFINITY ? l * ex2_approx(m - mr) : 0.f) + (o2.x > -INFINITY ? o2.y * ex2_approx(o2.x - mr) : 0.f);
-        const float inv_l = 1.0f / lr;
+        const float mr = (cexp >= 0.f ? fmaxf(m, o2.x) : fminf(mn, o2.y)) * cexp;
         named_bar_sync(1 + quad, 64);               // both halves have read red before it is reused
-        // pass 2: P = exp(s - max) / sum -> NVFP4 into the P buffers
+        float l = 0.f;
+        // pass 2: P = exp(s - max) in [0, 1] (exactly 1 at the row max), its row sums, P -> NVFP4 (fixed
+        // global 1/2688) into the P buffers; the 1/rowsum is applied to O
         for (int j = 0; j < nc && ok; ++j) {
           if (!(ok = load_s())) break;
           const int nvalid = min(64, S - j * 128 - 64 * half);
@@ -819,7 +818,8 @@ __global__ void __launch_bounds__(AttnCfg<DP>::THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
                 const int i = blk * 16 + e;
-                pv[e] = i < nvalid ? ex2_approx(__uint_as_float(v[i]) * cexp - mr) * inv_l : 0.f;
+                pv[e] = i < nvalid ? ex2_approx(__fmaf_rn(__uint_as_float(v[i]), cexp, -mr)) : 0.f;
+                l += pv[e];
               }
               float amax = 0.f;
 #pragma unroll
@@ -840,6 +840,10 @@ __global__ void __launch_bounds__(AttnCfg<DP>::THREADS, 1)
           if (lane == 0) mbar_arrive(p_full(pb));
           ++pc;
         }
+        red[half * 128 + r].x = l;
+        named_bar_sync(1 + quad, 64);
+        const float inv_l = 1.0f / (l + red[(1 - half) * 128 + r].x);
+        named_bar_sync(1 + quad, 64);               // read before the next tile's pass 1 rewrites red
         // epilogue: this warp's half of the head dim
         if (ok && (ok = mbar_wait(o_full, tcnt & 1u, err, kDevErrTimeoutTmem))) {
           tc_fence_after();
@@ -853,7 +857,7 @@ __global__ void __launch_bounds__(AttnCfg<DP>::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(o_free);
           if (tq < S) {
-            const float ao = kInv2688 * scal[2];
+            const float ao = kInv2688 * scal[2] * inv_l;
             const int b = (int)(bh / g.H), h = (int)(bh - (int64_t)b * g.H);
             __nv_bfloat16* o = out + b * osb + (int64_t)tq * oss + h * osh + half * DH;
 #pragma unroll

@@ -359,6 +359,13 @@ VF4_DEV float max3f(float a, float b, float c) {
   return d;
 }
 
+// min(a, b, c) in one instruction (three-operand min.f32, sm_100)
+VF4_DEV float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // max |v_i| over 16 values
 VF4_DEV float amax16(const float* v) {
   float m = max3f(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
