@@ -38,6 +38,18 @@ def test_mean16_order_matches_aten():
     assert np.array_equal(oracle.mean16_aten(g["mean_in"]), g["mean_out"])
 
 
+def test_mean16_order_matches_this_hosts_torch():
+    """The 16-term mean order (p_i = e_i + e_(i+8), a sequential sum of the eight, / 16) is ATen's
+    vectorised CPU reduction; it can change with the host's ATen CPU capability.  The golden vectors
+    pin the order of the machine that made them; this checks the host the tests run on, so a
+    mismatch shows up here rather than as FoS candidate flips."""
+    import torch
+    rng = np.random.default_rng(5)
+    e = (rng.standard_normal((4096, 16)) ** 2 * np.exp(rng.uniform(-20, 20, (4096, 1)))).astype(np.float32)
+    got = torch.from_numpy(e).mean(dim=-1).numpy()
+    assert np.array_equal(oracle.mean16_aten(e), got)
+
+
 @pytest.mark.parametrize("name", list(golden()["q_cases"]))
 def test_quantize_bit_exact(name):
     g = golden()
