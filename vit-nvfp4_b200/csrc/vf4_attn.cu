@@ -2484,14 +2484,17 @@ __global__ void __launch_bounds__(256) attn_fp8_pack_kernel(const __nv_bfloat16*
     muv[t] = reinterpret_cast<const float*>(ws + g.off_mu)[(int64_t)bh * g.DV + t];
     svs[t] = reinterpret_cast<const float*>(ws + g.off_sv)[(int64_t)bh * g.DV + t];
   }
-  // the chunk's v rows into shared memory (zeros past S)
+  // the chunk's v rows into shared memory (zeros past S) by asynchronous copies that run while the
+  // Q / K~ rows below are quantized
   for (int i = t; i < 128 * D8; i += 256) {
     const int rr = i / D8, cc = i - rr * D8, tok = j * 128 + rr;
-    const uint4 w = tok < S ? __ldg(reinterpret_cast<const uint4*>(vh + (int64_t)tok * ss + cc * 8))
-                            : make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4*>(tile + rr * D + cc * 8) = w;
+    const __nv_bfloat16* src = vh + (int64_t)(tok < S ? tok : 0) * ss + cc * 8;
+    const uint32_t dst = smem_u32(tile + rr * D + cc * 8);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(tok < S ? 16 : 0)
+                 : "memory");
   }
-  __syncthreads();
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  __syncthreads();   // the statistics above are visible to every thread
   // Q8 and K~8: 8 lanes per row (lane & 7 = 16-element chunk along d), 4 rows per warp
   {
     const int kc = lane & 7, nkc = g.DK / 16, dkc = D / 16;
@@ -2537,6 +2540,8 @@ __global__ void __launch_bounds__(256) attn_fp8_pack_kernel(const __nv_bfloat16*
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();   // every thread's copies of the v rows have landed
   // V~8^T of the chunk: one (16-key block, column d) per thread, consecutive threads on consecutive d
   {
     uint8_t* vp = ws + g.off_v + (int64_t)bh * g.v_head + (int64_t)j * g.DV * 128;
