@@ -172,9 +172,10 @@ VF4_API int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t
  *   smooth-K / smooth-V always on; global scales of Q, K~, V~ over the whole tensors, as the
  *   reference (a statistics kernel runs first); P quantized along keys with the fixed global
  *   1/(6*448) instead of the amax of the whole P tensor; no mask, not causal.
- *   D % 16 == 0, D <= 128; S <= 1152 for D > 64.  Head dim 64 with S <= 320 (ViT-S/B/L) runs
- *   as one fused kernel that quantizes P = exp(S - rowmax) and divides the output by the row
- *   sum; other shapes run prep + forward kernels with P normalised first.
+ *   D % 16 == 0, D <= 128; S <= 1152 for D > 64.  Every route quantizes P = exp(S - rowmax) (in
+ *   [0, 1], exactly 1 at the row max) and divides the output by the row sum.  Head dim 64 with
+ *   S <= 320 (ViT-S/B/L) runs as one fused kernel and needs scale >= 0 (VF4_ERR_UNSUPPORTED
+ *   otherwise); other shapes run prep + forward kernels and take any scale.
  *   workspace: at least vf4_attn_workspace_size(B, H, S, D) bytes, 16-byte aligned. */
 VF4_API int vf4_attn_nvfp4(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S,
                            int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_s, float scale,
@@ -196,7 +197,7 @@ VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B,
  * kept in bf16 (ptq/qattention.py:20-30 falls through to the model's own attention when quant
  * attention is off; timm's Attention.forward calls F.scaled_dot_product_attention).  No
  * counterpart kernel in the reference.  Same operand / output layout and strides as
- * vf4_attn_nvfp4; head dim 64 and S <= 288 (VF4_ERR_UNSUPPORTED otherwise); no workspace.
+ * vf4_attn_nvfp4; head dim 64, S <= 288 and scale >= 0 (VF4_ERR_UNSUPPORTED otherwise); no workspace.
  * out_amax (may be NULL): receives max |out| over the whole bf16 output -- the amax the next
  * QuantLinear's dynamic activation cast would compute (quant.py:48-54), so the caller can cast
  * with vf4_global_scale(out_amax) and skip that pass. */

@@ -446,3 +446,33 @@ def test_unified_attention_entry_routes_and_refusals():
     assert s3 == 6 and (o3 == 0).all()                                  # VF4_ERR_UNSUPPORTED
     s4, _ = run("nvfp4", "nvfp4", _lib.VF4_ATTN_HEAD_GLOBALS | _lib.VF4_ATTN_NO_SMOOTH_K)
     assert s4 == 6
+
+
+@pytest.mark.parametrize("qk,B,H,S,D", [("fp8", 2, 3, 197, 64), ("fp8", 1, 2, 300, 80), ("nvfp4", 1, 2, 400, 64)])
+def test_negative_softmax_scale(qk, B, H, S, D):
+    """A negative scale makes the row's largest score the smallest q.k: the FP8 kernels (both routes)
+    and the long-sequence FP4 route follow the sign; the fused FP4 kernel refuses it."""
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import quant_sdpa
+    q, k, v = _qkv(B, H, S, D, seed=90 + S)
+    scale = -(D ** -0.5)
+    out = quant_sdpa(q.cuda(), k.cuda(), v.cuda(), scale=scale, qk=qk, pv=qk).float().cpu().numpy()
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    ref = (oracle.quant_sdpa(qn, kn, vn, scale=scale, qk=qk, pv=qk) if qk == "fp8"
+           else _oracle_kernel_semantics(qn, kn, vn, scale))
+    assert np.isfinite(out).all() and cos(out, ref) >= 0.999, cos(out, ref)
+    assert _lib.device_error() == 0
+
+
+def test_negative_scale_refused_where_the_kernel_assumes_a_positive_one():
+    import ctypes
+    from vitfp4 import _lib
+    from vitfp4.nvfp4 import quant_sdpa
+    q, k, v = (t.cuda() for t in _qkv(1, 2, 197, 64, seed=3))
+    with pytest.raises(_lib.VitFp4Error, match="scale >= 0"):
+        quant_sdpa(q, k, v, scale=-0.125, qk="nvfp4", pv="nvfp4")
+    out = torch.zeros(1, 197, 2, 64, dtype=torch.bfloat16, device="cuda")
+    st = _lib.lib().vf4_attn_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, 197, 64, 2 * 197 * 64, 197 * 64, 64,
+                                  ctypes.c_float(-0.125), out.data_ptr(), 197 * 2 * 64, 64, 2 * 64, None,
+                                  torch.cuda.current_stream().cuda_stream)
+    assert st == 6 and (out == 0).all()

@@ -64,3 +64,13 @@ def test_whole_call_route(kernel_calls):
     qkv = torch.randn(1, S, 3 * H * D).bfloat16()
     out = _route(qkv, H, D)
     assert isinstance(out, torch.Tensor) and out.shape == (1, S, H * D) and not kernel_calls
+
+
+def test_negative_scale_leaves_the_bf16_kernel(kernel_calls):
+    """The bf16 kernel takes the row max of the raw scores, which is the softmax's max only for a
+    scale >= 0; a negative scale goes to torch SDPA, the reference's own route for bf16 blocks."""
+    from vitfp4.ptq.fused_block import _attention_route
+    H, D, S = 2, 64, 197
+    qkv = torch.randn(1, S, 3 * H * D).bfloat16()
+    out = _attention_route(qkv, H, -(D ** -0.5), "none", "none")
+    assert not kernel_calls and isinstance(out, torch.Tensor)

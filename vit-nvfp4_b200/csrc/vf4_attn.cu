@@ -1868,6 +1868,65 @@ VF4_DEV uint4 e4m3x16(const float* x, float mul) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; these
+// empty volatile statements keep the compiler from moving their first uses above the wait.
+VF4_DEV void reg_fence16(uint32_t* v) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+// Pass 1 on 16 of this warp's score columns: max of acc * sk (packed multiplies, three-input max);
+// kMask drops the columns >= nv (keys past S in the last chunk).
+template <bool kMask>
+VF4_DEV float f8l_half_max(const uint32_t* v, const float4* sk4, int nv) {
+  float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 k4 = sk4[i];
+    float a0, a1, a2, a3;
+    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), f32x2_pack(k4.x, k4.y)),
+                 &a0, &a1);
+    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                           f32x2_pack(k4.z, k4.w)), &a2, &a3);
+    if (kMask) {
+      a0 = 4 * i < nv ? a0 : -INFINITY;
+      a1 = 4 * i + 1 < nv ? a1 : -INFINITY;
+      a2 = 4 * i + 2 < nv ? a2 : -INFINITY;
+      a3 = 4 * i + 3 < nv ? a3 : -INFINITY;
+    }
+    ma = max3f(ma, a0, a1);
+    mb = max3f(mb, a2, a3);
+  }
+  return fmaxf(ma, mb);
+}
+
+// Pass 2 on 16 of this warp's score columns: p = 2^(acc sk sq - max + log2 448) (sq2, nm2: sq and
+// log2 448 - max in both halves), row sums accumulated in two packed pairs; kMask zeroes the columns
+// >= nv.
+template <bool kMask>
+VF4_DEV void f8l_half_exp(const uint32_t* v, const float4* sk4, int nv, unsigned long long sq2,
+                          unsigned long long nm2, float* p, unsigned long long& l2a, unsigned long long& l2b) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 k4 = sk4[i];
+    float e0, e1, e2, e3;
+    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                     f32x2_pack(k4.x, k4.y)), sq2, nm2), &e0, &e1);
+    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                     f32x2_pack(k4.z, k4.w)), sq2, nm2), &e2, &e3);
+    p[4 * i] = ex2_approx(e0);
+    p[4 * i + 1] = ex2_approx(e1);
+    p[4 * i + 2] = ex2_approx(e2);
+    p[4 * i + 3] = ex2_approx(e3);
+    if (kMask) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p[4 * i + e] = 4 * i + e < nv ? p[4 * i + e] : 0.f;
+    }
+    l2a = add_f32x2(l2a, f32x2_pack(p[4 * i], p[4 * i + 1]));
+    l2b = add_f32x2(l2b, f32x2_pack(p[4 * i + 2], p[4 * i + 3]));
+  }
+}
+
 __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     attn_fp8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                     const __grid_constant__ CUtensorMap tmO, const Fp8Geom g) {
@@ -2131,7 +2190,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         const float scl = __fdiv_rn(fmaxf(am, 1e-12f), 448.f);
         *reinterpret_cast<uint4*>(gb + g.fk + (uint32_t)(s >> 3) * sbo_q + (uint32_t)cb * 128u + (s & 7) * 16) =
             e4m3x16(x, __fdiv_rn(1.f, scl));
-        if (cb == 0) sk[s] = s < S ? scl : 0.f;
+        if (cb == 0) sk[s] = s < S ? (g.scale < 0.f ? -scl : scl) : 0.f;   // the score's sign folded in
       }
       // ---- V8^T: row d, 16-token blocks; a warp covers 32 consecutive d of one token block
       {
@@ -2156,7 +2215,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         mbar_arrive(raw_free);
       }
       named_bar_sync(1, kCT);   // sq / sk / sv visible to every compute warp
-      const float cbase = g.scale * 1.4426950408889634f;
+      const float cbase = fabsf(g.scale) * 1.4426950408889634f;
       const int c0 = cs * 8 / kSlices, c1 = (cs + 1) * 8 / kSlices;
       auto epilogue = [&](int itt, int tl) {
         const bool act = ok && tl * 128 + qd * 32 < S;
@@ -2211,17 +2270,22 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         if (ok) ok = mbar_wait(s_full, (uint32_t)it & 1u, err, kDevErrTimeoutFull);
         tc_fence_after();
         const uint32_t srow = tmem + lane_base + kFusedTmemS;
-        const float c = sq[t * 128 + r] * cbase;   // real score = acc * sq * sk * scale
-        // pass 1: max over keys of acc * sk (sq * scale > 0 is common to the row)
+        const float c = sq[t * 128 + r] * cbase;   // real score * log2 e = acc * sk * c, c >= 0
+        // pass 1: max over keys of acc * sk (c >= 0 is common to the row), 16 columns per TMEM load
+        // (a second load in flight spills registers at this kernel's 128-register budget)
         float m = -INFINITY;
-        if (active && ok) {
+        if (active && ok && b0 < b1) {
+          uint32_t va[16];
+          auto max16 = [&](int bk, const uint32_t* v) {
+            const float4* sk4 = reinterpret_cast<const float4*>(sk + 16 * bk);
+            const int nv = S - 16 * bk;
+            m = fmaxf(m, nv >= 16 ? f8l_half_max<false>(v, sk4, 16) : f8l_half_max<true>(v, sk4, nv));
+          };
           for (int bk = b0; bk < b1; ++bk) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(srow + 16 * bk, v);
+            tmem_ld_32x32b_x16(srow + 16 * bk, va);
             tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (16 * bk + e < S) m = fmaxf(m, __uint_as_float(v[e]) * sk[16 * bk + e]);
+            reg_fence16(va);
+            max16(bk, va);
           }
         }
         red_m[cs * 128 + r] = m;
@@ -2232,20 +2296,31 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
         // pass 2: P = exp(s - max), row sums, P8 = e4m3(448 P)
         const float nmc = -m * c;
         float lsum = 0.f;
-        if (active && ok) {
-          for (int bk = b0; bk < b1; ++bk) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(srow + 16 * bk, v);
-            tmem_wait_ld();
+        if (active && ok && b0 < b1) {
+          const unsigned long long c2 = f32x2_pack(c, c), nm2 = f32x2_pack(nmc, nmc);
+          unsigned long long l2a = f32x2_pack(0.f, 0.f), l2b = l2a;
+          uint32_t va[16];
+          auto exp16 = [&](int bk, const uint32_t* v) {
+            const float4* sk4 = reinterpret_cast<const float4*>(sk + 16 * bk);
+            const int nv = S - 16 * bk;
             float p[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              p[e] = 16 * bk + e < S ? ex2_approx(__fmaf_rn(__uint_as_float(v[e]) * sk[16 * bk + e], c, nmc)) : 0.f;
-              lsum += p[e];
-            }
+            if (nv >= 16)
+              f8l_half_exp<false>(v, sk4, 16, c2, nm2, p, l2a, l2b);
+            else
+              f8l_half_exp<true>(v, sk4, nv, c2, nm2, p, l2a, l2b);
             *reinterpret_cast<uint4*>(gb + g.fp + (uint32_t)(r >> 3) * sbo_kv + (uint32_t)bk * 128u + (r & 7) * 16) =
                 e4m3x16(p, 448.f);
+          };
+          for (int bk = b0; bk < b1; ++bk) {
+            tmem_ld_32x32b_x16(srow + 16 * bk, va);
+            tmem_wait_ld();
+            reg_fence16(va);
+            exp16(bk, va);
           }
+          float la0, la1, lb0, lb1;
+          f32x2_unpack(l2a, &la0, &la1);
+          f32x2_unpack(l2b, &lb0, &lb1);
+          lsum = (la0 + la1) + (lb0 + lb1);
         }
         tc_fence_before();
         __syncwarp();
@@ -2314,13 +2389,6 @@ static int launch_fp8(const void* q, const void* k, const void* v, int64_t B, in
 // quadrant x 32-key quarter of each chunk) and the epilogue (8-column groups of the head dim).
 // Every wait is bounded; a give-up records the device error and unwinds.
 // ---------------------------------------------------------------------------------------
-// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; these
-// empty volatile statements keep the compiler from moving their first uses above the wait.
-VF4_DEV void reg_fence16(uint32_t* v) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(v[i]));
-}
-
 constexpr int kF8LStages = 3;                       // V~8^T chunks in flight
 constexpr int kF8LSlices = 4;                       // softmax warps per TMEM lane quadrant
 constexpr int kF8LSoftmax = 4 * kF8LSlices;
@@ -2556,58 +2624,6 @@ __global__ void __launch_bounds__(256) attn_fp8_pack_kernel(const __nv_bfloat16*
       }
       *reinterpret_cast<uint4*>(vp + (d >> 3) * 1024 + kc * 128 + (d & 7) * 16) = e4m3x16_div(x, sc, __frcp_rn(sc));
     }
-  }
-}
-
-// Pass 1 on 16 of this warp's score columns: max of acc * sk (packed multiplies, three-input max);
-// kMask drops the columns >= nv (keys past S in the last chunk).
-template <bool kMask>
-VF4_DEV float f8l_half_max(const uint32_t* v, const float4* sk4, int nv) {
-  float ma = -INFINITY, mb = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 k4 = sk4[i];
-    float a0, a1, a2, a3;
-    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), f32x2_pack(k4.x, k4.y)),
-                 &a0, &a1);
-    f32x2_unpack(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
-                           f32x2_pack(k4.z, k4.w)), &a2, &a3);
-    if (kMask) {
-      a0 = 4 * i < nv ? a0 : -INFINITY;
-      a1 = 4 * i + 1 < nv ? a1 : -INFINITY;
-      a2 = 4 * i + 2 < nv ? a2 : -INFINITY;
-      a3 = 4 * i + 3 < nv ? a3 : -INFINITY;
-    }
-    ma = max3f(ma, a0, a1);
-    mb = max3f(mb, a2, a3);
-  }
-  return fmaxf(ma, mb);
-}
-
-// Pass 2 on 16 of this warp's score columns: p = 2^(acc sk sq - max + log2 448) (sq2, nm2: sq and
-// log2 448 - max in both halves), row sums accumulated in two packed pairs; kMask zeroes the columns
-// >= nv.
-template <bool kMask>
-VF4_DEV void f8l_half_exp(const uint32_t* v, const float4* sk4, int nv, unsigned long long sq2,
-                          unsigned long long nm2, float* p, unsigned long long& l2a, unsigned long long& l2b) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 k4 = sk4[i];
-    float e0, e1, e2, e3;
-    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
-                                     f32x2_pack(k4.x, k4.y)), sq2, nm2), &e0, &e1);
-    f32x2_unpack(fma_f32x2(mul_f32x2(f32x2_pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
-                                     f32x2_pack(k4.z, k4.w)), sq2, nm2), &e2, &e3);
-    p[4 * i] = ex2_approx(e0);
-    p[4 * i + 1] = ex2_approx(e1);
-    p[4 * i + 2] = ex2_approx(e2);
-    p[4 * i + 3] = ex2_approx(e3);
-    if (kMask) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) p[4 * i + e] = 4 * i + e < nv ? p[4 * i + e] : 0.f;
-    }
-    l2a = add_f32x2(l2a, f32x2_pack(p[4 * i], p[4 * i + 1]));
-    l2b = add_f32x2(l2b, f32x2_pack(p[4 * i + 2], p[4 * i + 3]));
   }
 }
 
@@ -3621,6 +3637,10 @@ int vf4_attn_nvfp4_ex(const void* q, const void* k, const void* v, int64_t B, in
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H too large");
   const bool tensor = !(flags & VF4_ATTN_HEAD_GLOBALS);
   const bool fused = fused_ok(S, D);
+  // the fused kernel takes the row max of the raw scores, which is the softmax's max only for scale >= 0
+  if (fused && !(scale >= 0.f))
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: head dim 64 and S <= 320 need a scale >= 0 (got %g)",
+                (double)scale);
   if (!fused && B * H > 65535) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_nvfp4: B*H must be <= 65535 for S=%lld D=%lld",
                                            (long long)S, (long long)D);
   const bool packed = (flags & VF4_ATTN_PACKED) && packed_ok(S, D);
@@ -3688,6 +3708,8 @@ int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_
   if (!bf16_attn_ok(S, D))
     return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: needs head dim 64 and S <= 288 (S=%lld D=%lld)", (long long)S,
                 (long long)D);
+  if (!(scale >= 0.f))   // the row max of the raw scores is the softmax's max only for scale >= 0
+    return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: needs a scale >= 0 (got %g)", (double)scale);
   if (!q || !k || !v || !out) return fail(VF4_ERR_ARG, "vf4_attn_bf16: null pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
       stride_b % 8 || stride_h % 8 || stride_s % 8 || out_stride_b % 8 || out_stride_h % 8 || out_stride_s % 8)

@@ -413,8 +413,9 @@ def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     return out
 
 
-def bf16_kernel_ok(S: int, D: int) -> bool:
-    return D == 64 and 1 <= S <= 288
+def bf16_kernel_ok(S: int, D: int, scale: float = 1.0) -> bool:
+    """Shapes (and softmax scales: >= 0) the bf16 attention kernel takes."""
+    return D == 64 and 1 <= S <= 288 and scale >= 0.0
 
 
 def attention_bf16_packed_qkv(qkv: torch.Tensor, num_heads: int, scale: float,

@@ -86,7 +86,7 @@ def _attention_route(qkv: torch.Tensor, H: int, scaling: float, qk: str, pv: str
     D = C3 // (3 * H)
     if qk == "nvfp4" and pv == "nvfp4":
         return ops.attention_packed_qkv(qkv, H, scaling)
-    if qk == "none" and qkv.dtype == torch.bfloat16 and ops.bf16_kernel_ok(S, D):
+    if qk == "none" and qkv.dtype == torch.bfloat16 and ops.bf16_kernel_ok(S, D, scaling):
         # the reference's bf16 route (torch SDPA) on the tcgen05 kernel: exact softmax, fp32 accumulation,
         # output (B, S, H*D) read by the proj cast as it is; the kernel also returns max |out|, the amax of
         # the proj's dynamic activation cast
