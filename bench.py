@@ -533,6 +533,9 @@ def secondary(args, peaks: dict) -> dict:
                                         "BASELINE config 3: ViT-B/16 W4A4, batch 256, FP4 QK^T/PV attention in all 12 blocks")
     out["config3_vit_b16_bf16_attention"] = model_rate(dict(vit.VIT_B16), 256, "bf16", 10, peaks, 197,
                                                        "config 3 model with the bf16 attention route, for comparison")
+    out["config3_vit_b16_fp8_attention"] = model_rate(dict(vit.VIT_B16), 256, "fp8", 10, peaks, 197,
+                                                      "config 3 model with the FP8 attention route (the reference's "
+                                                      "enable_quant_attention default), for comparison")
     for attn in ("bf16", "fp8", "nvfp4"):
         out[f"config5_vit_h14_448_{attn}_attention"] = model_rate(
             dict(vit.VIT_H14_448), 64, attn, 5, peaks, 1025,
