@@ -304,16 +304,21 @@ def _bf16_errors(q, k, v, scale, got):
     return (got.float() - ref).abs().max().item(), (sdpa - ref).abs().max().item()
 
 
+@pytest.mark.parametrize("kernel", ["slots", "tiles"])
 @pytest.mark.parametrize("B,H,S", [(2, 3, 257), (1, 4, 197), (1, 1, 1), (1, 2, 48), (2, 2, 256), (1, 3, 129),
-                                   (1, 2, 136), (1, 2, 288), (1, 1, 264), (4, 16, 257),
-                                   (24, 16, 257), (20, 16, 197)])
-def test_bf16_kernel_matches_sdpa(B, H, S):
-    """The bf16 kernel (exact softmax, P rounded to bf16 for the PV MMA, like flash attention)
+                                   (1, 2, 136), (1, 2, 288), (1, 1, 264), (4, 16, 257), (2, 3, 258),
+                                   (1, 2, 2), (1, 3, 16), (2, 2, 128), (24, 16, 257), (20, 16, 197),
+                                   (40, 16, 258)])
+def test_bf16_kernel_matches_sdpa(B, H, S, kernel, monkeypatch):
+    """The bf16 kernels (exact softmax, P rounded to bf16 for the PV MMA, like flash attention)
     against fp32 attention of the same bf16 inputs: no worse than twice torch's own bf16 SDPA
     error (and 4e-3 absolute), on (B, H, S, D) operands and on the strided views of a packed qkv
-    projection; S = 129 .. 132 and 257 .. 260 run the per-row tail; 384 and 320 heads give every
-    CTA two or three heads (buffer reuse and barrier phases across heads)."""
+    projection.  "slots" is the two-slot kernel (S <= 258; keys 256 and 257 on the CUDA cores, query
+    rows past 256 in a third tile), "tiles" the single-slot one (S <= 288; S = 129 .. 132 and
+    257 .. 260 run its per-row tail).  384, 320 and 640 heads give every CTA several heads (buffer
+    reuse and barrier phases across heads)."""
     from vitfp4.nvfp4 import ops
+    monkeypatch.setenv("VF4_BF16_ATTN", kernel)
     D = 64
     torch.manual_seed(S + 7 * H)
     qkv = (torch.randn(B, S, 3 * H * D, device="cuda") * 1.5).bfloat16()
@@ -344,13 +349,16 @@ def test_bf16_kernel_rejects_unsupported_shapes():
     assert not ops.bf16_kernel_ok(300, 64) and not ops.bf16_kernel_ok(257, 80) and ops.bf16_kernel_ok(257, 64)
 
 
-@pytest.mark.parametrize("S,row", [(257, 5), (257, 256), (130, 129)])
-def test_bf16_kernel_amax_propagates_nan(S, row):
+@pytest.mark.parametrize("kernel", ["slots", "tiles"])
+@pytest.mark.parametrize("S,row", [(257, 5), (257, 256), (130, 129), (258, 257)])
+def test_bf16_kernel_amax_propagates_nan(S, row, kernel, monkeypatch):
     """A NaN in the attention output reaches the fused max |out| as NaN, as the reference's torch amax
     of the SDPA output would give it (a float max would drop it and hand the proj cast a finite global).
     One NaN in v makes every query row's output NaN in that head's column; row picks a tile row or a
-    tail row (S = 257 / 130 run the per-row tail for the last rows)."""
+    tail row (S = 257 / 130 run the single-slot kernel's per-row tail for the last rows; in the
+    two-slot kernel v rows 256 and 257 enter through the extra keys' K = 16 step)."""
     from vitfp4.nvfp4 import ops
+    monkeypatch.setenv("VF4_BF16_ATTN", kernel)
     B, H, D = 2, 3, 64
     torch.manual_seed(S)
     qkv = torch.randn(B, S, 3 * H * D, device="cuda").bfloat16()

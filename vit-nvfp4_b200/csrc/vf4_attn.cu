@@ -3369,7 +3369,6 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       epilogue(it - 1, prev_head, prev_t);
     }
     if (g.amax) {
-#pragma unroll
       const uint32_t m = __reduce_max_sync(0xffffffffu, max(out_max2 & 0xFFFFu, out_max2 >> 16) << 16);
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), m);
     }
@@ -3502,7 +3501,6 @@ __global__ void __launch_bounds__(kB16Warps * 32, 1)
       named_bar_sync(kTailBar, 32 * kB16TailWarps);   // tp / to are reused by the next head
     }
     if (g.amax) {
-#pragma unroll
       tail_max = __reduce_max_sync(0xffffffffu, tail_max);
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), tail_max);
     }
@@ -3534,6 +3532,622 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
   if (int st = smem_optin(attn_bf16_kernel, (int)g.total)) return st;
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
   attn_bf16_kernel<<<grid, kB16Warps * 32, g.total, s>>>(tq, tk, tv, tt, g);
+  return launch_status("vf4_attn_bf16");
+}
+
+// ---------------------------------------------------------------------------------------
+// bf16 attention, two-slot form (head dim 64, S <= 256 + kB16sExtraMax): the same result as
+// attn_bf16_kernel (exact whole-row softmax, P rounded to bf16 after the row sum, O / rowsum) with
+// the softmax of one 128-query tile overlapping the MMAs of the next.  TMEM holds two 256-column
+// slots; a slot carries one tile through S = Q K^T (fp32, keys < 256) -> P = 2^((s - max) c) as
+// bf16 pairs written back over columns whose scores are read -> O = P V (kind::f16 with A = P read
+// from tensor memory) into 64 dead score columns, so the two slots alternate between the tensor
+// core and the softmax warps.
+//   Each query row's keys are split between two warps of its lane quadrant: the first half's P
+//   pairs go, in key order, to the first columns of its own scores; the second half walks its
+//   chunks backwards and puts chunk u's pairs at columns 8 (nchunk + u), also scores of its own it
+//   has read, so neither half overwrites a score the other still needs.
+//   Keys past 256 (S = 257, 258) are scored on the CUDA cores by the first-half threads (64 fused
+//   multiply-adds per row and key) and enter PV as one more K = 16 step whose A operand (those
+//   keys' P, zero-padded) sits in shared memory.
+//   Query rows past 256 form a third tile whose rows are copied (by TMA) into lanes 0, 32, 64 and
+//   96 + e: each lane quadrant takes a quarter of the keys of every such row, and the epilogue adds
+//   the four partial rows.
+//   warp 0        TMA: K and V of the head (two buffers each, 128-byte swizzle), Q one 128-row tile
+//                 per slot
+//   warp 1        TMEM allocator and MMA issuer: S of tile i + 2 as soon as the epilogue has read
+//                 slot i % 2, O of tile i as soon as its P is written
+//   warps 2-9     softmax of slot 0 (warps 2-5 the first key half of lane quadrants 2, 3, 0, 1;
+//                 warps 6-9 the second half)
+//   warps 10-17   softmax of slot 1
+//   warps 18-21   epilogue: O / rowsum -> bf16, each thread storing its row, and max |out|
+// ---------------------------------------------------------------------------------------
+constexpr int kB16sExtraMax = 2, kB16sTailMax = kB16sExtraMax, kB16sWarps = 22;
+constexpr uint32_t kB16sBarPair = 1, kB16sBarTail = 9, kB16sBarEpi = 11;   // named barrier ids
+
+struct B16sGeom {
+  int B, H, S, D;
+  int nt, extra, tail, skp, nchunk, c1;   // query tiles per head, keys past 256, query rows past 256,
+                                          // MMA keys, their 16-key chunks, the first half's chunks
+  int o_col;                              // O columns of a full tile within its slot
+  int box_rows, nbox, heads, kv_hs;
+  float scale;
+  __nv_bfloat16* out;
+  int64_t osb, osh, oss;
+  float* amax;
+  uint32_t qb[2], kb[2], vb[2], pe[2], red, to, bar, total, kv_bytes;
+};
+
+static bool b16s_ok(int64_t S, int64_t D) { return D == 64 && S >= 1 && S <= 256 + kB16sExtraMax; }
+
+static B16sGeom make_b16s_geom(int64_t B, int64_t H, int64_t S, int64_t D, float scale) {
+  B16sGeom g{};
+  g.B = (int)B;
+  g.H = (int)H;
+  g.S = (int)S;
+  g.D = (int)D;
+  g.nt = (int)((S + 127) / 128);
+  g.extra = S > 256 ? (int)(S - 256) : 0;
+  g.tail = g.extra;                                             // rows past 256 = keys past 256
+  g.skp = (int)align_up(S < 256 ? S : 256, 16);
+  g.nchunk = g.skp / 16;
+  g.c1 = (g.nchunk + 1) / 2;
+  g.o_col = g.nchunk >= 8 ? 8 * g.c1 : 16 * g.nchunk;
+  const int rows = g.extra ? 272 : g.skp;                       // K / V rows held (>= S zero-filled)
+  g.nbox = rows <= 256 ? 1 : 2;
+  g.box_rows = (int)align_up((rows + g.nbox - 1) / g.nbox, 8);
+  g.heads = (int)(B * H);
+  g.scale = scale;
+  g.kv_bytes = (uint32_t)(g.nbox * g.box_rows) * 128u;         // a multiple of 1024
+  uint32_t o = 0;
+  for (int i = 0; i < 2; ++i) { g.qb[i] = o; o += 128u * 128u; }
+  for (int i = 0; i < 2; ++i) { g.kb[i] = o; o += g.kv_bytes; }
+  for (int i = 0; i < 2; ++i) { g.vb[i] = o; o += g.kv_bytes; }
+  for (int i = 0; i < 2; ++i) { g.pe[i] = o; o += g.extra ? 4096u : 0u; }   // extra keys' P: 128 x 16 bf16
+  g.red = o; o += 2u * 2u * 2u * 128u * 4u;          // [max, sum][slot][half][row]
+  g.to = o;  o += g.tail ? 4u * kB16sTailMax * 64u * 4u : 0u;   // tail rows' partial O [quadrant][row][64]
+  g.bar = o; o += 256;
+  g.total = o + 1024;
+  return g;
+}
+
+VF4_DEV void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 32 lanes x 8 consecutive 32-bit columns from 8 registers per thread.
+VF4_DEV void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+VF4_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMEM column of the P pairs of 16-key chunk u (the PV MMA's A operand) in a full tile's slot
+VF4_DEV uint32_t b16s_pcol(int u, int nchunk, int c1) { return (uint32_t)(u < c1 ? 8 * u : 8 * (nchunk + u)); }
+
+__global__ void __launch_bounds__(kB16sWarps * 32, 1)
+    attn_bf16_slots_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
+                           const B16sGeom g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (base - raw0);
+  const uint32_t bar = base + g.bar;
+  auto q_full = [&](int i) { return bar + 8u * i; };
+  auto q_free = [&](int i) { return bar + 16u + 8u * i; };
+  auto k_full = [&](int i) { return bar + 32u + 8u * i; };
+  auto k_free = [&](int i) { return bar + 48u + 8u * i; };
+  auto v_full = [&](int i) { return bar + 64u + 8u * i; };
+  auto v_free = [&](int i) { return bar + 80u + 8u * i; };
+  auto s_full = [&](int i) { return bar + 96u + 8u * i; };
+  auto p_full = [&](int i) { return bar + 112u + 8u * i; };
+  auto o_full = [&](int i) { return bar + 128u + 8u * i; };
+  auto o_free = [&](int i) { return bar + 144u + 8u * i; };
+  const uint32_t drain = bar + 160u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 168);
+  float* red_m = reinterpret_cast<float*>(gb + g.red);   // [slot][half][row] partial row maxima
+  float* red_l = red_m + 4 * 128;                         // [slot][half][row] partial row sums
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = g.nt, S = g.S;
+  // tiles of this CTA: head blockIdx.x + j * gridDim.x, query tile t, flat index i = j * nt + t
+  const int my_heads = (int)blockIdx.x < g.heads ? (g.heads - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int T = my_heads * nt;
+  int* err = &g_attn_err;
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full(i), 1);
+      mbar_init(q_free(i), g.extra ? 5u : 1u);               // QK commit (+ the first-half warps' Q reads)
+      mbar_init(k_full(i), 1);
+      mbar_init(k_free(i), g.extra ? 1u + 4u * (uint32_t)nt : 1u);
+      mbar_init(v_full(i), 1);
+      mbar_init(v_free(i), 1);
+      mbar_init(s_full(i), 1);
+      mbar_init(p_full(i), 8);
+      mbar_init(o_full(i), 1);
+      mbar_init(o_free(i), 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch(&tmQ);
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+    if (g.tail) tma_prefetch(&tmT);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  fence_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA loads
+    if (lane == 0) {
+      bool ok = true;
+      int i = 0;
+      for (int j = 0; j < my_heads && ok; ++j) {
+        const int head = (int)blockIdx.x + j * (int)gridDim.x;
+        const int b = head / g.H, h = head - b * g.H, hb = j & 1;
+        if (j >= 2 && (!mbar_wait(k_free(hb), (uint32_t)((j - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty) ||
+                       !mbar_wait(v_free(hb), (uint32_t)((j - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty)))
+          break;
+        mbar_arrive_expect_tx(k_full(hb), g.kv_bytes);
+        for (int x = 0; x < g.nbox; ++x) {
+          const int row = x * g.box_rows;
+          tma_load_4d(base + g.kb[hb] + (uint32_t)row * 128u, &tmK, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b,
+                      k_full(hb));
+        }
+        mbar_arrive_expect_tx(v_full(hb), g.kv_bytes);
+        for (int x = 0; x < g.nbox; ++x) {
+          const int row = x * g.box_rows;
+          tma_load_4d(base + g.vb[hb] + (uint32_t)row * 128u, &tmV, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b,
+                      v_full(hb));
+        }
+        for (int t = 0; t < nt; ++t, ++i) {
+          const int sl = i & 1;
+          if (i >= 2 && !mbar_wait(q_free(sl), (uint32_t)((i - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (t * 128 < 256) {
+            const int row = t * 128;
+            mbar_arrive_expect_tx(q_full(sl), 128u * 128u);
+            tma_load_4d(base + g.qb[sl], &tmQ, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, q_full(sl));
+          } else {   // rows 256.. (zero past S) into lanes 0, 32, 64 and 96 of the tile
+            mbar_arrive_expect_tx(q_full(sl), 4u * 1024u);
+            for (int x = 0; x < 4; ++x)
+              tma_load_4d(base + g.qb[sl] + 4096u * (uint32_t)x, &tmT, 0, g.kv_hs ? h : 256, g.kv_hs ? 256 : h, b,
+                          q_full(sl));
+          }
+        }
+      }
+      // no copy may still be writing shared memory when the CTA exits
+      for (int x = i - 2 < 0 ? 0 : i - 2; x < i; ++x)
+        mbar_wait(q_full(x & 1), (uint32_t)(x >> 1) & 1u, err, kDevErrTimeoutFull);
+      for (int x = my_heads - 2 < 0 ? 0 : my_heads - 2; x < my_heads; ++x) {
+        mbar_wait(k_full(x & 1), (uint32_t)(x >> 1) & 1u, err, kDevErrTimeoutFull);
+        mbar_wait(v_full(x & 1), (uint32_t)(x >> 1) & 1u, err, kDevErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    bool ok = true;
+    // S = Q K^T of tile i into slot i % 2, once the epilogue has read that slot's previous O
+    auto issue_qk = [&](int i) {
+      const int j = i / nt, t = i - j * nt, sl = i & 1, hb = j & 1;
+      if (i >= 2 && !mbar_wait(o_free(sl), (uint32_t)((i - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty)) return false;
+      if (t == 0 && !mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull)) return false;
+      if (!mbar_wait(q_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t qa = base + g.qb[sl], ka = base + g.kb[hb];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16(tmem + 256u * (uint32_t)sl, smem_desc(qa + 32u * kk, 16, 1024, 2), smem_desc(ka + 32u * kk, 16, 1024, 2),
+                  idesc_bf16((uint32_t)g.skp, false), kk > 0 ? 1u : 0u);
+        tc_commit(s_full(sl));
+        tc_commit(q_free(sl));
+        if (t == nt - 1) tc_commit(k_free(hb));
+      }
+      __syncwarp();
+      return true;
+    };
+    if (T > 0) ok = issue_qk(0);
+    if (ok && T > 1) ok = issue_qk(1);
+    for (int i = 0; i < T && ok; ++i) {
+      const int j = i / nt, t = i - j * nt, sl = i & 1, hb = j & 1;
+      if (!mbar_wait(p_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull) ||
+          (t == 0 && !mbar_wait(v_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull)))
+        break;
+      tc_fence_after();
+      if (lane == 0) {
+        const bool tail = t * 128 >= 256;
+        const uint32_t slot = tmem + 256u * (uint32_t)sl, va = base + g.vb[hb];
+        const uint32_t o_t = slot + (tail ? 128u : (uint32_t)g.o_col);
+        for (int kk = 0; kk < g.nchunk; ++kk)
+          mma_f16_tmem_a(o_t, slot + (tail ? 8u * (uint32_t)kk : b16s_pcol(kk, g.nchunk, g.c1)),
+                         smem_desc(va + 2048u * kk, 1024, 1024, 2), idesc_bf16(64, true), kk > 0 ? 1u : 0u);
+        if (g.extra)
+          mma_f16(o_t, smem_desc(base + g.pe[sl], 128, 256, 0), smem_desc(va + 2048u * 16u, 1024, 1024, 2),
+                  idesc_bf16(64, true), 1u);
+        tc_commit(o_full(sl));
+        if (t == nt - 1) tc_commit(v_free(hb));
+      }
+      __syncwarp();
+      if (i + 2 < T) ok = issue_qk(i + 2);
+    }
+    if (lane == 0) {
+      tc_commit(drain);
+      mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp < 18) {
+    // ------------------------------------------------------------ softmax: slot, key half, quadrant
+    const int sl = (warp - 2) >> 3, hh = ((warp - 2) >> 2) & 1, qd = warp & 3, r = qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t srow = tmem + lane_base + 256u * (uint32_t)sl;
+    float* my_m = red_m + (sl * 2) * 128;
+    float* my_l = red_l + (sl * 2) * 128;
+    const float c = g.scale * 1.4426950408889634f;
+    const int keys = S < 256 ? S : 256;   // keys scored by the MMA
+    const int nchunk = g.nchunk, c1 = g.c1;
+    const int nmine = hh ? nchunk - c1 : c1;   // chunks of this half: u = k (first) or nchunk - 1 - k
+    bool ok = true;
+    for (int i = sl; i < T; i += 2) {
+      const int j = i / nt, t = i - j * nt, hb = j & 1;
+      const bool tail = t * 128 >= 256;
+      const bool wact = t * 128 + qd * 32 < S || tail;   // any query row of this warp's lanes valid
+      if (ok) ok = mbar_wait(s_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull);
+      tc_fence_after();
+      // keys past 256 on the CUDA cores (first half; in the tail tile lane quadrant 0 only):
+      // s_e = q_r . k_(256 + e) in fp32
+      float se[kB16sExtraMax];
+#pragma unroll
+      for (int e = 0; e < kB16sExtraMax; ++e) se[e] = -INFINITY;
+      if (g.extra && hh == 0) {
+        if (ok) ok = mbar_wait(q_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull) &&
+                     mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
+        if (ok && wact && (!tail || qd == 0)) {
+          const uint8_t* qt = gb + g.qb[sl] + r * 128;
+#pragma unroll
+          for (int e = 0; e < kB16sExtraMax; ++e) {
+            if (e < g.extra) {
+              const int key = 256 + e;
+              const uint8_t* kt = gb + g.kb[hb] + key * 128;
+              unsigned long long acc0 = f32x2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+              for (int x = 0; x < 8; ++x) {
+                const uint4 a = *reinterpret_cast<const uint4*>(qt + ((x ^ (r & 7)) << 4));
+                const uint4 w = *reinterpret_cast<const uint4*>(kt + ((x ^ (key & 7)) << 4));
+                acc0 = fma_f32x2(bf16x2_to_f32x2(w.x), bf16x2_to_f32x2(a.x), acc0);
+                acc1 = fma_f32x2(bf16x2_to_f32x2(w.y), bf16x2_to_f32x2(a.y), acc1);
+                acc0 = fma_f32x2(bf16x2_to_f32x2(w.z), bf16x2_to_f32x2(a.z), acc0);
+                acc1 = fma_f32x2(bf16x2_to_f32x2(w.w), bf16x2_to_f32x2(a.w), acc1);
+              }
+              float a0, a1, b0, b1;
+              f32x2_unpack(acc0, &a0, &a1);
+              f32x2_unpack(acc1, &b0, &b1);
+              se[e] = (a0 + a1) + (b0 + b1);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {   // this warp is done with the tile's Q rows and the head's extra K rows
+          mbar_arrive(q_free(sl));
+          mbar_arrive(k_free(hb));
+        }
+      }
+      float m = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kB16sExtraMax; ++e) m = fmaxf(m, se[e]);
+      float lsum = 0.f;
+      const unsigned long long c2 = f32x2_pack(c, c);
+      // P = 2^((s - max) c) of 16 scores -> 8 bf16 pairs (zero past the valid keys), row sum in fp32
+      auto exp16 = [&](int u, const uint32_t* v, uint32_t* w, unsigned long long nmc2, unsigned long long& lsum2) {
+        float p[16];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          float x0, x1;
+          f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1])), c2, nmc2), &x0,
+                       &x1);
+          p[2 * x] = ex2_approx(x0);
+          p[2 * x + 1] = ex2_approx(x1);
+        }
+        if (16 * u + 16 > keys) {
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            if (16 * u + x >= keys) p[x] = 0.f;
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * x], p[2 * x + 1]));
+          __nv_bfloat162 pv = __floats2bfloat162_rn(p[2 * x], p[2 * x + 1]);
+          w[x] = *reinterpret_cast<uint32_t*>(&pv);
+        }
+      };
+      auto max16 = [&](int u, const uint32_t* v) {
+        if (16 * u + 16 <= keys) {
+#pragma unroll
+          for (int x = 0; x < 16; x += 2) m = max3f(m, __uint_as_float(v[x]), __uint_as_float(v[x + 1]));
+        } else {
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            if (16 * u + x < keys) m = fmaxf(m, __uint_as_float(v[x]));
+        }
+      };
+      if (!tail) {
+        // pass 1: this half's row max, combined with the other half's through shared memory
+        if (ok && wact && nmine > 0) {
+          uint32_t va[16], vb[16];
+          auto uk = [&](int k) { return hh ? nchunk - 1 - k : k; };
+          tmem_ld_32x32b_x16(srow + 16 * uk(0), va);
+          tmem_wait_ld();
+          reg_fence16(va);
+          for (int k = 0; k < nmine; k += 2) {
+            if (k + 1 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 1), vb);
+            max16(uk(k), va);
+            tmem_wait_ld();
+            reg_fence16(vb);
+            if (k + 1 < nmine) {
+              if (k + 2 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 2), va);
+              max16(uk(k + 1), vb);
+              tmem_wait_ld();
+              reg_fence16(va);
+            }
+          }
+        }
+        my_m[hh * 128 + r] = m;
+        named_bar_sync(kB16sBarPair + (uint32_t)(sl * 4 + qd), 64);
+        m = fmaxf(my_m[r], my_m[128 + r]);
+        // pass 2: P pairs of chunk u to columns b16s_pcol(u) -- the first half walks forwards, the
+        // second backwards, each overwriting only scores it has already read
+        if (ok && wact && nmine > 0) {
+          const float nmc = -m * c;
+          const unsigned long long nmc2 = f32x2_pack(nmc, nmc);
+          unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
+          uint32_t va[16], vb[16], w[8];
+          auto uk = [&](int k) { return hh ? nchunk - 1 - k : k; };
+          tmem_ld_32x32b_x16(srow + 16 * uk(0), va);
+          tmem_wait_ld();
+          reg_fence16(va);
+          for (int k = 0; k < nmine; k += 2) {
+            if (k + 1 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 1), vb);
+            exp16(uk(k), va, w, nmc2, lsum2);
+            tmem_st_32x32b_x8(srow + b16s_pcol(uk(k), nchunk, c1), w);
+            tmem_wait_ld();
+            reg_fence16(vb);
+            if (k + 1 < nmine) {
+              if (k + 2 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 2), va);
+              exp16(uk(k + 1), vb, w, nmc2, lsum2);
+              tmem_st_32x32b_x8(srow + b16s_pcol(uk(k + 1), nchunk, c1), w);
+              tmem_wait_ld();
+              reg_fence16(va);
+            }
+          }
+          float l0, l1;
+          f32x2_unpack(lsum2, &l0, &l1);
+          lsum = l0 + l1;
+          if (g.extra && hh == 0) {
+            // the extra keys' P row (zero past S) as the A operand of one more K = 16 step:
+            // K-major core matrices, 8-row groups 256 bytes apart, the two 8-key halves 128 apart
+            uint32_t pw[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) pw[x] = 0u;
+#pragma unroll
+            for (int e = 0; e < kB16sExtraMax; ++e) {
+              if (e < g.extra) {
+                const float pe = ex2_approx(fmaf(se[e], c, nmc));
+                lsum += pe;
+                const uint32_t hbits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(pe));
+                pw[e >> 1] |= (e & 1) ? hbits << 16 : hbits;
+              }
+            }
+            uint8_t* prow = gb + g.pe[sl] + (uint32_t)(r >> 3) * 256u + (uint32_t)(r & 7) * 16u;
+            *reinterpret_cast<uint4*>(prow) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+            *reinterpret_cast<uint4*>(prow + 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+          }
+          tmem_wait_st();
+        }
+        my_l[hh * 128 + r] = lsum;
+      } else if (hh == 0) {
+        // tail tile: lanes 32 q + e hold query row 256 + e; quadrant q scores keys [64 q, 64 q + 64)
+        // (q = 0 also the extra keys) and writes P in key order, zero outside its quarter
+        if (ok) {
+          {
+            uint32_t va[16], vb[16];
+            tmem_ld_32x32b_x16(srow + 16 * (4 * qd), va);
+            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 1), vb);
+            tmem_wait_ld();
+            reg_fence16(va);
+            reg_fence16(vb);
+            max16(4 * qd, va);
+            max16(4 * qd + 1, vb);
+            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 2), va);
+            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 3), vb);
+            tmem_wait_ld();
+            reg_fence16(va);
+            reg_fence16(vb);
+            max16(4 * qd + 2, va);
+            max16(4 * qd + 3, vb);
+          }
+          my_m[r] = m;
+          named_bar_sync(kB16sBarTail + (uint32_t)sl, 128);
+          m = fmaxf(fmaxf(my_m[lane], my_m[32 + lane]), fmaxf(my_m[64 + lane], my_m[96 + lane]));
+          const float nmc = -m * c;
+          const unsigned long long nmc2 = f32x2_pack(nmc, nmc);
+          unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
+          // chunk u = 4 q + x: its pairs go to columns 8u, which for q = 0 are scores of chunk u / 2
+          // (read), for q > 0 scores outside this thread's quarter; the zeros follow once every
+          // score of the quarter has been read
+#pragma unroll 1
+          for (int x = 0; x < 4; ++x) {
+            uint32_t v[16], w[8];
+            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + x), v);
+            tmem_wait_ld();
+            reg_fence16(v);
+            exp16(4 * qd + x, v, w, nmc2, lsum2);
+            tmem_st_32x32b_x8(srow + 8u * (uint32_t)(4 * qd + x), w);
+          }
+          uint32_t zero[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) zero[x] = 0u;
+          for (int u = 0; u < nchunk; ++u)
+            if (u < 4 * qd || u >= 4 * qd + 4) tmem_st_32x32b_x8(srow + 8u * (uint32_t)u, zero);
+          float l0, l1;
+          f32x2_unpack(lsum2, &l0, &l1);
+          lsum = l0 + l1;
+          if (g.extra) {
+            uint32_t pw[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) pw[x] = 0u;
+            if (qd == 0) {
+#pragma unroll
+              for (int e = 0; e < kB16sExtraMax; ++e) {
+                if (e < g.extra) {
+                  const float pe = ex2_approx(fmaf(se[e], c, nmc));
+                  lsum += pe;
+                  const uint32_t hbits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(pe));
+                  pw[e >> 1] |= (e & 1) ? hbits << 16 : hbits;
+                }
+              }
+            }
+            uint8_t* prow = gb + g.pe[sl] + (uint32_t)(r >> 3) * 256u + (uint32_t)(r & 7) * 16u;
+            *reinterpret_cast<uint4*>(prow) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+            *reinterpret_cast<uint4*>(prow + 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+          }
+          tmem_wait_st();
+        } else {
+          named_bar_sync(kB16sBarTail + (uint32_t)sl, 128);
+        }
+        my_l[r] = lsum;
+      }
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(sl));
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue: O / rowsum -> bf16
+    const int qd = warp & 3, r = qd * 32 + lane, et = threadIdx.x - 18 * 32;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    float* tail_o = reinterpret_cast<float*>(gb + g.to);   // [quadrant][tail row][64]
+    // max |out| as bf16 magnitude bits in two 16-bit lanes: unsigned order of non-negative bf16
+    // bits is numeric order and a NaN (0x7FC0) sorts above +inf, so a NaN output reaches the amax
+    // as torch's amax would give it
+    uint32_t out_max2 = 0;
+    bool ok = true;
+    for (int i = 0; i < T; ++i) {
+      const int j = i / nt, t = i - j * nt, sl = i & 1;
+      const int head = (int)blockIdx.x + j * (int)gridDim.x;
+      const int b = head / g.H, h = head - b * g.H, row = t * 128 + r;
+      const bool tail = t * 128 >= 256;
+      const bool wact = t * 128 + qd * 32 < S || tail;
+      if (ok) ok = mbar_wait(o_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutTmem) &&
+                   mbar_wait(p_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutTmem);
+      tc_fence_after();
+      const float* sl_l = red_l + (sl * 2) * 128;
+      float lsum;
+      if (!tail) {
+        lsum = sl_l[r] + sl_l[128 + r];
+      } else {   // this thread's tail row (et / 64) sums the four quadrants' partial sums
+        const int e = (et >> 6) & 1;
+        lsum = (sl_l[e] + sl_l[32 + e]) + (sl_l[64 + e] + sl_l[96 + e]);
+      }
+      const float f = 1.0f / lsum;
+      __nv_bfloat16* orow = g.out + (int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss;
+      const bool store = ok && wact && !tail && row < S;
+      // O in two 32-column halves; the slot is released once both are in registers
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ov[32];
+        if (ok && wact) {
+          tmem_ld_32x32b_x32(tmem + lane_base + 256u * (uint32_t)sl + (tail ? 128u : (uint32_t)g.o_col) + 32u * half, ov);
+          tmem_wait_ld();
+        }
+        if (half == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free(sl));
+        }
+        if (store) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t w[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+              __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[8 * cc + 2 * x]) * f,
+                                                        __uint_as_float(ov[8 * cc + 2 * x + 1]) * f);
+              w[x] = *reinterpret_cast<uint32_t*>(&hv);
+              out_max2 = umax_u16x2(out_max2, w[x] & 0x7FFF7FFFu);
+            }
+            *reinterpret_cast<uint4*>(orow + 32 * half + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        if (ok && tail && lane < g.tail) {
+#pragma unroll
+          for (int d = 0; d < 32; ++d)
+            tail_o[(qd * kB16sTailMax + lane) * 64 + 32 * half + d] = __uint_as_float(ov[d]);
+        }
+      }
+      if (tail) {
+        // the tail rows' four partial outputs (lanes e of each quadrant) through shared memory; every
+        // epilogue warp reaches both barriers, whatever its wait results
+        named_bar_sync(kB16sBarEpi, 128);
+        if (ok && et < g.tail * 64) {
+          const int e = et >> 6, d = et & 63;
+          const float o = (tail_o[(0 * kB16sTailMax + e) * 64 + d] + tail_o[(1 * kB16sTailMax + e) * 64 + d]) +
+                          (tail_o[(2 * kB16sTailMax + e) * 64 + d] + tail_o[(3 * kB16sTailMax + e) * 64 + d]);
+          const __nv_bfloat16 ob = __float2bfloat16_rn(o * f);
+          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)(256 + e) * g.oss + d] = ob;
+          out_max2 = umax_u16x2(out_max2, (uint32_t)(__bfloat16_as_ushort(ob) & 0x7FFFu));
+        }
+        named_bar_sync(kB16sBarEpi, 128);   // tail_o is written again at the next tail tile
+      }
+    }
+    if (g.amax) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, max(out_max2 & 0xFFFFu, out_max2 >> 16) << 16);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), m);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static int launch_bf16_slots(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t S, int64_t D,
+                             int64_t sb, int64_t sh, int64_t ss, float scale, void* out, int64_t osb, int64_t osh,
+                             int64_t oss, float* amax, cudaStream_t s) {
+  B16sGeom g = make_b16s_geom(B, H, S, D, scale);
+  g.amax = amax;
+  if (amax && cudaMemsetAsync(amax, 0, sizeof(float), s) != cudaSuccess)
+    return fail(VF4_ERR_CUDA, "vf4_attn_bf16: amax reset failed");
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.osb = osb;
+  g.osh = osh;
+  g.oss = oss;
+  g.kv_hs = sh < ss;
+  FusedGeom fg = make_fused_geom(B, H, S, D, scale);   // the head-view maps take D, S, H, B from it
+  CUtensorMap tq, tk, tv, tt;
+  memset(&tt, 0, sizeof(tt));
+  if (int st = make_head_map(&tq, q, fg, sb, sh, ss, 128, g.kv_hs)) return st;
+  if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
+  if (g.tail && make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return VF4_ERR_CUDA;
+  if (int st = smem_optin(attn_bf16_slots_kernel, (int)g.total)) return st;
+  const int grid = g.heads < num_sms() ? g.heads : num_sms();
+  attn_bf16_slots_kernel<<<grid, kB16sWarps * 32, g.total, s>>>(tq, tk, tv, tt, g);
   return launch_status("vf4_attn_bf16");
 }
 
@@ -3717,6 +4331,11 @@ int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: B*H too large");
   if (out_amax && (reinterpret_cast<uintptr_t>(out_amax) & 3u))
     return fail(VF4_ERR_ALIGN, "vf4_attn_bf16: out_amax must be 4-byte aligned");
+  // VF4_BF16_ATTN=slots selects the two-slot kernel (S <= 258), otherwise the single-slot one runs
+  const char* mode = getenv("VF4_BF16_ATTN");
+  if (b16s_ok(S, D) && mode && mode[0] == 's')
+    return launch_bf16_slots(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b,
+                             out_stride_h, out_stride_s, out_amax, reinterpret_cast<cudaStream_t>(stream));
   return launch_bf16(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
                      out_stride_s, out_amax, reinterpret_cast<cudaStream_t>(stream));
 }
