@@ -339,6 +339,28 @@ def test_bf16_kernel_matches_sdpa(B, H, S, kernel, monkeypatch):
     assert torch.equal(got2, got) and torch.equal(am, ops.amax(got))
 
 
+@pytest.mark.parametrize("kernel", ["slots", "tiles"])
+@pytest.mark.parametrize("S,late", [(256, 200), (257, 131), (197, 190), (258, 257)])
+def test_bf16_kernel_late_row_max(S, late, kernel, monkeypatch):
+    """A key far past the first 16 whose score exceeds every earlier one by more than 2^32 after
+    scaling: the two-slot kernel's running row max jumps there and the P chunks already written are
+    rescaled in place (key 257 of S = 258 is one of the keys scored on the CUDA cores)."""
+    from vitfp4.nvfp4 import ops
+    monkeypatch.setenv("VF4_BF16_ATTN", kernel)
+    B, H, D = 2, 2, 64
+    torch.manual_seed(S + late)
+    qkv = torch.randn(B, S, 3 * H * D, device="cuda") * 0.5
+    qkv[:, :, 0] = 12.0                     # q of head 0: a large first coordinate in every row
+    qkv[:, late, H * D] = 18.0              # k of head 0 at the late key: q . k ~ 216 there
+    qkv = qkv.bfloat16()
+    scale = D ** -0.5
+    got = ops.attention_bf16_packed_qkv(qkv, H, scale)
+    q, k, v = qkv.reshape(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+    err, ref_err = _bf16_errors(q, k, v, scale, got.reshape(B, S, H, D).transpose(1, 2))
+    assert torch.isfinite(got).all()
+    assert err <= max(2 * ref_err, 4e-3), (err, ref_err)
+
+
 def test_bf16_kernel_rejects_unsupported_shapes():
     from vitfp4 import _lib
     from vitfp4.nvfp4 import ops

@@ -3539,43 +3539,47 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
 // bf16 attention, two-slot form (head dim 64, S <= 256 + kB16sExtraMax): the same result as
 // attn_bf16_kernel (exact whole-row softmax, P rounded to bf16 after the row sum, O / rowsum) with
 // the softmax of one 128-query tile overlapping the MMAs of the next.  TMEM holds two 256-column
-// slots; a slot carries one tile through S = Q K^T (fp32, keys < 256) -> P = 2^((s - max) c) as
-// bf16 pairs written back over columns whose scores are read -> O = P V (kind::f16 with A = P read
-// from tensor memory) into 64 dead score columns, so the two slots alternate between the tensor
-// core and the softmax warps.
-//   Each query row's keys are split between two warps of its lane quadrant: the first half's P
-//   pairs go, in key order, to the first columns of its own scores; the second half walks its
-//   chunks backwards and puts chunk u's pairs at columns 8 (nchunk + u), also scores of its own it
-//   has read, so neither half overwrites a score the other still needs.
-//   Keys past 256 (S = 257, 258) are scored on the CUDA cores by the first-half threads (64 fused
-//   multiply-adds per row and key) and enter PV as one more K = 16 step whose A operand (those
-//   keys' P, zero-padded) sits in shared memory.
-//   Query rows past 256 form a third tile whose rows are copied (by TMA) into lanes 0, 32, 64 and
-//   96 + e: each lane quadrant takes a quarter of the keys of every such row, and the epilogue adds
-//   the four partial rows.
-//   warp 0        TMA: K and V of the head (two buffers each, 128-byte swizzle), Q one 128-row tile
-//                 per slot
-//   warp 1        TMEM allocator and MMA issuer: S of tile i + 2 as soon as the epilogue has read
-//                 slot i % 2, O of tile i as soon as its P is written
-//   warps 2-9     softmax of slot 0 (warps 2-5 the first key half of lane quadrants 2, 3, 0, 1;
-//                 warps 6-9 the second half)
-//   warps 10-17   softmax of slot 1
-//   warps 18-21   epilogue: O / rowsum -> bf16, each thread storing its row, and max |out|
+// slots; a slot carries one tile through
+//   S = Q K^T (fp32, keys < 256)  ->  P = 2^((s - max) c) as bf16 pairs written back over the first
+//   128 columns of S  ->  O = P V (kind::f16 with A = P read from tensor memory) into columns
+//   128..191 of the slot, whose scores the softmax has finished with
+// so the two slots alternate between the tensor core and the softmax warps.  Keys past 256 (S =
+// 257, 258) are scored on the CUDA cores by the softmax threads (64 fused multiply-adds per row and
+// key) and enter PV as one more K = 16 step whose A operand (those keys' P, zero-padded) sits in
+// shared memory.  Query rows past 256 (one or two) are computed whole on the CUDA cores by four
+// warps of their own, from the head's K and V in shared memory, while the tiles run: a 128-row
+// MMA tile for them would cost a full slot cycle.
+//   warp 0       TMA: K (with the query rows past 256) and V of the head (two buffers each,
+//                128-byte swizzle), Q one 128-row tile per slot
+//   warp 1       TMEM allocator and MMA issuer: S of tile i + 2 as soon as the epilogue has read
+//                slot i % 2, O of tile i as soon as its P is written
+//   warps 2-5    softmax of slot 0 (one thread per query row, lane quadrant warp % 4)
+//   warps 6-9    softmax of slot 1
+//   warps 10-13  epilogue: O / rowsum -> bf16, each thread storing its row, and max |out|
+//   warps 14-17  the rows past 256 (idle when S <= 256)
 // ---------------------------------------------------------------------------------------
-constexpr int kB16sExtraMax = 2, kB16sTailMax = kB16sExtraMax, kB16sWarps = 22;
-constexpr uint32_t kB16sBarPair = 1, kB16sBarTail = 9, kB16sBarEpi = 11;   // named barrier ids
+constexpr int kB16sExtraMax = 2, kB16sWarps = 18;
+#ifndef VF4_B16S_ROLES
+#define VF4_B16S_ROLES 0
+#endif
+// first warp of each role (the warp scheduler favours lower warp ids when several are ready)
+constexpr int kB16sSoftW = VF4_B16S_ROLES == 0 ? 2 : VF4_B16S_ROLES == 1 ? 6 : 10;
+constexpr int kB16sEpiW = VF4_B16S_ROLES == 0 ? 10 : VF4_B16S_ROLES == 1 ? 14 : 2;
+constexpr int kB16sTailW = VF4_B16S_ROLES == 0 ? 14 : VF4_B16S_ROLES == 1 ? 2 : 6;
+constexpr uint32_t kB16sBarTail = 1;   // named barrier id of the tail warps
+// Working storage of the rows past 256 (floats): q [2][64], p [2][272], o partials [4][2][64],
+// per-warp maxima and sums [4][2][2]
+constexpr uint32_t kB16sTailBytes = (2 * 64 + 2 * 272 + 4 * 2 * 64 + 4 * 2 * 2) * 4;
 
 struct B16sGeom {
   int B, H, S, D;
-  int nt, extra, tail, skp, nchunk, c1;   // query tiles per head, keys past 256, query rows past 256,
-                                          // MMA keys, their 16-key chunks, the first half's chunks
-  int o_col;                              // O columns of a full tile within its slot
+  int nt, extra, skp;      // MMA query tiles per head, keys (= query rows) past 256, MMA keys
   int box_rows, nbox, heads, kv_hs;
   float scale;
   __nv_bfloat16* out;
   int64_t osb, osh, oss;
   float* amax;
-  uint32_t qb[2], kb[2], vb[2], pe[2], red, to, bar, total, kv_bytes;
+  uint32_t qb[2], kb[2], vb[2], pe[2], qt[2], tw, red, bar, total, kv_bytes;
 };
 
 static bool b16s_ok(int64_t S, int64_t D) { return D == 64 && S >= 1 && S <= 256 + kB16sExtraMax; }
@@ -3586,13 +3590,9 @@ static B16sGeom make_b16s_geom(int64_t B, int64_t H, int64_t S, int64_t D, float
   g.H = (int)H;
   g.S = (int)S;
   g.D = (int)D;
-  g.nt = (int)((S + 127) / 128);
+  g.nt = (int)(((S < 256 ? S : 256) + 127) / 128);
   g.extra = S > 256 ? (int)(S - 256) : 0;
-  g.tail = g.extra;                                             // rows past 256 = keys past 256
   g.skp = (int)align_up(S < 256 ? S : 256, 16);
-  g.nchunk = g.skp / 16;
-  g.c1 = (g.nchunk + 1) / 2;
-  g.o_col = g.nchunk >= 8 ? 8 * g.c1 : 16 * g.nchunk;
   const int rows = g.extra ? 272 : g.skp;                       // K / V rows held (>= S zero-filled)
   g.nbox = rows <= 256 ? 1 : 2;
   g.box_rows = (int)align_up((rows + g.nbox - 1) / g.nbox, 8);
@@ -3604,8 +3604,9 @@ static B16sGeom make_b16s_geom(int64_t B, int64_t H, int64_t S, int64_t D, float
   for (int i = 0; i < 2; ++i) { g.kb[i] = o; o += g.kv_bytes; }
   for (int i = 0; i < 2; ++i) { g.vb[i] = o; o += g.kv_bytes; }
   for (int i = 0; i < 2; ++i) { g.pe[i] = o; o += g.extra ? 4096u : 0u; }   // extra keys' P: 128 x 16 bf16
-  g.red = o; o += 2u * 2u * 2u * 128u * 4u;          // [max, sum][slot][half][row]
-  g.to = o;  o += g.tail ? 4u * kB16sTailMax * 64u * 4u : 0u;   // tail rows' partial O [quadrant][row][64]
+  for (int i = 0; i < 2; ++i) { g.qt[i] = o; o += g.extra ? 1024u : 0u; }   // query rows 256.. (8-row box)
+  g.tw = o;  o += g.extra ? kB16sTailBytes : 0u;                            // their working storage
+  g.red = o; o += 2u * 128u * 4u;                                          // row sums per slot
   g.bar = o; o += 256;
   g.total = o + 1024;
   return g;
@@ -3628,9 +3629,6 @@ VF4_DEV void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t* r) {
 
 VF4_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// TMEM column of the P pairs of 16-key chunk u (the PV MMA's A operand) in a full tile's slot
-VF4_DEV uint32_t b16s_pcol(int u, int nchunk, int c1) { return (uint32_t)(u < c1 ? 8 * u : 8 * (nchunk + u)); }
-
 __global__ void __launch_bounds__(kB16sWarps * 32, 1)
     attn_bf16_slots_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
@@ -3652,8 +3650,6 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
   auto o_free = [&](int i) { return bar + 144u + 8u * i; };
   const uint32_t drain = bar + 160u;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 168);
-  float* red_m = reinterpret_cast<float*>(gb + g.red);   // [slot][half][row] partial row maxima
-  float* red_l = red_m + 4 * 128;                         // [slot][half][row] partial row sums
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = g.nt, S = g.S;
   // tiles of this CTA: head blockIdx.x + j * gridDim.x, query tile t, flat index i = j * nt + t
@@ -3664,13 +3660,15 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(q_full(i), 1);
-      mbar_init(q_free(i), g.extra ? 5u : 1u);               // QK commit (+ the first-half warps' Q reads)
+      mbar_init(q_free(i), g.extra ? 5u : 1u);               // QK commit (+ the softmax warps' Q reads)
       mbar_init(k_full(i), 1);
-      mbar_init(k_free(i), g.extra ? 1u + 4u * (uint32_t)nt : 1u);
+      // K: the last QK commit, the softmax warps' extra-key reads and the epilogue warps' rows past
+      // 256; V: the last PV commit and those rows
+      mbar_init(k_free(i), g.extra ? 1u + 4u * (uint32_t)nt + 4u : 1u);
       mbar_init(v_full(i), 1);
-      mbar_init(v_free(i), 1);
+      mbar_init(v_free(i), g.extra ? 5u : 1u);
       mbar_init(s_full(i), 1);
-      mbar_init(p_full(i), 8);
+      mbar_init(p_full(i), 4);
       mbar_init(o_full(i), 1);
       mbar_init(o_free(i), 4);
     }
@@ -3679,7 +3677,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
-    if (g.tail) tma_prefetch(&tmT);
+    if (g.extra) tma_prefetch(&tmT);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
@@ -3702,12 +3700,14 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
         if (j >= 2 && (!mbar_wait(k_free(hb), (uint32_t)((j - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty) ||
                        !mbar_wait(v_free(hb), (uint32_t)((j - 2) >> 1) & 1u, err, kDevErrTimeoutEmpty)))
           break;
-        mbar_arrive_expect_tx(k_full(hb), g.kv_bytes);
+        mbar_arrive_expect_tx(k_full(hb), g.kv_bytes + (g.extra ? 1024u : 0u));
         for (int x = 0; x < g.nbox; ++x) {
           const int row = x * g.box_rows;
           tma_load_4d(base + g.kb[hb] + (uint32_t)row * 128u, &tmK, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b,
                       k_full(hb));
         }
+        if (g.extra)   // query rows 256.. (zero past S)
+          tma_load_4d(base + g.qt[hb], &tmT, 0, g.kv_hs ? h : 256, g.kv_hs ? 256 : h, b, k_full(hb));
         mbar_arrive_expect_tx(v_full(hb), g.kv_bytes);
         for (int x = 0; x < g.nbox; ++x) {
           const int row = x * g.box_rows;
@@ -3720,16 +3720,9 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
             ok = false;
             break;
           }
-          if (t * 128 < 256) {
-            const int row = t * 128;
-            mbar_arrive_expect_tx(q_full(sl), 128u * 128u);
-            tma_load_4d(base + g.qb[sl], &tmQ, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, q_full(sl));
-          } else {   // rows 256.. (zero past S) into lanes 0, 32, 64 and 96 of the tile
-            mbar_arrive_expect_tx(q_full(sl), 4u * 1024u);
-            for (int x = 0; x < 4; ++x)
-              tma_load_4d(base + g.qb[sl] + 4096u * (uint32_t)x, &tmT, 0, g.kv_hs ? h : 256, g.kv_hs ? 256 : h, b,
-                          q_full(sl));
-          }
+          const int row = t * 128;
+          mbar_arrive_expect_tx(q_full(sl), 128u * 128u);
+          tma_load_4d(base + g.qb[sl], &tmQ, 0, g.kv_hs ? h : row, g.kv_hs ? row : h, b, q_full(sl));
         }
       }
       // no copy may still be writing shared memory when the CTA exits
@@ -3772,14 +3765,13 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
         break;
       tc_fence_after();
       if (lane == 0) {
-        const bool tail = t * 128 >= 256;
         const uint32_t slot = tmem + 256u * (uint32_t)sl, va = base + g.vb[hb];
-        const uint32_t o_t = slot + (tail ? 128u : (uint32_t)g.o_col);
-        for (int kk = 0; kk < g.nchunk; ++kk)
-          mma_f16_tmem_a(o_t, slot + (tail ? 8u * (uint32_t)kk : b16s_pcol(kk, g.nchunk, g.c1)),
-                         smem_desc(va + 2048u * kk, 1024, 1024, 2), idesc_bf16(64, true), kk > 0 ? 1u : 0u);
+        const int nk = g.skp / 16;
+        for (int kk = 0; kk < nk; ++kk)
+          mma_f16_tmem_a(slot + 128u, slot + 8u * (uint32_t)kk, smem_desc(va + 2048u * kk, 1024, 1024, 2),
+                         idesc_bf16(64, true), kk > 0 ? 1u : 0u);
         if (g.extra)
-          mma_f16(o_t, smem_desc(base + g.pe[sl], 128, 256, 0), smem_desc(va + 2048u * 16u, 1024, 1024, 2),
+          mma_f16(slot + 128u, smem_desc(base + g.pe[sl], 128, 256, 0), smem_desc(va + 2048u * 16u, 1024, 1024, 2),
                   idesc_bf16(64, true), 1u);
         tc_commit(o_full(sl));
         if (t == nt - 1) tc_commit(v_free(hb));
@@ -3792,33 +3784,29 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       mbar_wait(drain, 0, err, kDevErrTimeoutDrain);
     }
     __syncwarp();
-  } else if (warp < 18) {
-    // ------------------------------------------------------------ softmax: slot, key half, quadrant
-    const int sl = (warp - 2) >> 3, hh = ((warp - 2) >> 2) & 1, qd = warp & 3, r = qd * 32 + lane;
+  } else if (warp >= kB16sSoftW && warp < kB16sSoftW + 8) {
+    // ------------------------------------------------------------ softmax, one slot per warp group
+    const int sl = (warp - kB16sSoftW) >> 2, qd = warp & 3, r = qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t srow = tmem + lane_base + 256u * (uint32_t)sl;
-    float* my_m = red_m + (sl * 2) * 128;
-    float* my_l = red_l + (sl * 2) * 128;
+    float* red_l = reinterpret_cast<float*>(gb + g.red) + sl * 128;
     const float c = g.scale * 1.4426950408889634f;
     const int keys = S < 256 ? S : 256;   // keys scored by the MMA
-    const int nchunk = g.nchunk, c1 = g.c1;
-    const int nmine = hh ? nchunk - c1 : c1;   // chunks of this half: u = k (first) or nchunk - 1 - k
+    const int nchunk = g.skp / 16;
     bool ok = true;
     for (int i = sl; i < T; i += 2) {
       const int j = i / nt, t = i - j * nt, hb = j & 1;
-      const bool tail = t * 128 >= 256;
-      const bool wact = t * 128 + qd * 32 < S || tail;   // any query row of this warp's lanes valid
+      const bool wact = t * 128 + qd * 32 < S;   // any query row of this warp's quadrant valid
       if (ok) ok = mbar_wait(s_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull);
       tc_fence_after();
-      // keys past 256 on the CUDA cores (first half; in the tail tile lane quadrant 0 only):
-      // s_e = q_r . k_(256 + e) in fp32
+      // keys past 256 on the CUDA cores: s_e = q_r . k_(256 + e) in fp32
       float se[kB16sExtraMax];
 #pragma unroll
       for (int e = 0; e < kB16sExtraMax; ++e) se[e] = -INFINITY;
-      if (g.extra && hh == 0) {
+      if (g.extra) {
         if (ok) ok = mbar_wait(q_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull) &&
                      mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
-        if (ok && wact && (!tail || qd == 0)) {
+        if (ok && wact) {
           const uint8_t* qt = gb + g.qb[sl] + r * 128;
 #pragma unroll
           for (int e = 0; e < kB16sExtraMax; ++e) {
@@ -3848,200 +3836,121 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
           mbar_arrive(k_free(hb));
         }
       }
-      float m = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < kB16sExtraMax; ++e) m = fmaxf(m, se[e]);
       float lsum = 0.f;
-      const unsigned long long c2 = f32x2_pack(c, c);
-      // P = 2^((s - max) c) of 16 scores -> 8 bf16 pairs (zero past the valid keys), row sum in fp32
-      auto exp16 = [&](int u, const uint32_t* v, uint32_t* w, unsigned long long nmc2, unsigned long long& lsum2) {
-        float p[16];
+      if (ok && wact) {
+        // pass 1: row max over the valid keys
+        float m = -INFINITY;
 #pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          float x0, x1;
-          f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1])), c2, nmc2), &x0,
-                       &x1);
-          p[2 * x] = ex2_approx(x0);
-          p[2 * x + 1] = ex2_approx(x1);
-        }
-        if (16 * u + 16 > keys) {
+        for (int e = 0; e < kB16sExtraMax; ++e) m = fmaxf(m, se[e]);
+        auto max16 = [&](int u, const uint32_t* v) {
+          if (16 * u + 16 <= keys) {
 #pragma unroll
-          for (int x = 0; x < 16; ++x)
-            if (16 * u + x >= keys) p[x] = 0.f;
-        }
+            for (int x = 0; x < 16; x += 2) m = max3f(m, __uint_as_float(v[x]), __uint_as_float(v[x + 1]));
+          } else {
 #pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * x], p[2 * x + 1]));
-          __nv_bfloat162 pv = __floats2bfloat162_rn(p[2 * x], p[2 * x + 1]);
-          w[x] = *reinterpret_cast<uint32_t*>(&pv);
-        }
-      };
-      auto max16 = [&](int u, const uint32_t* v) {
-        if (16 * u + 16 <= keys) {
-#pragma unroll
-          for (int x = 0; x < 16; x += 2) m = max3f(m, __uint_as_float(v[x]), __uint_as_float(v[x + 1]));
-        } else {
-#pragma unroll
-          for (int x = 0; x < 16; ++x)
-            if (16 * u + x < keys) m = fmaxf(m, __uint_as_float(v[x]));
-        }
-      };
-      if (!tail) {
-        // pass 1: this half's row max, combined with the other half's through shared memory
-        if (ok && wact && nmine > 0) {
+            for (int x = 0; x < 16; ++x)
+              if (16 * u + x < keys) m = fmaxf(m, __uint_as_float(v[x]));
+          }
+        };
+        {
           uint32_t va[16], vb[16];
-          auto uk = [&](int k) { return hh ? nchunk - 1 - k : k; };
-          tmem_ld_32x32b_x16(srow + 16 * uk(0), va);
+          tmem_ld_32x32b_x16(srow, va);
           tmem_wait_ld();
           reg_fence16(va);
-          for (int k = 0; k < nmine; k += 2) {
-            if (k + 1 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 1), vb);
-            max16(uk(k), va);
+          for (int u = 0; u < nchunk; u += 2) {
+            if (u + 1 < nchunk) tmem_ld_32x32b_x16(srow + 16 * (u + 1), vb);
+            max16(u, va);
             tmem_wait_ld();
             reg_fence16(vb);
-            if (k + 1 < nmine) {
-              if (k + 2 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 2), va);
-              max16(uk(k + 1), vb);
+            if (u + 1 < nchunk) {
+              if (u + 2 < nchunk) tmem_ld_32x32b_x16(srow + 16 * (u + 2), va);
+              max16(u + 1, vb);
               tmem_wait_ld();
               reg_fence16(va);
             }
           }
         }
-        my_m[hh * 128 + r] = m;
-        named_bar_sync(kB16sBarPair + (uint32_t)(sl * 4 + qd), 64);
-        m = fmaxf(my_m[r], my_m[128 + r]);
-        // pass 2: P pairs of chunk u to columns b16s_pcol(u) -- the first half walks forwards, the
-        // second backwards, each overwriting only scores it has already read
-        if (ok && wact && nmine > 0) {
-          const float nmc = -m * c;
-          const unsigned long long nmc2 = f32x2_pack(nmc, nmc);
-          unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
-          uint32_t va[16], vb[16], w[8];
-          auto uk = [&](int k) { return hh ? nchunk - 1 - k : k; };
-          tmem_ld_32x32b_x16(srow + 16 * uk(0), va);
+        // pass 2: P = 2^((s - max) c) -> bf16 pairs over the slot's first 128 columns (chunk u's
+        // pairs land in columns 8u..8u+7, scores this thread has already read), row sums in fp32
+        const float nmc = -m * c;
+        const unsigned long long c2 = f32x2_pack(c, c), nmc2 = f32x2_pack(nmc, nmc);
+        unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
+        auto exp16 = [&](int u, const uint32_t* v) {
+          float p[16];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            float x0, x1;
+            f32x2_unpack(fma_f32x2(f32x2_pack(__uint_as_float(v[2 * x]), __uint_as_float(v[2 * x + 1])), c2, nmc2), &x0,
+                         &x1);
+            p[2 * x] = ex2_approx(x0);
+            p[2 * x + 1] = ex2_approx(x1);
+          }
+          if (16 * u + 16 > keys) {
+#pragma unroll
+            for (int x = 0; x < 16; ++x)
+              if (16 * u + x >= keys) p[x] = 0.f;
+          }
+          uint32_t w[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            lsum2 = add_f32x2(lsum2, f32x2_pack(p[2 * x], p[2 * x + 1]));
+            __nv_bfloat162 pv = __floats2bfloat162_rn(p[2 * x], p[2 * x + 1]);
+            w[x] = *reinterpret_cast<uint32_t*>(&pv);
+          }
+          tmem_st_32x32b_x8(srow + 8 * u, w);
+        };
+        {
+          uint32_t va[16], vb[16];
+          tmem_ld_32x32b_x16(srow, va);
           tmem_wait_ld();
           reg_fence16(va);
-          for (int k = 0; k < nmine; k += 2) {
-            if (k + 1 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 1), vb);
-            exp16(uk(k), va, w, nmc2, lsum2);
-            tmem_st_32x32b_x8(srow + b16s_pcol(uk(k), nchunk, c1), w);
+          for (int u = 0; u < nchunk; u += 2) {
+            if (u + 1 < nchunk) tmem_ld_32x32b_x16(srow + 16 * (u + 1), vb);
+            exp16(u, va);
             tmem_wait_ld();
             reg_fence16(vb);
-            if (k + 1 < nmine) {
-              if (k + 2 < nmine) tmem_ld_32x32b_x16(srow + 16 * uk(k + 2), va);
-              exp16(uk(k + 1), vb, w, nmc2, lsum2);
-              tmem_st_32x32b_x8(srow + b16s_pcol(uk(k + 1), nchunk, c1), w);
+            if (u + 1 < nchunk) {
+              if (u + 2 < nchunk) tmem_ld_32x32b_x16(srow + 16 * (u + 2), va);
+              exp16(u + 1, vb);
               tmem_wait_ld();
               reg_fence16(va);
             }
           }
-          float l0, l1;
-          f32x2_unpack(lsum2, &l0, &l1);
-          lsum = l0 + l1;
-          if (g.extra && hh == 0) {
-            // the extra keys' P row (zero past S) as the A operand of one more K = 16 step:
-            // K-major core matrices, 8-row groups 256 bytes apart, the two 8-key halves 128 apart
-            uint32_t pw[8];
-#pragma unroll
-            for (int x = 0; x < 8; ++x) pw[x] = 0u;
-#pragma unroll
-            for (int e = 0; e < kB16sExtraMax; ++e) {
-              if (e < g.extra) {
-                const float pe = ex2_approx(fmaf(se[e], c, nmc));
-                lsum += pe;
-                const uint32_t hbits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(pe));
-                pw[e >> 1] |= (e & 1) ? hbits << 16 : hbits;
-              }
-            }
-            uint8_t* prow = gb + g.pe[sl] + (uint32_t)(r >> 3) * 256u + (uint32_t)(r & 7) * 16u;
-            *reinterpret_cast<uint4*>(prow) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-            *reinterpret_cast<uint4*>(prow + 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
-          }
-          tmem_wait_st();
         }
-        my_l[hh * 128 + r] = lsum;
-      } else if (hh == 0) {
-        // tail tile: lanes 32 q + e hold query row 256 + e; quadrant q scores keys [64 q, 64 q + 64)
-        // (q = 0 also the extra keys) and writes P in key order, zero outside its quarter
-        if (ok) {
-          {
-            uint32_t va[16], vb[16];
-            tmem_ld_32x32b_x16(srow + 16 * (4 * qd), va);
-            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 1), vb);
-            tmem_wait_ld();
-            reg_fence16(va);
-            reg_fence16(vb);
-            max16(4 * qd, va);
-            max16(4 * qd + 1, vb);
-            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 2), va);
-            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + 3), vb);
-            tmem_wait_ld();
-            reg_fence16(va);
-            reg_fence16(vb);
-            max16(4 * qd + 2, va);
-            max16(4 * qd + 3, vb);
-          }
-          my_m[r] = m;
-          named_bar_sync(kB16sBarTail + (uint32_t)sl, 128);
-          m = fmaxf(fmaxf(my_m[lane], my_m[32 + lane]), fmaxf(my_m[64 + lane], my_m[96 + lane]));
-          const float nmc = -m * c;
-          const unsigned long long nmc2 = f32x2_pack(nmc, nmc);
-          unsigned long long lsum2 = f32x2_pack(0.f, 0.f);
-          // chunk u = 4 q + x: its pairs go to columns 8u, which for q = 0 are scores of chunk u / 2
-          // (read), for q > 0 scores outside this thread's quarter; the zeros follow once every
-          // score of the quarter has been read
-#pragma unroll 1
-          for (int x = 0; x < 4; ++x) {
-            uint32_t v[16], w[8];
-            tmem_ld_32x32b_x16(srow + 16 * (4 * qd + x), v);
-            tmem_wait_ld();
-            reg_fence16(v);
-            exp16(4 * qd + x, v, w, nmc2, lsum2);
-            tmem_st_32x32b_x8(srow + 8u * (uint32_t)(4 * qd + x), w);
-          }
-          uint32_t zero[8];
+        float l0, l1;
+        f32x2_unpack(lsum2, &l0, &l1);
+        lsum = l0 + l1;
+        if (g.extra) {
+          // the extra keys' P row (zero past S) as the A operand of one more K = 16 step:
+          // K-major core matrices, 8-row groups 256 bytes apart, the two 8-key halves 128 bytes apart
+          uint32_t w[8];
 #pragma unroll
-          for (int x = 0; x < 8; ++x) zero[x] = 0u;
-          for (int u = 0; u < nchunk; ++u)
-            if (u < 4 * qd || u >= 4 * qd + 4) tmem_st_32x32b_x8(srow + 8u * (uint32_t)u, zero);
-          float l0, l1;
-          f32x2_unpack(lsum2, &l0, &l1);
-          lsum = l0 + l1;
-          if (g.extra) {
-            uint32_t pw[8];
+          for (int x = 0; x < 8; ++x) w[x] = 0u;
 #pragma unroll
-            for (int x = 0; x < 8; ++x) pw[x] = 0u;
-            if (qd == 0) {
-#pragma unroll
-              for (int e = 0; e < kB16sExtraMax; ++e) {
-                if (e < g.extra) {
-                  const float pe = ex2_approx(fmaf(se[e], c, nmc));
-                  lsum += pe;
-                  const uint32_t hbits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(pe));
-                  pw[e >> 1] |= (e & 1) ? hbits << 16 : hbits;
-                }
-              }
+          for (int e = 0; e < kB16sExtraMax; ++e) {
+            if (e < g.extra) {
+              const float pe = ex2_approx(fmaf(se[e], c, nmc));
+              lsum += pe;
+              const uint32_t hbits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(pe));
+              w[e >> 1] |= (e & 1) ? hbits << 16 : hbits;
             }
-            uint8_t* prow = gb + g.pe[sl] + (uint32_t)(r >> 3) * 256u + (uint32_t)(r & 7) * 16u;
-            *reinterpret_cast<uint4*>(prow) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-            *reinterpret_cast<uint4*>(prow + 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
           }
-          tmem_wait_st();
-        } else {
-          named_bar_sync(kB16sBarTail + (uint32_t)sl, 128);
+          uint8_t* prow = gb + g.pe[sl] + (uint32_t)(r >> 3) * 256u + (uint32_t)(r & 7) * 16u;
+          *reinterpret_cast<uint4*>(prow) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(prow + 128) = make_uint4(w[4], w[5], w[6], w[7]);
         }
-        my_l[r] = lsum;
+        tmem_wait_st();
       }
+      red_l[r] = lsum;
       fence_async_shared();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(sl));
     }
-  } else {
+  } else if (warp >= kB16sEpiW && warp < kB16sEpiW + 4) {
     // ------------------------------------------------------------ epilogue: O / rowsum -> bf16
-    const int qd = warp & 3, r = qd * 32 + lane, et = threadIdx.x - 18 * 32;
+    const int qd = warp & 3, r = qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    float* tail_o = reinterpret_cast<float*>(gb + g.to);   // [quadrant][tail row][64]
     // max |out| as bf16 magnitude bits in two 16-bit lanes: unsigned order of non-negative bf16
     // bits is numeric order and a NaN (0x7FC0) sorts above +inf, so a NaN output reaches the amax
     // as torch's amax would give it
@@ -4051,72 +3960,187 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       const int j = i / nt, t = i - j * nt, sl = i & 1;
       const int head = (int)blockIdx.x + j * (int)gridDim.x;
       const int b = head / g.H, h = head - b * g.H, row = t * 128 + r;
-      const bool tail = t * 128 >= 256;
-      const bool wact = t * 128 + qd * 32 < S || tail;
+      const bool wact = t * 128 + qd * 32 < S;
       if (ok) ok = mbar_wait(o_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutTmem) &&
                    mbar_wait(p_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutTmem);
       tc_fence_after();
-      const float* sl_l = red_l + (sl * 2) * 128;
-      float lsum;
-      if (!tail) {
-        lsum = sl_l[r] + sl_l[128 + r];
-      } else {   // this thread's tail row (et / 64) sums the four quadrants' partial sums
-        const int e = (et >> 6) & 1;
-        lsum = (sl_l[e] + sl_l[32 + e]) + (sl_l[64 + e] + sl_l[96 + e]);
+      uint32_t ov[64];
+      if (ok && wact) {
+        const uint32_t ta = tmem + lane_base + 256u * (uint32_t)sl + 128u;
+        tmem_ld_32x32b_x32(ta, ov);
+        tmem_ld_32x32b_x32(ta + 32, ov + 32);
+        tmem_wait_ld();
       }
-      const float f = 1.0f / lsum;
-      __nv_bfloat16* orow = g.out + (int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss;
-      const bool store = ok && wact && !tail && row < S;
-      // O in two 32-column halves; the slot is released once both are in registers
+      const float lsum = reinterpret_cast<const float*>(gb + g.red)[sl * 128 + r];
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free(sl));
+      if (ok && wact && row < S) {
+        const float f = 1.0f / lsum;
+        __nv_bfloat16* orow = g.out + (int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)row * g.oss;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t ov[32];
-        if (ok && wact) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 256u * (uint32_t)sl + (tail ? 128u : (uint32_t)g.o_col) + 32u * half, ov);
-          tmem_wait_ld();
-        }
-        if (half == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(o_free(sl));
-        }
-        if (store) {
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t w[4];
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t w[4];
-#pragma unroll
-            for (int x = 0; x < 4; ++x) {
-              __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[8 * cc + 2 * x]) * f,
-                                                        __uint_as_float(ov[8 * cc + 2 * x + 1]) * f);
-              w[x] = *reinterpret_cast<uint32_t*>(&hv);
-              out_max2 = umax_u16x2(out_max2, w[x] & 0x7FFF7FFFu);
-            }
-            *reinterpret_cast<uint4*>(orow + 32 * half + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int x = 0; x < 4; ++x) {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(ov[8 * cc + 2 * x]) * f,
+                                                      __uint_as_float(ov[8 * cc + 2 * x + 1]) * f);
+            w[x] = *reinterpret_cast<uint32_t*>(&hv);
+            out_max2 = umax_u16x2(out_max2, w[x] & 0x7FFF7FFFu);
           }
+          *reinterpret_cast<uint4*>(orow + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        if (ok && tail && lane < g.tail) {
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            tail_o[(qd * kB16sTailMax + lane) * 64 + 32 * half + d] = __uint_as_float(ov[d]);
-        }
-      }
-      if (tail) {
-        // the tail rows' four partial outputs (lanes e of each quadrant) through shared memory; every
-        // epilogue warp reaches both barriers, whatever its wait results
-        named_bar_sync(kB16sBarEpi, 128);
-        if (ok && et < g.tail * 64) {
-          const int e = et >> 6, d = et & 63;
-          const float o = (tail_o[(0 * kB16sTailMax + e) * 64 + d] + tail_o[(1 * kB16sTailMax + e) * 64 + d]) +
-                          (tail_o[(2 * kB16sTailMax + e) * 64 + d] + tail_o[(3 * kB16sTailMax + e) * 64 + d]);
-          const __nv_bfloat16 ob = __float2bfloat16_rn(o * f);
-          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)(256 + e) * g.oss + d] = ob;
-          out_max2 = umax_u16x2(out_max2, (uint32_t)(__bfloat16_as_ushort(ob) & 0x7FFFu));
-        }
-        named_bar_sync(kB16sBarEpi, 128);   // tail_o is written again at the next tail tile
       }
     }
     if (g.amax) {
       const uint32_t m = __reduce_max_sync(0xffffffffu, max(out_max2 & 0xFFFFu, out_max2 >> 16) << 16);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), m);
+    }
+  } else if (warp >= kB16sTailW && g.extra) {
+    // ------------------------------------------------------------ query rows 256 .. S - 1 of every
+    // head on the CUDA cores, from the head's K (with those rows) and V in shared memory; each tail
+    // warp takes every barrier below, whatever its wait results
+    const int et = threadIdx.x - kB16sTailW * 32, ew = et >> 5;
+    uint32_t out_max2 = 0;
+    bool ok = true;
+    for (int j = 0; j < my_heads; ++j) {
+      const int head = (int)blockIdx.x + j * (int)gridDim.x;
+      const int b = head / g.H, h = head - b * g.H;
+      {
+        const int hb = j & 1, ne = g.extra;
+        float* tq = reinterpret_cast<float*>(gb + g.tw);   // q rows in fp32 [2][64]
+        float* tp = tq + 2 * 64;                           // probabilities [2][272]
+        float* to = tp + 2 * 272;                          // partial outputs [key quarter][2][64]
+        float* tr = to + 4 * 2 * 64;                       // per-warp [2 rows][max, sum]
+        if (ok) ok = mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull) &&
+                     mbar_wait(v_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
+        if (ok && et < ne * 64) {
+          const int e = et >> 6, d = et & 63;
+          const uint8_t* qrow = gb + g.qt[hb] + e * 128;
+          const uint32_t bits = *reinterpret_cast<const uint16_t*>(qrow + ((((d >> 3) ^ (e & 7)) << 4) | ((d & 7) << 1)));
+          tq[e * 64 + d] = __uint_as_float(bits << 16);
+        }
+        named_bar_sync(kB16sBarTail, 128);
+        // scores of keys et, et + 128, et + 256 (< S) against both rows
+        float sc[3][kB16sExtraMax], mloc[kB16sExtraMax];
+#pragma unroll
+        for (int e = 0; e < kB16sExtraMax; ++e) mloc[e] = -INFINITY;
+#pragma unroll
+        for (int x = 0; x < 3; ++x) {
+          const int key = et + 128 * x;
+#pragma unroll
+          for (int e = 0; e < kB16sExtraMax; ++e) sc[x][e] = -INFINITY;
+          if (ok && key < S) {
+            const uint8_t* kr = gb + g.kb[hb] + key * 128;
+            unsigned long long a[kB16sExtraMax];
+#pragma unroll
+            for (int e = 0; e < kB16sExtraMax; ++e) a[e] = f32x2_pack(0.f, 0.f);
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              const uint4 w = *reinterpret_cast<const uint4*>(kr + ((cc ^ (key & 7)) << 4));
+              const unsigned long long k0 = bf16x2_to_f32x2(w.x), k1 = bf16x2_to_f32x2(w.y),
+                                       k2 = bf16x2_to_f32x2(w.z), k3 = bf16x2_to_f32x2(w.w);
+#pragma unroll
+              for (int e = 0; e < kB16sExtraMax; ++e) {
+                if (e < ne) {
+                  const float4 q0 = *reinterpret_cast<const float4*>(tq + e * 64 + 8 * cc);
+                  const float4 q1 = *reinterpret_cast<const float4*>(tq + e * 64 + 8 * cc + 4);
+                  a[e] = fma_f32x2(k0, f32x2_pack(q0.x, q0.y), a[e]);
+                  a[e] = fma_f32x2(k1, f32x2_pack(q0.z, q0.w), a[e]);
+                  a[e] = fma_f32x2(k2, f32x2_pack(q1.x, q1.y), a[e]);
+                  a[e] = fma_f32x2(k3, f32x2_pack(q1.z, q1.w), a[e]);
+                }
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < kB16sExtraMax; ++e) {
+              if (e < ne) {
+                float a0, a1;
+                f32x2_unpack(a[e], &a0, &a1);
+                sc[x][e] = a0 + a1;
+                mloc[e] = fmaxf(mloc[e], sc[x][e]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < kB16sExtraMax; ++e) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mloc[e] = fmaxf(mloc[e], __shfl_xor_sync(0xffffffffu, mloc[e], o));
+          if (lane == 0) tr[(ew * 2 + e) * 2] = mloc[e];
+        }
+        named_bar_sync(kB16sBarTail, 128);
+        const float c = g.scale * 1.4426950408889634f;
+        float lloc[kB16sExtraMax];
+#pragma unroll
+        for (int e = 0; e < kB16sExtraMax; ++e) {
+          const float mx = fmaxf(fmaxf(tr[(0 * 2 + e) * 2], tr[(1 * 2 + e) * 2]), fmaxf(tr[(2 * 2 + e) * 2], tr[(3 * 2 + e) * 2]));
+          const float nmc = -mx * c;
+          lloc[e] = 0.f;
+#pragma unroll
+          for (int x = 0; x < 3; ++x) {
+            const int key = et + 128 * x;
+            if (e < ne && key < S) {
+              const float pv = ex2_approx(fmaf(sc[x][e], c, nmc));
+              tp[e * 272 + key] = pv;
+              lloc[e] += pv;
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) lloc[e] += __shfl_xor_sync(0xffffffffu, lloc[e], o);
+        }
+        named_bar_sync(kB16sBarTail, 128);   // the maxima are read; the sums reuse their neighbours
+#pragma unroll
+        for (int e = 0; e < kB16sExtraMax; ++e)
+          if (lane == 0) tr[(ew * 2 + e) * 2 + 1] = lloc[e];
+        {
+          // O partials: dims 2 dp, 2 dp + 1 over a quarter of the keys, P rounded to bf16 as the MMA sees it
+          const int dp = et & 31, kq = et >> 5, quarter = (S + 3) / 4;
+          const int k0 = kq * quarter, k1 = min(S, k0 + quarter);
+          unsigned long long acc[kB16sExtraMax];
+#pragma unroll
+          for (int e = 0; e < kB16sExtraMax; ++e) acc[e] = f32x2_pack(0.f, 0.f);
+          if (ok) {
+#pragma unroll 4
+            for (int key = k0; key < k1; ++key) {
+              const uint32_t vv = *reinterpret_cast<const uint32_t*>(gb + g.vb[hb] + key * 128 +
+                                                                   ((((dp >> 2) ^ (key & 7)) << 4) | ((dp & 3) << 2)));
+              const unsigned long long vf = bf16x2_to_f32x2(vv);
+#pragma unroll
+              for (int e = 0; e < kB16sExtraMax; ++e) {
+                if (e < ne) {
+                  const float pb = bf16_round(tp[e * 272 + key]);
+                  acc[e] = fma_f32x2(vf, f32x2_pack(pb, pb), acc[e]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < kB16sExtraMax; ++e) {
+            float o0, o1;
+            f32x2_unpack(acc[e], &o0, &o1);
+            to[(kq * 2 + e) * 64 + 2 * dp] = o0;
+            to[(kq * 2 + e) * 64 + 2 * dp + 1] = o1;
+          }
+        }
+        named_bar_sync(kB16sBarTail, 128);
+        if (ok && et < ne * 64) {
+          const int e = et >> 6, d = et & 63;
+          const float l = (tr[(0 * 2 + e) * 2 + 1] + tr[(1 * 2 + e) * 2 + 1]) + (tr[(2 * 2 + e) * 2 + 1] + tr[(3 * 2 + e) * 2 + 1]);
+          const float o = (to[(0 * 2 + e) * 64 + d] + to[(1 * 2 + e) * 64 + d]) + (to[(2 * 2 + e) * 64 + d] + to[(3 * 2 + e) * 64 + d]);
+          const __nv_bfloat16 ob = __float2bfloat16_rn(o * (1.0f / l));
+          g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)(256 + e) * g.oss + d] = ob;
+          out_max2 = umax_u16x2(out_max2, (uint32_t)(__bfloat16_as_ushort(ob) & 0x7FFFu));
+        }
+        named_bar_sync(kB16sBarTail, 128);   // the working storage is written again at the next head
+        if (lane == 0) {   // this warp is done with the head's K (and its rows past 256) and V
+          mbar_arrive(k_free(hb));
+          mbar_arrive(v_free(hb));
+        }
+      }
+    }
+    if (g.amax) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, out_max2 << 16);
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(g.amax), m);
     }
   }
@@ -4144,7 +4168,9 @@ static int launch_bf16_slots(const void* q, const void* k, const void* v, int64_
   if (int st = make_head_map(&tq, q, fg, sb, sh, ss, 128, g.kv_hs)) return st;
   if (int st = make_head_map(&tk, k, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
   if (int st = make_head_map(&tv, v, fg, sb, sh, ss, g.box_rows, g.kv_hs)) return st;
-  if (g.tail && make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return VF4_ERR_CUDA;
+  if (g.extra) {
+    if (int st = make_head_map(&tt, q, fg, sb, sh, ss, 8, g.kv_hs)) return st;
+  }
   if (int st = smem_optin(attn_bf16_slots_kernel, (int)g.total)) return st;
   const int grid = g.heads < num_sms() ? g.heads : num_sms();
   attn_bf16_slots_kernel<<<grid, kB16sWarps * 32, g.total, s>>>(tq, tk, tv, tt, g);
