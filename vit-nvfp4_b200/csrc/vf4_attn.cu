@@ -3567,9 +3567,9 @@ constexpr int kB16sSoftW = VF4_B16S_ROLES == 0 ? 2 : VF4_B16S_ROLES == 1 ? 6 : 1
 constexpr int kB16sEpiW = VF4_B16S_ROLES == 0 ? 10 : VF4_B16S_ROLES == 1 ? 14 : 2;
 constexpr int kB16sTailW = VF4_B16S_ROLES == 0 ? 14 : VF4_B16S_ROLES == 1 ? 2 : 6;
 constexpr uint32_t kB16sBarTail = 1;   // named barrier id of the tail warps
-// Working storage of the rows past 256 (floats): q [2][64], p [2][272], o partials [4][2][64],
+// Working storage of the rows past 256 (floats): p [2][272], o partials [4][2][64],
 // per-warp maxima and sums [4][2][2]
-constexpr uint32_t kB16sTailBytes = (2 * 64 + 2 * 272 + 4 * 2 * 64 + 4 * 2 * 2) * 4;
+constexpr uint32_t kB16sTailBytes = (2 * 272 + 4 * 2 * 64 + 4 * 2 * 2) * 4;
 
 struct B16sGeom {
   int B, H, S, D;
@@ -4008,56 +4008,47 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       const int b = head / g.H, h = head - b * g.H;
       {
         const int hb = j & 1, ne = g.extra;
-        float* tq = reinterpret_cast<float*>(gb + g.tw);   // q rows in fp32 [2][64]
-        float* tp = tq + 2 * 64;                           // probabilities [2][272]
+        float* tp = reinterpret_cast<float*>(gb + g.tw);   // probabilities, rounded to bf16 [2][272]
         float* to = tp + 2 * 272;                          // partial outputs [key quarter][2][64]
         float* tr = to + 4 * 2 * 64;                       // per-warp [2 rows][max, sum]
         if (ok) ok = mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull) &&
                      mbar_wait(v_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
-        if (ok && et < ne * 64) {
-          const int e = et >> 6, d = et & 63;
-          const uint8_t* qrow = gb + g.qt[hb] + e * 128;
-          const uint32_t bits = *reinterpret_cast<const uint16_t*>(qrow + ((((d >> 3) ^ (e & 7)) << 4) | ((d & 7) << 1)));
-          tq[e * 64 + d] = __uint_as_float(bits << 16);
-        }
-        named_bar_sync(kB16sBarTail, 128);
-        // scores of keys et, et + 128, et + 256 (< S) against both rows
+        // scores of keys et, et + 128, et + 256 (< S), one row at a time with the row's q in registers
         float sc[3][kB16sExtraMax], mloc[kB16sExtraMax];
 #pragma unroll
-        for (int e = 0; e < kB16sExtraMax; ++e) mloc[e] = -INFINITY;
+        for (int e = 0; e < kB16sExtraMax; ++e) {
+          mloc[e] = -INFINITY;
 #pragma unroll
-        for (int x = 0; x < 3; ++x) {
-          const int key = et + 128 * x;
-#pragma unroll
-          for (int e = 0; e < kB16sExtraMax; ++e) sc[x][e] = -INFINITY;
-          if (ok && key < S) {
-            const uint8_t* kr = gb + g.kb[hb] + key * 128;
-            unsigned long long a[kB16sExtraMax];
-#pragma unroll
-            for (int e = 0; e < kB16sExtraMax; ++e) a[e] = f32x2_pack(0.f, 0.f);
+          for (int x = 0; x < 3; ++x) sc[x][e] = -INFINITY;
+          if (ok && e < ne) {
+            unsigned long long q2[32];
+            const uint8_t* qrow = gb + g.qt[hb] + e * 128;
 #pragma unroll
             for (int cc = 0; cc < 8; ++cc) {
-              const uint4 w = *reinterpret_cast<const uint4*>(kr + ((cc ^ (key & 7)) << 4));
-              const unsigned long long k0 = bf16x2_to_f32x2(w.x), k1 = bf16x2_to_f32x2(w.y),
-                                       k2 = bf16x2_to_f32x2(w.z), k3 = bf16x2_to_f32x2(w.w);
-#pragma unroll
-              for (int e = 0; e < kB16sExtraMax; ++e) {
-                if (e < ne) {
-                  const float4 q0 = *reinterpret_cast<const float4*>(tq + e * 64 + 8 * cc);
-                  const float4 q1 = *reinterpret_cast<const float4*>(tq + e * 64 + 8 * cc + 4);
-                  a[e] = fma_f32x2(k0, f32x2_pack(q0.x, q0.y), a[e]);
-                  a[e] = fma_f32x2(k1, f32x2_pack(q0.z, q0.w), a[e]);
-                  a[e] = fma_f32x2(k2, f32x2_pack(q1.x, q1.y), a[e]);
-                  a[e] = fma_f32x2(k3, f32x2_pack(q1.z, q1.w), a[e]);
-                }
-              }
+              const uint4 a = *reinterpret_cast<const uint4*>(qrow + ((cc ^ e) << 4));
+              q2[4 * cc] = bf16x2_to_f32x2(a.x);
+              q2[4 * cc + 1] = bf16x2_to_f32x2(a.y);
+              q2[4 * cc + 2] = bf16x2_to_f32x2(a.z);
+              q2[4 * cc + 3] = bf16x2_to_f32x2(a.w);
             }
 #pragma unroll
-            for (int e = 0; e < kB16sExtraMax; ++e) {
-              if (e < ne) {
-                float a0, a1;
-                f32x2_unpack(a[e], &a0, &a1);
-                sc[x][e] = a0 + a1;
+            for (int x = 0; x < 3; ++x) {
+              const int key = et + 128 * x;
+              if (key < S) {
+                const uint8_t* kr = gb + g.kb[hb] + key * 128;
+                unsigned long long a0 = f32x2_pack(0.f, 0.f), a1 = a0;
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                  const uint4 w = *reinterpret_cast<const uint4*>(kr + ((cc ^ (key & 7)) << 4));
+                  a0 = fma_f32x2(bf16x2_to_f32x2(w.x), q2[4 * cc], a0);
+                  a1 = fma_f32x2(bf16x2_to_f32x2(w.y), q2[4 * cc + 1], a1);
+                  a0 = fma_f32x2(bf16x2_to_f32x2(w.z), q2[4 * cc + 2], a0);
+                  a1 = fma_f32x2(bf16x2_to_f32x2(w.w), q2[4 * cc + 3], a1);
+                }
+                float b0, b1, b2, b3;
+                f32x2_unpack(a0, &b0, &b1);
+                f32x2_unpack(a1, &b2, &b3);
+                sc[x][e] = (b0 + b1) + (b2 + b3);
                 mloc[e] = fmaxf(mloc[e], sc[x][e]);
               }
             }
@@ -4082,7 +4073,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
             const int key = et + 128 * x;
             if (e < ne && key < S) {
               const float pv = ex2_approx(fmaf(sc[x][e], c, nmc));
-              tp[e * 272 + key] = pv;
+              tp[e * 272 + key] = bf16_round(pv);   // the weight PV applies; the sum takes the fp32 value
               lloc[e] += pv;
             }
           }
@@ -4109,7 +4100,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
 #pragma unroll
               for (int e = 0; e < kB16sExtraMax; ++e) {
                 if (e < ne) {
-                  const float pb = bf16_round(tp[e * 272 + key]);
+                  const float pb = tp[e * 272 + key];
                   acc[e] = fma_f32x2(vf, f32x2_pack(pb, pb), acc[e]);
                 }
               }
@@ -4357,9 +4348,10 @@ int vf4_attn_bf16(const void* q, const void* k, const void* v, int64_t B, int64_
   if (B * H > INT32_MAX) return fail(VF4_ERR_UNSUPPORTED, "vf4_attn_bf16: B*H too large");
   if (out_amax && (reinterpret_cast<uintptr_t>(out_amax) & 3u))
     return fail(VF4_ERR_ALIGN, "vf4_attn_bf16: out_amax must be 4-byte aligned");
-  // VF4_BF16_ATTN=slots selects the two-slot kernel (S <= 258), otherwise the single-slot one runs
+  // the two-slot kernel up to S = 258, the single-slot one past that; VF4_BF16_ATTN=tiles selects the
+  // single-slot kernel for every S
   const char* mode = getenv("VF4_BF16_ATTN");
-  if (b16s_ok(S, D) && mode && mode[0] == 's')
+  if (b16s_ok(S, D) && !(mode && mode[0] == 't'))
     return launch_bf16_slots(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b,
                              out_stride_h, out_stride_s, out_amax, reinterpret_cast<cudaStream_t>(stream));
   return launch_bf16(q, k, v, B, H, S, D, stride_b, stride_h, stride_s, scale, out, out_stride_b, out_stride_h,
