@@ -3579,7 +3579,7 @@ struct B16sGeom {
   __nv_bfloat16* out;
   int64_t osb, osh, oss;
   float* amax;
-  uint32_t qb[2], kb[2], vb[2], pe[2], qt[2], tw, red, bar, total, kv_bytes;
+  uint32_t qb[2], kb[2], vb[2], pe[2], qt[2], tw, se, red, bar, total, kv_bytes;
 };
 
 static bool b16s_ok(int64_t S, int64_t D) { return D == 64 && S >= 1 && S <= 256 + kB16sExtraMax; }
@@ -3606,6 +3606,7 @@ static B16sGeom make_b16s_geom(int64_t B, int64_t H, int64_t S, int64_t D, float
   for (int i = 0; i < 2; ++i) { g.pe[i] = o; o += g.extra ? 4096u : 0u; }   // extra keys' P: 128 x 16 bf16
   for (int i = 0; i < 2; ++i) { g.qt[i] = o; o += g.extra ? 1024u : 0u; }   // query rows 256.. (8-row box)
   g.tw = o;  o += g.extra ? kB16sTailBytes : 0u;                            // their working storage
+  g.se = o;  o += g.extra ? 2u * 128u * kB16sExtraMax * 4u : 0u;  // extra keys' scores [slot][row][key]
   g.red = o; o += 2u * 128u * 4u;                                          // row sums per slot
   g.bar = o; o += 256;
   g.total = o + 1024;
@@ -3648,8 +3649,9 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
   auto p_full = [&](int i) { return bar + 112u + 8u * i; };
   auto o_full = [&](int i) { return bar + 128u + 8u * i; };
   auto o_free = [&](int i) { return bar + 144u + 8u * i; };
+  auto se_full = [&](int i) { return bar + 168u + 8u * i; };
   const uint32_t drain = bar + 160u;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 168);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + g.bar + 184);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = g.nt, S = g.S;
   // tiles of this CTA: head blockIdx.x + j * gridDim.x, query tile t, flat index i = j * nt + t
@@ -3660,7 +3662,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(q_full(i), 1);
-      mbar_init(q_free(i), g.extra ? 5u : 1u);               // QK commit (+ the softmax warps' Q reads)
+      mbar_init(q_free(i), g.extra ? 5u : 1u);               // QK commit (+ the epilogue warps' Q reads)
       mbar_init(k_full(i), 1);
       // K: the last QK commit, the softmax warps' extra-key reads and the epilogue warps' rows past
       // 256; V: the last PV commit and those rows
@@ -3671,6 +3673,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       mbar_init(p_full(i), 4);
       mbar_init(o_full(i), 1);
       mbar_init(o_free(i), 4);
+      mbar_init(se_full(i), 4);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -3799,49 +3802,13 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       const bool wact = t * 128 + qd * 32 < S;   // any query row of this warp's quadrant valid
       if (ok) ok = mbar_wait(s_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull);
       tc_fence_after();
-      // keys past 256 on the CUDA cores: s_e = q_r . k_(256 + e) in fp32
       float se[kB16sExtraMax];
 #pragma unroll
       for (int e = 0; e < kB16sExtraMax; ++e) se[e] = -INFINITY;
-      if (g.extra) {
-        if (ok) ok = mbar_wait(q_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull) &&
-                     mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
-        if (ok && wact) {
-          const uint8_t* qt = gb + g.qb[sl] + r * 128;
-#pragma unroll
-          for (int e = 0; e < kB16sExtraMax; ++e) {
-            if (e < g.extra) {
-              const int key = 256 + e;
-              const uint8_t* kt = gb + g.kb[hb] + key * 128;
-              unsigned long long acc0 = f32x2_pack(0.f, 0.f), acc1 = acc0;
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const uint4 a = *reinterpret_cast<const uint4*>(qt + ((x ^ (r & 7)) << 4));
-                const uint4 w = *reinterpret_cast<const uint4*>(kt + ((x ^ (key & 7)) << 4));
-                acc0 = fma_f32x2(bf16x2_to_f32x2(w.x), bf16x2_to_f32x2(a.x), acc0);
-                acc1 = fma_f32x2(bf16x2_to_f32x2(w.y), bf16x2_to_f32x2(a.y), acc1);
-                acc0 = fma_f32x2(bf16x2_to_f32x2(w.z), bf16x2_to_f32x2(a.z), acc0);
-                acc1 = fma_f32x2(bf16x2_to_f32x2(w.w), bf16x2_to_f32x2(a.w), acc1);
-              }
-              float a0, a1, b0, b1;
-              f32x2_unpack(acc0, &a0, &a1);
-              f32x2_unpack(acc1, &b0, &b1);
-              se[e] = (a0 + a1) + (b0 + b1);
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) {   // this warp is done with the tile's Q rows and the head's extra K rows
-          mbar_arrive(q_free(sl));
-          mbar_arrive(k_free(hb));
-        }
-      }
       float lsum = 0.f;
       if (ok && wact) {
         // pass 1: row max over the valid keys
         float m = -INFINITY;
-#pragma unroll
-        for (int e = 0; e < kB16sExtraMax; ++e) m = fmaxf(m, se[e]);
         auto max16 = [&](int u, const uint32_t* v) {
           if (16 * u + 16 <= keys) {
 #pragma unroll
@@ -3867,6 +3834,17 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
               max16(u + 1, vb);
               tmem_wait_ld();
               reg_fence16(va);
+            }
+          }
+        }
+        if (g.extra) {   // the keys past 256, scored by the epilogue warps
+          ok = mbar_wait(se_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull);
+          const float* ser = reinterpret_cast<const float*>(gb + g.se) + (sl * 128 + r) * kB16sExtraMax;
+#pragma unroll
+          for (int e = 0; e < kB16sExtraMax; ++e) {
+            if (e < g.extra) {
+              se[e] = ser[e];
+              m = fmaxf(m, se[e]);
             }
           }
         }
@@ -3956,6 +3934,49 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
     // as torch's amax would give it
     uint32_t out_max2 = 0;
     bool ok = true;
+    // the scores of the keys past 256 for the rows of tile i (s_e = q_r . k_(256 + e) in fp32), handed
+    // to the softmax warps through shared memory once the tile's Q and the head's K are in; this
+    // warp's Q and extra-K reads then count towards releasing those buffers
+    auto extra_scores = [&](int i) {
+      const int j = i / nt, sl = i & 1, hb = j & 1;
+      if (ok) ok = mbar_wait(q_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull) &&
+                   mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
+      float* ser = reinterpret_cast<float*>(gb + g.se) + (sl * 128 + r) * kB16sExtraMax;
+      if (ok) {
+        const uint8_t* qt = gb + g.qb[sl] + r * 128;
+#pragma unroll
+        for (int e = 0; e < kB16sExtraMax; ++e) {
+          if (e < g.extra) {
+            const int key = 256 + e;
+            const uint8_t* kt = gb + g.kb[hb] + key * 128;
+            unsigned long long acc0 = f32x2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+            for (int x = 0; x < 8; ++x) {
+              const uint4 a = *reinterpret_cast<const uint4*>(qt + ((x ^ (r & 7)) << 4));
+              const uint4 w = *reinterpret_cast<const uint4*>(kt + ((x ^ (key & 7)) << 4));
+              acc0 = fma_f32x2(bf16x2_to_f32x2(w.x), bf16x2_to_f32x2(a.x), acc0);
+              acc1 = fma_f32x2(bf16x2_to_f32x2(w.y), bf16x2_to_f32x2(a.y), acc1);
+              acc0 = fma_f32x2(bf16x2_to_f32x2(w.z), bf16x2_to_f32x2(a.z), acc0);
+              acc1 = fma_f32x2(bf16x2_to_f32x2(w.w), bf16x2_to_f32x2(a.w), acc1);
+            }
+            float a0, a1, b0, b1;
+            f32x2_unpack(acc0, &a0, &a1);
+            f32x2_unpack(acc1, &b0, &b1);
+            ser[e] = (a0 + a1) + (b0 + b1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(se_full(sl));
+        mbar_arrive(q_free(sl));
+        mbar_arrive(k_free(hb));
+      }
+    };
+    if (g.extra) {
+      if (T > 0) extra_scores(0);
+      if (T > 1) extra_scores(1);
+    }
     for (int i = 0; i < T; ++i) {
       const int j = i / nt, t = i - j * nt, sl = i & 1;
       const int head = (int)blockIdx.x + j * (int)gridDim.x;
@@ -3991,6 +4012,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
           *reinterpret_cast<uint4*>(orow + 8 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      if (g.extra && i + 2 < T) extra_scores(i + 2);
     }
     if (g.amax) {
       const uint32_t m = __reduce_max_sync(0xffffffffu, max(out_max2 & 0xFFFFu, out_max2 >> 16) << 16);
