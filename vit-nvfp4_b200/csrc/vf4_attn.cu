@@ -3544,8 +3544,9 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
 //   128 columns of S  ->  O = P V (kind::f16 with A = P read from tensor memory) into columns
 //   128..191 of the slot, whose scores the softmax has finished with
 // so the two slots alternate between the tensor core and the softmax warps.  Keys past 256 (S =
-// 257, 258) are scored on the CUDA cores by the softmax threads (64 fused multiply-adds per row and
-// key) and enter PV as one more K = 16 step whose A operand (those keys' P, zero-padded) sits in
+// 257, 258) are scored on the CUDA cores (64 fused multiply-adds per row and key) by the epilogue
+// warps, for the tile two ahead of the one they finish, and handed to the softmax through shared
+// memory; they enter PV as one more K = 16 step whose A operand (those keys' P, zero-padded) sits in
 // shared memory.  Query rows past 256 (one or two) are computed whole on the CUDA cores by four
 // warps of their own, from the head's K and V in shared memory, while the tiles run: a 128-row
 // MMA tile for them would cost a full slot cycle.
@@ -3555,7 +3556,8 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
 //                slot i % 2, O of tile i as soon as its P is written
 //   warps 2-5    softmax of slot 0 (one thread per query row, lane quadrant warp % 4)
 //   warps 6-9    softmax of slot 1
-//   warps 10-13  epilogue: O / rowsum -> bf16, each thread storing its row, and max |out|
+//   warps 10-13  epilogue: O / rowsum -> bf16, each thread storing its row, and max |out|; the
+//                scores of the keys past 256
 //   warps 14-17  the rows past 256 (idle when S <= 256)
 // ---------------------------------------------------------------------------------------
 constexpr int kB16sExtraMax = 2, kB16sWarps = 18;
