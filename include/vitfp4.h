@@ -198,6 +198,9 @@ VF4_API int vf4_attn_fp8(const void* q, const void* k, const void* v, int64_t B,
  * attention is off; timm's Attention.forward calls F.scaled_dot_product_attention).  No
  * counterpart kernel in the reference.  Same operand / output layout and strides as
  * vf4_attn_nvfp4; head dim 64, S <= 288 and scale >= 0 (VF4_ERR_UNSUPPORTED otherwise); no workspace.
+ * Up to S = 258 a two-slot kernel runs (the softmax of one 128-query tile overlapping the MMAs of
+ * the next; the environment variable VF4_BF16_ATTN=tiles selects the single-slot kernel instead),
+ * past that the single-slot kernel; both give the same arithmetic to fp32 rounding order.
  * out_amax (may be NULL): receives max |out| over the whole bf16 output -- the amax the next
  * QuantLinear's dynamic activation cast would compute (quant.py:48-54), so the caller can cast
  * with vf4_global_scale(out_amax) and skip that pass. */
