@@ -3569,9 +3569,9 @@ constexpr int kB16sSoftW = VF4_B16S_ROLES == 0 ? 2 : VF4_B16S_ROLES == 1 ? 6 : 1
 constexpr int kB16sEpiW = VF4_B16S_ROLES == 0 ? 10 : VF4_B16S_ROLES == 1 ? 14 : 2;
 constexpr int kB16sTailW = VF4_B16S_ROLES == 0 ? 14 : VF4_B16S_ROLES == 1 ? 2 : 6;
 constexpr uint32_t kB16sBarTail = 1;   // named barrier id of the tail warps
-// Working storage of the rows past 256 (floats): p [2][272], o partials [4][2][64],
+// Working storage of the rows past 256 (floats): p [2][272], o partials [16][2][64],
 // per-warp maxima and sums [4][2][2]
-constexpr uint32_t kB16sTailBytes = (2 * 272 + 4 * 2 * 64 + 4 * 2 * 2) * 4;
+constexpr uint32_t kB16sTailBytes = (2 * 272 + 16 * 2 * 64 + 4 * 2 * 2) * 4;
 
 struct B16sGeom {
   int B, H, S, D;
@@ -4033,8 +4033,8 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
       {
         const int hb = j & 1, ne = g.extra;
         float* tp = reinterpret_cast<float*>(gb + g.tw);   // probabilities, rounded to bf16 [2][272]
-        float* to = tp + 2 * 272;                          // partial outputs [key quarter][2][64]
-        float* tr = to + 4 * 2 * 64;                       // per-warp [2 rows][max, sum]
+        float* to = tp + 2 * 272;                          // partial outputs [key group][2][64]
+        float* tr = to + 16 * 2 * 64;                      // per-warp [2 rows][max, sum]
         if (ok) ok = mbar_wait(k_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull) &&
                      mbar_wait(v_full(hb), (uint32_t)(j >> 1) & 1u, err, kDevErrTimeoutFull);
         // scores of keys et, et + 128, et + 256 (< S), one row at a time with the row's q in registers
@@ -4109,40 +4109,52 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
         for (int e = 0; e < kB16sExtraMax; ++e)
           if (lane == 0) tr[(ew * 2 + e) * 2 + 1] = lloc[e];
         {
-          // O partials: dims 2 dp, 2 dp + 1 over a quarter of the keys, P rounded to bf16 as the MMA sees it
-          const int dp = et & 31, kq = et >> 5, quarter = (S + 3) / 4;
-          const int k0 = kq * quarter, k1 = min(S, k0 + quarter);
-          unsigned long long acc[kB16sExtraMax];
+          // O partials: dims 8 dg .. 8 dg + 7 (one 16-byte piece of each V row) over the keys
+          // kg, kg + 16, ..., with P rounded to bf16 as the MMA sees it
+          const int dg = et & 7, kg = et >> 3;
+          unsigned long long acc[kB16sExtraMax][4];
 #pragma unroll
-          for (int e = 0; e < kB16sExtraMax; ++e) acc[e] = f32x2_pack(0.f, 0.f);
+          for (int e = 0; e < kB16sExtraMax; ++e)
+#pragma unroll
+            for (int x = 0; x < 4; ++x) acc[e][x] = f32x2_pack(0.f, 0.f);
           if (ok) {
-#pragma unroll 4
-            for (int key = k0; key < k1; ++key) {
-              const uint32_t vv = *reinterpret_cast<const uint32_t*>(gb + g.vb[hb] + key * 128 +
-                                                                   ((((dp >> 2) ^ (key & 7)) << 4) | ((dp & 3) << 2)));
-              const unsigned long long vf = bf16x2_to_f32x2(vv);
+#pragma unroll 2
+            for (int key = kg; key < S; key += 16) {
+              const uint4 vv = *reinterpret_cast<const uint4*>(gb + g.vb[hb] + key * 128 + ((dg ^ (key & 7)) << 4));
+              const unsigned long long v0 = bf16x2_to_f32x2(vv.x), v1 = bf16x2_to_f32x2(vv.y),
+                                       v2 = bf16x2_to_f32x2(vv.z), v3 = bf16x2_to_f32x2(vv.w);
 #pragma unroll
               for (int e = 0; e < kB16sExtraMax; ++e) {
                 if (e < ne) {
                   const float pb = tp[e * 272 + key];
-                  acc[e] = fma_f32x2(vf, f32x2_pack(pb, pb), acc[e]);
+                  const unsigned long long p2 = f32x2_pack(pb, pb);
+                  acc[e][0] = fma_f32x2(v0, p2, acc[e][0]);
+                  acc[e][1] = fma_f32x2(v1, p2, acc[e][1]);
+                  acc[e][2] = fma_f32x2(v2, p2, acc[e][2]);
+                  acc[e][3] = fma_f32x2(v3, p2, acc[e][3]);
                 }
               }
             }
           }
 #pragma unroll
           for (int e = 0; e < kB16sExtraMax; ++e) {
-            float o0, o1;
-            f32x2_unpack(acc[e], &o0, &o1);
-            to[(kq * 2 + e) * 64 + 2 * dp] = o0;
-            to[(kq * 2 + e) * 64 + 2 * dp + 1] = o1;
+            if (e < ne) {
+              float4* dst = reinterpret_cast<float4*>(to + (kg * 2 + e) * 64 + 8 * dg);
+              float o[8];
+#pragma unroll
+              for (int x = 0; x < 4; ++x) f32x2_unpack(acc[e][x], &o[2 * x], &o[2 * x + 1]);
+              dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+              dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+            }
           }
         }
         named_bar_sync(kB16sBarTail, 128);
         if (ok && et < ne * 64) {
           const int e = et >> 6, d = et & 63;
           const float l = (tr[(0 * 2 + e) * 2 + 1] + tr[(1 * 2 + e) * 2 + 1]) + (tr[(2 * 2 + e) * 2 + 1] + tr[(3 * 2 + e) * 2 + 1]);
-          const float o = (to[(0 * 2 + e) * 64 + d] + to[(1 * 2 + e) * 64 + d]) + (to[(2 * 2 + e) * 64 + d] + to[(3 * 2 + e) * 64 + d]);
+          float o = 0.f;
+#pragma unroll
+          for (int kg = 0; kg < 16; ++kg) o += to[(kg * 2 + e) * 64 + d];
           const __nv_bfloat16 ob = __float2bfloat16_rn(o * (1.0f / l));
           g.out[(int64_t)b * g.osb + (int64_t)h * g.osh + (int64_t)(256 + e) * g.oss + d] = ob;
           out_max2 = umax_u16x2(out_max2, (uint32_t)(__bfloat16_as_ushort(ob) & 0x7FFFu));
