@@ -161,6 +161,25 @@ VF4_API int vf4_gemm_nvfp4_residual(const uint8_t* a_packed, const uint8_t* a_sf
                                     int64_t M, int64_t N, int64_t K, const void* bias, const void* residual,
                                     const void* gamma, void* out, vf4_stream_t stream);
 
+/* B scale image: the weight-side copy of b_sf that lets the GEMM load a 256-row tile's scales for a
+ * K64 block with one tensor-memory copy instead of two (each atom of the to_blocked layout held four
+ * times over: per 256-row tile and K64 block [rows 0-127 atom x4][rows 128-255 atom x4], 4 KB).  No
+ * counterpart in the reference (cuBLASLt takes the to_blocked scales as they are); built once per
+ * weight, like the reference's packed weight cache.  vf4_b_scale_image_bytes(N, K) is its size;
+ * vf4_b_scale_image writes it from b_sf ((N, K) weight, to_blocked scales; 16-byte aligned). */
+VF4_API int64_t vf4_b_scale_image_bytes(int64_t N, int64_t K);
+VF4_API int vf4_b_scale_image(const uint8_t* b_sf, int64_t N, int64_t K, uint8_t* image, vf4_stream_t stream);
+
+/* vf4_gemm_nvfp4 / vf4_gemm_nvfp4_residual with every option in one call: epilogue any VF4_EPI_*
+ * (residual and gamma for VF4_EPI_BIAS_RESIDUAL, else NULL) and b_image (NULL or the B scale image of
+ * b_sf): with it the streaming kernel (K > 1024, N >= 256) copies each K64 block's B scales with one
+ * tensor-memory copy (fc2 of ViT-L/14, K = 4096: about 10% faster); results are bit-identical. */
+VF4_API int vf4_gemm_nvfp4_ex(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                              const uint8_t* b_packed, const uint8_t* b_sf, const uint8_t* b_image,
+                              const float* b_gs, int64_t M, int64_t N, int64_t K, const void* bias, int epilogue,
+                              void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed, uint8_t* out_sf,
+                              const void* residual, const void* gamma, vf4_stream_t stream);
+
 /* Bytes of workspace vf4_attn_nvfp4 needs for (B, H, S, D) (0 for invalid sizes). */
 VF4_API int64_t vf4_attn_workspace_size(int64_t B, int64_t H, int64_t S, int64_t D);
 

@@ -232,6 +232,34 @@ def test_gemm_resident_b_scales_kernel(M, K, N, monkeypatch):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("M,K,N", [(300, 2048, 512), (1300, 4096, 1024), (333, 1536, 832), (64, 1088, 256)])
+def test_gemm_b_scale_image(M, K, N):
+    """The B scale image (each to_blocked atom held four times, per 256-row tile and K64 block) and the
+    streaming kernel that copies a K64 block's B scales with one 128x256b tcgen05.cp from it: the
+    image equals its definition, and every epilogue (bf16, + bias, fp32, residual) is bit-equal to the
+    two-copy kernel; N = 832 has an odd count of 128-row scale blocks (the last tile repeats its first
+    atom), K = 1088 a last stage of one K64 block, M = 333 and 300 a partial last row tile."""
+    ops = _ops()
+    A, B = _operands(M, N, K, seed=K + N)
+    ap, asf, ag = to_cuda_operand(A[3], A[4], A[2])
+    bp, bsf, bg = to_cuda_operand(B[3], B[4], B[2])
+    img = ops.b_scale_image(bsf, N, K)
+    n_rb, n_kb, ntn = (N + 127) // 128, (K + 63) // 64, (N + 255) // 256
+    atoms = bsf.view(torch.uint8).reshape(n_rb, n_kb, 512)
+    if n_rb % 2:
+        atoms = torch.cat([atoms, atoms[-1:]], 0)   # the last tile's first atom
+    want = atoms.reshape(ntn, 2, n_kb, 512).permute(0, 2, 1, 3).unsqueeze(3).expand(ntn, n_kb, 2, 4, 512)
+    assert torch.equal(img.reshape(ntn, n_kb, 2, 4, 512), want)
+    g = torch.Generator(device="cpu").manual_seed(7)
+    bias = (torch.randn(N, generator=g) * 0.1).cuda().bfloat16()
+    res = torch.randn(M, N, generator=g).cuda().bfloat16()
+    gam = (torch.rand(N, generator=g) * 0.5 + 1e-5).cuda().bfloat16()
+    for kw in ({}, {"bias": bias}, {"out_dtype": torch.float32}):
+        assert torch.equal(ops.gemm(ap, asf, ag, bp, bsf, bg, **kw), ops.gemm(ap, asf, ag, bp, bsf, bg, b_image=img, **kw))
+    assert torch.equal(ops.gemm_residual(ap, asf, ag, bp, bsf, bg, bias, res, gamma=gam),
+                       ops.gemm_residual(ap, asf, ag, bp, bsf, bg, bias, res, gamma=gam, b_image=img))
+
+
 def test_bounded_wait_gives_up_and_reports():
     """The failure detector in the allowed form: a kernel's bounded mbarrier wait, given a 2 ms limit
     and a barrier nothing arrives on, gives up, records device error 1 (producer data never arrived)

@@ -659,6 +659,12 @@ VF4_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
                : "memory");
 }
 
+// 128 lanes x 256 bits: lane l takes row l of a K-major no-swizzle shared-memory matrix (two
+// 16-byte core-matrix columns, LBO apart; 8-row groups SBO apart) into 8 consecutive columns.
+VF4_DEV void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 VF4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.

@@ -54,18 +54,31 @@ __host__ __device__ constexpr bool epi_gelu(int e) { return e == VF4_EPI_GELU_NV
 // The bf16 epilogues of the 128x256 tile stage 32 rows x 16 columns (1 KB) per warp so that a
 // fourth pipeline stage fits; the GELU epilogue keeps 3 stages (its staging is 2 KB per warp) and
 // the fp32 epilogue stores directly.
-template <int BN, int EPI = VF4_EPI_BIAS, bool kF32 = false>
+// With a B scale image (kRepB: the 128x256 tile and a caller-built image, vf4_b_scale_image) the
+// stage holds B's scale atoms four times over -- per K64 block [atom of rows 0-127 x4][atom of rows
+// 128-255 x4], 4 KB, one bulk copy of the image per stage -- so that one 128x256b tcgen05.cp (lane l
+// reads row l: atom row l % 32 of each half) fills the 8 scale columns the MMA reads, where two
+// 32x128b.warpx4 copies were needed: each copy costs the tensor pipe 25-45 clocks whatever its
+// size.  That region leads the stage (a 16 KB block at its 1024-byte-aligned start); it costs the
+// fourth stage, which measured no faster than three.
+template <int BN, int EPI = VF4_EPI_BIAS, bool kF32 = false, bool REP = false>
 struct GemmCfg {
   static constexpr bool kGeluEpi = EPI == VF4_EPI_GELU_NVFP4 || EPI == VF4_EPI_GELU_ERF_NVFP4;
   static constexpr int BM = 128;
   static constexpr int KB_PER_STAGE = 4;                   // 4 x K64 MMAs = 256 elements = 128 B
-  static constexpr int STAGES = BN == 256 ? (kGeluEpi ? 3 : 4) : 4;
+  static constexpr bool kRepB = REP && BN == 256;
+  static constexpr int STAGES = kRepB ? 3 : BN == 256 ? (kGeluEpi ? 3 : 4) : 4;
   static constexpr int EPI_CW = BN == 256 ? 16 : 64;        // bf16 staging chunk (columns)
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int SFA_BYTES = KB_PER_STAGE * 512;
-  static constexpr int SFB_BYTES = (BN / 128) * KB_PER_STAGE * 512;
+  static constexpr int SFB_BYTES = kRepB ? KB_PER_STAGE * 4096 : (BN / 128) * KB_PER_STAGE * 512;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  // offsets inside a stage (A and B 1024-byte aligned for the 128-byte swizzle)
+  static constexpr int SFB_OFF = kRepB ? 0 : A_BYTES + B_BYTES + SFA_BYTES;
+  static constexpr int A_OFF = kRepB ? SFB_BYTES : 0;
+  static constexpr int B_OFF = A_OFF + A_BYTES;
+  static constexpr int SFA_OFF = B_OFF + B_BYTES;
   static constexpr int ACC_STAGES = BN == 256 ? 1 : 2;
   static constexpr int SFA_TCOL = 256;                      // TMEM columns of the scale slots
   static constexpr int SFA_SLOT = KB_PER_STAGE * 4;         // 4 columns per K64 block (M=128)
@@ -89,6 +102,7 @@ struct GemmCfg {
 struct GemmParams {
   const uint8_t* a_sf;
   const uint8_t* b_sf;
+  const uint8_t* b_img;   // B scale image (vf4_b_scale_image) or NULL
   const float* a_gs;
   const float* b_gs;
   int M, N, K;
@@ -315,11 +329,11 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
   }
 }
 
-template <int BN, int EPI, bool kF32>
+template <int BN, int EPI, bool kF32, bool REP>
 __global__ void __launch_bounds__(320, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
-  using C = GemmCfg<BN, EPI, kF32>;
+  using C = GemmCfg<BN, EPI, kF32, REP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -382,11 +396,9 @@ __global__ void __launch_bounds__(320, 1)
           const int kb0 = st * C::KB_PER_STAGE;
           const int nkb = min(C::KB_PER_STAGE, p.n_kb - kb0);
           const uint32_t sf_bytes = (uint32_t)nkb * 512u;
-          mbar_arrive_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES + sf_bytes * (1 + BN / 128));
-          const uint32_t sa = base + s * C::STAGE_BYTES;
-          const uint32_t sb = sa + C::A_BYTES;
-          const uint32_t ssfa = sb + C::B_BYTES;
-          const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES + sf_bytes * (1 + (C::kRepB ? 8 : BN / 128)));
+          const uint32_t stg = base + s * C::STAGE_BYTES;
+          const uint32_t sa = stg + C::A_OFF, sb = stg + C::B_OFF, ssfa = stg + C::SFA_OFF, ssfb = stg + C::SFB_OFF;
           tma_load_2d(sa, &tmA, st * 128, mb * 128, full_bar(s));
           tma_load_2d(sb, &tmB, st * 128, nb * BN, full_bar(s));
           bulk_load(ssfa, p.a_sf + ((int64_t)mb * p.n_kb + kb0) * 512, sf_bytes, full_bar(s));
@@ -394,8 +406,13 @@ __global__ void __launch_bounds__(320, 1)
           for (int j = 0; j < BN / 128; ++j) {
             int rb = nb * (BN / 128) + j;
             if (rb >= p.n_rb_b) rb = nb * (BN / 128);  // N tail: finite stand-in, columns discarded
-            bulk_load(ssfb + j * C::KB_PER_STAGE * 512, p.b_sf + ((int64_t)rb * p.n_kb + kb0) * 512,
-                      sf_bytes, full_bar(s));
+            if constexpr (C::kRepB) {   // the image's [kb][half][copy][512 B] blocks of this N tile
+              if (j == 0)
+                bulk_load(ssfb, p.b_img + ((int64_t)nb * p.n_kb + kb0) * 4096, (uint32_t)nkb * 4096u, full_bar(s));
+            } else {
+              bulk_load(ssfb + j * C::KB_PER_STAGE * 512, p.b_sf + ((int64_t)rb * p.n_kb + kb0) * 512, sf_bytes,
+                        full_bar(s));
+            }
           }
         }
       }
@@ -427,18 +444,21 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t slot = (uint32_t)(it & 1);
           const uint32_t sfa_t = tmem + C::SFA_TCOL + slot * C::SFA_SLOT;
           const uint32_t sfb_t = tmem + C::SFB_TCOL + slot * C::SFB_SLOT;
-          const uint32_t sa = base + s * C::STAGE_BYTES;
-          const uint32_t sb = sa + C::A_BYTES;
-          const uint32_t ssfa = sb + C::B_BYTES;
-          const uint32_t ssfb = ssfa + C::SFA_BYTES;
+          const uint32_t stg = base + s * C::STAGE_BYTES;
+          const uint32_t sa = stg + C::A_OFF, sb = stg + C::B_OFF, ssfa = stg + C::SFA_OFF, ssfb = stg + C::SFB_OFF;
           // scale copies of K-block kb are issued right before its MMA (the tensor pipe runs
           // copies and MMAs in issue order; interleaving lets the copies overlap earlier MMAs)
           for (int kb = 0; kb < nkb; ++kb) {
             tmem_cp_32x128b_x4(sfa_t + kb * 4, smem_desc(ssfa + kb * 512, 0, 128, 0));
+            if constexpr (C::kRepB) {
+              // 128 rows of 32 bytes: the two 16-byte halves 2048 bytes apart, 8-row groups 128 apart
+              tmem_cp_128x256b(sfb_t + kb * C::SFB_PER_KB, smem_desc(ssfb + kb * 4096, 2048, 128, 0));
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tmem_cp_32x128b_x4(sfb_t + kb * C::SFB_PER_KB + j * 4,
-                                 smem_desc(ssfb + j * C::KB_PER_STAGE * 512 + kb * 512, 0, 128, 0));
+              for (int j = 0; j < BN / 128; ++j)
+                tmem_cp_32x128b_x4(sfb_t + kb * C::SFB_PER_KB + j * 4,
+                                   smem_desc(ssfb + j * C::KB_PER_STAGE * 512 + kb * 512, 0, 128, 0));
+            }
             const uint64_t ad = smem_desc(sa + kb * 32, 16, 1024, 2);
             const uint64_t bd = smem_desc(sb + kb * 32, 16, 1024, 2);
             mma_mxf4nvf4(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::SFB_PER_KB,
@@ -1016,9 +1036,9 @@ static int make_out_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, b
   return VF4_OK;
 }
 
-template <int BN, int EPI, bool kF32>
-static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
-  using C = GemmCfg<BN, EPI, kF32>;
+template <int BN, int EPI, bool kF32, bool REP>
+static int launch_gemm_t(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
+  using C = GemmCfg<BN, EPI, kF32, REP>;
   CUtensorMap ta, tb, to;
   memset(&to, 0, sizeof(to));
   if (int st = make_kmajor_map(&ta, a, p.M, p.K / 2, 128)) return st;
@@ -1028,7 +1048,7 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   } else if (!kF32) {
     if (int st = make_out_map(&to, p.out, p.M, p.N, false, BN, C::EPI_CW)) return st;
   }
-  auto kern = gemm_nvfp4_kernel<BN, EPI, kF32>;
+  auto kern = gemm_nvfp4_kernel<BN, EPI, kF32, REP>;
   if (int st = smem_optin(kern, C::SMEM)) return st;
   p.tiles_m = (p.M + 127) / 128;
   p.tiles_n = (p.N + BN - 1) / BN;
@@ -1036,6 +1056,14 @@ static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaSt
   int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, to, p);
   return launch_status("vf4_gemm_nvfp4");
+}
+
+template <int BN, int EPI, bool kF32>
+static int launch_gemm(const uint8_t* a, const uint8_t* b, GemmParams& p, cudaStream_t s) {
+  if constexpr (BN == 256) {
+    if (p.b_img) return launch_gemm_t<BN, EPI, kF32, true>(a, b, p, s);
+  }
+  return launch_gemm_t<BN, EPI, kF32, false>(a, b, p, s);
 }
 
 template <int EPI, bool kF32>
@@ -1122,7 +1150,8 @@ using namespace vf4;
 static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs, const uint8_t* b_packed,
                       const uint8_t* b_sf, const float* b_gs, int64_t M, int64_t N, int64_t K, const void* bias,
                       int epilogue, void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed,
-                      uint8_t* out_sf, const void* residual, const void* gamma, vf4_stream_t stream) {
+                      uint8_t* out_sf, const void* residual, const void* gamma, vf4_stream_t stream,
+                      const uint8_t* b_img = nullptr) {
   if (int st = check_device()) return st;
   if (M < 0 || N <= 0 || K <= 0) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4: bad sizes M=%lld N=%lld K=%lld",
                                              (long long)M, (long long)N, (long long)K);
@@ -1138,6 +1167,7 @@ static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float*
   if (!aligned16(a_packed) || !aligned16(b_packed) || !aligned16(a_sf) || !aligned16(b_sf) ||
       (bias && !aligned16(bias)))
     return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4: operands, scales and bias must be 16-byte aligned");
+  if (b_img && !aligned16(b_img)) return fail(VF4_ERR_ALIGN, "vf4_gemm_nvfp4_ex: b_image must be 16-byte aligned");
   if (epilogue == VF4_EPI_BIAS_RESIDUAL) {
     if (!residual) return fail(VF4_ERR_ARG, "vf4_gemm_nvfp4_residual: residual is NULL");
     if (!aligned16(residual) || (gamma && !aligned16(gamma)))
@@ -1157,6 +1187,7 @@ static int gemm_entry(const uint8_t* a_packed, const uint8_t* a_sf, const float*
   GemmParams p{};
   p.a_sf = a_sf;
   p.b_sf = b_sf;
+  p.b_img = b_img;
   p.a_gs = a_gs;
   p.b_gs = b_gs;
   p.M = (int)M;
@@ -1211,4 +1242,46 @@ extern "C" int vf4_gemm_nvfp4_residual(const uint8_t* a_packed, const uint8_t* a
                                        const void* gamma, void* out, vf4_stream_t stream) {
   return gemm_entry(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, M, N, K, bias, VF4_EPI_BIAS_RESIDUAL, out, VF4_BF16,
                     nullptr, nullptr, nullptr, residual, gamma, stream);
+}
+
+// B scale image: for every 256-row tile tn of B and K64 block kb, 4 KB = [rows 0-127 atom x4][rows
+// 128-255 atom x4] of the 512-byte to_blocked atoms (a tile past N repeats its first atom: finite
+// scales for columns the epilogue discards).  One thread per 16 bytes.
+__global__ void b_scale_image_kernel(const uint8_t* __restrict__ sf, int n_rb, int n_kb, int64_t words,
+                                     uint8_t* __restrict__ img) {
+  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (w >= words) return;
+  const int64_t a = w >> 5;                     // 512-byte block of the image
+  const int j = (int)((a >> 2) & 1);
+  const int64_t tk = a >> 3;                    // tn * n_kb + kb
+  const int kb = (int)(tk % n_kb), tn = (int)(tk / n_kb);
+  int rb = 2 * tn + j;
+  if (rb >= n_rb) rb = 2 * tn;
+  reinterpret_cast<uint4*>(img)[w] =
+      __ldg(reinterpret_cast<const uint4*>(sf + ((int64_t)rb * n_kb + kb) * 512) + (w & 31));
+}
+
+extern "C" int64_t vf4_b_scale_image_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0) return 0;
+  return (N + 255) / 256 * ((K + 63) / 64) * 4096;
+}
+
+extern "C" int vf4_b_scale_image(const uint8_t* b_sf, int64_t N, int64_t K, uint8_t* image, vf4_stream_t stream) {
+  if (int st = check_device()) return st;
+  if (N <= 0 || K <= 0 || N > 65535 * 128 || K > (1 << 20)) return fail(VF4_ERR_ARG, "vf4_b_scale_image: bad sizes");
+  if (!b_sf || !image) return fail(VF4_ERR_ARG, "vf4_b_scale_image: null pointer");
+  if (!aligned16(b_sf) || !aligned16(image)) return fail(VF4_ERR_ALIGN, "vf4_b_scale_image: 16-byte alignment");
+  const int64_t words = vf4_b_scale_image_bytes(N, K) / 16;
+  b_scale_image_kernel<<<(unsigned)((words + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      b_sf, (int)((N + 127) / 128), (int)((K + 63) / 64), words, image);
+  return launch_status("vf4_b_scale_image");
+}
+
+extern "C" int vf4_gemm_nvfp4_ex(const uint8_t* a_packed, const uint8_t* a_sf, const float* a_gs,
+                                 const uint8_t* b_packed, const uint8_t* b_sf, const uint8_t* b_image,
+                                 const float* b_gs, int64_t M, int64_t N, int64_t K, const void* bias, int epilogue,
+                                 void* out, int out_dtype, const float* epi_gs, uint8_t* out_packed, uint8_t* out_sf,
+                                 const void* residual, const void* gamma, vf4_stream_t stream) {
+  return gemm_entry(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, M, N, K, bias, epilogue, out, out_dtype, epi_gs,
+                    out_packed, out_sf, residual, gamma, stream, b_image);
 }

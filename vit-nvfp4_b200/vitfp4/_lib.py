@@ -43,6 +43,9 @@ SIGNATURES: dict[str, list] = {
     "vf4_to_blocked": [_P, _L, _L, _P, _P],
     "vf4_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _I, _P, _I, _P, _P, _P, _P],
     "vf4_gemm_nvfp4_residual": [_P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _P, _P, _P, _P],
+    "vf4_gemm_nvfp4_ex": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P],
+    "vf4_b_scale_image": [_P, _L, _L, _P, _P],
+    "vf4_b_scale_image_bytes": [_L, _L],
     "vf4_attn_workspace_size": [_L, _L, _L, _L],
     "vf4_attn_workspace_size_ex": [_L, _L, _L, _L, _I],
     "vf4_patchify": [_P, _L, _L, _L, _L, _L, _L, _P, _P],
@@ -58,7 +61,8 @@ SIGNATURES: dict[str, list] = {
     "vf4_gptq_block": [_P, _L, _P, _L, _P, _L, _P, _L, _L, _L, _P, _L, _P, _L, _P],
 }
 _RESTYPE = {"vf4_last_error_string": ctypes.c_char_p, "vf4_attn_workspace_size": ctypes.c_int64,
-            "vf4_attn_workspace_size_ex": ctypes.c_int64, "vf4_attn_workspace_size_modes": ctypes.c_int64}
+            "vf4_attn_workspace_size_ex": ctypes.c_int64, "vf4_attn_workspace_size_modes": ctypes.c_int64,
+            "vf4_b_scale_image_bytes": ctypes.c_int64}
 
 
 class VitFp4Error(RuntimeError):

@@ -235,8 +235,9 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
 
 def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packed: torch.Tensor,
          b_sf: torch.Tensor, b_gs: torch.Tensor, bias: torch.Tensor | None = None,
-         out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-    """(M, K/2) x (N, K/2) packed NVFP4 with swizzled scales -> (M, N) out_dtype (+bias)."""
+         out_dtype: torch.dtype = torch.bfloat16, b_image: torch.Tensor | None = None) -> torch.Tensor:
+    """(M, K/2) x (N, K/2) packed NVFP4 with swizzled scales -> (M, N) out_dtype (+bias); ``b_image``
+    (``b_scale_image`` of b_sf) speeds the K > 1024 kernel up."""
     _need_cuda(a_packed, b_packed)
     a, b = _u8(a_packed), _u8(b_packed)
     M, Kh = a.shape
@@ -255,9 +256,15 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
             bb = bias.to(torch.bfloat16).contiguous()
             epi = _lib.VF4_EPI_BIAS
     with _Timed(f"gemm_{'bias' if epi else 'none'}_{M}x{N}x{K}", 2.0 * M * N * K):
-        _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
-                  _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
-                  _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
+        if b_image is None:
+            _lib.call("vf4_gemm_nvfp4", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                      _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi, _ptr(out),
+                      _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, _stream())
+        else:
+            _lib.call("vf4_gemm_nvfp4_ex", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                      _ptr(_u8(b_sf)), _ptr(_u8(b_image)), _ptr(b_gs.float().contiguous()), M, N, K, _ptr(bb), epi,
+                      _ptr(out), _lib.VF4_F32 if od == torch.float32 else _lib.VF4_BF16, None, None, None, None,
+                      None, _stream())
     _launched()
     if post_bias is not None:
         out += post_bias
@@ -266,11 +273,24 @@ def gemm(a_packed: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, b_packe
     return out
 
 
+def b_scale_image(b_sf: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """The B scale image of an (N, K) weight's to_blocked scales (``vf4_b_scale_image``): with it the
+    streaming GEMM kernel (K > 1024, N >= 256) copies each K64 block's B scales into tensor memory
+    with one instruction instead of two.  Build it once per weight."""
+    sf = _u8(b_sf)
+    _need_cuda(sf)
+    img = torch.empty(int(_lib.lib().vf4_b_scale_image_bytes(N, K)), dtype=torch.uint8, device=sf.device)
+    _lib.call("vf4_b_scale_image", _ptr(sf), N, K, _ptr(img), _stream())
+    _launched()
+    return img
+
+
 def gemm_residual(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, residual: torch.Tensor,
-                  gamma: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                  gamma: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  b_image: torch.Tensor | None = None) -> torch.Tensor:
     """``residual + gamma * (A @ B^T + bias)`` in bf16 with the unfused block's roundings (GEMM
     result, bias add, LayerScale product and residual add each round to bf16); ``out`` may be
-    ``residual`` itself."""
+    ``residual`` itself; ``b_image`` (``b_scale_image`` of b_sf) speeds the K > 1024 kernel up."""
     _need_cuda(a_packed, b_packed, residual)
     a, b = _u8(a_packed), _u8(b_packed)
     M, Kh = a.shape
@@ -281,9 +301,15 @@ def gemm_residual(a_packed, a_sf, a_gs, b_packed, b_sf, b_gs, bias, residual: to
     bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
     gg = None if gamma is None else gamma.to(torch.bfloat16).contiguous()
     with _Timed(f"gemm_residual_{M}x{N}x{Kh * 2}", 2.0 * M * N * Kh * 2):
-        _lib.call("vf4_gemm_nvfp4_residual", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
-                  _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb), _ptr(residual),
-                  _ptr(gg), _ptr(out), _stream())
+        if b_image is None:
+            _lib.call("vf4_gemm_nvfp4_residual", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                      _ptr(_u8(b_sf)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb), _ptr(residual),
+                      _ptr(gg), _ptr(out), _stream())
+        else:
+            _lib.call("vf4_gemm_nvfp4_ex", _ptr(a), _ptr(_u8(a_sf)), _ptr(a_gs.float().contiguous()), _ptr(b),
+                      _ptr(_u8(b_sf)), _ptr(_u8(b_image)), _ptr(b_gs.float().contiguous()), M, N, Kh * 2, _ptr(bb),
+                      _lib.VF4_EPI_BIAS_RESIDUAL, _ptr(out), _lib.VF4_BF16, None, None, None, _ptr(residual),
+                      _ptr(gg), _stream())
     _launched()
     return out
 

@@ -59,7 +59,7 @@ class FusedNVFP4Block(nn.Module):
             wp2, wsf2, proj_l.w_global_scale, proj_l.bias, proj_l.x_global_scale, _gamma(self.ls1),
             self.norm2.weight, self.norm2.bias, float(self.norm2.eps),
             _u8(mlp.w1q), _u8(mlp.w1sf), mlp.w1g, mlp.b1, _u8(mlp.w2q), _u8(mlp.w2sf), mlp.w2g, mlp.b2, mlp.gx, mlp.gh,
-            _gamma(self.ls2), int(a.num_heads), float(a.scaling), qk, pv, bool(mlp.exact_gelu))
+            _gamma(self.ls2), int(a.num_heads), float(a.scaling), qk, pv, bool(mlp.exact_gelu), mlp.w2_image())
 
     @torch.no_grad()
     def _calibrate(self, x: torch.Tensor) -> None:
@@ -134,7 +134,7 @@ def fused_block_op(x: torch.Tensor, n1w: torch.Tensor, n1b: torch.Tensor, eps1: 
                    w1sf: torch.Tensor, w1g: torch.Tensor, b1: torch.Tensor | None, w2q: torch.Tensor,
                    w2sf: torch.Tensor, w2g: torch.Tensor, b2: torch.Tensor | None, gx: torch.Tensor,
                    gh: torch.Tensor, ls2: torch.Tensor | None, num_heads: int, scaling: float, qk: str, pv: str,
-                   exact_gelu: bool) -> torch.Tensor:
+                   exact_gelu: bool, w2img: torch.Tensor | None = None) -> torch.Tensor:
     """One converted transformer block on the fused kernels (FusedNVFP4Block.forward after calibration):
     (B, S, C) -> (B, S, C) bf16."""
     B, S, C = x.shape
@@ -146,13 +146,14 @@ def fused_block_op(x: torch.Tensor, n1w: torch.Tensor, n1b: torch.Tensor, eps1: 
     # x + ls1(y) -> norm2 -> NVFP4 with the MLP's static gx; the new residual x_mid is written once
     hp, hsf, gxx, x_mid = ops.ln_cast(x2, n2w, n2b, eps2, gs=gx, y=y, gamma=ls1)
     gp, gsf = ops.gemm_gelu_nvfp4(hp, hsf, gxx, w1q, w1sf, w1g, b1, gh, exact=exact_gelu)
-    out = ops.gemm_residual(gp, gsf, gh, w2q, w2sf, w2g, b2, x_mid, gamma=ls2, out=x_mid)
+    out = ops.gemm_residual(gp, gsf, gh, w2q, w2sf, w2g, b2, x_mid, gamma=ls2, out=x_mid, b_image=w2img)
     return out.reshape(B, S, C)
 
 
 @fused_block_op.register_fake
 def _(x, n1w, n1b, eps1, qkv_wp, qkv_wsf, qkv_wg, qkv_b, qkv_xg, proj_wp, proj_wsf, proj_wg, proj_b, proj_xg, ls1,
-      n2w, n2b, eps2, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, ls2, num_heads, scaling, qk, pv, exact_gelu):
+      n2w, n2b, eps2, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, ls2, num_heads, scaling, qk, pv, exact_gelu,
+      w2img=None):
     return x.new_empty(x.shape, dtype=torch.bfloat16)
 
 

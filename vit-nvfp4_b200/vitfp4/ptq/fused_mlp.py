@@ -48,17 +48,17 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
 def fused_mlp_op(x: torch.Tensor, w1q: torch.Tensor, w1sf: torch.Tensor, w1g: torch.Tensor,
                  b1: torch.Tensor | None, w2q: torch.Tensor, w2sf: torch.Tensor, w2g: torch.Tensor,
                  b2: torch.Tensor | None, gx: torch.Tensor, gh: torch.Tensor, k1: int, n2: int,
-                 exact_gelu: bool = True) -> torch.Tensor:
+                 exact_gelu: bool = True, w2img: torch.Tensor | None = None) -> torch.Tensor:
     M = x.numel() // k1
     x2 = x.reshape(M, k1)
     ap, asf, _, _ = ops.cast(x2, gx, "six")
     hp, hsf = ops.gemm_gelu_nvfp4(ap, asf, gx, _u8(w1q), _u8(w1sf), w1g, b1, gh, exact=exact_gelu)
-    y = ops.gemm(hp, hsf, gh, _u8(w2q), _u8(w2sf), w2g, bias=b2, out_dtype=torch.bfloat16)
+    y = ops.gemm(hp, hsf, gh, _u8(w2q), _u8(w2sf), w2g, bias=b2, out_dtype=torch.bfloat16, b_image=w2img)
     return y.reshape(*x.shape[:-1], n2)
 
 
 @fused_mlp_op.register_fake
-def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2, exact_gelu=True):
+def _(x, w1q, w1sf, w1g, b1, w2q, w2sf, w2g, b2, gx, gh, k1, n2, exact_gelu=True, w2img=None):
     return x.new_empty(*x.shape[:-1], n2, dtype=torch.bfloat16)
 
 
@@ -86,6 +86,24 @@ class FusedNVFP4MLP(nn.Module):
         self.n2 = fc2.out_features
         self.register_buffer("gx", None)
         self.register_buffer("gh", None)
+        self._w2img = None       # (w2sf version stamp, B scale image of w2sf): derived, not saved
+
+    def w2_image(self) -> torch.Tensor:
+        """fc2's B scale image (``ops.b_scale_image`` of w2sf), rebuilt when w2sf moves, is written in
+        place (tracked by its version counter; inference tensors have none) or is loaded from a
+        state_dict."""
+        try:
+            version = self.w2sf._version
+        except RuntimeError:
+            version = None
+        stamp = (self.w2sf.data_ptr(), version, self.w2sf.device)
+        if self._w2img is None or self._w2img[0] != stamp:
+            self._w2img = (stamp, ops.b_scale_image(self.w2sf, self.n2, self.w2q.shape[1] * 2))
+        return self._w2img[1]
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        self._w2img = None
+        super()._load_from_state_dict(*args, **kwargs)
 
     @torch.no_grad()
     def _calibrate(self, x: torch.Tensor) -> None:
@@ -101,7 +119,7 @@ class FusedNVFP4MLP(nn.Module):
             self._calibrate(x)
         return fused_mlp_op(x.to(torch.bfloat16) if x.dtype != torch.bfloat16 else x,
                             self.w1q, self.w1sf, self.w1g, self.b1, self.w2q, self.w2sf, self.w2g,
-                            self.b2, self.gx, self.gh, self.k1, self.n2, self.exact_gelu)
+                            self.b2, self.gx, self.gh, self.k1, self.n2, self.exact_gelu, self.w2_image())
 
     def extra_repr(self) -> str:
         return f"in={self.k1}, hidden={self.w1q.shape[0]}, out={self.n2}, nvfp4=W4A4+gelu_fused"
