@@ -380,7 +380,8 @@ def _graph_time(fn, iters: int, repeats: int = 3) -> float:
 
 
 def gemm_sweep(shapes, M: int, peaks: dict, label: str, with_cast: bool = True) -> list:
-    """Cast (static global) and GEMM (plain bf16 output) at (M, K, N) per shape, plus cuBLASLt's
+    """Cast (static global) and GEMM (plain bf16 output; with the weight's B scale image, which the
+    K > 1024 kernel uses as the model's fc2 does) at (M, K, N) per shape, plus cuBLASLt's
     torch._scaled_mm_v2 on the same packed operands.  Activations N(0,1) bf16 with 0.1% of channels
     x20 (seeded), weights N(0, 0.02).  Buffers rotate so each call's working set misses L2."""
     import torch
@@ -400,6 +401,7 @@ def gemm_sweep(shapes, M: int, peaks: dict, label: str, with_cast: bool = True) 
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
         gx = ops.global_scale(ops.amax(x))
         wp, wsf, _, wg = ops.cast(w, None, "mse")
+        wimg = ops.b_scale_image(wsf, N, K)   # the weight's B scale image, as the model's fused MLPs hold it
         ap, asf, _, ag = ops.cast(x, gx, "six")
         ws_bytes = M * K * 2 + M * K // 2 + M * N * 2
         R = max(1, -(-3 * 128 * 2 ** 20 // ws_bytes))          # working set of R rotations > 3 x L2
@@ -422,9 +424,9 @@ def gemm_sweep(shapes, M: int, peaks: dict, label: str, with_cast: bool = True) 
             row["cast_frac_hbm"] = round(gbs / hbm, 4)
 
         def gemm_call(i):
-            _lib.call("vf4_gemm_nvfp4", aps[i % R].data_ptr(), asfs[i % R].data_ptr(), ag.data_ptr(), wp.data_ptr(),
-                      wsf.data_ptr(), wg.data_ptr(), M, N, K, None, _lib.VF4_EPI_NONE, outs[i % R].data_ptr(),
-                      _lib.VF4_BF16, None, None, None, stream())
+            _lib.call("vf4_gemm_nvfp4_ex", aps[i % R].data_ptr(), asfs[i % R].data_ptr(), ag.data_ptr(), wp.data_ptr(),
+                      wsf.data_ptr(), wimg.data_ptr(), wg.data_ptr(), M, N, K, None, _lib.VF4_EPI_NONE,
+                      outs[i % R].data_ptr(), _lib.VF4_BF16, None, None, None, None, None, stream())
         ms = _graph_time(gemm_call, 20)
         tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
         row.update(gemm_ms=round(ms, 4), gemm_tflops=round(tf, 1), gemm_frac_fp4_nominal=round(tf / FP4_NOMINAL_TFLOPS, 4),

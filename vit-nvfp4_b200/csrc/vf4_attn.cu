@@ -2063,7 +2063,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1)
     float* sv = sk + g.skp;                             // per head-dim column
     const uint8_t* rk = gb + g.raw_k;
     const uint8_t* rv = gb + g.raw_v;
-    const int S = g.S, D = g.D;
+    const int S = g.S;
     const int nvb = (S + 15) / 16;
     const int b0 = cs * nvb / kSlices, b1 = (cs + 1) * nvb / kSlices;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
@@ -3561,13 +3561,8 @@ static int launch_bf16(const void* q, const void* k, const void* v, int64_t B, i
 //   warps 14-17  the rows past 256 (idle when S <= 256)
 // ---------------------------------------------------------------------------------------
 constexpr int kB16sExtraMax = 2, kB16sWarps = 18;
-#ifndef VF4_B16S_ROLES
-#define VF4_B16S_ROLES 0
-#endif
-// first warp of each role (the warp scheduler favours lower warp ids when several are ready)
-constexpr int kB16sSoftW = VF4_B16S_ROLES == 0 ? 2 : VF4_B16S_ROLES == 1 ? 6 : 10;
-constexpr int kB16sEpiW = VF4_B16S_ROLES == 0 ? 10 : VF4_B16S_ROLES == 1 ? 14 : 2;
-constexpr int kB16sTailW = VF4_B16S_ROLES == 0 ? 14 : VF4_B16S_ROLES == 1 ? 2 : 6;
+// first warp of each role (other orders of the roles measured the same)
+constexpr int kB16sSoftW = 2, kB16sEpiW = 10, kB16sTailW = 14;
 constexpr uint32_t kB16sBarTail = 1;   // named barrier id of the tail warps
 // Working storage of the rows past 256 (floats): p [2][272], o partials [16][2][64],
 // per-warp maxima and sums [4][2][2]
@@ -3800,7 +3795,7 @@ __global__ void __launch_bounds__(kB16sWarps * 32, 1)
     const int nchunk = g.skp / 16;
     bool ok = true;
     for (int i = sl; i < T; i += 2) {
-      const int j = i / nt, t = i - j * nt, hb = j & 1;
+      const int t = i - i / nt * nt;
       const bool wact = t * 128 + qd * 32 < S;   // any query row of this warp's quadrant valid
       if (ok) ok = mbar_wait(s_full(sl), (uint32_t)(i >> 1) & 1u, err, kDevErrTimeoutFull);
       tc_fence_after();
