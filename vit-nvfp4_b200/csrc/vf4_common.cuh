@@ -463,8 +463,9 @@ VF4_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
 VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
   constexpr float kP = 0.3275911f * 0.70710678118654752f;   // p / sqrt 2
   constexpr float kS = 0.84932180028801904272f;              // sqrt(log2(e) / 2)
-  constexpr float kA1 = 0.5f * 0.254829592f, kA2 = 0.5f * -0.284496736f, kA3 = 0.5f * 1.421413741f,
-                  kA4 = 0.5f * -1.453152027f, kA5 = 0.5f * 1.061405429f;
+  // -0.5 a_k: the polynomial comes out negated, -E / exp(-x^2 / 2), exactly (RN is sign-symmetric)
+  constexpr float kA1 = -0.5f * 0.254829592f, kA2 = -0.5f * -0.284496736f, kA3 = -0.5f * 1.421413741f,
+                  kA4 = -0.5f * -1.453152027f, kA5 = -0.5f * 1.061405429f;
   float x0, x1;
   f32x2_unpack(x2, &x0, &x1);
   // |x| capped below +inf, so that |x| * exp(-x^2 / 2) is 0 rather than inf * 0 for x = +-inf; the
@@ -490,7 +491,7 @@ VF4_DEV unsigned long long gelu_erf_x2(unsigned long long x2) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(-q1));
   const unsigned long long m = mul_f32x2(z, f32x2_pack(e0, e1));              // |x| exp(-x^2 / 2)
   const unsigned long long relu = f32x2_pack(fmaxf(x0, 0.f), fmaxf(x1, 0.f));
-  return fma_f32x2(m, poly ^ 0x8000000080000000ull, relu);                  // relu(x) - |x| E
+  return fma_f32x2(m, poly, relu);                                          // relu(x) - |x| E
 }
 
 // Offset of scale factor (row r, column c) inside the 128x4-tiled ("to_blocked") layout.

@@ -131,6 +131,60 @@ VF4_DEV void fill_rcp_tab(float* tab, int et, float s_enc) {
   if (et >= 0 && et < 128) tab[et] = __fdiv_rn(s_enc, e4m3_to_f32((uint32_t)et));
 }
 
+// NVFP4 "six" cast and store of one warp's 32-row slab of GELU outputs: row row0 + lane, columns
+// [col0, col0 + NC); make_h(blk, col, h) writes the 16 fp32 values of the slab's block blk (columns
+// col .. col + 15).  The cast is the Triton cast's arithmetic (triton_cast.py:318-340): block scale
+// e4m3(min(RN(amax / 6) * s_enc, 448)), values times rcp_tab[scale byte] = RN(s_enc / scale),
+// nearest-even E2M1.  Packed codes (NC/2 bytes per row) are staged in shared memory with the 64-byte
+// (NC = 128) or 32-byte (NC = 64) swizzle, so a warp's 16-byte stores spread over all banks, and
+// stored by TMA; the 4-byte scale words go straight to the 128x4-tiled layout.
+template <int NC, class MakeH>
+VF4_DEV void nvfp4_slab_store(MakeH&& make_h, const GemmParams& p, const CUtensorMap* tmOut, int row0, int col0,
+                              int lane, float esenc, uint32_t ebuf, uint8_t* ebuf_g, const float* rcp_tab) {
+  const int64_t row = (int64_t)row0 + lane;
+  if (lane == 0) bulk_wait_read();
+  __syncwarp();
+#pragma unroll
+  for (int g4 = 0; g4 < NC / 64; ++g4) {
+    uint32_t sfw = 0;
+    uint64_t pk[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int blk = g4 * 4 + b;
+      const int col = col0 + blk * 16;
+      uint64_t packed = 0;
+      if (col < p.N) {
+        float h[16];
+        make_h(blk, col, h);
+        const float bs_f = fminf(__fmul_rn(div6_rn(fmaxf(amax16(h), 1e-12f)), esenc), 448.f);
+        const uint32_t sf = f32_to_e4m3(bs_f);
+        packed = encode16_inv(h, rcp_tab[sf], sf == 0u);
+        if (row < p.M) sfw |= sf << (8 * b);
+      }
+      pk[b] = packed;
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int c = g4 * 2 + hh;   // 16-byte chunk of the row
+      const int cs = NC == 128 ? (c ^ ((lane >> 1) & 3)) : (c ^ ((lane >> 2) & 1));
+      *reinterpret_cast<uint4*>(ebuf_g + lane * (NC / 2) + (cs << 4)) =
+          make_uint4((uint32_t)pk[2 * hh], (uint32_t)(pk[2 * hh] >> 32), (uint32_t)pk[2 * hh + 1],
+                     (uint32_t)(pk[2 * hh + 1] >> 32));
+    }
+    const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
+    if (col0 + g4 * 64 < p.N && row < (((int64_t)p.M + 127) & ~int64_t(127))) {
+      int64_t off = ((row >> 7) * p.out_ncb + (c0 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+      *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
+    }
+  }
+  fence_async_shared();
+  __syncwarp();
+  if (lane == 0 && col0 < p.N) {
+    tma_store_2d(tmOut, ebuf, col0 / 2, row0);
+    bulk_commit();
+  }
+}
+
 // Epilogue for one warp's 32-row slab of a tile: v holds this lane's NC accumulator columns
 // [col0, col0 + NC) of row row0 + lane; ebuf is the warp's 4 KB staging buffer.
 template <int NC, int EPI, bool kF32, int CW = 64>
@@ -228,37 +282,21 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
     //    + b1 in bf16 (gemm_packed's bf16 output, then y1 + b1), erf-GELU in fp32 on that bf16
     //    value (the Triton cast's apply_gelu, triton_cast.py:302-303), then the cast.
     //  * VF4_EPI_GELU_NVFP4: fp32 acc * gs_a * gs_b + b1 without roundings, tanh-form GELU.
-    // The cast is the Triton cast's arithmetic (triton_cast.py:318-340): block scale
-    // e4m3(min(RN(amax / 6) * s_enc, 448)), values times rcp_tab[scale byte] = RN(s_enc / scale),
-    // nearest-even E2M1.  Element pairs go through the packed fp32 ops (fma / mul.rn.f32x2, the
-    // scalar ops' roundings); bias_f, when the caller staged the bias in shared memory, holds fp32
-    // values (tanh form) or bf16 pairs (erf form).
-    // Packed codes (NC/2 bytes per row) are staged in shared memory with the 64-byte (NC = 128)
-    // or 32-byte (NC = 64) swizzle, so a warp's 16-byte stores spread over all banks, and stored
-    // by TMA; the 4-byte scale words go straight to the 128x4-tiled layout.
-    if (lane == 0) bulk_wait_read();
-    __syncwarp();
+    // Element pairs go through the packed fp32 ops (fma / mul.rn.f32x2, the scalar ops' roundings);
+    // bias_f, when the caller staged the bias in shared memory, holds fp32 values (tanh form) or
+    // bf16 pairs (erf form).
     const unsigned long long alpha2 = f32x2_pack(alpha, alpha);
-#pragma unroll
-    for (int g4 = 0; g4 < NC / 64; ++g4) {
-      uint32_t sfw = 0;
-      uint64_t pk[4];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int blk = g4 * 4 + b;
-        const int col = col0 + blk * 16;
-        uint64_t packed = 0;
-        if (col < p.N) {
-          float h[16];
+    nvfp4_slab_store<NC>(
+        [&](int blk, int col, float* h) {
           if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {
             uint32_t bw[8];
-            const bool has_bias = bias_f != nullptr || p.bias != nullptr;
+            const bool has_bias = p.bias != nullptr;
             if (bias_f) {
               const uint4* bp = reinterpret_cast<const uint4*>(bias_f) + blk * 2;
               const uint4 b0 = bp[0], b1 = bp[1];
               bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
               bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
-            } else if (p.bias) {
+            } else if (has_bias) {
               const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
               const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
               bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
@@ -299,33 +337,8 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
               f32x2_unpack(gelu_tanh_x2(a2), &h[2 * i], &h[2 * i + 1]);
             }
           }
-          const float bs_f = fminf(__fmul_rn(div6_rn(fmaxf(amax16(h), 1e-12f)), esenc), 448.f);
-          const uint32_t sf = f32_to_e4m3(bs_f);
-          packed = encode16_inv(h, rcp_tab[sf], sf == 0u);
-          if (row < p.M) sfw |= sf << (8 * b);
-        }
-        pk[b] = packed;
-      }
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int c = g4 * 2 + hh;   // 16-byte chunk of the row
-        const int cs = NC == 128 ? (c ^ ((lane >> 1) & 3)) : (c ^ ((lane >> 2) & 1));
-        *reinterpret_cast<uint4*>(ebuf_g + lane * (NC / 2) + (cs << 4)) =
-            make_uint4((uint32_t)pk[2 * hh], (uint32_t)(pk[2 * hh] >> 32), (uint32_t)pk[2 * hh + 1],
-                       (uint32_t)(pk[2 * hh + 1] >> 32));
-      }
-      const int c0 = (col0 >> 4) + g4 * 4;  // first scale column of this group (multiple of 4)
-      if (col0 + g4 * 64 < p.N && row < (((int64_t)p.M + 127) & ~int64_t(127))) {
-        int64_t off = ((row >> 7) * p.out_ncb + (c0 >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
-        *reinterpret_cast<uint32_t*>(p.out_sf + off) = sfw;  // rows >= M write the zero padding
-      }
-    }
-    fence_async_shared();
-    __syncwarp();
-    if (lane == 0 && col0 < p.N) {
-      tma_store_2d(tmOut, ebuf, col0 / 2, row0);
-      bulk_commit();
-    }
+        },
+        p, tmOut, row0, col0, lane, esenc, ebuf, ebuf_g, rcp_tab);
   }
 }
 
@@ -753,6 +766,33 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar);
+      if constexpr (EPI == VF4_EPI_GELU_ERF_NVFP4) {
+        // The reference's bf16 values x = RN(RN(acc * alpha) + b1) first, for the whole slab: the
+        // slab then lives in NC/2 registers of bf16 pairs through the GELU and the cast.
+        const unsigned long long alpha2 = f32x2_pack(alpha, alpha);
+        const uint4* bp = reinterpret_cast<const uint4*>(bias_f) + part * NC / 8;
+        uint32_t y[NC / 2];
+#pragma unroll
+        for (int i = 0; i < NC / 8; ++i) {
+          const uint4 bb = bp[i];
+          const uint32_t b4[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = 8 * i + 2 * k;
+            const uint32_t r = bf16x2_round(mul_f32x2(f32x2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), alpha2));
+            y[4 * i + k] = p.bias ? add_bf16x2(r, b4[k]) : r;
+          }
+        }
+        nvfp4_slab_store<NC>(
+            [&](int blk, int, float* h) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f32x2_unpack(gelu_erf_x2(bf16x2_to_f32x2(y[blk * 8 + i])), &h[2 * i], &h[2 * i + 1]);
+            },
+            p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, esenc,
+            epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES, gbase + (epi0 - base) + (warp - 2) * C::EPI_WARP_BYTES,
+            rcp_tab);
+        continue;
+      }
       epilogue_slab<NC, EPI, kF32, C::EPI_CW>(v, p, &tmOut, mb * 128 + q * 32, nb * BN + part * NC, lane, alpha,
                                                egs, esenc,
                                    epi0 + (uint32_t)(warp - 2) * C::EPI_WARP_BYTES,
