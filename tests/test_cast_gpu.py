@@ -230,3 +230,28 @@ def test_cast_full_size_sampled_rows():
     assert np.array_equal(packed[rows.cuda()].cpu().numpy(), oracle.pack_e2m1(c))
     sf_full = oracle.from_blocked(sfs.cpu().numpy(), M, K // 16)
     assert np.array_equal(sf_full[rows.numpy()], b)
+
+
+@pytest.mark.parametrize("M,K,ld,mode,dtype,gelu", [
+    (50432, 3072, 3072, "six", "bf16", False),    # BASELINE config-2 cast
+    (1025, 80, 80, "mse", "f32", False),
+    (300, 768, 1024, "six", "bf16", False),       # strided rows
+    (197, 512, 512, "six", "bf16", True),         # GELU + bias prologue
+])
+def test_cast_index_widths_agree(M, K, ld, mode, dtype, gelu, monkeypatch):
+    """The cast runs with 32-bit indices whenever every offset of the call fits; the 64-bit kernel
+    (kept for larger tensors, forced here with VF4_CAST_INDEX64) writes the same bytes."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    full = torch.randn(M, ld, device="cuda", generator=g)
+    xt = (full if dtype == "f32" else full.to(torch.bfloat16))[:, :K]
+    bias = (torch.randn(K, device="cuda", generator=g) * 0.1).to(xt.dtype) if gelu else None
+    gs = torch.tensor(float(xt.float().abs().max()) / 2688.0, device="cuda")
+    outs = []
+    for force64 in (False, True):
+        if force64:
+            monkeypatch.setenv("VF4_CAST_INDEX64", "1")
+        packed, sfs, sfl, _ = _ops().cast(xt, gs, mode, gelu=gelu, bias=bias, swizzled=True, linear=True)
+        torch.cuda.synchronize()
+        outs.append((packed.cpu(), sfs.cpu(), sfl.cpu()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)

@@ -191,35 +191,39 @@ __global__ void global_scale_kernel(const float* amax, float denom, float* gs) {
 template <typename T, bool kGelu, bool kBias>
 constexpr bool kBf16Exact = std::is_same<T, __nv_bfloat16>::value && !kGelu && !kBias;
 
-template <typename T, bool kMse, bool kGelu, bool kBias>
-__global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int64_t M, int64_t K,
-                                                   int64_t ld, const float* __restrict__ gs_ptr,
+// I: the index type, int32_t when every flat index and element offset of the call fits (the
+// launcher checks), else int64_t; 32-bit index arithmetic takes about a tenth of the kernel's
+// instructions off.
+template <typename T, bool kMse, bool kGelu, bool kBias, typename I = int64_t>
+__global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int64_t M_, int64_t K_,
+                                                   int64_t ld_, const float* __restrict__ gs_ptr,
                                                    const T* __restrict__ bias,
                                                    uint8_t* __restrict__ out_packed,
                                                    uint8_t* __restrict__ sf_swz,
                                                    uint8_t* __restrict__ sf_lin) {
-  const int64_t nb = K / 16;
-  const int64_t nb4 = (nb + 3) & ~int64_t(3);
-  const int64_t ncb = nb4 >> 2;
-  const int64_t Mp = (M + 127) & ~int64_t(127);
-  const int64_t total = Mp * nb4;
+  const I M = (I)M_, K = (I)K_, ld = (I)ld_;
+  const I nb = K / 16;
+  const I nb4 = (nb + 3) & ~I(3);
+  const I ncb = nb4 >> 2;
+  const I Mp = (M + 127) & ~I(127);
+  const I total = Mp * nb4;
   const float gs = *gs_ptr;
   const float s_enc = __fdiv_rn(1.0f, gs);
   const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const I stride = (I)gridDim.x * (I)blockDim.x;
   // (row, blk) of this thread's flat index, advanced by the grid stride without dividing
-  const int64_t t_first = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t d_row = stride / nb4, d_blk = stride - d_row * nb4;
-  int64_t row = t_first / nb4, blk = t_first - row * nb4;
+  const I t_first = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x;
+  const I d_row = stride / nb4, d_blk = stride - d_row * nb4;
+  I row = t_first / nb4, blk = t_first - row * nb4;
   Raw16<T> raw;
   if (t_first < total && row < M && blk < nb) load_raw16<T>(x + row * ld + blk * 16, raw);
-  for (int64_t t0 = t_first - lane; t0 < total; t0 += stride) {
-    const int64_t t = t0 + lane;
+  for (I t0 = t_first - lane; t0 < total; t0 += stride) {
+    const I t = t0 + lane;
     const bool in_grid = t < total;
     const bool valid = in_grid && row < M && blk < nb;
     const Raw16<T> cur = raw;
     // the next item of this thread, loaded now and used in the next iteration
-    int64_t nrow = row + d_row, nblk = blk + d_blk;
+    I nrow = row + d_row, nblk = blk + d_blk;
     if (nblk >= nb4) {
       nblk -= nb4;
       ++nrow;
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
     w |= __shfl_xor_sync(0xffffffffu, w, 1);
     w |= __shfl_xor_sync(0xffffffffu, w, 2);
     if (sf_swz && in_grid && (blk & 3) == 0) {
-      int64_t off = ((row >> 7) * ncb + (blk >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+      const I off = ((row >> 7) * ncb + (blk >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
       *reinterpret_cast<uint32_t*>(sf_swz + off) = w;
     }
     row = nrow;
@@ -354,8 +358,18 @@ static void launch_cast(const void* x, int64_t M, int64_t K, int64_t ld, const f
                         const void* bias, uint8_t* op, uint8_t* sfs, uint8_t* sfl, cudaStream_t s) {
   int64_t nb4 = ((K / 16) + 3) & ~int64_t(3);
   int64_t Mp = (M + 127) & ~int64_t(127);
-  cast_kernel<T, kMse, kGelu, kBias><<<grid_for(Mp * nb4), 256, 0, s>>>(
-      static_cast<const T*>(x), M, K, ld, gs, static_cast<const T*>(bias), op, sfs, sfl);
+  const int grid = grid_for(Mp * nb4);
+  // 32-bit indices when the flat block index (plus one grid stride), the element offsets of x and
+  // the byte offsets of the codes and scales all stay below 2^31 (VF4_CAST_INDEX64 set in the
+  // environment keeps the 64-bit kernel, which the tests compare with the 32-bit one)
+  const int64_t lim = int64_t(1) << 31;
+  if (Mp * nb4 + (int64_t)grid * 256 < lim && Mp * (ld > K ? ld : K) < lim && Mp * nb4 * 16 < lim &&
+      !getenv("VF4_CAST_INDEX64"))
+    cast_kernel<T, kMse, kGelu, kBias, int32_t><<<grid, 256, 0, s>>>(
+        static_cast<const T*>(x), M, K, ld, gs, static_cast<const T*>(bias), op, sfs, sfl);
+  else
+    cast_kernel<T, kMse, kGelu, kBias, int64_t><<<grid, 256, 0, s>>>(
+        static_cast<const T*>(x), M, K, ld, gs, static_cast<const T*>(bias), op, sfs, sfl);
 }
 
 template <typename T>

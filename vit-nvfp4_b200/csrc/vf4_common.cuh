@@ -272,8 +272,9 @@ VF4_DEV uint32_t bf16x2_round(unsigned long long p) {
   return r;
 }
 
+// The fast path is computed whatever dec is and then checked once, together with dec's range (one
+// branch to the exact path instead of two); out of range its codes are discarded.
 VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
-  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode16_exact_call(v, dec);
   float inv;
   asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
   const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
@@ -291,13 +292,13 @@ VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
     wa[h] = cvt_e2m1x8(a);
     wb[h] = cvt_e2m1x8(b);
   }
-  if ((wa[0] != wb[0]) | (wa[1] != wb[1])) return encode16_exact_call(v, dec);
+  const bool fast = (dec >= 0x1p-120f) & (dec <= dec_max) & (wa[0] == wb[0]) & (wa[1] == wb[1]);
+  if (!fast) return encode16_exact_call(v, dec);
   return (uint64_t)wa[0] | ((uint64_t)wa[1] << 32);
 }
 
 // Half a block (8 values) with the bracketing scheme of encode16_bracket.
 VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
-  if (!(dec >= 0x1p-120f && dec <= dec_max)) return encode8_exact_call(v, dec);
   float inv;
   asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
   const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
@@ -310,7 +311,8 @@ VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
     f32x2_unpack(fma_f32x2(x2, hi2, z2), &b[2 * i], &b[2 * i + 1]);
   }
   const uint32_t wa = cvt_e2m1x8(a), wb = cvt_e2m1x8(b);
-  return wa == wb ? wa : encode8_exact_call(v, dec);
+  const bool fast = (dec >= 0x1p-120f) & (dec <= dec_max) & (wa == wb);
+  return fast ? wa : encode8_exact_call(v, dec);
 }
 
 // Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
