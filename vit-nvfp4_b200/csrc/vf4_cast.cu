@@ -202,6 +202,13 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
                                                    uint8_t* __restrict__ sf_swz,
                                                    uint8_t* __restrict__ sf_lin) {
   const I M = (I)M_, K = (I)K_, ld = (I)ld_;
+  // six rule: {dec, lo, hi} of every scale byte (scale_entry), looked up per block
+  __shared__ float4 s_q[kMse ? 1 : 128];
+  if constexpr (!kMse) {
+    const float gsv = *gs_ptr;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) s_q[i] = scale_entry((uint32_t)i, gsv);
+    __syncthreads();
+  }
   const I nb = K / 16;
   const I nb4 = (nb + 3) & ~I(3);
   const I ncb = nb4 >> 2;
@@ -235,9 +242,17 @@ __global__ void __launch_bounds__(256) cast_kernel(const T* __restrict__ x, int6
       raw16_to_f32<T>(cur, v);
       prologue16<T, kGelu, kBias>(v, bias, blk * 16);
       // bf16 inputs are >= 2^-133 in magnitude when non-zero (see encode16_bracket)
-      BlockQ q = quantize_block<kMse>(v, gs, s_enc, kBf16Exact<T, kGelu, kBias> ? 0x1p17f : 2.0f);
-      *reinterpret_cast<uint64_t*>(out_packed + row * (K / 2) + blk * 8) = q.packed;
-      sf = q.sf;
+      constexpr float dec_max = kBf16Exact<T, kGelu, kBias> ? 0x1p17f : 2.0f;
+      uint64_t packed;
+      if constexpr (kMse) {
+        const BlockQ q = quantize_block<kMse>(v, gs, s_enc, dec_max);
+        packed = q.packed;
+        sf = q.sf;
+      } else {   // quantize_block's six rule with the table
+        sf = six_code(amax16(v), s_enc);
+        packed = encode16_bracket_q(v, s_q[sf], dec_max);
+      }
+      *reinterpret_cast<uint64_t*>(out_packed + row * (K / 2) + blk * 8) = packed;
       if (sf_lin) sf_lin[row * nb + blk] = (uint8_t)sf;
     }
     // merge the 4 scale bytes of an aligned lane quad (same row, blk%4 = 0..3)
@@ -447,6 +462,11 @@ __global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_
   // (consecutive lanes read consecutive 16 bytes: conflict-free)
   __shared__ float4 s_wb[NC * 128];
   __shared__ float4 s_g[kRes ? NC * 64 : 1];
+  __shared__ float4 s_q[kMode != 0 ? 128 : 1];   // {dec, lo, hi} per scale byte (scale_entry)
+  if constexpr (kMode != 0) {
+    const float gsv = *gs_ptr;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) s_q[i] = scale_entry((uint32_t)i, gsv);
+  }
   for (int i = threadIdx.x; i < NC * 128; i += blockDim.x) {
     const int e = 256 * (i >> 7) + 8 * (i & 31) + 2 * ((i >> 5) & 3);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -629,18 +649,18 @@ __global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_
         lane_amax = fmaxf(lane_amax, am);
       } else {
         const float bam = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-        float dec;
-        const uint32_t sf = six_scale(bam, s_enc, gs, &dec);
-        const uint32_t codes = encode8_bracket(h, dec, 0x1p17f);   // h is bf16-rounded
+        const uint32_t sf = six_code(bam, s_enc);
+        const uint32_t codes = encode8_bracket_q(h, s_q[sf], 0x1p17f);   // h is bf16-rounded
         if (in) *reinterpret_cast<uint32_t*>(out_packed + row * code_ld + e0 / 2) = codes;
-        // scale bytes of SF columns 16c + 4g .. +3 live in lanes 8g, 8g+2, 8g+4, 8g+6
-        uint32_t b1 = __shfl_down_sync(0xffffffffu, sf, 2);
-        uint32_t b2 = __shfl_down_sync(0xffffffffu, sf, 4);
-        uint32_t b3 = __shfl_down_sync(0xffffffffu, sf, 6);
+        // scale bytes of SF columns 16c + 4g .. +3 live in lanes 8g, 8g+2, 8g+4, 8g+6 (a lane pair
+        // holds one block's byte): each lane places its byte, two xor-shuffles OR the four together
+        uint32_t w = sf << (8 * ((lane >> 1) & 3));
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        w |= __shfl_xor_sync(0xffffffffu, w, 4);
         if (in && (lane & 7) == 0) {
           const int col = e0 / 16;
           *reinterpret_cast<uint32_t*>(out_sf + ((row >> 7) * ncb + (col >> 2)) * 512 + (row & 31) * 16 +
-                                       ((row >> 5) & 3) * 4) = sf | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                                       ((row >> 5) & 3) * 4) = w;
         }
       }
     }

@@ -272,12 +272,19 @@ VF4_DEV uint32_t bf16x2_round(unsigned long long p) {
   return r;
 }
 
-// The fast path is computed whatever dec is and then checked once, together with dec's range (one
-// branch to the exact path instead of two); out of range its codes are discarded.
-VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
+// The bracketing multipliers lo < 1/dec < hi of the encoders below.
+VF4_DEV void bracket_mults(float dec, float* lo, float* hi) {
   float inv;
   asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
-  const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
+  *lo = __fmul_rn(inv, 1.0f - 0x1p-20f);
+  *hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
+}
+
+// The fast path is computed whatever dec is and then checked once, together with dec's range (one
+// branch to the exact path instead of two); out of range its codes are discarded.  q = {dec, lo,
+// hi} (bracket_mults of dec): the form whose caller looked them up in a per-scale-byte table.
+VF4_DEV uint64_t encode16_bracket_q(const float* v, float4 q, float dec_max) {
+  const float dec = q.x, lo = q.y, hi = q.z;
   const unsigned long long lo2 = f32x2_pack(lo, lo), hi2 = f32x2_pack(hi, hi), z2 = f32x2_pack(0.f, 0.f);
   uint32_t wa[2], wb[2];
 #pragma unroll
@@ -297,11 +304,15 @@ VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
   return (uint64_t)wa[0] | ((uint64_t)wa[1] << 32);
 }
 
+VF4_DEV uint64_t encode16_bracket(const float* v, float dec, float dec_max) {
+  float lo, hi;
+  bracket_mults(dec, &lo, &hi);
+  return encode16_bracket_q(v, make_float4(dec, lo, hi, 0.f), dec_max);
+}
+
 // Half a block (8 values) with the bracketing scheme of encode16_bracket.
-VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
-  float inv;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(inv) : "f"(dec));
-  const float lo = __fmul_rn(inv, 1.0f - 0x1p-20f), hi = __fmul_rn(inv, 1.0f + 0x1p-20f);
+VF4_DEV uint32_t encode8_bracket_q(const float* v, float4 q, float dec_max) {
+  const float dec = q.x, lo = q.y, hi = q.z;
   const unsigned long long lo2 = f32x2_pack(lo, lo), hi2 = f32x2_pack(hi, hi), z2 = f32x2_pack(0.f, 0.f);
   float a[8], b[8];
 #pragma unroll
@@ -313,6 +324,12 @@ VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
   const uint32_t wa = cvt_e2m1x8(a), wb = cvt_e2m1x8(b);
   const bool fast = (dec >= 0x1p-120f) & (dec <= dec_max) & (wa == wb);
   return fast ? wa : encode8_exact_call(v, dec);
+}
+
+VF4_DEV uint32_t encode8_bracket(const float* v, float dec, float dec_max) {
+  float lo, hi;
+  bracket_mults(dec, &lo, &hi);
+  return encode8_bracket_q(v, make_float4(dec, lo, hi, 0.f), dec_max);
 }
 
 // Epilogue encoding: quotient by reciprocal multiply and hardware nearest-even rounding
@@ -384,6 +401,20 @@ VF4_DEV float div6_rn(float a) {
   const float y = 0.16666667163372039795f;   // RN(1/6) = 0x3E2AAAAB
   const float q = __fmul_rn(a, y);
   return __fmaf_rn(__fmaf_rn(-q, 6.0f, a), y, q);
+}
+
+// The six rule's E4M3 scale byte of a block with maximum |x| amax (0 .. 126).
+VF4_DEV uint32_t six_code(float amax, float s_enc) {
+  return f32_to_e4m3(fminf(__fmul_rn(div6_rn(fmaxf(amax, 1e-12f)), s_enc), 448.f));
+}
+
+// {dec, lo, hi} of scale byte b under the global scale gs: the decode scale six_scale returns and
+// its bracketing multipliers, for a per-CTA table indexed by the scale byte.
+VF4_DEV float4 scale_entry(uint32_t b, float gs) {
+  const float dec = __fmul_rn(e4m3_to_f32(b), gs);
+  float lo, hi;
+  bracket_mults(dec, &lo, &hi);
+  return make_float4(dec, lo, hi, 0.f);
 }
 
 VF4_DEV uint32_t six_scale(float amax, float s_enc, float gs, float* dec) {
