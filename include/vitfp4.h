@@ -100,7 +100,9 @@ VF4_API int vf4_gelu_erf_f32(const float* x, int64_t n, float* out, vf4_stream_t
  *   bias     : optional (K,) vector of the same dtype added before GELU / quantization
  *   out_packed (M, K/2); out_sf_swizzled (ceil128(M)*ceil4(K/16) bytes, pads zeroed) and/or
  *   out_sf_linear (M, K/16) — either may be NULL; gs_out (1 fp32) receives the scale used
- *   (may be NULL when gs != NULL). */
+ *   (may be NULL when gs != NULL).
+ * Calls whose flat block index and offsets all fit in 31 bits run a kernel with 32-bit index
+ * arithmetic; the environment variable VF4_CAST_INDEX64 keeps the 64-bit kernel (same bytes). */
 VF4_API int vf4_cast_nvfp4(const void* x, int dtype, int64_t M, int64_t K, int64_t ld, const float* gs,
                    int block_select, int gelu, const void* bias, uint8_t* out_packed,
                    uint8_t* out_sf_swizzled, uint8_t* out_sf_linear, float* gs_out,
