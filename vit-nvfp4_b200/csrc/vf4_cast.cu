@@ -458,10 +458,10 @@ __global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_
     uint8_t* out_packed, uint8_t* __restrict__ out_sf) {
   static_assert(!(kRes && kMode == 2), "the statistics pass runs without the residual");
   // s_wb[(4c + j) * 32 + l] = {w[e], w[e+1], b[e], b[e+1]}, e = 256c + 8l + 2j
-  // s_g [(2c + j) * 32 + l] = {g[e], .., g[e+3]},          e = 256c + 8l + 4j
-  // (consecutive lanes read consecutive 16 bytes: conflict-free)
+  // s_g [(2c + j) * 32 + l] = {g[e], .., g[e+3]} as two bf16 pairs, e = 256c + 8l + 4j
+  // (consecutive lanes read consecutive 16 / 8 bytes: conflict-free)
   __shared__ float4 s_wb[NC * 128];
-  __shared__ float4 s_g[kRes ? NC * 64 : 1];
+  __shared__ uint2 s_g[kRes ? NC * 64 : 1];
   __shared__ float4 s_q[kMode != 0 ? 128 : 1];   // {dec, lo, hi} per scale byte (scale_entry)
   if constexpr (kMode != 0) {
     const float gsv = *gs_ptr;
@@ -481,10 +481,12 @@ __global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_
   if constexpr (kRes) {
     for (int i = threadIdx.x; i < NC * 64; i += blockDim.x) {
       const int e = 256 * (i >> 6) + 8 * (i & 31) + 4 * ((i >> 5) & 1);
-      float4 v = make_float4(1.f, 1.f, 1.f, 1.f);
-      if (gamma && e < K)
-        v = make_float4(__bfloat162float(gamma[e]), __bfloat162float(gamma[e + 1]), __bfloat162float(gamma[e + 2]),
-                        __bfloat162float(gamma[e + 3]));
+      uint2 v = make_uint2(0x3F803F80u, 0x3F803F80u);   // 1.0 pairs
+      if (gamma && e < K) {
+        const uint32_t g0 = __bfloat16_as_ushort(gamma[e]), g1 = __bfloat16_as_ushort(gamma[e + 1]),
+                       g2 = __bfloat16_as_ushort(gamma[e + 2]), g3 = __bfloat16_as_ushort(gamma[e + 3]);
+        v = make_uint2(g0 | (g1 << 16), g2 | (g3 << 16));
+      }
       s_g[i] = v;
     }
   }
@@ -564,14 +566,13 @@ __global__ void __launch_bounds__(256, (LnCfg<NC, kRes, kMode>::kMinBlocks)) ln_
             uint32_t rw[4];
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
-              const float4 g4 = s_g[(2 * c + jj) * 32 + lane];
-              const unsigned long long g2[2] = {f32x2_pack(g4.x, g4.y), f32x2_pack(g4.z, g4.w)};
+              const uint2 gg = s_g[(2 * c + jj) * 32 + lane];
+              const uint32_t g2[2] = {gg.x, gg.y};
 #pragma unroll
               for (int t = 0; t < 2; ++t) {
                 const int i = 2 * jj + t;
-                // x' = bf16(x + bf16(y * gamma))
-                const uint32_t yg = bf16x2_round(mul_f32x2(bf16x2_to_f32x2(yw[i]), g2[t]));
-                rw[i] = bf16x2_round(add_f32x2(bf16x2_to_f32x2(xw[i]), bf16x2_to_f32x2(yg)));
+                // x' = bf16(x + bf16(y * gamma)) in bf16 pair arithmetic (the same roundings)
+                rw[i] = add_bf16x2(xw[i], mul_bf16x2(yw[i], g2[t]));
                 if constexpr (kHold) v[c][i] = bf16x2_to_f32x2(rw[i]);
               }
             }

@@ -485,6 +485,15 @@ VF4_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
   return d;
 }
 
+// RN(a * b) of two bf16 pairs.  The exact product of two bf16 values has at most 16 significant
+// bits, so the fp32 product is exact (outside fp32's subnormal range) and torch's bf16 multiply (an
+// fp32 multiply, then one rounding to bf16) gives the same bf16 value.
+VF4_DEV uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // erf-GELU, 0.5 x (1 + erf(x / sqrt 2)), on an element pair in packed fp32 arithmetic.  Since erf
 // is odd, gelu(x) = relu(x) - |x| E with E = 0.5 erfc(|x| / sqrt 2), and E comes from Abramowitz &
 // Stegun 7.1.26 (|error of erf| <= 1.5e-7):
