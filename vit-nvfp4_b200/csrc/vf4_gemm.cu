@@ -229,41 +229,33 @@ VF4_DEV void epilogue_slab(const uint32_t* v, const GemmParams& p, const CUtenso
 #pragma unroll
         for (int j = 0; j < CW / 8; ++j) {
           const int col = colc + j * 8;
-          float y[8];
+          // bf16 pair arithmetic with the reference's roundings: RN(acc * alpha) (the bf16 GEMM
+          // output), + b in bf16, then for the residual form RN(y * gamma) and RN(x + that); each
+          // bf16 pair op rounds the exact result once, as torch's bf16 ops do (fp32 op, one rounding)
+          const unsigned long long alpha2 = f32x2_pack(alpha, alpha);
+          uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[c * CW + j * 8 + i]) * alpha;
+          for (int i = 0; i < 4; ++i)
+            w[i] = bf16x2_round(mul_f32x2(f32x2_pack(__uint_as_float(v[c * CW + j * 8 + 2 * i]),
+                                                     __uint_as_float(v[c * CW + j * 8 + 2 * i + 1])), alpha2));
           if (EPI != VF4_EPI_NONE && p.bias && col < p.N) {
-            // the reference rounds the GEMM to bf16, then adds the bf16 bias in bf16
-            uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+            const uint4 bw = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
             const uint32_t b4[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              y[2 * i] = bf16_round(y[2 * i]) + bf16_lo(b4[i]);
-              y[2 * i + 1] = bf16_round(y[2 * i + 1]) + bf16_hi(b4[i]);
-            }
+            for (int i = 0; i < 4; ++i) w[i] = add_bf16x2(w[i], b4[i]);
           }
           if constexpr (EPI == VF4_EPI_BIAS_RESIDUAL) {
-            // x + ls(y): round y, round the LayerScale product, add the residual (rounded below);
-            // this lane's 8 residual values are 16 contiguous bytes of its row
+            // x + ls(y); this lane's 8 residual values are 16 contiguous bytes of its row
             uint4 rw = make_uint4(0, 0, 0, 0);
             if (row < p.M && col < p.N) rw = *reinterpret_cast<const uint4*>(p.res + row * p.N + col);
             const uint32_t r4[4] = {rw.x, rw.y, rw.z, rw.w};
             uint32_t g4[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};   // 1.0 pairs
             if (p.gamma && col < p.N) {
-              uint4 gw = __ldg(reinterpret_cast<const uint4*>(p.gamma + col));
+              const uint4 gw = __ldg(reinterpret_cast<const uint4*>(p.gamma + col));
               g4[0] = gw.x; g4[1] = gw.y; g4[2] = gw.z; g4[3] = gw.w;
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              y[2 * i] = bf16_lo(r4[i]) + bf16_round(bf16_round(y[2 * i]) * bf16_lo(g4[i]));
-              y[2 * i + 1] = bf16_hi(r4[i]) + bf16_round(bf16_round(y[2 * i + 1]) * bf16_hi(g4[i]));
-            }
-          }
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
-            w[i] = *reinterpret_cast<uint32_t*>(&h);
+            for (int i = 0; i < 4; ++i) w[i] = add_bf16x2(r4[i], mul_bf16x2(w[i], g4[i]));
           }
           const int js = CW == 64 ? (j ^ (lane & 7)) : CW == 32 ? (j ^ ((lane >> 1) & 3)) : (j ^ ((lane >> 2) & 1));
           *reinterpret_cast<uint4*>(ebuf_g + lane * (2 * CW) + js * 16) = make_uint4(w[0], w[1], w[2], w[3]);
